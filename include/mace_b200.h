@@ -1,0 +1,243 @@
+/*
+ * mace_b200.h -- C ABI of the B200 MACE energy + forces + virial step.
+ *
+ * This is the boundary a Python (ctypes) or any other FFI caller binds to.
+ * Plain pointers and sizes only; no torch or C++ types cross it.  Every entry
+ * point returns a status code (MACE_OK == 0); on failure the message is kept
+ * in a thread-local buffer readable with mace_last_error().
+ *
+ * The entry points replace the reference's compute path, which is Python on
+ * MLX (mace_mlx, v0.5.0):
+ *   mace_nl_build           <- calculators.py:51-62, 292-317  (_build_neighbor_list,
+ *                              matscipy/ASE "ijS" list with cutoff r_max + skin)
+ *   mace_forward_backward   <- calculators.py:431-483 (energy + forces through
+ *                              mx.value_and_grad of model.py:440-483) and
+ *                              calculators.py:489-570 (virial through the
+ *                              symmetric displacement); the model body is
+ *                              model.py:373-438 with blocks.py / the op modules
+ *   mace_ctx_create         <- model.py:664-720 (load_model: config.json +
+ *                              weights.npz) -- the host packs the converted
+ *                              weights into the flat tables described below
+ *
+ * Conventions
+ *   - All device pointers are caller-owned device memory on the context's
+ *     device.  Hot calls allocate nothing; scratch lives in the context's
+ *     workspace, sized by mace_ctx_reserve().
+ *   - Edges are directed (sender -> receiver), sorted by receiver, with a
+ *     CSR row pointer over receivers and, for every edge, the index of its
+ *     reverse edge (j -> i, -S).  mace_nl_build produces exactly this.
+ *     v_e = pos[receiver] - pos[sender] + shift_e @ cell  (reference utils.py:47-84).
+ *   - One context per device; contexts are independent (no global state
+ *     except the per-thread error string).  Calls on one context must not
+ *     overlap in time on different streams.
+ */
+#ifndef MACE_B200_H
+#define MACE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define MACE_OK 0
+#define MACE_ERR_BAD_ARG 1
+#define MACE_ERR_CUDA 2
+#define MACE_ERR_NL_OVERFLOW 3
+#define MACE_ERR_TIMEOUT 4
+#define MACE_ERR_NCCL 5
+#define MACE_ERR_UNSUPPORTED 6
+#define MACE_ERR_EDGES 7
+
+#define MACE_ABI_VERSION 1
+
+/* limits of the packed model description */
+#define MACE_MAX_LAYERS 4
+#define MACE_MAX_IN 4     /* irrep slots of a node-feature table (l <= 3)      */
+#define MACE_MAX_MID 24   /* conv_tp output slots per layer                   */
+#define MACE_MAX_SRC 6    /* mid slots feeding one interaction-linear output  */
+#define MACE_MAX_CORR 3   /* symmetric-contraction correlation order          */
+
+/* flags of mace_forward_backward */
+#define MACE_WANT_FORCES 1
+#define MACE_WANT_VIRIAL 2
+
+typedef struct mace_ctx mace_ctx;
+
+/* Offsets below index the float table `floats` (f_*) or the int table `ints`
+ * (i_*) of mace_model_desc.  Node-feature tables are stored channel-last per
+ * irrep slot: row n, slot s, component m, channel u at
+ * n*dim + off[s] + m*C + u.  Weights have their path weights folded in. */
+
+typedef struct {
+  int32_t n;                      /* number of slots                    */
+  int32_t l[MACE_MAX_IN];         /* degree of each slot                */
+  int32_t off[MACE_MAX_IN];       /* offset of each slot within a row   */
+  int32_t dim;                    /* row length = C * sum(2l+1)         */
+} mace_slots;
+
+typedef struct {
+  int32_t l1, l2, l3;             /* degrees of x1 (node), Y (edge), out */
+  int32_t src;                    /* input slot of x1                   */
+  int32_t off;                    /* offset of this slot in the mid row */
+  int32_t m_off;                  /* offset of its (2l1+1)(2l3+1) block in a per-edge M row */
+  int64_t f_cg;                   /* path-weighted 3j, (2l1+1)(2l2+1)(2l3+1) */
+} mace_conv_slot;
+
+typedef struct {
+  int32_t n_src;                  /* mid slots with this degree         */
+  int32_t src[MACE_MAX_SRC];      /* their indices                      */
+  int64_t f_w;                    /* (n_src*C, C) row-major, concat-K   */
+  int64_t f_wt;                   /* (C, n_src*C) transpose             */
+} mace_lin_group;
+
+typedef struct {
+  int32_t L;                      /* output degree                      */
+  int32_t corr;                   /* correlation order                  */
+  int32_t K[MACE_MAX_CORR];       /* number of paths for nu = 1..corr   */
+  int64_t f_w[MACE_MAX_CORR];     /* (num_elements, K, C) for nu = 1..corr */
+  int32_t nnz[MACE_MAX_CORR];     /* non-zeros of U_nu                  */
+  int64_t i_idx[MACE_MAX_CORR];   /* packed indices of the non-zeros    */
+  int64_t f_val[MACE_MAX_CORR];   /* values of the non-zeros            */
+} mace_sc_out;
+
+typedef struct {
+  int32_t C;                      /* channels (multiplicity)            */
+  int32_t residual;               /* 1: skip before message; 0: skip on message */
+  mace_slots in;                  /* layer input irreps                 */
+  mace_slots hid;                 /* product output irreps              */
+  mace_slots mid;                 /* conv_tp output row: only `dim` is used (slots are in conv[]) */
+  mace_slots inter;               /* interaction irreps 0..lmax         */
+  /* skip_tp: species-indexed (num_elements, C, C) blocks per pair in->out */
+  int32_t n_skip;
+  int32_t skip_in[MACE_MAX_IN], skip_out[MACE_MAX_IN];
+  int64_t f_skip[MACE_MAX_IN], f_skip_t[MACE_MAX_IN];
+  /* linear_up: one (C, C) block per input slot (1-to-1) */
+  int64_t f_up[MACE_MAX_IN], f_up_t[MACE_MAX_IN];
+  /* radial MLP */
+  int32_t n_mlp;                  /* number of Linear layers            */
+  int32_t mlp_w[8];               /* widths: in, hidden..., out         */
+  int64_t f_mlp[7], f_mlp_t[7];   /* (in, out) and (out, in) per layer   */
+  /* conv_tp */
+  int32_t n_mid;
+  int32_t m_tot;                  /* length of a per-edge M row          */
+  int32_t wnumel;                 /* per-edge weights = n_mid * C        */
+  mace_conv_slot conv[MACE_MAX_MID];
+  /* interaction linear (mid -> inter), one group per output degree */
+  mace_lin_group lin[MACE_MAX_IN];
+  /* symmetric contraction: one entry per hidden slot */
+  mace_sc_out sc[MACE_MAX_IN];
+  /* product linear: one (C, C) block per hidden slot */
+  int64_t f_prod[MACE_MAX_IN], f_prod_t[MACE_MAX_IN];
+  /* readout */
+  int32_t readout_nonlinear;
+  int32_t readout_hidden;         /* 16 */
+  int64_t f_ro1;                  /* linear: (C); nonlinear: (C, hidden) */
+  int64_t f_ro2;                  /* nonlinear: (hidden)                 */
+} mace_layer_desc;
+
+typedef struct {
+  int32_t abi_version;            /* MACE_ABI_VERSION                    */
+  int32_t num_layers;
+  int32_t num_elements;
+  int32_t num_bessel;
+  int32_t max_ell;                /* <= 3                                */
+  int32_t poly_p;
+  int32_t scale_shift;            /* 1: ScaleShiftMACE energy assembly   */
+  int32_t C;
+  float r_max;
+  float inv_avg_num_neighbors;
+  float scale, shift;
+  int64_t f_e0;                   /* (num_elements) atomic energies      */
+  int64_t f_emb;                  /* (num_elements, C) embedding, 1/sqrt(E) folded */
+  int64_t f_bessel;               /* (num_bessel) frequencies            */
+  int64_t f_sh;                   /* SH recursion tensors T_2, T_3       */
+  mace_layer_desc layers[MACE_MAX_LAYERS];
+  const float* floats; int64_t n_floats;    /* host pointers, copied at create */
+  const int32_t* ints; int64_t n_ints;
+} mace_model_desc;
+
+/* Device pointers describing one (batch of) structure(s). */
+typedef struct {
+  int64_t n_nodes;
+  int64_t n_edges;
+  int32_t num_graphs;
+  const float* pos;               /* (n_nodes, 3)                        */
+  const float* cell;              /* (9) row-major lattice vectors, may be NULL if no shifts */
+  const int32_t* species;         /* (n_nodes) model element index       */
+  const int32_t* graph_ptr;       /* (num_graphs + 1) node ranges per graph */
+  const int32_t* sender;          /* (n_edges)                           */
+  const int32_t* receiver;        /* (n_edges) non-decreasing            */
+  const int32_t* shifts;          /* (n_edges, 3) integer lattice shifts */
+  const int32_t* row_ptr;         /* (n_nodes + 1) CSR over receivers    */
+  const int32_t* rev;             /* (n_edges) index of the reverse edge */
+} mace_system;
+
+/* Device pointers receiving the results (NULL = not wanted). */
+typedef struct {
+  double* energy;                 /* (num_graphs)                        */
+  float* node_energy;             /* (n_nodes)                           */
+  float* forces;                  /* (n_nodes, 3) = -dE/dpos              */
+  double* virial;                 /* (9) sum_e v_e (x) dE/dv_e (un-symmetrised) */
+} mace_outputs;
+
+/* Message of the last failed call on this thread (always NUL-terminated). */
+int mace_last_error(char* buf, size_t len);
+
+/* Copy the packed model to `device` and create a context. */
+int mace_ctx_create(const mace_model_desc* desc, int device, mace_ctx** out);
+int mace_ctx_destroy(mace_ctx* ctx);
+
+/* Size the workspace for systems up to max_nodes / max_edges (allocates; not a hot call). */
+int mace_ctx_reserve(mace_ctx* ctx, int64_t max_nodes, int64_t max_edges);
+
+/* Bytes of device workspace the context currently holds. */
+int mace_ctx_workspace_bytes(const mace_ctx* ctx, int64_t* bytes);
+
+/*
+ * Neighbour list on the GPU: every (i, j, S) with |x_j - x_i + S @ cell| < r_cut,
+ * except i == j with S == 0, restricted to pairs in the same graph; S is zero
+ * along non-periodic axes.  The distance test runs in float64.
+ *   pos        (n, 3) float64 device, cell (9) float64 device (ignored if no pbc)
+ *   pbc        three host ints
+ *   graph_ptr  (num_graphs + 1) int32 device
+ * Outputs (device, capacity entries): sender, receiver, shifts (capacity, 3),
+ * row_ptr (n + 1), rev.  Edges are sorted by (receiver, sender, S).
+ * *n_edges (host) receives the edge count.  Returns MACE_ERR_NL_OVERFLOW, with
+ * *n_edges set to the required capacity, when capacity is too small.
+ * Synchronises `stream` (the count is returned to the host).
+ */
+int mace_nl_build(mace_ctx* ctx, const double* pos, const double* cell, const int32_t* pbc,
+                  const int32_t* graph_ptr, int32_t num_graphs, int64_t n, double r_cut,
+                  int32_t* sender, int32_t* receiver, int32_t* shifts, int32_t* row_ptr,
+                  int32_t* rev, int64_t capacity, int64_t* n_edges, void* stream);
+
+/*
+ * One energy (+ forces, + virial) evaluation on `stream` (a cudaStream_t).
+ * Asynchronous: results are valid once the stream reaches this point.  An
+ * inconsistent reverse-edge index is recorded in the context's error flag
+ * (see mace_ctx_error_flag); the forces of the affected atoms are then wrong.
+ */
+int mace_forward_backward(mace_ctx* ctx, const mace_system* sys, const mace_outputs* out,
+                          int32_t flags, void* stream);
+
+/*
+ * Debug/parity access to an internal per-stage buffer after the last call:
+ * id = layer * 16 + stage (see mace_mlx_b200/native.py for the stage list).
+ * Returns the device pointer and length in floats.
+ */
+int mace_debug_buffer(mace_ctx* ctx, int32_t id, const float** ptr, int64_t* len);
+
+/* Number of kernel launches the last mace_forward_backward issued. */
+int mace_last_launch_count(const mace_ctx* ctx, int32_t* count);
+
+/* Synchronise the device, return and clear the context's device error flag
+ * (1 = an edge's reverse index did not point back to it). */
+int mace_ctx_error_flag(mace_ctx* ctx, int32_t* flag);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MACE_B200_H */

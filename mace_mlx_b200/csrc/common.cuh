@@ -1,0 +1,280 @@
+// Internal declarations shared by the CUDA translation units of libmace_b200.
+// Not part of the public ABI (include/mace_b200.h is).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/mace_b200.h"
+
+namespace mace {
+
+// ---------------------------------------------------------------------------
+// error plumbing (thread-local message, status codes of the C ABI)
+// ---------------------------------------------------------------------------
+void set_error(const std::string& msg);
+int fail(int code, const std::string& msg);
+
+#define MACE_CUDA_TRY(expr)                                                      \
+  do {                                                                           \
+    cudaError_t _e = (expr);                                                     \
+    if (_e != cudaSuccess)                                                       \
+      return ::mace::fail(MACE_ERR_CUDA, std::string(#expr) + ": " +            \
+                                             cudaGetErrorString(_e));          \
+  } while (0)
+
+#define MACE_LAUNCH_CHECK(name)                                                  \
+  do {                                                                           \
+    cudaError_t _e = cudaGetLastError();                                         \
+    if (_e != cudaSuccess)                                                       \
+      return ::mace::fail(MACE_ERR_CUDA, std::string("launch ") + name + ": " + \
+                                             cudaGetErrorString(_e));          \
+  } while (0)
+
+__host__ __device__ __forceinline__ int64_t imin64(int64_t a, int64_t b) { return a < b ? a : b; }
+
+__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
+__device__ __forceinline__ float silu_grad_f(float x) {
+  float s = 1.0f / (1.0f + expf(-x));
+  return s * (1.0f + x * (1.0f - s));
+}
+
+// ---------------------------------------------------------------------------
+// edge front end
+// ---------------------------------------------------------------------------
+struct EdgeParams {
+  int64_t E;
+  const float* pos;
+  const float* cell;  // may be null
+  const int32_t* snd;
+  const int32_t* rcv;
+  const int32_t* shifts;
+  int max_ell;
+  int nb;
+  float r_max;
+  int poly_p;
+  const float* bessel_w;  // (nb)
+  const float* sh_T;      // T2 (3*3*5) then T3 (5*3*7)
+  float* v;               // (E,3)
+  float* Y;               // (E,16)
+  float* b;               // (E,nb)
+  // backward
+  const float* dY;  // (E,16)
+  const float* db;  // (E,nb)
+  float* dv;        // (E,3)
+  double* virial_part;  // (gridDim, 9)
+};
+int launch_edge_fwd(const EdgeParams& p, cudaStream_t s);
+int launch_edge_bwd(const EdgeParams& p, int* n_blocks, cudaStream_t s);
+
+struct ForceParams {
+  int64_t N;
+  const int32_t* row_ptr;
+  const int32_t* snd;
+  const int32_t* rcv;
+  const int32_t* rev;
+  const float* dv;
+  float* forces;
+  int* err_flag;
+};
+int launch_forces(const ForceParams& p, cudaStream_t s);
+int launch_virial_reduce(const double* part, int n_part, double* out, cudaStream_t s);
+
+// ---------------------------------------------------------------------------
+// radial MLP
+// ---------------------------------------------------------------------------
+struct MlpParams {
+  int64_t E;
+  int n_layers;          // Linear layers (last has no activation)
+  int widths[8];         // in, hidden..., out
+  const float* w[7];     // (in, out) row-major
+  const float* wt[7];    // (out, in) row-major
+  const float* b;        // (E, widths[0])
+  float* act;            // (E, sum hidden) pre-activations of hidden layers
+  float* out;            // (E, widths[n_layers])
+  // backward
+  const float* dout;     // (E, widths[n_layers])
+  float* db;             // (E, widths[0]) accumulated (+=)
+};
+int launch_mlp_fwd(const MlpParams& p, cudaStream_t s);
+int launch_mlp_bwd(const MlpParams& p, cudaStream_t s);
+
+// ---------------------------------------------------------------------------
+// conv tensor product + segmented scatter (receiver CSR)
+// ---------------------------------------------------------------------------
+struct ConvSlotDev {
+  int l1, l2, l3, combo;
+  int src_off;   // offset of the x1 slot inside an input row
+  int src_ch;    // per-channel offset of x1 slot (sum of dims of earlier input slots)
+  int off;       // offset of the slot inside a mid row
+  int m_off;     // offset inside a per-edge M row
+  const float* cg;  // (2l1+1)(2l2+1)(2l3+1)
+};
+struct ConvParams {
+  int64_t N;
+  int C;
+  int n_mid;
+  int m_tot;
+  int wnumel;
+  int in_dim;
+  int in_ch;       // in_dim / C
+  int mid_dim;
+  ConvSlotDev slot[MACE_MAX_MID];
+  const int32_t* row_ptr;
+  const int32_t* snd;
+  const float* Y;        // (E,16)
+  const float* up;       // (N,in_dim)
+  const float* w;        // (E,wnumel)
+  float* A;              // (N,mid_dim)
+  // backward
+  const float* dA;       // (N,mid_dim)
+  float* dw;             // (E,wnumel)
+  float* dY;             // (E,16) accumulated
+  float* dup;            // (N,in_dim)
+};
+int launch_conv_fwd(const ConvParams& p, cudaStream_t s);
+int launch_conv_bwd(const ConvParams& p, cudaStream_t s);
+
+// ---------------------------------------------------------------------------
+// node-level ops
+// ---------------------------------------------------------------------------
+struct LinJob {
+  int d;            // 2l+1 rows per node
+  int n_k;          // number of C-wide input slots (concat-K)
+  int k_off[MACE_MAX_SRC];
+  int out_off;
+  int ldb;          // row stride of the weight matrix
+  const float* w;   // (n_k*C, ldb) row-major, first C columns used
+  float alpha;
+  int accumulate;
+};
+struct LinParams {
+  int64_t N;
+  int C;
+  const float* in;
+  int in_row;
+  float* out;
+  int out_row;
+  int n_jobs;
+  LinJob job[MACE_MAX_MID];
+};
+int launch_linear(const LinParams& p, cudaStream_t s);
+
+struct SkipParams {
+  int64_t N;
+  int C;
+  const int32_t* species;
+  const float* in;
+  int in_row;
+  float* out;
+  int out_row;
+  int n_jobs;
+  int d[MACE_MAX_IN];
+  int in_off[MACE_MAX_IN];
+  int out_off[MACE_MAX_IN];
+  const float* w[MACE_MAX_IN];  // (num_elements, C, C)
+  int accumulate;
+};
+int launch_skip(const SkipParams& p, cudaStream_t s);
+
+struct ScTabDev {
+  int nnz;
+  const int32_t* seg;   // (2L+2) segment starts by M
+  const int32_t* idx;   // packed M | i1<<4 | i2<<8 | i3<<12 | k<<16
+  const float* val;
+  const float* w;       // (num_elements, K, C)
+  int K;
+};
+struct ScParams {
+  int64_t N;
+  int C;
+  const int32_t* species;
+  const float* f;   // (N, ncoup*C) coupling-major rows
+  int ncoup;        // (max_ell+1)^2
+  int n_out;
+  int L[MACE_MAX_IN];
+  int corr[MACE_MAX_IN];
+  int out_off[MACE_MAX_IN];
+  ScTabDev tab[MACE_MAX_IN][MACE_MAX_CORR];
+  float* out;       // (N, out_row)
+  int out_row;
+  // backward
+  const float* dout;
+  float* df;        // (N, ncoup*C)
+};
+int launch_sc_fwd(const ScParams& p, cudaStream_t s);
+int launch_sc_bwd(const ScParams& p, cudaStream_t s);
+
+struct ReadoutParams {
+  int64_t N;
+  int C;
+  const float* h;
+  int h_row;
+  int nonlinear;
+  int hidden;
+  const float* w1;
+  const float* w2;
+  float* e;       // (N) readout energy of this layer
+  float* dh;      // (N, h_row) gradient seed (overwritten; zero outside the 0e slot)
+  float dscale;   // dE/d e
+};
+int launch_readout(const ReadoutParams& p, cudaStream_t s);
+
+struct EmbedParams {
+  int64_t N;
+  int C;
+  const int32_t* species;
+  const float* emb;
+  float* h;
+};
+int launch_embed(const EmbedParams& p, cudaStream_t s);
+
+struct EnergyParams {
+  int64_t N;
+  int num_graphs;
+  int T;
+  const int32_t* species;
+  const int32_t* graph_ptr;
+  const float* e0;
+  const float* e_layers;  // (T, N)
+  int scale_shift;
+  float scale, shift;
+  float* node_energy;
+  double* energy;
+};
+int launch_energy(const EnergyParams& p, cudaStream_t s);
+
+// ---------------------------------------------------------------------------
+// neighbour list
+// ---------------------------------------------------------------------------
+struct NlParams {
+  int64_t n;
+  const double* pos;
+  const double* cell;
+  const double* inv_cell;  // device (9)
+  int pbc[3];
+  double r_cut;
+  double reach[3];  // r_cut / (perpendicular width) per axis
+  const int32_t* graph_ptr;
+  int num_graphs;
+  const int32_t* node_graph;  // (n)
+  const int32_t* wrap;        // (n,3) floor of fractional coordinates
+  int32_t* count;             // (n+1)
+  int32_t* row_ptr;
+  int32_t* snd;
+  int32_t* rcv;
+  int32_t* shifts;
+  int32_t* rev;
+  int* err_flag;
+};
+int launch_nl_prep(const NlParams& p, int32_t* node_graph, int32_t* wrap, cudaStream_t s);
+int launch_nl_count(const NlParams& p, cudaStream_t s);
+int launch_nl_fill(const NlParams& p, cudaStream_t s);
+int launch_nl_rev(const NlParams& p, int64_t E, cudaStream_t s);
+int scan_counts(int32_t* count, int32_t* row_ptr, int64_t n, void* tmp, size_t tmp_bytes,
+                cudaStream_t s);
+size_t scan_tmp_bytes(int64_t n);
+
+}  // namespace mace

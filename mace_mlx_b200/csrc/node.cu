@@ -1,0 +1,374 @@
+// Node-level ops: o3.Linear (grouped per irrep degree, concat-K), the species-
+// indexed skip tensor product, the symmetric contraction and its backward,
+// readouts, the one-hot embedding and the energy assembly.
+//
+// Reference semantics:
+//   o3.Linear                      mace_mlx/linear.py:41-77, 421-446
+//   skip_tp (uvw with one-hot)     mace_mlx/tensor_product.py:1046-1305
+//   symmetric contraction          mace_mlx/symmetric_contraction.py:95-121, 505-595
+//   product block                  mace_mlx/blocks.py:493-537
+//   readouts                       mace_mlx/blocks.py:540-608
+//   energy assembly                mace_mlx/model.py:403-438, 550-589
+// Node-feature rows are channel-last per irrep slot (slot offset + m*C + u),
+// so a degree-l slot of N nodes is an (N*(2l+1), C) row-major matrix.
+#include "common.cuh"
+
+namespace mace {
+
+namespace {
+
+// ---------------------------------------------------------------------------
+// o3.Linear: out[(n,m), c] (+)= alpha * sum_{ks,u} in[n, k_off[ks] + m*C + u] * W[ks*C+u][c]
+// 64 x 128 output tile per 256-thread CTA, 8 x 4 outputs per thread.
+// ---------------------------------------------------------------------------
+constexpr int LR = 64;   // rows per tile
+constexpr int LK = 32;   // k chunk
+
+__global__ void __launch_bounds__(256) k_linear(LinParams p) {
+  __shared__ float sA[LK][LR + 1];
+  __shared__ __align__(16) float sB[LK][128];
+  const LinJob& jb = p.job[blockIdx.y];
+  const int C = p.C;
+  const int64_t rows = p.N * jb.d;
+  const int64_t r0 = (int64_t)blockIdx.x * LR;
+  if (r0 >= rows) return;
+  const int tid = threadIdx.x;
+  const int ty = tid >> 5, tx = tid & 31;
+  float acc[8][4];
+#pragma unroll
+  for (int a = 0; a < 8; ++a)
+#pragma unroll
+    for (int b = 0; b < 4; ++b) acc[a][b] = 0.f;
+  for (int ks = 0; ks < jb.n_k; ++ks) {
+    for (int kc = 0; kc < C; kc += LK) {
+#pragma unroll
+      for (int q = 0; q < (LR * LK) / 256; ++q) {
+        int idx = tid + 256 * q;
+        int r = idx / LK, kk = idx % LK;
+        int64_t row = r0 + r;
+        float v = 0.f;
+        if (row < rows) {
+          int64_t node = row / jb.d;
+          int m = (int)(row % jb.d);
+          v = p.in[node * p.in_row + jb.k_off[ks] + m * C + kc + kk];
+        }
+        sA[kk][r] = v;
+      }
+      for (int idx = tid; idx < LK * 128; idx += 256) {
+        int kk = idx >> 7, c = idx & 127;
+        sB[kk][c] = (c < C) ? __ldg(jb.w + (int64_t)(ks * C + kc + kk) * jb.ldb + c) : 0.f;
+      }
+      __syncthreads();
+#pragma unroll 8
+      for (int kk = 0; kk < LK; ++kk) {
+        float4 b4 = *reinterpret_cast<const float4*>(&sB[kk][tx * 4]);
+#pragma unroll
+        for (int a = 0; a < 8; ++a) {
+          float av = sA[kk][ty * 8 + a];
+          acc[a][0] = fmaf(av, b4.x, acc[a][0]);
+          acc[a][1] = fmaf(av, b4.y, acc[a][1]);
+          acc[a][2] = fmaf(av, b4.z, acc[a][2]);
+          acc[a][3] = fmaf(av, b4.w, acc[a][3]);
+        }
+      }
+      __syncthreads();
+    }
+  }
+#pragma unroll
+  for (int a = 0; a < 8; ++a) {
+    int64_t row = r0 + ty * 8 + a;
+    if (row >= rows) continue;
+    int64_t node = row / jb.d;
+    int m = (int)(row % jb.d);
+    float* o = p.out + node * p.out_row + jb.out_off + m * C;
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      int c = tx * 4 + b;
+      if (c < C) {
+        float v = jb.alpha * acc[a][b];
+        o[c] = jb.accumulate ? o[c] + v : v;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// skip_tp: out[n, out_off + m*C + w] (+)= sum_u in[n, in_off + m*C + u] * W[z_n][u][w]
+// one CTA per node, one thread per output channel
+// ---------------------------------------------------------------------------
+__global__ void k_skip(SkipParams p) {
+  extern __shared__ float sIn[];
+  const int64_t n = blockIdx.x;
+  const int C = p.C, w = threadIdx.x;
+  const int z = p.species[n];
+  for (int jb = 0; jb < p.n_jobs; ++jb) {
+    const int d = p.d[jb];
+    for (int q = w; q < d * C; q += blockDim.x) sIn[q] = p.in[n * p.in_row + p.in_off[jb] + q];
+    __syncthreads();
+    const float* W = p.w[jb] + (int64_t)z * C * C;
+    float acc[7];
+#pragma unroll
+    for (int m = 0; m < 7; ++m) acc[m] = 0.f;
+    for (int u = 0; u < C; ++u) {
+      float wv = __ldg(W + (int64_t)u * C + w);
+#pragma unroll
+      for (int m = 0; m < 7; ++m)
+        if (m < d) acc[m] = fmaf(sIn[m * C + u], wv, acc[m]);
+    }
+    float* o = p.out + n * p.out_row + p.out_off[jb] + w;
+#pragma unroll
+    for (int m = 0; m < 7; ++m)
+      if (m < d) o[m * C] = p.accumulate ? o[m * C] + acc[m] : acc[m];
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// symmetric contraction
+//   out[n][o][M][c] = sum_nu sum_{nz of U_nu with index M} U * W_nu[z_n][k][c] * prod f[n][c][i_a]
+// one CTA per node, one thread per channel; f and W staged per thread column.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int ix(int v, int sh) { return (v >> sh) & 15; }
+
+__global__ void k_sc_fwd(ScParams p) {
+  extern __shared__ float sm[];
+  const int C = p.C, c = threadIdx.x;
+  const int64_t n = blockIdx.x;
+  const int z = p.species[n];
+  const int nc = p.ncoup;
+  float* sf = sm;             // ncoup x C
+  float* sw = sm + 16 * C;    // sum_nu K_nu x C
+  for (int i = 0; i < nc; ++i) sf[i * C + c] = p.f[n * nc * C + i * C + c];
+  for (int o = 0; o < p.n_out; ++o) {
+    const int L = p.L[o], corr = p.corr[o];
+    int kofs[MACE_MAX_CORR];
+    int tot = 0;
+    for (int nu = 0; nu < corr; ++nu) {
+      kofs[nu] = tot;
+      const ScTabDev& t = p.tab[o][nu];
+      for (int k = 0; k < t.K; ++k) sw[(tot + k) * C + c] = __ldg(t.w + ((int64_t)z * t.K + k) * C + c);
+      tot += t.K;
+    }
+    for (int M = 0; M < 2 * L + 1; ++M) {
+      float acc = 0.f;
+      for (int nu = 0; nu < corr; ++nu) {
+        const ScTabDev& t = p.tab[o][nu];
+        const float* swn = sw + kofs[nu] * C + c;
+        const int b = __ldg(t.seg + M), e = __ldg(t.seg + M + 1);
+        for (int q = b; q < e; ++q) {
+          const int id = __ldg(t.idx + q);
+          float v = __ldg(t.val + q) * swn[(id >> 16) * C];
+          v *= sf[ix(id, 4) * C + c];
+          if (nu >= 1) v *= sf[ix(id, 8) * C + c];
+          if (nu >= 2) v *= sf[ix(id, 12) * C + c];
+          acc += v;
+        }
+      }
+      p.out[n * p.out_row + p.out_off[o] + M * C + c] = acc;
+    }
+  }
+}
+
+__global__ void k_sc_bwd(ScParams p) {
+  extern __shared__ float sm[];
+  const int C = p.C, c = threadIdx.x;
+  const int64_t n = blockIdx.x;
+  const int z = p.species[n];
+  const int nc = p.ncoup;
+  float* sf = sm;             // ncoup x C (16 rows reserved)
+  float* sdf = sm + 16 * C;   // ncoup x C
+  float* sw = sdf + 16 * C;
+  for (int i = 0; i < nc; ++i) {
+    sf[i * C + c] = p.f[n * nc * C + i * C + c];
+    sdf[i * C + c] = 0.f;
+  }
+  for (int o = 0; o < p.n_out; ++o) {
+    const int L = p.L[o], corr = p.corr[o];
+    int kofs[MACE_MAX_CORR];
+    int tot = 0;
+    for (int nu = 0; nu < corr; ++nu) {
+      kofs[nu] = tot;
+      const ScTabDev& t = p.tab[o][nu];
+      for (int k = 0; k < t.K; ++k) sw[(tot + k) * C + c] = __ldg(t.w + ((int64_t)z * t.K + k) * C + c);
+      tot += t.K;
+    }
+    for (int M = 0; M < 2 * L + 1; ++M) {
+      const float g = p.dout[n * p.out_row + p.out_off[o] + M * C + c];
+      for (int nu = 0; nu < corr; ++nu) {
+        const ScTabDev& t = p.tab[o][nu];
+        const float* swn = sw + kofs[nu] * C + c;
+        const int b = __ldg(t.seg + M), e = __ldg(t.seg + M + 1);
+        for (int q = b; q < e; ++q) {
+          const int id = __ldg(t.idx + q);
+          const float v = __ldg(t.val + q) * swn[(id >> 16) * C] * g;
+          const int a0 = ix(id, 4);
+          if (nu == 0) {
+            sdf[a0 * C + c] += v;
+          } else if (nu == 1) {
+            const int a1 = ix(id, 8);
+            const float f0 = sf[a0 * C + c], f1 = sf[a1 * C + c];
+            sdf[a0 * C + c] += v * f1;
+            sdf[a1 * C + c] += v * f0;
+          } else {
+            const int a1 = ix(id, 8), a2 = ix(id, 12);
+            const float f0 = sf[a0 * C + c], f1 = sf[a1 * C + c], f2 = sf[a2 * C + c];
+            sdf[a0 * C + c] += v * f1 * f2;
+            sdf[a1 * C + c] += v * f0 * f2;
+            sdf[a2 * C + c] += v * f0 * f1;
+          }
+        }
+      }
+    }
+  }
+  for (int i = 0; i < nc; ++i) p.df[n * nc * C + i * C + c] = sdf[i * C + c];
+}
+
+// ---------------------------------------------------------------------------
+// readout of one layer (warp per node) and its gradient seed
+// ---------------------------------------------------------------------------
+__global__ void k_readout(ReadoutParams p) {
+  const int64_t n = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (n >= p.N) return;
+  const float* h = p.h + n * p.h_row;
+  float* dh = p.dh + n * p.h_row;
+  for (int q = p.C + lane; q < p.h_row; q += 32) dh[q] = 0.f;
+  if (!p.nonlinear) {
+    float a = 0.f;
+    for (int c = lane; c < p.C; c += 32) {
+      a = fmaf(h[c], __ldg(p.w1 + c), a);
+      dh[c] = p.dscale * __ldg(p.w1 + c);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+    if (lane == 0) p.e[n] = a;
+    return;
+  }
+  const int H = p.hidden;  // <= 32
+  float z = 0.f;
+  // z_j for j = lane (lanes >= H idle)
+  for (int c = 0; c < p.C; ++c) {
+    float hv = h[c];
+    if (lane < H) z = fmaf(hv, __ldg(p.w1 + c * H + lane), z);
+  }
+  float e = 0.f, dz = 0.f;
+  if (lane < H) {
+    float w2 = __ldg(p.w2 + lane);
+    e = silu_f(z) * w2;
+    dz = p.dscale * w2 * silu_grad_f(z);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) e += __shfl_xor_sync(0xffffffffu, e, o);
+  if (lane == 0) p.e[n] = e;
+  for (int c = lane; c < p.C; c += 32) {
+    float a = 0.f;
+    for (int j = 0; j < H; ++j) a = fmaf(__ldg(p.w1 + c * H + j), __shfl_sync(0xffffffffu, dz, j), a);
+    dh[c] = a;
+  }
+}
+
+__global__ void k_embed(EmbedParams p) {
+  const int64_t n = blockIdx.x;
+  const int z = p.species[n];
+  for (int c = threadIdx.x; c < p.C; c += blockDim.x) p.h[n * p.C + c] = __ldg(p.emb + (int64_t)z * p.C + c);
+}
+
+__global__ void k_energy(EnergyParams p) {
+  __shared__ double red[256];
+  const int g = blockIdx.x;
+  const int64_t b = p.graph_ptr[g], e = p.graph_ptr[g + 1];
+  double acc = 0.0;
+  for (int64_t n = b + threadIdx.x; n < e; n += blockDim.x) {
+    float inter = 0.f;
+    for (int t = 0; t < p.T; ++t) inter += p.e_layers[t * p.N + n];
+    float e0 = __ldg(p.e0 + p.species[n]);
+    float ne = p.scale_shift ? e0 + (p.scale * inter + p.shift) : e0 + inter;
+    if (p.node_energy) p.node_energy[n] = ne;
+    acc += (double)ne;
+  }
+  red[threadIdx.x] = acc;
+  __syncthreads();
+  for (int w = blockDim.x / 2; w > 0; w >>= 1) {
+    if ((int)threadIdx.x < w) red[threadIdx.x] += red[threadIdx.x + w];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0 && p.energy) p.energy[g] = red[0];
+}
+
+}  // namespace
+
+int launch_linear(const LinParams& p, cudaStream_t s) {
+  if (p.N == 0 || p.n_jobs == 0) return MACE_OK;
+  if (p.C > 128 || p.C % 32 != 0) return fail(MACE_ERR_UNSUPPORTED, "linear: C must be a multiple of 32, <= 128");
+  int dmax = 1;
+  for (int j = 0; j < p.n_jobs; ++j) dmax = p.job[j].d > dmax ? p.job[j].d : dmax;
+  dim3 grid((unsigned)((p.N * dmax + LR - 1) / LR), (unsigned)p.n_jobs);
+  k_linear<<<grid, 256, 0, s>>>(p);
+  MACE_LAUNCH_CHECK("linear");
+  return MACE_OK;
+}
+
+int launch_skip(const SkipParams& p, cudaStream_t s) {
+  if (p.N == 0 || p.n_jobs == 0) return MACE_OK;
+  int dmax = 1;
+  for (int j = 0; j < p.n_jobs; ++j) dmax = p.d[j] > dmax ? p.d[j] : dmax;
+  size_t smem = (size_t)dmax * p.C * sizeof(float);
+  k_skip<<<(unsigned)p.N, p.C, smem, s>>>(p);
+  MACE_LAUNCH_CHECK("skip");
+  return MACE_OK;
+}
+
+static size_t sc_smem(const ScParams& p, int extra) {
+  int kmax = 0;
+  for (int o = 0; o < p.n_out; ++o) {
+    int tot = 0;
+    for (int nu = 0; nu < p.corr[o]; ++nu) tot += p.tab[o][nu].K;
+    kmax = tot > kmax ? tot : kmax;
+  }
+  return (size_t)(16 * extra + kmax) * p.C * sizeof(float);
+}
+
+int launch_sc_fwd(const ScParams& p, cudaStream_t s) {
+  if (p.N == 0) return MACE_OK;
+  size_t smem = sc_smem(p, 1);
+  if (smem > 48 * 1024)
+    MACE_CUDA_TRY(cudaFuncSetAttribute(k_sc_fwd, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  k_sc_fwd<<<(unsigned)p.N, p.C, smem, s>>>(p);
+  MACE_LAUNCH_CHECK("sc_fwd");
+  return MACE_OK;
+}
+
+int launch_sc_bwd(const ScParams& p, cudaStream_t s) {
+  if (p.N == 0) return MACE_OK;
+  size_t smem = sc_smem(p, 2);
+  if (smem > 48 * 1024)
+    MACE_CUDA_TRY(cudaFuncSetAttribute(k_sc_bwd, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  k_sc_bwd<<<(unsigned)p.N, p.C, smem, s>>>(p);
+  MACE_LAUNCH_CHECK("sc_bwd");
+  return MACE_OK;
+}
+
+int launch_readout(const ReadoutParams& p, cudaStream_t s) {
+  if (p.N == 0) return MACE_OK;
+  if (p.nonlinear && p.hidden > 32) return fail(MACE_ERR_UNSUPPORTED, "readout hidden width must be <= 32");
+  int64_t threads = p.N * 32;
+  k_readout<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(p);
+  MACE_LAUNCH_CHECK("readout");
+  return MACE_OK;
+}
+
+int launch_embed(const EmbedParams& p, cudaStream_t s) {
+  if (p.N == 0) return MACE_OK;
+  k_embed<<<(unsigned)p.N, 128, 0, s>>>(p);
+  MACE_LAUNCH_CHECK("embed");
+  return MACE_OK;
+}
+
+int launch_energy(const EnergyParams& p, cudaStream_t s) {
+  if (p.num_graphs == 0) return MACE_OK;
+  k_energy<<<(unsigned)p.num_graphs, 256, 0, s>>>(p);
+  MACE_LAUNCH_CHECK("energy");
+  return MACE_OK;
+}
+
+}  // namespace mace

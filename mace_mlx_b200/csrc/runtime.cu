@@ -1,0 +1,774 @@
+// Context, workspace and the C ABI of libmace_b200 (include/mace_b200.h).
+//
+// mace_forward_backward issues, on one stream, the whole energy + forces
+// (+ virial) step: edge features, then per interaction layer the node linears,
+// radial MLP, conv tensor product with receiver-segmented sum, symmetric
+// contraction, product linear and readout; then the hand-written backward in
+// reverse layer order, the edge backward, and the force/virial assembly.  It
+// replaces the reference's mx.value_and_grad step (calculators.py:431-483,
+// 533-570) with explicit kernels; nothing is allocated on this path.
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "common.cuh"
+
+namespace mace {
+
+static thread_local std::string g_last_error;
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+}  // namespace mace
+
+using namespace mace;
+
+namespace {
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+struct LayerBufs {
+  float* up = nullptr;    // (N, in_dim)
+  float* w = nullptr;     // (E, wnumel)
+  float* act = nullptr;   // (E, nh*H)
+  float* A = nullptr;     // (N, mid_dim)
+  float* msg = nullptr;   // (N, 16C)
+  float* msg2 = nullptr;  // (N, 16C) non-residual skip output
+  float* B = nullptr;     // (N, hid_dim)
+  float* dB = nullptr;    // (N, hid_dim)
+  float* dmsg = nullptr;  // (N, 16C)
+  float* dmsg2 = nullptr; // (N, 16C)
+  float* dA = nullptr;    // (N, mid_dim)
+  float* dup = nullptr;   // (N, in_dim)
+};
+
+}  // namespace
+
+struct mace_ctx {
+  int device = 0;
+  mace_model_desc desc{};
+  float* d_floats = nullptr;
+  int32_t* d_ints = nullptr;
+  int64_t cap_nodes = 0, cap_edges = 0;
+  std::vector<void*> allocs;
+  int64_t ws_bytes = 0;
+  // edge buffers
+  float *v = nullptr, *Y = nullptr, *b = nullptr, *dY = nullptr, *db = nullptr, *dv = nullptr,
+        *dw = nullptr;
+  double* vir_part = nullptr;
+  // node buffers
+  std::vector<float*> h;   // h[t], t = 0..T   (N, row_t)
+  std::vector<float*> dh;  // dh[t]
+  std::vector<int> h_row;
+  float* e_layers = nullptr;  // (T, N)
+  LayerBufs lb[MACE_MAX_LAYERS];
+  // neighbour-list scratch
+  int32_t *nl_count = nullptr, *nl_graph = nullptr, *nl_wrap = nullptr;
+  double* nl_inv = nullptr;
+  void* scan_tmp = nullptr;
+  size_t scan_bytes = 0;
+  int* d_err = nullptr;
+  // bookkeeping
+  int launches = 0;
+  int64_t last_N = 0, last_E = 0;
+};
+
+namespace {
+
+const float* F(const mace_ctx* c, int64_t off) { return c->d_floats + off; }
+const int32_t* I(const mace_ctx* c, int64_t off) { return c->d_ints + off; }
+
+int max_wnumel(const mace_model_desc& d) {
+  int m = 0;
+  for (int t = 0; t < d.num_layers; ++t) m = d.layers[t].wnumel > m ? d.layers[t].wnumel : m;
+  return m;
+}
+
+void free_ws(mace_ctx* c) {
+  for (void* p : c->allocs) cudaFree(p);
+  c->allocs.clear();
+  c->ws_bytes = 0;
+  c->cap_nodes = c->cap_edges = 0;
+}
+
+template <typename T>
+int alloc(mace_ctx* c, T** p, int64_t count) {
+  size_t bytes = (size_t)(count > 0 ? count : 1) * sizeof(T);
+  bytes = (bytes + 255) & ~(size_t)255;
+  void* q = nullptr;
+  cudaError_t e = cudaMalloc(&q, bytes);
+  if (e != cudaSuccess) return fail(MACE_ERR_CUDA, std::string("workspace cudaMalloc: ") + cudaGetErrorString(e));
+  c->allocs.push_back(q);
+  c->ws_bytes += (int64_t)bytes;
+  *p = reinterpret_cast<T*>(q);
+  return MACE_OK;
+}
+
+#define TRY(x)              \
+  do {                      \
+    int _rc = (x);          \
+    if (_rc) return _rc;    \
+  } while (0)
+
+int reserve(mace_ctx* c, int64_t N, int64_t E) {
+  const mace_model_desc& d = c->desc;
+  free_ws(c);
+  const int C = d.C;
+  const int T = d.num_layers;
+  const int wmax = max_wnumel(d);
+  TRY(alloc(c, &c->v, E * 3));
+  TRY(alloc(c, &c->Y, E * 16));
+  TRY(alloc(c, &c->b, E * d.num_bessel));
+  TRY(alloc(c, &c->dY, E * 16));
+  TRY(alloc(c, &c->db, E * d.num_bessel));
+  TRY(alloc(c, &c->dv, E * 3));
+  TRY(alloc(c, &c->dw, E * wmax));
+  TRY(alloc(c, &c->vir_part, ((E + 255) / 256 + 1) * 9));
+  c->h.assign(T + 1, nullptr);
+  c->dh.assign(T + 1, nullptr);
+  c->h_row.assign(T + 1, 0);
+  c->h_row[0] = C;
+  for (int t = 0; t < T; ++t) c->h_row[t + 1] = d.layers[t].hid.dim;
+  for (int t = 0; t <= T; ++t) {
+    TRY(alloc(c, &c->h[t], N * c->h_row[t]));
+    TRY(alloc(c, &c->dh[t], N * c->h_row[t]));
+  }
+  TRY(alloc(c, &c->e_layers, (int64_t)T * N));
+  for (int t = 0; t < T; ++t) {
+    const mace_layer_desc& L = d.layers[t];
+    LayerBufs& B = c->lb[t];
+    int nh = L.n_mlp - 1, H = L.mlp_w[1];
+    TRY(alloc(c, &B.up, N * L.in.dim));
+    TRY(alloc(c, &B.w, E * L.wnumel));
+    TRY(alloc(c, &B.act, E * nh * H));
+    TRY(alloc(c, &B.A, N * L.mid.dim));
+    TRY(alloc(c, &B.msg, N * L.inter.dim));
+    TRY(alloc(c, &B.B, N * L.hid.dim));
+    TRY(alloc(c, &B.dB, N * L.hid.dim));
+    TRY(alloc(c, &B.dmsg, N * L.inter.dim));
+    TRY(alloc(c, &B.dA, N * L.mid.dim));
+    TRY(alloc(c, &B.dup, N * L.in.dim));
+    if (!L.residual) {
+      TRY(alloc(c, &B.msg2, N * L.inter.dim));
+      TRY(alloc(c, &B.dmsg2, N * L.inter.dim));
+    }
+  }
+  TRY(alloc(c, &c->nl_count, N + 1));
+  TRY(alloc(c, &c->nl_graph, N));
+  TRY(alloc(c, &c->nl_wrap, N * 3));
+  TRY(alloc(c, &c->nl_inv, 9));
+  c->scan_bytes = scan_tmp_bytes(N);
+  TRY(alloc(c, reinterpret_cast<char**>(&c->scan_tmp), (int64_t)c->scan_bytes));
+  TRY(alloc(c, &c->d_err, 1));
+  MACE_CUDA_TRY(cudaMemset(c->d_err, 0, sizeof(int)));
+  c->cap_nodes = N;
+  c->cap_edges = E;
+  return MACE_OK;
+}
+
+// ---------------------------------------------------------------------------
+// job builders for the node linears
+// ---------------------------------------------------------------------------
+LinJob make_job(int d, int n_k, const int* k_off, int out_off, const float* w, int ldb, float alpha,
+                int accumulate) {
+  LinJob j{};
+  j.d = d;
+  j.n_k = n_k;
+  for (int q = 0; q < n_k; ++q) j.k_off[q] = k_off[q];
+  j.out_off = out_off;
+  j.w = w;
+  j.ldb = ldb;
+  j.alpha = alpha;
+  j.accumulate = accumulate;
+  return j;
+}
+
+int run_linear_slots(mace_ctx* c, int64_t N, const mace_slots& in_slots, const mace_slots& out_slots,
+                     const int64_t* f_w, const float* in, float* out, int accumulate, cudaStream_t s) {
+  // 1-to-1 linears: slot q of `in_slots` -> slot q of `out_slots`
+  LinParams p{};
+  p.N = N;
+  p.C = c->desc.C;
+  p.in = in;
+  p.in_row = in_slots.dim;
+  p.out = out;
+  p.out_row = out_slots.dim;
+  p.n_jobs = in_slots.n;
+  for (int q = 0; q < in_slots.n; ++q) {
+    int ko = in_slots.off[q];
+    p.job[q] = make_job(2 * in_slots.l[q] + 1, 1, &ko, out_slots.off[q], F(c, f_w[q]), p.C, 1.f, accumulate);
+  }
+  ++c->launches;
+  return launch_linear(p, s);
+}
+
+ConvParams conv_params(mace_ctx* c, int t, int64_t N, const mace_system* sys) {
+  const mace_layer_desc& L = c->desc.layers[t];
+  ConvParams p{};
+  p.N = N;
+  p.C = L.C;
+  p.n_mid = L.n_mid;
+  p.m_tot = L.m_tot;
+  p.wnumel = L.wnumel;
+  p.in_dim = L.in.dim;
+  p.in_ch = L.in.dim / L.C;
+  p.mid_dim = L.mid.dim;
+  for (int k = 0; k < L.n_mid; ++k) {
+    const mace_conv_slot& cs = L.conv[k];
+    ConvSlotDev& d = p.slot[k];
+    d.l1 = cs.l1;
+    d.l2 = cs.l2;
+    d.l3 = cs.l3;
+    d.combo = cs.l1 * 16 + cs.l2 * 4 + cs.l3;
+    d.src_off = L.in.off[cs.src];
+    d.src_ch = L.in.off[cs.src] / L.C;
+    d.off = cs.off;
+    d.m_off = cs.m_off;
+    d.cg = F(c, cs.f_cg);
+  }
+  p.row_ptr = sys->row_ptr;
+  p.snd = sys->sender;
+  p.Y = c->Y;
+  p.up = c->lb[t].up;
+  p.w = c->lb[t].w;
+  p.A = c->lb[t].A;
+  p.dA = c->lb[t].dA;
+  p.dw = c->dw;
+  p.dY = c->dY;
+  p.dup = c->lb[t].dup;
+  return p;
+}
+
+MlpParams mlp_params(mace_ctx* c, int t, int64_t E) {
+  const mace_layer_desc& L = c->desc.layers[t];
+  MlpParams p{};
+  p.E = E;
+  p.n_layers = L.n_mlp;
+  for (int j = 0; j <= L.n_mlp; ++j) p.widths[j] = L.mlp_w[j];
+  for (int j = 0; j < L.n_mlp; ++j) {
+    p.w[j] = F(c, L.f_mlp[j]);
+    p.wt[j] = F(c, L.f_mlp_t[j]);
+  }
+  p.b = c->b;
+  p.act = c->lb[t].act;
+  p.out = c->lb[t].w;
+  p.dout = c->dw;
+  p.db = c->db;
+  return p;
+}
+
+ScParams sc_params(mace_ctx* c, int t, int64_t N, const int32_t* species, const float* f, float* out,
+                   const float* dout, float* df) {
+  const mace_layer_desc& L = c->desc.layers[t];
+  ScParams p{};
+  p.N = N;
+  p.C = L.C;
+  p.species = species;
+  p.f = f;
+  p.ncoup = L.inter.dim / L.C;
+  p.n_out = L.hid.n;
+  p.out = out;
+  p.out_row = L.hid.dim;
+  p.dout = dout;
+  p.df = df;
+  for (int o = 0; o < L.hid.n; ++o) {
+    const mace_sc_out& so = L.sc[o];
+    p.L[o] = so.L;
+    p.corr[o] = so.corr;
+    p.out_off[o] = L.hid.off[o];
+    for (int nu = 0; nu < so.corr; ++nu) {
+      ScTabDev& tb = p.tab[o][nu];
+      tb.nnz = so.nnz[nu];
+      tb.seg = I(c, so.i_idx[nu]);
+      tb.idx = I(c, so.i_idx[nu]) + (2 * so.L + 2);
+      tb.val = F(c, so.f_val[nu]);
+      tb.w = F(c, so.f_w[nu]);
+      tb.K = so.K[nu];
+    }
+  }
+  return p;
+}
+
+SkipParams skip_params(mace_ctx* c, int t, int64_t N, const int32_t* species, bool transpose,
+                       const mace_slots& in_s, const mace_slots& out_s, const float* in, float* out,
+                       int accumulate) {
+  const mace_layer_desc& L = c->desc.layers[t];
+  SkipParams p{};
+  p.N = N;
+  p.C = L.C;
+  p.species = species;
+  p.n_jobs = L.n_skip;
+  p.in = in;
+  p.out = out;
+  p.accumulate = accumulate;
+  p.in_row = transpose ? out_s.dim : in_s.dim;
+  p.out_row = transpose ? in_s.dim : out_s.dim;
+  for (int q = 0; q < L.n_skip; ++q) {
+    int si = L.skip_in[q], so = L.skip_out[q];
+    p.d[q] = 2 * in_s.l[si] + 1;
+    if (!transpose) {
+      p.in_off[q] = in_s.off[si];
+      p.out_off[q] = out_s.off[so];
+      p.w[q] = F(c, L.f_skip[q]);
+    } else {
+      p.in_off[q] = out_s.off[so];
+      p.out_off[q] = in_s.off[si];
+      p.w[q] = F(c, L.f_skip_t[q]);
+    }
+  }
+  return p;
+}
+
+int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* out, int flags,
+                     cudaStream_t s) {
+  const mace_model_desc& d = c->desc;
+  const int64_t N = sys->n_nodes, E = sys->n_edges;
+  if (N > c->cap_nodes || E > c->cap_edges)
+    return fail(MACE_ERR_BAD_ARG, "system larger than the reserved workspace (call mace_ctx_reserve)");
+  if (N <= 0) return fail(MACE_ERR_BAD_ARG, "empty system");
+  const int T = d.num_layers;
+  const int C = d.C;
+  c->launches = 0;
+  c->last_N = N;
+  c->last_E = E;
+  const bool want_grad = (flags & (MACE_WANT_FORCES | MACE_WANT_VIRIAL)) != 0;
+
+  EdgeParams ep{};
+  ep.E = E;
+  ep.pos = sys->pos;
+  ep.cell = sys->cell;
+  ep.snd = sys->sender;
+  ep.rcv = sys->receiver;
+  ep.shifts = sys->shifts;
+  ep.max_ell = d.max_ell;
+  ep.nb = d.num_bessel;
+  ep.r_max = d.r_max;
+  ep.poly_p = d.poly_p;
+  ep.bessel_w = F(c, d.f_bessel);
+  ep.sh_T = F(c, d.f_sh);
+  ep.v = c->v;
+  ep.Y = c->Y;
+  ep.b = c->b;
+  ep.dY = c->dY;
+  ep.db = c->db;
+  ep.dv = c->dv;
+  ep.virial_part = (flags & MACE_WANT_VIRIAL) ? c->vir_part : nullptr;
+  if (E > 0) {
+    ++c->launches;
+    TRY(launch_edge_fwd(ep, s));
+  }
+  {
+    EmbedParams p{N, C, sys->species, F(c, d.f_emb), c->h[0]};
+    ++c->launches;
+    TRY(launch_embed(p, s));
+  }
+  const float dscale = d.scale_shift ? d.scale : 1.0f;
+  for (int t = 0; t < T; ++t) {
+    const mace_layer_desc& L = d.layers[t];
+    LayerBufs& B = c->lb[t];
+    // skip connection written first; the product linear accumulates onto it
+    MACE_CUDA_TRY(cudaMemsetAsync(c->h[t + 1], 0, sizeof(float) * N * L.hid.dim, s));
+    if (L.residual) {
+      SkipParams sp = skip_params(c, t, N, sys->species, false, L.in, L.hid, c->h[t], c->h[t + 1], 0);
+      ++c->launches;
+      TRY(launch_skip(sp, s));
+    }
+    TRY(run_linear_slots(c, N, L.in, L.in, L.f_up, c->h[t], B.up, 0, s));
+    MlpParams mp = mlp_params(c, t, E);
+    if (E > 0) {
+      ++c->launches;
+      TRY(launch_mlp_fwd(mp, s));
+    }
+    ConvParams cp = conv_params(c, t, N, sys);
+    ++c->launches;
+    TRY(launch_conv_fwd(cp, s));
+    {
+      LinParams lp{};
+      lp.N = N;
+      lp.C = C;
+      lp.in = B.A;
+      lp.in_row = L.mid.dim;
+      lp.out = B.msg;
+      lp.out_row = L.inter.dim;
+      lp.n_jobs = L.inter.n;
+      for (int l = 0; l < L.inter.n; ++l) {
+        const mace_lin_group& g = L.lin[l];
+        int ko[MACE_MAX_SRC];
+        for (int q = 0; q < g.n_src; ++q) ko[q] = L.conv[g.src[q]].off;
+        lp.job[l] = make_job(2 * l + 1, g.n_src, ko, L.inter.off[l], F(c, g.f_w), C, d.inv_avg_num_neighbors, 0);
+      }
+      ++c->launches;
+      TRY(launch_linear(lp, s));
+    }
+    const float* sc_in = B.msg;
+    if (!L.residual) {
+      SkipParams sp = skip_params(c, t, N, sys->species, false, L.inter, L.inter, B.msg, B.msg2, 0);
+      MACE_CUDA_TRY(cudaMemsetAsync(B.msg2, 0, sizeof(float) * N * L.inter.dim, s));
+      ++c->launches;
+      TRY(launch_skip(sp, s));
+      sc_in = B.msg2;
+    }
+    ScParams scp = sc_params(c, t, N, sys->species, sc_in, B.B, nullptr, nullptr);
+    ++c->launches;
+    TRY(launch_sc_fwd(scp, s));
+    TRY(run_linear_slots(c, N, L.hid, L.hid, L.f_prod, B.B, c->h[t + 1], 1, s));
+    ReadoutParams rp{};
+    rp.N = N;
+    rp.C = C;
+    rp.h = c->h[t + 1];
+    rp.h_row = L.hid.dim;
+    rp.nonlinear = L.readout_nonlinear;
+    rp.hidden = L.readout_hidden;
+    rp.w1 = F(c, L.f_ro1);
+    rp.w2 = L.readout_nonlinear ? F(c, L.f_ro2) : nullptr;
+    rp.e = c->e_layers + (int64_t)t * N;
+    rp.dh = c->dh[t + 1];
+    rp.dscale = dscale;
+    ++c->launches;
+    TRY(launch_readout(rp, s));
+  }
+  {
+    EnergyParams p{};
+    p.N = N;
+    p.num_graphs = sys->num_graphs;
+    p.T = T;
+    p.species = sys->species;
+    p.graph_ptr = sys->graph_ptr;
+    p.e0 = F(c, d.f_e0);
+    p.e_layers = c->e_layers;
+    p.scale_shift = d.scale_shift;
+    p.scale = d.scale;
+    p.shift = d.shift;
+    p.node_energy = out ? out->node_energy : nullptr;
+    p.energy = out ? out->energy : nullptr;
+    ++c->launches;
+    TRY(launch_energy(p, s));
+  }
+  if (!want_grad) return MACE_OK;
+
+  if (E > 0) {
+    MACE_CUDA_TRY(cudaMemsetAsync(c->dY, 0, sizeof(float) * E * 16, s));
+    MACE_CUDA_TRY(cudaMemsetAsync(c->db, 0, sizeof(float) * E * d.num_bessel, s));
+  }
+  for (int t = T - 1; t >= 0; --t) {
+    const mace_layer_desc& L = d.layers[t];
+    LayerBufs& B = c->lb[t];
+    TRY(run_linear_slots(c, N, L.hid, L.hid, L.f_prod_t, c->dh[t + 1], B.dB, 0, s));
+    float* dsc_in = B.dmsg;
+    ScParams scp = sc_params(c, t, N, sys->species, L.residual ? B.msg : B.msg2, nullptr, B.dB,
+                             L.residual ? B.dmsg : B.dmsg2);
+    ++c->launches;
+    TRY(launch_sc_bwd(scp, s));
+    if (!L.residual) {
+      MACE_CUDA_TRY(cudaMemsetAsync(B.dmsg, 0, sizeof(float) * N * L.inter.dim, s));
+      SkipParams sp = skip_params(c, t, N, sys->species, true, L.inter, L.inter, B.dmsg2, B.dmsg, 1);
+      ++c->launches;
+      TRY(launch_skip(sp, s));
+    }
+    {
+      // dA[mid slot k] = inv_avg * dmsg[inter slot l_k] @ W_l^T (block q of the concat-K)
+      LinParams lp{};
+      lp.N = N;
+      lp.C = C;
+      lp.in = dsc_in;
+      lp.in_row = L.inter.dim;
+      lp.out = B.dA;
+      lp.out_row = L.mid.dim;
+      lp.n_jobs = 0;
+      for (int l = 0; l < L.inter.n; ++l) {
+        const mace_lin_group& g = L.lin[l];
+        for (int q = 0; q < g.n_src; ++q) {
+          int ko = L.inter.off[l];
+          lp.job[lp.n_jobs++] = make_job(2 * l + 1, 1, &ko, L.conv[g.src[q]].off, F(c, g.f_wt) + q * C,
+                                         g.n_src * C, d.inv_avg_num_neighbors, 0);
+        }
+      }
+      ++c->launches;
+      TRY(launch_linear(lp, s));
+    }
+    ConvParams cp = conv_params(c, t, N, sys);
+    ++c->launches;
+    TRY(launch_conv_bwd(cp, s));
+    MlpParams mp = mlp_params(c, t, E);
+    if (E > 0) {
+      ++c->launches;
+      TRY(launch_mlp_bwd(mp, s));
+    }
+    if (t > 0) {
+      // dh[t] holds the readout seed of layer t-1
+      TRY(run_linear_slots(c, N, L.in, L.in, L.f_up_t, B.dup, c->dh[t], 1, s));
+      if (L.residual) {
+        SkipParams sp = skip_params(c, t, N, sys->species, true, L.in, L.hid, c->dh[t + 1], c->dh[t], 1);
+        ++c->launches;
+        TRY(launch_skip(sp, s));
+      }
+    }
+  }
+  int n_blocks = 0;
+  if (E > 0) {
+    ++c->launches;
+    TRY(launch_edge_bwd(ep, &n_blocks, s));
+  }
+  if (out && out->forces) {
+    if (E > 0) {
+      ForceParams fp{N, sys->row_ptr, sys->sender, sys->receiver, sys->rev, c->dv, out->forces, c->d_err};
+      ++c->launches;
+      TRY(launch_forces(fp, s));
+    } else {
+      MACE_CUDA_TRY(cudaMemsetAsync(out->forces, 0, sizeof(float) * 3 * N, s));
+    }
+  }
+  if ((flags & MACE_WANT_VIRIAL) && out && out->virial) {
+    if (E > 0) {
+      ++c->launches;
+      TRY(launch_virial_reduce(c->vir_part, n_blocks, out->virial, s));
+    } else {
+      MACE_CUDA_TRY(cudaMemsetAsync(out->virial, 0, sizeof(double) * 9, s));
+    }
+  }
+  return MACE_OK;
+}
+
+}  // namespace
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+extern "C" {
+
+int mace_last_error(char* buf, size_t len) {
+  if (!buf || len == 0) return MACE_ERR_BAD_ARG;
+  std::snprintf(buf, len, "%s", g_last_error.c_str());
+  return MACE_OK;
+}
+
+int mace_ctx_create(const mace_model_desc* desc, int device, mace_ctx** out) {
+  if (!desc || !out) return fail(MACE_ERR_BAD_ARG, "null argument");
+  if (desc->abi_version != MACE_ABI_VERSION) return fail(MACE_ERR_BAD_ARG, "model description ABI version mismatch");
+  if (desc->num_layers < 1 || desc->num_layers > MACE_MAX_LAYERS)
+    return fail(MACE_ERR_UNSUPPORTED, "number of interaction layers out of range");
+  if (desc->max_ell < 0 || desc->max_ell > 3) return fail(MACE_ERR_UNSUPPORTED, "max_ell must be <= 3");
+  if (desc->C % 32 != 0 || desc->C > 128) return fail(MACE_ERR_UNSUPPORTED, "channels must be 32, 64, 96 or 128");
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev)
+    return fail(MACE_ERR_CUDA, "no such CUDA device");
+  DeviceGuard g(device);
+  mace_ctx* c = new mace_ctx();
+  c->device = device;
+  c->desc = *desc;
+  cudaError_t e1 = cudaMalloc(&c->d_floats, sizeof(float) * (desc->n_floats > 0 ? desc->n_floats : 1));
+  cudaError_t e2 = cudaMalloc(&c->d_ints, sizeof(int32_t) * (desc->n_ints > 0 ? desc->n_ints : 1));
+  if (e1 != cudaSuccess || e2 != cudaSuccess) {
+    cudaFree(c->d_floats);
+    cudaFree(c->d_ints);
+    delete c;
+    return fail(MACE_ERR_CUDA, "model table allocation failed");
+  }
+  cudaMemcpy(c->d_floats, desc->floats, sizeof(float) * desc->n_floats, cudaMemcpyHostToDevice);
+  cudaError_t e3 = cudaMemcpy(c->d_ints, desc->ints, sizeof(int32_t) * desc->n_ints, cudaMemcpyHostToDevice);
+  if (e3 != cudaSuccess) {
+    cudaFree(c->d_floats);
+    cudaFree(c->d_ints);
+    delete c;
+    return fail(MACE_ERR_CUDA, std::string("model table upload: ") + cudaGetErrorString(e3));
+  }
+  c->desc.floats = nullptr;
+  c->desc.ints = nullptr;
+  *out = c;
+  return MACE_OK;
+}
+
+int mace_ctx_destroy(mace_ctx* c) {
+  if (!c) return MACE_OK;
+  DeviceGuard g(c->device);
+  free_ws(c);
+  cudaFree(c->d_floats);
+  cudaFree(c->d_ints);
+  delete c;
+  return MACE_OK;
+}
+
+int mace_ctx_reserve(mace_ctx* c, int64_t max_nodes, int64_t max_edges) {
+  if (!c || max_nodes < 0 || max_edges < 0) return fail(MACE_ERR_BAD_ARG, "bad reserve arguments");
+  if (max_nodes <= c->cap_nodes && max_edges <= c->cap_edges && c->cap_nodes > 0) return MACE_OK;
+  DeviceGuard g(c->device);
+  int64_t N = max_nodes > c->cap_nodes ? max_nodes : c->cap_nodes;
+  int64_t E = max_edges > c->cap_edges ? max_edges : c->cap_edges;
+  MACE_CUDA_TRY(cudaDeviceSynchronize());
+  return reserve(c, N < 1 ? 1 : N, E < 1 ? 1 : E);
+}
+
+int mace_ctx_workspace_bytes(const mace_ctx* c, int64_t* bytes) {
+  if (!c || !bytes) return fail(MACE_ERR_BAD_ARG, "null argument");
+  *bytes = c->ws_bytes;
+  return MACE_OK;
+}
+
+int mace_nl_build(mace_ctx* c, const double* pos, const double* cell, const int32_t* pbc,
+                  const int32_t* graph_ptr, int32_t num_graphs, int64_t n, double r_cut,
+                  int32_t* sender, int32_t* receiver, int32_t* shifts, int32_t* row_ptr, int32_t* rev,
+                  int64_t capacity, int64_t* n_edges, void* stream) {
+  if (!c || !pos || !pbc || !graph_ptr || !n_edges || !row_ptr) return fail(MACE_ERR_BAD_ARG, "null argument");
+  if (n <= 0 || num_graphs <= 0 || !(r_cut > 0)) return fail(MACE_ERR_BAD_ARG, "bad sizes or cutoff");
+  if (n > c->cap_nodes) return fail(MACE_ERR_BAD_ARG, "more atoms than reserved (call mace_ctx_reserve)");
+  DeviceGuard g(c->device);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  NlParams p{};
+  p.n = n;
+  p.pos = pos;
+  p.cell = cell;
+  p.r_cut = r_cut;
+  p.graph_ptr = graph_ptr;
+  p.num_graphs = num_graphs;
+  bool any_pbc = false;
+  for (int d = 0; d < 3; ++d) {
+    p.pbc[d] = pbc[d] ? 1 : 0;
+    any_pbc |= pbc[d] != 0;
+  }
+  double hc[9] = {0}, inv[9] = {0};
+  if (any_pbc) {
+    if (!cell) return fail(MACE_ERR_BAD_ARG, "periodic system without a cell");
+    MACE_CUDA_TRY(cudaMemcpyAsync(hc, cell, sizeof(hc), cudaMemcpyDeviceToHost, s));
+    MACE_CUDA_TRY(cudaStreamSynchronize(s));
+    double det = hc[0] * (hc[4] * hc[8] - hc[5] * hc[7]) - hc[1] * (hc[3] * hc[8] - hc[5] * hc[6]) +
+                 hc[2] * (hc[3] * hc[7] - hc[4] * hc[6]);
+    if (!(std::fabs(det) > 1e-12)) return fail(MACE_ERR_BAD_ARG, "periodic cell is singular");
+    inv[0] = (hc[4] * hc[8] - hc[5] * hc[7]) / det;
+    inv[1] = (hc[2] * hc[7] - hc[1] * hc[8]) / det;
+    inv[2] = (hc[1] * hc[5] - hc[2] * hc[4]) / det;
+    inv[3] = (hc[5] * hc[6] - hc[3] * hc[8]) / det;
+    inv[4] = (hc[0] * hc[8] - hc[2] * hc[6]) / det;
+    inv[5] = (hc[2] * hc[3] - hc[0] * hc[5]) / det;
+    inv[6] = (hc[3] * hc[7] - hc[4] * hc[6]) / det;
+    inv[7] = (hc[1] * hc[6] - hc[0] * hc[7]) / det;
+    inv[8] = (hc[0] * hc[4] - hc[1] * hc[3]) / det;
+    const double vol = std::fabs(det);
+    for (int d = 0; d < 3; ++d) {
+      const double* a = hc + 3 * ((d + 1) % 3);
+      const double* b = hc + 3 * ((d + 2) % 3);
+      double cx = a[1] * b[2] - a[2] * b[1], cy = a[2] * b[0] - a[0] * b[2], cz = a[0] * b[1] - a[1] * b[0];
+      double h = vol / std::sqrt(cx * cx + cy * cy + cz * cz);
+      p.reach[d] = r_cut / h * (1.0 + 1e-9) + 1e-9;
+    }
+  }
+  MACE_CUDA_TRY(cudaMemcpyAsync(c->nl_inv, inv, sizeof(inv), cudaMemcpyHostToDevice, s));
+  p.inv_cell = c->nl_inv;
+  p.count = c->nl_count;
+  p.row_ptr = row_ptr;
+  p.snd = sender;
+  p.rcv = receiver;
+  p.shifts = shifts;
+  p.rev = rev;
+  p.err_flag = c->d_err;
+  p.node_graph = c->nl_graph;
+  p.wrap = c->nl_wrap;
+  TRY(launch_nl_prep(p, c->nl_graph, c->nl_wrap, s));
+  TRY(launch_nl_count(p, s));
+  MACE_CUDA_TRY(cudaMemsetAsync(c->nl_count + n, 0, sizeof(int32_t), s));
+  TRY(scan_counts(c->nl_count, row_ptr, n, c->scan_tmp, c->scan_bytes, s));
+  int32_t total = 0;
+  MACE_CUDA_TRY(cudaMemcpyAsync(&total, row_ptr + n, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+  MACE_CUDA_TRY(cudaStreamSynchronize(s));
+  *n_edges = total;
+  if (total > capacity) return fail(MACE_ERR_NL_OVERFLOW, "edge capacity too small");
+  if (total > 0 && (!sender || !receiver || !shifts || !rev)) return fail(MACE_ERR_BAD_ARG, "null edge output");
+  MACE_CUDA_TRY(cudaMemsetAsync(c->d_err, 0, sizeof(int), s));
+  TRY(launch_nl_fill(p, s));
+  TRY(launch_nl_rev(p, total, s));
+  int err = 0;
+  MACE_CUDA_TRY(cudaMemcpyAsync(&err, c->d_err, sizeof(int), cudaMemcpyDeviceToHost, s));
+  MACE_CUDA_TRY(cudaStreamSynchronize(s));
+  if (err) return fail(MACE_ERR_EDGES, "neighbour list is not closed under edge reversal");
+  return MACE_OK;
+}
+
+int mace_forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* out, int32_t flags,
+                          void* stream) {
+  if (!c || !sys) return fail(MACE_ERR_BAD_ARG, "null argument");
+  if (sys->num_graphs < 1 || !sys->graph_ptr || !sys->species || !sys->pos || !sys->row_ptr)
+    return fail(MACE_ERR_BAD_ARG, "incomplete system description");
+  if (sys->n_edges > 0 && (!sys->sender || !sys->receiver || !sys->shifts || !sys->rev))
+    return fail(MACE_ERR_BAD_ARG, "edges without sender/receiver/shift/rev arrays");
+  DeviceGuard g(c->device);
+  return forward_backward(c, sys, out, flags, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int mace_debug_buffer(mace_ctx* c, int32_t id, const float** ptr, int64_t* len) {
+  if (!c || !ptr || !len) return fail(MACE_ERR_BAD_ARG, "null argument");
+  const int64_t N = c->last_N, E = c->last_E;
+  const int layer = id / 16, stage = id % 16;
+  *ptr = nullptr;
+  *len = 0;
+  if (layer == 15) {
+    switch (stage) {
+      case 0: *ptr = c->v; *len = E * 3; break;
+      case 1: *ptr = c->Y; *len = E * 16; break;
+      case 2: *ptr = c->b; *len = E * c->desc.num_bessel; break;
+      case 3: *ptr = c->dY; *len = E * 16; break;
+      case 4: *ptr = c->db; *len = E * c->desc.num_bessel; break;
+      case 5: *ptr = c->dv; *len = E * 3; break;
+      case 6: *ptr = c->h[0]; *len = N * c->h_row[0]; break;
+      case 7: *ptr = c->e_layers; *len = N * c->desc.num_layers; break;
+      default: return fail(MACE_ERR_BAD_ARG, "unknown debug buffer");
+    }
+    return MACE_OK;
+  }
+  if (layer < 0 || layer >= c->desc.num_layers) return fail(MACE_ERR_BAD_ARG, "unknown debug layer");
+  const mace_layer_desc& L = c->desc.layers[layer];
+  const LayerBufs& B = c->lb[layer];
+  switch (stage) {
+    case 0: *ptr = B.up; *len = N * L.in.dim; break;
+    case 1: *ptr = B.w; *len = E * L.wnumel; break;
+    case 2: *ptr = B.A; *len = N * L.mid.dim; break;
+    case 3: *ptr = B.msg; *len = N * L.inter.dim; break;
+    case 4: *ptr = B.B; *len = N * L.hid.dim; break;
+    case 5: *ptr = c->h[layer + 1]; *len = N * L.hid.dim; break;
+    case 6: *ptr = c->dh[layer + 1]; *len = N * L.hid.dim; break;
+    case 7: *ptr = B.dB; *len = N * L.hid.dim; break;
+    case 8: *ptr = B.dmsg; *len = N * L.inter.dim; break;
+    case 9: *ptr = B.dA; *len = N * L.mid.dim; break;
+    case 10: *ptr = B.dup; *len = N * L.in.dim; break;
+    case 11: *ptr = B.act; *len = E * (L.n_mlp - 1) * L.mlp_w[1]; break;
+    case 12: *ptr = c->dh[layer]; *len = N * c->h_row[layer]; break;
+    case 13: *ptr = B.msg2; *len = B.msg2 ? N * L.inter.dim : 0; break;
+    default: return fail(MACE_ERR_BAD_ARG, "unknown debug stage");
+  }
+  return MACE_OK;
+}
+
+int mace_last_launch_count(const mace_ctx* c, int32_t* count) {
+  if (!c || !count) return fail(MACE_ERR_BAD_ARG, "null argument");
+  *count = c->launches;
+  return MACE_OK;
+}
+
+int mace_ctx_error_flag(mace_ctx* c, int32_t* flag) {
+  if (!c || !flag) return fail(MACE_ERR_BAD_ARG, "null argument");
+  DeviceGuard g(c->device);
+  int v = 0;
+  MACE_CUDA_TRY(cudaDeviceSynchronize());
+  MACE_CUDA_TRY(cudaMemcpy(&v, c->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+  MACE_CUDA_TRY(cudaMemset(c->d_err, 0, sizeof(int)));
+  *flag = v;
+  return MACE_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,203 @@
+"""Host engine of the B200 MACE step.
+
+``MACEModel`` loads a converted model directory (the reference's
+``config.json`` + ``weights.npz``, ``model.py:664-720``), packs it once, and
+drives ``libmace_b200`` through its C ABI.  torch is used only to own device
+memory and streams; every computation of the step runs in the library's
+kernels.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import native as nv
+from .pack import PackedModel
+from .spec import ModelSpec
+from .weights import check_weights, load_model_dir
+
+
+class _CudaArray:
+    """Zero-copy view of a device buffer owned by the library."""
+
+    def __init__(self, ptr: int, n: int, typestr: str = "<f4"):
+        self.__cuda_array_interface__ = {
+            "shape": (n,), "typestr": typestr, "data": (ptr, False), "version": 2, "strides": None,
+        }
+
+
+@dataclass
+class EdgeSet:
+    """Receiver-sorted directed edges on the device (output of the GPU neighbour list)."""
+
+    sender: torch.Tensor  # (cap,) int32
+    receiver: torch.Tensor  # (cap,) int32
+    shifts: torch.Tensor  # (cap, 3) int32
+    row_ptr: torch.Tensor  # (N+1,) int32
+    rev: torch.Tensor  # (cap,) int32
+    n_edges: int
+
+    def numpy(self):
+        e = self.n_edges
+        return (self.sender[:e].cpu().numpy(), self.receiver[:e].cpu().numpy(),
+                self.shifts[:e].cpu().numpy())
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+class MACEModel:
+    def __init__(self, model_dir: str | os.PathLike | None = None, *, config: dict | None = None,
+                 weights: dict | None = None, device: int | str | torch.device = 0):
+        if model_dir is not None:
+            config, weights = load_model_dir(model_dir)
+        if config is None or weights is None:
+            raise ValueError("give a model directory or (config, weights)")
+        self.config = config
+        self.spec = ModelSpec.from_config(config)
+        check_weights(self.spec, weights)
+        dev = torch.device(device) if not isinstance(device, int) else torch.device("cuda", device)
+        if dev.type != "cuda":
+            raise ValueError("MACEModel runs on a CUDA device only")
+        if not torch.cuda.is_available():
+            raise RuntimeError("no CUDA device available: the B200 step has no CPU fallback")
+        self.device = torch.device("cuda", dev.index if dev.index is not None else torch.cuda.current_device())
+        self.lib = nv.load_library()
+        self.packed = PackedModel(self.spec, weights)
+        ctx = C.c_void_p()
+        nv.check(self.lib.mace_ctx_create(C.byref(self.packed.desc), self.device.index, C.byref(ctx)), self.lib)
+        self.ctx = ctx
+        self.z_table = self.spec.z_table
+        self.r_max = self.spec.r_max
+        self._cap = (0, 0)
+        self._edge_cap = 0
+
+    def close(self):
+        if getattr(self, "ctx", None) is not None and self.ctx.value:
+            self.lib.mace_ctx_destroy(self.ctx)
+            self.ctx = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ------------------------------------------------------------------
+    def species_index(self, numbers) -> np.ndarray:
+        """Atomic numbers -> model element indices (raises for unsupported Z)."""
+        numbers = np.asarray(numbers, dtype=np.int64)
+        if self.z_table is None:
+            idx = numbers.copy()
+            ok = (idx >= 0) & (idx < self.spec.num_elements)
+        else:
+            lut = np.full(max(max(self.z_table), int(numbers.max(initial=0))) + 1, -1, dtype=np.int64)
+            lut[np.asarray(self.z_table)] = np.arange(len(self.z_table))
+            idx = lut[numbers]
+            ok = idx >= 0
+        if not np.all(ok):
+            bad = int(numbers[~ok][0])
+            supported = sorted(self.z_table) if self.z_table is not None else list(range(self.spec.num_elements))
+            raise ValueError(f"Atomic number {bad} is not supported by this model. Supported: {supported}")
+        return idx.astype(np.int32)
+
+    def reserve(self, n_nodes: int, n_edges: int) -> None:
+        if n_nodes > self._cap[0] or n_edges > self._cap[1]:
+            N = max(n_nodes, self._cap[0])
+            E = max(n_edges, self._cap[1])
+            nv.check(self.lib.mace_ctx_reserve(self.ctx, N, E), self.lib)
+            self._cap = (N, E)
+
+    def workspace_bytes(self) -> int:
+        b = C.c_int64()
+        nv.check(self.lib.mace_ctx_workspace_bytes(self.ctx, C.byref(b)), self.lib)
+        return b.value
+
+    # ------------------------------------------------------------------
+    def neighbour_list(self, pos64: torch.Tensor, cell64: torch.Tensor | None, pbc, graph_ptr: torch.Tensor,
+                       r_cut: float, edges: EdgeSet | None = None) -> EdgeSet:
+        """GPU "ijS" list (cutoff r_cut) for positions already on the device."""
+        n = pos64.shape[0]
+        self.reserve(n, self._cap[1])
+        pbc_arr = (C.c_int32 * 3)(*[int(bool(x)) for x in pbc])
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        cap = edges.sender.shape[0] if edges is not None and edges.row_ptr.shape[0] == n + 1 else 0
+        if cap == 0:
+            cap = max(1024, int(n * 64))
+        for _ in range(3):
+            if edges is None or edges.sender.shape[0] < cap or edges.row_ptr.shape[0] != n + 1:
+                i32 = dict(dtype=torch.int32, device=self.device)
+                edges = EdgeSet(torch.empty(cap, **i32), torch.empty(cap, **i32), torch.empty(cap, 3, **i32),
+                                torch.empty(n + 1, **i32), torch.empty(cap, **i32), 0)
+            ne = C.c_int64()
+            rc = self.lib.mace_nl_build(
+                self.ctx, pos64.data_ptr(), _ptr(cell64), pbc_arr, graph_ptr.data_ptr(), graph_ptr.shape[0] - 1,
+                n, float(r_cut), edges.sender.data_ptr(), edges.receiver.data_ptr(), edges.shifts.data_ptr(),
+                edges.row_ptr.data_ptr(), edges.rev.data_ptr(), edges.sender.shape[0], C.byref(ne), stream)
+            if rc == nv.MACE_ERR_NL_OVERFLOW:
+                cap = int(ne.value * 1.25) + 1024
+                edges = None
+                continue
+            nv.check(rc, self.lib)
+            edges.n_edges = int(ne.value)
+            return edges
+        raise RuntimeError("neighbour list did not fit after resizing")
+
+    # ------------------------------------------------------------------
+    def evaluate(self, pos: torch.Tensor, cell: torch.Tensor | None, species: torch.Tensor,
+                 graph_ptr: torch.Tensor, edges: EdgeSet, *, forces: bool = True, virial: bool = False,
+                 out: dict | None = None) -> dict:
+        """Energy per graph (float64), node energies, forces and the raw virial.
+
+        All inputs are device tensors: pos (N,3) float32, cell (3,3) float32 or
+        None, species (N,) int32 model indices, graph_ptr (G+1,) int32.
+        Asynchronous on the current stream.
+        """
+        N = pos.shape[0]
+        E = edges.n_edges
+        self.reserve(N, E)
+        G = graph_ptr.shape[0] - 1
+        if out is None:
+            out = {
+                "energy": torch.empty(G, dtype=torch.float64, device=self.device),
+                "node_energy": torch.empty(N, dtype=torch.float32, device=self.device),
+                "forces": torch.empty(N, 3, dtype=torch.float32, device=self.device) if forces else None,
+                "virial": torch.empty(9, dtype=torch.float64, device=self.device) if virial else None,
+            }
+        sysd = nv.System(
+            n_nodes=N, n_edges=E, num_graphs=G, pos=pos.data_ptr(), cell=_ptr(cell),
+            species=species.data_ptr(), graph_ptr=graph_ptr.data_ptr(), sender=edges.sender.data_ptr(),
+            receiver=edges.receiver.data_ptr(), shifts=edges.shifts.data_ptr(), row_ptr=edges.row_ptr.data_ptr(),
+            rev=edges.rev.data_ptr())
+        outs = nv.Outputs(energy=_ptr(out["energy"]), node_energy=_ptr(out["node_energy"]),
+                          forces=_ptr(out.get("forces")), virial=_ptr(out.get("virial")))
+        flags = (nv.WANT_FORCES if forces else 0) | (nv.WANT_VIRIAL if virial else 0)
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        nv.check(self.lib.mace_forward_backward(self.ctx, C.byref(sysd), C.byref(outs), flags, stream), self.lib)
+        return out
+
+    def last_launch_count(self) -> int:
+        c = C.c_int32()
+        nv.check(self.lib.mace_last_launch_count(self.ctx, C.byref(c)), self.lib)
+        return c.value
+
+    def error_flag(self) -> int:
+        c = C.c_int32()
+        nv.check(self.lib.mace_ctx_error_flag(self.ctx, C.byref(c)), self.lib)
+        return c.value
+
+    def debug_buffer(self, stage: str, layer: int | None = None) -> torch.Tensor:
+        """Copy of an internal per-stage buffer of the last evaluation (parity tests)."""
+        bid = 15 * 16 + nv.EDGE_STAGES[stage] if layer is None else layer * 16 + nv.STAGES[stage]
+        ptr, n = C.c_void_p(), C.c_int64()
+        nv.check(self.lib.mace_debug_buffer(self.ctx, bid, C.byref(ptr), C.byref(n)), self.lib)
+        if not ptr.value or n.value == 0:
+            return torch.empty(0, device=self.device)
+        torch.cuda.synchronize(self.device)
+        return torch.as_tensor(_CudaArray(ptr.value, n.value), device=self.device).clone()

@@ -1,0 +1,247 @@
+"""Pack a converted model (spec + weights.npz arrays) into the flat tables of
+``mace_model_desc`` (``include/mace_b200.h``).
+
+Conversions done here, once per model:
+* path weights (and the constant CG diagonal of the skip product) are folded
+  into the weight matrices;
+* every node-feature table uses a channel-last layout per irrep slot
+  (``off[s] + m*C + u``) instead of the reference's irreps-major ``u*(2l+1)+m``;
+* both a matrix and its transpose are stored where the backward needs one;
+* the symmetric-contraction tensors ``U`` become per-output lists of non-zeros,
+  segmented by the output component ``M``.
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+from . import native as nv
+from .cg import sh_coupling
+from .spec import LayerSpec, ModelSpec, UnsupportedModel
+
+U_EPS = 1e-12  # |U| below this is rounding noise of the coupling recursion
+
+
+class _Tables:
+    def __init__(self):
+        self.f: list[np.ndarray] = []
+        self.nf = 0
+        self.i: list[np.ndarray] = []
+        self.ni = 0
+
+    def addf(self, a) -> int:
+        a = np.ascontiguousarray(np.asarray(a, dtype=np.float32).ravel())
+        off = self.nf
+        # keep every table 16-byte aligned for vector loads
+        pad = (-a.size) % 4
+        self.f.append(a)
+        if pad:
+            self.f.append(np.zeros(pad, np.float32))
+        self.nf += a.size + pad
+        return off
+
+    def addi(self, a) -> int:
+        a = np.ascontiguousarray(np.asarray(a, dtype=np.int32).ravel())
+        off = self.ni
+        self.i.append(a)
+        self.ni += a.size
+        return off
+
+    def arrays(self):
+        f = np.concatenate(self.f) if self.f else np.zeros(1, np.float32)
+        i = np.concatenate(self.i) if self.i else np.zeros(1, np.int32)
+        return f, i
+
+
+def _slots(irreps, C: int) -> nv.Slots:
+    s = nv.Slots()
+    if len(irreps) > nv.MAX_IN:
+        raise UnsupportedModel("too many irrep slots in a node-feature table")
+    s.n = len(irreps)
+    o = 0
+    for q, m in enumerate(irreps):
+        if m.mul != C:
+            raise UnsupportedModel("all irrep slots must have the model's channel count")
+        s.l[q] = m.ir.l
+        s.off[q] = o
+        o += C * m.ir.dim
+    s.dim = o
+    return s
+
+
+def _sc_tables(U: np.ndarray, L: int, nu: int, tb: _Tables) -> tuple[int, int, int]:
+    """Non-zeros of U_nu as (segment starts by M, packed indices, values)."""
+    if L == 0:
+        U = U[None]
+    dM = U.shape[0]
+    K = U.shape[-1]
+    if K >= (1 << 15) or U.shape[1] > 16:
+        raise UnsupportedModel("symmetric-contraction tensor too large to pack")
+    nz = np.argwhere(np.abs(U) > U_EPS)  # rows (M, a_1..a_nu, k), lexicographic
+    vals = U[tuple(nz.T)]
+    seg = np.zeros(dM + 1, dtype=np.int64)
+    for M in range(dM):
+        seg[M + 1] = seg[M] + np.count_nonzero(nz[:, 0] == M)
+    packed = nz[:, 0].astype(np.int64)
+    for a in range(nu):
+        packed |= nz[:, 1 + a].astype(np.int64) << (4 + 4 * a)
+    packed |= nz[:, -1].astype(np.int64) << 16
+    i_off = tb.addi(np.concatenate([seg, packed]).astype(np.int32))
+    f_off = tb.addf(vals)
+    return i_off, f_off, len(vals)
+
+
+def _layer(spec: ModelSpec, lay: LayerSpec, w: dict, tb: _Tables) -> nv.LayerDesc:
+    C = spec.C
+    t = lay.index
+    d = nv.LayerDesc()
+    d.C = C
+    d.residual = int(lay.residual)
+    d.in_ = _slots(lay.irreps_in, C)
+    d.hid = _slots(lay.hidden, C)
+    d.inter = _slots(spec.interaction_irreps, C)
+    if lay.hidden[0].ir.l != 0:
+        raise UnsupportedModel("hidden irreps must start with the scalar block")
+    # skip_tp
+    sk = lay.skip
+    d.n_skip = len(sk.instrs)
+    for q, ins in enumerate(sk.instrs):
+        W = w[f"interactions.{t}.skip_tp.tp.weights.{q}"].astype(np.float64) * (ins.path_weight * ins.cg)
+        d.skip_in[q] = ins.i_in1
+        d.skip_out[q] = ins.i_out
+        d.f_skip[q] = tb.addf(W.transpose(1, 0, 2))  # (z, u, w)
+        d.f_skip_t[q] = tb.addf(W.transpose(1, 2, 0))  # (z, w, u)
+    # linear_up (1-to-1)
+    for q, ins in enumerate(lay.linear_up.instrs):
+        if ins.i_in != q or ins.i_out != q:
+            raise UnsupportedModel("linear_up must map each slot to itself")
+        W = w[f"interactions.{t}.linear_up.weights.{q}"].astype(np.float64) * ins.path_weight
+        d.f_up[q] = tb.addf(W)
+        d.f_up_t[q] = tb.addf(W.T)
+    # radial MLP
+    widths = lay.mlp_widths
+    d.n_mlp = len(widths) - 1
+    if d.n_mlp > 7:
+        raise UnsupportedModel("radial MLP too deep")
+    for j, wd in enumerate(widths):
+        d.mlp_w[j] = wd
+    for j in range(d.n_mlp):
+        Wm = w[f"interactions.{t}.conv_tp_weights.layers.{2 * j}.weight"].astype(np.float64)  # (out, in)
+        d.f_mlp[j] = tb.addf(Wm.T)
+        d.f_mlp_t[j] = tb.addf(Wm)
+    # conv_tp slots
+    cv = lay.conv
+    if len(cv.instrs) > nv.MAX_MID:
+        raise UnsupportedModel("too many conv_tp output slots")
+    d.n_mid = len(cv.instrs)
+    off = m_off = 0
+    for k, ins in enumerate(cv.instrs):
+        cs = d.conv[k]
+        cs.l1, cs.l2, cs.l3, cs.src = ins.l1, ins.l2, ins.l3, ins.i_in1
+        cs.off = off
+        cs.m_off = m_off
+        cs.f_cg = tb.addf(ins.cg)
+        off += C * (2 * ins.l3 + 1)
+        m_off += (2 * ins.l1 + 1) * (2 * ins.l3 + 1)
+    d.m_tot = m_off
+    d.wnumel = cv.weight_numel
+    d.mid.n = 0
+    d.mid.dim = off
+    # interaction linear: one concat-K group per output slot
+    groups: dict[int, list] = {}
+    for q, ins in enumerate(lay.linear.instrs):
+        groups.setdefault(ins.i_out, []).append((ins.i_in, w[f"interactions.{t}.linear.weights.{q}"], ins.path_weight))
+    for io in range(len(spec.interaction_irreps)):
+        g = groups.get(io, [])
+        if len(g) > nv.MAX_SRC or not g:
+            raise UnsupportedModel("interaction linear group size out of range")
+        lg = d.lin[io]
+        lg.n_src = len(g)
+        mats = []
+        for q, (src, W, pw) in enumerate(g):
+            lg.src[q] = src
+            mats.append(W.astype(np.float64) * pw)
+        Wc = np.concatenate(mats, axis=0)
+        lg.f_w = tb.addf(Wc)
+        lg.f_wt = tb.addf(Wc.T)
+    # symmetric contraction
+    for o, out in enumerate(lay.sc.outputs):
+        so = d.sc[o]
+        so.L = out.ir_out.l
+        so.corr = out.correlation
+        if out.correlation > nv.MAX_CORR:
+            raise UnsupportedModel("correlation order above 3 is not supported")
+        pre = f"products.{t}.symmetric_contractions.contractions.{o}"
+        for nu in range(1, out.correlation + 1):
+            if nu == out.correlation:
+                Wn = w[f"{pre}.weights_max"]
+            else:
+                Wn = w[f"{pre}.weights.{out.correlation - 1 - nu}"]
+            so.K[nu - 1] = Wn.shape[1]
+            so.f_w[nu - 1] = tb.addf(Wn)
+            i_off, f_off, nnz = _sc_tables(out.U[nu - 1], so.L, nu, tb)
+            so.i_idx[nu - 1] = i_off
+            so.f_val[nu - 1] = f_off
+            so.nnz[nu - 1] = nnz
+    # product linear (1-to-1)
+    for q, ins in enumerate(lay.prod_linear.instrs):
+        if ins.i_in != q or ins.i_out != q:
+            raise UnsupportedModel("product linear must map each slot to itself")
+        W = w[f"products.{t}.linear.weights.{q}"].astype(np.float64) * ins.path_weight
+        d.f_prod[q] = tb.addf(W)
+        d.f_prod_t[q] = tb.addf(W.T)
+    # readout
+    if lay.readout_linear is not None:
+        (ins,) = lay.readout_linear.instrs
+        if ins.i_in != 0:
+            raise UnsupportedModel("linear readout must read the scalar slot")
+        d.readout_nonlinear = 0
+        d.f_ro1 = tb.addf(w[f"readouts.{t}.linear.weights.0"][:, 0].astype(np.float64) * ins.path_weight)
+    else:
+        (i1,) = lay.readout_1.instrs
+        (i2,) = lay.readout_2.instrs
+        d.readout_nonlinear = 1
+        d.readout_hidden = i1.mul_out
+        d.f_ro1 = tb.addf(w[f"readouts.{t}.linear_1.weights.0"].astype(np.float64) * i1.path_weight)
+        d.f_ro2 = tb.addf(w[f"readouts.{t}.linear_2.weights.0"][:, 0].astype(np.float64) * i2.path_weight)
+    return d
+
+
+class PackedModel:
+    """Owns the numpy tables that ``desc`` points into."""
+
+    def __init__(self, spec: ModelSpec, weights: dict):
+        if spec.max_ell > 3:
+            raise UnsupportedModel("max_ell above 3 is not supported")
+        if spec.num_interactions > nv.MAX_LAYERS:
+            raise UnsupportedModel("too many interaction layers")
+        tb = _Tables()
+        d = nv.ModelDesc()
+        d.abi_version = nv.ABI_VERSION
+        d.num_layers = spec.num_interactions
+        d.num_elements = spec.num_elements
+        d.num_bessel = spec.num_bessel
+        d.max_ell = spec.max_ell
+        d.poly_p = spec.poly_p
+        d.scale_shift = int(spec.model_type == "ScaleShiftMACE")
+        d.C = spec.C
+        d.r_max = spec.r_max
+        d.inv_avg_num_neighbors = 1.0 / spec.avg_num_neighbors
+        d.scale = spec.scale
+        d.shift = spec.shift
+        ae = np.asarray(weights.get("atomic_energies_fn.atomic_energies", spec.atomic_energies), dtype=np.float64)
+        d.f_e0 = tb.addf(ae.reshape(-1)[-spec.num_elements:])
+        d.f_emb = tb.addf(weights["node_embedding.linear.weights.0"].astype(np.float64) / math.sqrt(spec.num_elements))
+        d.f_bessel = tb.addf(weights["radial_embedding.bessel_fn.bessel_weights"])
+        d.f_sh = tb.addf(np.concatenate([sh_coupling(2).ravel(), sh_coupling(3).ravel()]))
+        for t, lay in enumerate(spec.layers):
+            d.layers[t] = _layer(spec, lay, weights, tb)
+        self.floats, self.ints = tb.arrays()
+        d.floats = self.floats.ctypes.data_as(nv.C.POINTER(nv.f32))
+        d.n_floats = self.floats.size
+        d.ints = self.ints.ctypes.data_as(nv.C.POINTER(nv.i32))
+        d.n_ints = self.ints.size
+        self.desc = d
+        self.spec = spec

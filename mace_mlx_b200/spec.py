@@ -1,0 +1,392 @@
+"""MACE architecture description derived from a converted-model ``config.json``.
+
+Everything here is construction-time metadata: which irreps each layer carries,
+the instruction lists of every equivariant op, their path weights, and the
+flat weight-key names of the converted layout.  The construction mirrors the
+reference's module tree so that a ``weights.npz`` written for the reference
+(``converter.py``) loads unchanged:
+
+* layer irreps and block choice: ``model.py:59-278``
+* conv_tp instructions/paths: ``utils.py:87-156`` (uvu, path weight
+  ``sqrt(dim_out / sum mul2)``, stable sort of the output slots)
+* o3.Linear instructions: ``linear.py:41-77`` (outer loop over input slots,
+  inner over output slots, path weight ``1/sqrt(sum mul_in)`` per output)
+* skip_tp (FullyConnectedTensorProduct, uvw): ``tensor_product.py:1046-1110``
+* symmetric contraction weights: ``symmetric_contraction.py:159-261``
+* readouts: ``blocks.py:540-608``
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from .cg import U_matrix_real, wigner_3j
+from .irreps import Irrep, Irreps
+
+SUPPORTED_INTERACTIONS = (
+    "RealAgnosticResidualInteractionBlock",
+    "RealAgnosticInteractionBlock",
+)
+
+
+class UnsupportedModel(NotImplementedError):
+    pass
+
+
+@dataclass
+class LinearInstr:
+    i_in: int
+    i_out: int
+    mul_in: int
+    mul_out: int
+    dim: int
+    path_weight: float
+
+
+@dataclass
+class LinearSpec:
+    """e3nn o3.Linear between two Irreps (weights shared over m)."""
+
+    irreps_in: Irreps
+    irreps_out: Irreps
+    instrs: list[LinearInstr]
+
+    @staticmethod
+    def build(irreps_in: Irreps, irreps_out: Irreps) -> "LinearSpec":
+        tot = {
+            io: sum(m.mul for m in irreps_in if m.ir == mo.ir)
+            for io, mo in enumerate(irreps_out)
+        }
+        instrs = []
+        for ii, mi in enumerate(irreps_in):
+            for io, mo in enumerate(irreps_out):
+                if mi.ir != mo.ir:
+                    continue
+                pw = 1.0 / math.sqrt(tot[io]) if tot[io] > 0 else 1.0
+                instrs.append(LinearInstr(ii, io, mi.mul, mo.mul, mi.ir.dim, pw))
+        return LinearSpec(irreps_in, irreps_out, instrs)
+
+    def weight_shapes(self) -> list[tuple[int, int]]:
+        return [(i.mul_in, i.mul_out) for i in self.instrs]
+
+
+@dataclass
+class SkipInstr:
+    i_in1: int
+    i_out: int
+    mul1: int
+    mul2: int
+    mul_out: int
+    dim: int
+    path_weight: float
+    cg: float  # the diagonal value of wigner_3j(l, 0, l)
+
+
+@dataclass
+class SkipSpec:
+    """FullyConnectedTensorProduct(x, one_hot(species)) -> irreps_out (uvw)."""
+
+    irreps_in1: Irreps
+    num_elements: int
+    irreps_out: Irreps
+    instrs: list[SkipInstr]
+
+    @staticmethod
+    def build(irreps_in1: Irreps, num_elements: int, irreps_out: Irreps) -> "SkipSpec":
+        attrs = Irreps(f"{num_elements}x0e")
+        raw = []
+        for i1, m1 in enumerate(irreps_in1):
+            for i2, m2 in enumerate(attrs):
+                for io, mo in enumerate(irreps_out):
+                    if m1.ir.p * m2.ir.p != mo.ir.p:
+                        continue
+                    if not (abs(m1.ir.l - m2.ir.l) <= mo.ir.l <= m1.ir.l + m2.ir.l):
+                        continue
+                    raw.append((i1, i2, io))
+        alpha: dict[int, float] = {}
+        for i1, i2, io in raw:
+            alpha[io] = alpha.get(io, 0.0) + irreps_in1[i1].mul * attrs[i2].mul
+        instrs = []
+        for i1, i2, io in raw:
+            dim = irreps_out[io].ir.dim
+            pw = math.sqrt(dim / alpha[io]) if alpha[io] > 0 else 1.0
+            l = irreps_in1[i1].ir.l
+            c = float(wigner_3j(l, 0, l)[0, 0, 0])
+            instrs.append(
+                SkipInstr(i1, io, irreps_in1[i1].mul, num_elements, irreps_out[io].mul,
+                          irreps_in1[i1].ir.dim, pw, c)
+            )
+        return SkipSpec(irreps_in1, num_elements, irreps_out, instrs)
+
+    def weight_shapes(self) -> list[tuple[int, int, int]]:
+        return [(i.mul1, i.mul2, i.mul_out) for i in self.instrs]
+
+
+@dataclass
+class ConvInstr:
+    """One uvu path of the conv tensor product (mul2 == 1, one per output slot)."""
+
+    i_in1: int
+    l1: int
+    l2: int
+    l3: int
+    p3: int
+    path_weight: float
+    mul: int
+
+    @property
+    def cg(self) -> np.ndarray:
+        """Path-weighted coupling tensor (2l1+1, 2l2+1, 2l3+1)."""
+        return wigner_3j(self.l1, self.l2, self.l3) * self.path_weight
+
+
+@dataclass
+class ConvSpec:
+    irreps_in1: Irreps
+    irreps_sh: Irreps
+    irreps_mid: Irreps
+    instrs: list[ConvInstr]  # instrs[k] writes mid slot k, weight slice k
+
+    @staticmethod
+    def build(irreps_in1: Irreps, irreps_sh: Irreps, target: Irreps) -> "ConvSpec":
+        outs: list = []
+        raw = []
+        for i, (mul, ir_in) in enumerate(irreps_in1):
+            for j, (mul2, ir_edge) in enumerate(irreps_sh):
+                for ir_out in ir_in.couple(ir_edge):
+                    if target.has(ir_out):
+                        k = len(outs)
+                        outs.append((mul, ir_out))
+                        raw.append((i, j, k, mul2))
+        alpha: dict[int, float] = {}
+        for i, j, k, mul2 in raw:
+            alpha[k] = alpha.get(k, 0.0) + mul2
+        mid = Irreps(outs)
+        mid_sorted, _, inv = mid.sort()
+        instrs = []
+        for i, j, k, mul2 in raw:
+            ir_out = outs[k][1]
+            pw = math.sqrt(ir_out.dim / alpha[k]) if alpha[k] > 0 else 1.0
+            instrs.append((inv[k], i, j, ir_out, pw))
+        instrs.sort(key=lambda t: t[0])
+        if [t[0] for t in instrs] != list(range(len(instrs))):
+            raise UnsupportedModel("conv_tp must have exactly one path per output slot")
+        out = []
+        for k, i, j, ir_out, pw in instrs:
+            l1 = irreps_in1[i].ir.l
+            l2 = irreps_sh[j].ir.l
+            out.append(ConvInstr(i, l1, l2, ir_out.l, ir_out.p, pw, irreps_in1[i].mul))
+        return ConvSpec(irreps_in1, irreps_sh, mid_sorted, out)
+
+    @property
+    def weight_numel(self) -> int:
+        return sum(i.mul for i in self.instrs)
+
+
+@dataclass
+class SCOutput:
+    """Symmetric contraction for one output irrep (one ``Contraction``)."""
+
+    ir_out: Irrep
+    correlation: int
+    U: list[np.ndarray]  # U[nu-1] for nu = 1..correlation, shape ([d_out,] 16^nu, K_nu)
+    num_params: list[int]  # K_nu
+
+
+@dataclass
+class SCSpec:
+    irreps_in: Irreps
+    irreps_out: Irreps
+    coupling: Irreps
+    num_elements: int
+    C: int
+    outputs: list[SCOutput]
+
+    @staticmethod
+    def build(irreps_in: Irreps, irreps_out: Irreps, correlation: int, num_elements: int) -> "SCSpec":
+        coupling = Irreps([(1, m.ir) for m in irreps_in])
+        C = irreps_in.count("0e")
+        outs = []
+        for mul, ir in irreps_out:
+            Us = [U_matrix_real(coupling, ir, nu) for nu in range(1, correlation + 1)]
+            outs.append(SCOutput(ir, correlation, Us, [u.shape[-1] for u in Us]))
+        return SCSpec(irreps_in, irreps_out, coupling, num_elements, C, outs)
+
+
+@dataclass
+class LayerSpec:
+    index: int
+    irreps_in: Irreps
+    hidden: Irreps  # product output irreps of this layer
+    residual: bool
+    skip: SkipSpec
+    linear_up: LinearSpec
+    conv: ConvSpec
+    mlp_widths: list[int]  # [num_bessel, *radial_MLP, weight_numel]
+    linear: LinearSpec
+    sc: SCSpec
+    prod_linear: LinearSpec
+    readout_nonlinear: bool
+    readout_linear: LinearSpec | None = None  # linear readout (not last)
+    readout_1: LinearSpec | None = None  # nonlinear readout
+    readout_2: LinearSpec | None = None
+
+
+@dataclass
+class ModelSpec:
+    config: dict
+    r_max: float
+    num_bessel: int
+    poly_p: int
+    max_ell: int
+    num_interactions: int
+    num_elements: int
+    hidden: Irreps
+    C: int
+    avg_num_neighbors: float
+    radial_MLP: list[int]
+    model_type: str
+    scale: float
+    shift: float
+    z_table: list[int] | None
+    atomic_energies: np.ndarray
+    irreps_sh: Irreps
+    interaction_irreps: Irreps
+    layers: list[LayerSpec] = field(default_factory=list)
+
+    # ------------------------------------------------------------------
+    @staticmethod
+    def from_config(config: dict) -> "ModelSpec":
+        cfg = dict(config)
+        model_type = cfg.get("model_type", "ScaleShiftMACE")
+        for key in ("distance_transform", "pair_repulsion"):
+            if cfg.get(key):
+                raise UnsupportedModel(
+                    f"config key {key!r} (Agnesi transform / ZBL repulsion) is not "
+                    "supported by the B200 step yet"
+                )
+        if cfg.get("use_density_normalization"):
+            raise UnsupportedModel("density-normalised interaction blocks are not supported yet")
+        if cfg.get("use_agnostic_product"):
+            raise UnsupportedModel("agnostic product blocks are not supported yet")
+        if cfg.get("apply_cutoff", True) is False:
+            raise UnsupportedModel("apply_cutoff=False models are not supported yet")
+        heads = cfg.get("heads")
+        if heads and len(heads) > 1:
+            raise UnsupportedModel("multi-head models are not supported yet")
+        inter_cls = cfg.get("interaction_cls", "RealAgnosticResidualInteractionBlock")
+        if inter_cls not in SUPPORTED_INTERACTIONS:
+            raise UnsupportedModel(f"interaction block {inter_cls} is not supported yet")
+        gate = cfg.get("gate", "silu")
+        if gate not in ("silu", None):
+            raise UnsupportedModel(f"gate {gate!r} is not supported")
+
+        r_max = float(cfg["r_max"])
+        num_bessel = int(cfg.get("num_bessel", 10))
+        poly_p = int(cfg.get("num_polynomial_cutoff", 5))
+        max_ell = int(cfg.get("max_ell", 3))
+        T = int(cfg.get("num_interactions", 2))
+        hidden = Irreps(cfg.get("hidden_irreps", "128x0e"))
+        corr = cfg.get("correlation", 3)
+        corr = [int(corr)] * T if isinstance(corr, int) else [int(c) for c in corr]
+        num_elements = int(cfg.get("num_elements", 89))
+        avg = float(cfg.get("avg_num_neighbors", 1.0))
+        radial_MLP = list(cfg.get("radial_MLP") or [64, 64, 64])
+        first_nonres = bool(cfg.get("first_interaction_nonresidual", False))
+        ae = cfg.get("atomic_energies")
+        ae = np.zeros(num_elements) if ae is None else np.asarray(ae, dtype=np.float64)
+        if ae.ndim == 2:
+            if ae.shape[0] != 1:
+                raise UnsupportedModel("multi-head atomic energies are not supported yet")
+            ae = ae[0]
+
+        sh = Irreps.spherical_harmonics(max_ell)
+        C = hidden[0].mul
+        if any(m.mul != C for m in hidden):
+            raise UnsupportedModel("hidden irreps must share one multiplicity")
+        inter_irreps = Irreps([(C, ir) for _, ir in sh])
+        hidden_scalar = hidden.scalars()
+
+        spec = ModelSpec(
+            config=config, r_max=r_max, num_bessel=num_bessel, poly_p=poly_p,
+            max_ell=max_ell, num_interactions=T, num_elements=num_elements,
+            hidden=hidden, C=C, avg_num_neighbors=avg, radial_MLP=radial_MLP,
+            model_type=model_type, scale=float(cfg.get("scale", 1.0)),
+            shift=float(cfg.get("shift", 0.0)), z_table=cfg.get("z_table"),
+            atomic_energies=ae, irreps_sh=sh, interaction_irreps=inter_irreps,
+        )
+        if isinstance(spec.scale, list) or isinstance(spec.shift, list):
+            raise UnsupportedModel("per-head scale/shift is not supported yet")
+
+        layer_in = hidden_scalar
+        for t in range(T):
+            layer_hidden = hidden if t < T - 1 else hidden_scalar
+            residual = not (t == 0 and first_nonres)
+            if residual:
+                skip = SkipSpec.build(layer_in, num_elements, layer_hidden)
+            else:
+                skip = SkipSpec.build(inter_irreps, num_elements, inter_irreps)
+            conv = ConvSpec.build(layer_in, sh, inter_irreps)
+            lay = LayerSpec(
+                index=t,
+                irreps_in=layer_in,
+                hidden=layer_hidden,
+                residual=residual,
+                skip=skip,
+                linear_up=LinearSpec.build(layer_in, layer_in),
+                conv=conv,
+                mlp_widths=[num_bessel, *radial_MLP, conv.weight_numel],
+                linear=LinearSpec.build(conv.irreps_mid, inter_irreps),
+                sc=SCSpec.build(inter_irreps, layer_hidden, corr[t], num_elements),
+                prod_linear=LinearSpec.build(layer_hidden, layer_hidden),
+                readout_nonlinear=(t == T - 1),
+            )
+            if t < T - 1:
+                lay.readout_linear = LinearSpec.build(layer_hidden, Irreps("1x0e"))
+            else:
+                lay.readout_1 = LinearSpec.build(layer_hidden, Irreps("16x0e"))
+                lay.readout_2 = LinearSpec.build(Irreps("16x0e"), Irreps("1x0e"))
+            spec.layers.append(lay)
+            layer_in = layer_hidden
+        return spec
+
+    # ------------------------------------------------------------------
+    def weight_shapes(self) -> dict[str, tuple[int, ...]]:
+        """Every array of the converted ``weights.npz`` with its shape."""
+        s: dict[str, tuple[int, ...]] = {
+            "atomic_energies_fn.atomic_energies": (self.num_elements,),
+            "node_embedding.linear.weights.0": (self.num_elements, self.C),
+            "radial_embedding.bessel_fn.bessel_weights": (self.num_bessel,),
+        }
+        for lay in self.layers:
+            p = f"interactions.{lay.index}"
+            for k, sh in enumerate(lay.linear_up.weight_shapes()):
+                s[f"{p}.linear_up.weights.{k}"] = sh
+            w = lay.mlp_widths
+            for j in range(len(w) - 1):
+                s[f"{p}.conv_tp_weights.layers.{2 * j}.weight"] = (w[j + 1], w[j])
+            for k, sh in enumerate(lay.linear.weight_shapes()):
+                s[f"{p}.linear.weights.{k}"] = sh
+            for k, sh in enumerate(lay.skip.weight_shapes()):
+                s[f"{p}.skip_tp.tp.weights.{k}"] = sh
+            q = f"products.{lay.index}"
+            for c, out in enumerate(lay.sc.outputs):
+                cp = f"{q}.symmetric_contractions.contractions.{c}"
+                s[f"{cp}.weights_max"] = (self.num_elements, out.num_params[-1], lay.sc.C)
+                for j, nu in enumerate(range(out.correlation - 1, 0, -1)):
+                    s[f"{cp}.weights.{j}"] = (self.num_elements, out.num_params[nu - 1], lay.sc.C)
+            for k, sh in enumerate(lay.prod_linear.weight_shapes()):
+                s[f"{q}.linear.weights.{k}"] = sh
+            r = f"readouts.{lay.index}"
+            if lay.readout_linear is not None:
+                for k, sh in enumerate(lay.readout_linear.weight_shapes()):
+                    s[f"{r}.linear.weights.{k}"] = sh
+            else:
+                for k, sh in enumerate(lay.readout_1.weight_shapes()):
+                    s[f"{r}.linear_1.weights.{k}"] = sh
+                for k, sh in enumerate(lay.readout_2.weight_shapes()):
+                    s[f"{r}.linear_2.weights.{k}"] = sh
+        return s
