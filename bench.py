@@ -1,0 +1,347 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 MACE energy + forces step (driver contract).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Workload (the headline): medium MACE
+(128x0e + 128x1o, lmax 3, correlation 3, 2 layers, r_max 6 A, 8 Bessel,
+radial MLP [64,64,64]) with seeded random-init weights (seed 1), on diamond Si
+5x5x5 = 1000 atoms rattled by 0.05 A (seed 1); energy + forces per step.  The
+neighbour list is the calculator's cached one (cutoff r_max + 0.5 A skin), as in
+the reference's own MD timing.  All data are synthetic.
+
+One JSON line (rank 0).  ``value`` is device-timed with CUDA events, inputs
+resident in HBM, L2 flushed between timed steps; ``e2e`` is the same metric
+through the public calculator API (host positions in, host forces out);
+``roofline`` is the dominant kernel's algorithmic work over its event-timed
+launch duration; ``cpu_baseline`` times the CPU oracle port on this host.
+
+With N > 1 (torchrun), every rank evaluates its own independent Si1000
+structure (structure sharding, no data-path collective): weak scaling.
+
+``--impl reference`` times the reference algorithm's CPU restatement (the
+reference itself runs on MLX/Metal, absent here) on the host cores, rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "energy+forces atom-steps/s, medium-MACE Si1000 fp32"
+UNIT = "atom-steps/s"
+AVG_NUM_NEIGHBORS = 44.0
+WORKLOAD = ("config1: medium MACE (128x0e+128x1o, lmax3, corr3, 2 layers, r_max 6.0) random-init seed 1; "
+            "diamond Si 5x5x5 = 1000 atoms rattled 0.05 A (seed 1); energy+forces; cached NL r_max+0.5 skin")
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=20.0, help="budget of the CPU baseline sample")
+    return ap.parse_args()
+
+
+def make_structure(rank: int):
+    from mace_mlx_b200.structures import diamond_si
+
+    return diamond_si(5, 0.05, 1 + 1000 * rank)
+
+
+def make_model_dir(tmp: str) -> str:
+    from mace_mlx_b200.weights import write_random_model
+
+    d = Path(tmp) / "medium_seed1"
+    write_random_model(d, "medium", seed=1, z_table=list(range(1, 90)), avg_num_neighbors=AVG_NUM_NEIGHBORS)
+    return str(d)
+
+
+# ---------------------------------------------------------------------------
+# clocks sampling during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:  # noqa: BLE001
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:  # noqa: BLE001
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# CPU oracle port timing (cpu_baseline and --impl reference)
+# ---------------------------------------------------------------------------
+def time_cpu_port(st, model_dir: str, budget_s: float, max_steps: int, warmup: int = 1):
+    import torch
+
+    from mace_mlx_b200.weights import load_model_dir
+    from oracle.model import OracleMACE
+    from oracle.nl import neighbour_list
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    config, weights = load_model_dir(model_dir)
+    orc = OracleMACE(config, weights, dtype=torch.float32)
+    r_cut = float(config["r_max"]) + 0.5
+    i, j, S = neighbour_list(st.positions, st.cell, st.pbc, r_cut)
+    species = st.numbers - 1
+    for _ in range(max(0, warmup)):
+        orc.compute(st.positions, species, i, j, S, st.cell)
+    times = []
+    t_start = time.perf_counter()
+    while len(times) < max(1, max_steps):
+        t0 = time.perf_counter()
+        orc.compute(st.positions, species, i, j, S, st.cell)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_start > budget_s:
+            break
+    t = statistics.median(times)
+    return len(st) / t, threads, len(times), t
+
+
+def reference_arm(args, rank: int, world: int):
+    if rank != 0:
+        return 0
+    st = make_structure(0)
+    with tempfile.TemporaryDirectory() as tmp:
+        md = make_model_dir(tmp)
+        budget = max(30.0, min(150.0, 6.0 * max(1, args.steps)))
+        value, threads, n, t = time_cpu_port(st, md, budget, args.steps, warmup=min(args.warmup, 1))
+    sample = (f"{n} full steps of the 1000-atom Si workload (median {t:.2f} s/step) with the torch-CPU fp32 "
+              f"restatement of the reference algorithm; warm-up {min(args.warmup, 1)}; MLX absent on this host")
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": n, "warmup": min(args.warmup, 1),
+        "ms_per_step": t * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "impl": "reference",
+        "config": {"workload": WORKLOAD, "parallelism": "single host process"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# B200 arm
+# ---------------------------------------------------------------------------
+def b200_arm(args, rank: int, world: int, local_rank: int):
+    import torch
+    import torch.distributed as dist
+
+    from mace_mlx_b200.atoms import Atoms
+    from mace_mlx_b200.calculators import MACECalculator
+    from mace_mlx_b200.workmodel import kernel_work
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    st = make_structure(rank)
+    tmp = tempfile.mkdtemp(prefix=f"bench_r{rank}_")
+    md = make_model_dir(tmp)
+    calc = MACECalculator(model_path=md, device=f"cuda:{local_rank}", skin=0.5)
+    atoms = Atoms(st.numbers, st.positions, st.cell, st.pbc)
+    calc.calculate(atoms, ["energy", "forces"])
+    model = calc.model
+    edges = calc._nl_cache
+    N, E = len(atoms), edges.n_edges
+    out = calc._out
+    pos = out["pos"]
+    cell = out["cell"]
+    species = calc._species_dev
+    gptr = calc._graph_ptr_dev
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)  # 256 MB > L2
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    def step():
+        model.evaluate(pos, cell, species, gptr, edges, forces=True, virial=False, out=out)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    barrier()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with ClockSampler(local_rank) as clk:
+        barrier()
+        for k in range(args.steps):
+            flush.zero_()
+            ev[k][0].record()
+            step()
+            ev[k][1].record()
+        barrier()
+    dev_ms = [a.elapsed_time(b) for a, b in ev]
+    total_ms = float(sum(dev_ms))
+    launches = model.last_launch_count()
+    # e2e through the public API: host positions in, host energy/forces out
+    rng = np.random.default_rng(7 + rank)
+    jitter = [st.positions + rng.normal(0, 1e-4, st.positions.shape) for _ in range(args.steps + args.warmup)]
+    for k in range(args.warmup):
+        atoms.positions = jitter[k]
+        calc.calculate(atoms, ["energy", "forces"])
+    barrier()
+    t0 = time.perf_counter()
+    for k in range(args.steps):
+        atoms.positions = jitter[args.warmup + k]
+        calc.calculate(atoms, ["energy", "forces"])
+    e2e_s = time.perf_counter() - t0
+    barrier()
+    # per-kernel event timing (separate pass, same inputs)
+    model.profile_enable(True)
+    for _ in range(args.steps):
+        step()
+    prof = model.profile_read()
+    model.profile_enable(False)
+    if world > 1:
+        tt = torch.tensor([total_ms, e2e_s], dtype=torch.float64, device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        total_ms, e2e_s = float(tt[0]), float(tt[1])
+    if rank != 0:
+        return 0
+    value = world * N * args.steps / (total_ms / 1e3)
+    e2e_value = world * N * args.steps / e2e_s
+    # roofline of the dominant kernel
+    work = kernel_work(model.spec, N, E)
+    peaks = {}
+    pp = ROOT / "MEASURED_PEAKS.json"
+    if pp.exists():
+        peaks = json.loads(pp.read_text())
+    hbm = float(peaks.get("hbm_gbs", 6650.0))
+    bf16 = float(peaks.get("bf16_tflops", 1590.0))
+    peak_src = "measured" if pp.exists() else "fallback"
+    prof.sort(key=lambda r: -r["ms"])
+    tot_prof = sum(r["ms"] for r in prof)
+    top = prof[0]
+    avg_ms = top["ms"] / top["count"]
+    wk = work.get((top["name"], top["layer"]), {"flops": 0, "bytes": 0})
+    intensity = wk["flops"] / max(wk["bytes"], 1)
+    ridge = bf16 * 1e12 / (hbm * 1e9)
+    if intensity > ridge * 0.05:  # compute-heavy: compare with the tensor pipe
+        ach = wk["flops"] / (avg_ms * 1e-3) / 1e12
+        roof = {"bound": "tensor", "achieved": ach, "peak": bf16, "unit": "TFLOP/s", "frac": ach / bf16}
+    else:
+        ach = wk["bytes"] / (avg_ms * 1e-3) / 1e9
+        roof = {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm}
+    traffic = None
+    tp = ROOT / "profiles" / "ncu_traffic.json"
+    if tp.exists():
+        tr = json.loads(tp.read_text())
+        traffic = tr.get(f"{top['name']}/{top['layer']}")
+    roof.update({
+        "traffic": traffic, "kernel": f"{top['name']} layer {top['layer']}",
+        "kernel_share": top["ms"] / tot_prof, "avg_launch_ms": avg_ms,
+        "algorithmic_flops": wk["flops"], "algorithmic_bytes": wk["bytes"], "peak_source": peak_src,
+        "all_kernels_ms_per_step": {f"{r['name']}/{r['layer']}": r["ms"] / max(1, r["count"]) for r in prof},
+    })
+    cpu = None
+    if world == 1:
+        try:
+            v, threads, n, t = time_cpu_port(st, md, args.cpu_seconds, 3)
+            cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
+                   "sample": f"{n} full 1000-atom Si steps (median {t:.2f} s) of the torch-CPU fp32 oracle port"}
+        except Exception as e:  # noqa: BLE001
+            cpu = {"value": None, "unit": UNIT, "cores": os.cpu_count(), "kind": "port", "sample": f"failed: {e}"}
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "n_atoms_per_gpu": N, "n_edges_per_gpu": E,
+                   "l2": "flushed between timed steps (256 MB write)",
+                   "parallelism": f"structure-sharded x{world} (one independent Si1000 per GPU)"},
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": N * 3 * 4 + 9 * 4,
+                "d2h_bytes_per_step": 8 + N * 3 * 4 + N * 4, "ms_per_step": e2e_s * 1e3 / args.steps},
+        "gpu_launches": launches * args.steps,
+        "clocks": clk.summary(),
+        "roofline": roof,
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return reference_arm(args, rank, world)
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        return b200_arm(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    sys.exit(main())

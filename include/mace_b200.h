@@ -233,6 +233,17 @@ int mace_debug_buffer(mace_ctx* ctx, int32_t id, const float** ptr, int64_t* len
 /* Number of kernel launches the last mace_forward_backward issued. */
 int mace_last_launch_count(const mace_ctx* ctx, int32_t* count);
 
+/*
+ * Opt-in timing of every launch with CUDA events recorded on the launching
+ * stream (for benchmarks; adds an event pair per kernel).  Enabling resets the
+ * totals.  mace_profile_read synchronises, then returns per (kernel, layer):
+ * name (32 bytes each in `names`), layer (-1 = not per layer), launch count and
+ * total milliseconds since the previous read.
+ */
+int mace_profile_enable(mace_ctx* ctx, int32_t enable);
+int mace_profile_read(mace_ctx* ctx, int32_t max_entries, char* names, int32_t* layers,
+                      int32_t* counts, double* total_ms, int32_t* n_entries);
+
 /* Synchronise the device, return and clear the context's device error flag
  * (1 = an edge's reverse index did not point back to it). */
 int mace_ctx_error_flag(mace_ctx* ctx, int32_t* flag);

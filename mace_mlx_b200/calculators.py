@@ -1,0 +1,253 @@
+"""ASE calculator drop-in: ``MACECalculator`` / ``mace_mp`` / ``mace_off``.
+
+Same constructor arguments, results dictionary, neighbour-list skin cache and
+error behaviour as the reference's ``mace_mlx/calculators.py`` (line numbers
+below refer to that file); the step itself runs on a B200 through
+``libmace_b200``:
+
+* constructor and ``model_paths`` / committee handling     -- :94-125
+* model resolution and the converted-model cache layout    -- :28-38, :201-267
+* neighbour-list rebuild rule (r_max + skin, skin/2 drift) -- :273-317
+* species validation message                               -- :341-371
+* sticky stress, results keys, Voigt stress                 -- :384-425, :489-531
+* ``mace_mp`` / ``mace_off`` / ``mace_anicc`` / ``mace_omol`` -- :573-640
+
+Differences: ``device`` names a CUDA device ("cuda", "gpu", "cuda:1", or an
+index); "cpu" is rejected because this build has no CPU path.  ``use_compile``
+is accepted for compatibility and ignored (the step is a fixed kernel
+sequence).  Only float32 is computed.
+"""
+
+from __future__ import annotations
+
+import os
+import warnings
+from pathlib import Path
+
+import numpy as np
+import torch
+
+from .atoms import Calculator, all_changes
+from .model import EdgeSet, MACEModel
+
+_CONVERTER_CACHE_VERSION = 2
+_NAMED = ("small", "medium", "large", "medium-mpa-0", "small-0b", "medium-0b", "small-0b2",
+          "medium-0b2", "large-0b2", "medium-0b3", "medium-omat-0", "mh-1")
+
+
+def _conversion_cache_root() -> Path:
+    env = os.environ.get("MACE_MLX_CACHE_DIR")
+    if env:
+        return Path(env).expanduser()
+    return Path.home() / ".cache" / "mace_mlx"
+
+
+def _resolve_device(device) -> torch.device:
+    if isinstance(device, torch.device):
+        return device
+    if isinstance(device, int):
+        return torch.device("cuda", device)
+    d = str(device or "cuda").lower()
+    if d in ("gpu", "cuda", "mps", ""):
+        return torch.device("cuda", torch.cuda.current_device() if torch.cuda.is_available() else 0)
+    if d.startswith("cuda:") or d.startswith("gpu:"):
+        return torch.device("cuda", int(d.split(":", 1)[1]))
+    if d == "cpu":
+        raise ValueError("device='cpu' is not supported: this MACE build computes on a CUDA GPU only")
+    raise ValueError(f"unknown device {device!r}")
+
+
+class MACEMLXCalculator(Calculator):
+    """ASE calculator computing MACE energy, forces and stress on a B200."""
+
+    implemented_properties = ["energy", "energies", "free_energy", "node_energy", "forces", "stress"]
+    _converted_cache: dict[str, str] = {}
+
+    def __init__(self, model_path: str | None = None, device="cuda", default_dtype: str = "float32",
+                 head: str | None = None, skin: float = 0.5, use_compile: bool = True, **kwargs):
+        if model_path is None:
+            model_path = kwargs.pop("model_paths", None)
+            if isinstance(model_path, (list, tuple)):
+                if len(model_path) > 1:
+                    raise NotImplementedError(
+                        "committee models are not supported; "
+                        f"got {len(model_path)} model paths. Pass a single model."
+                    )
+                model_path = model_path[0] if model_path else None
+        if model_path is None:
+            model_path = "medium-mpa-0"
+        if default_dtype == "float64":
+            warnings.warn(
+                "float64 is not computed on this build; falling back to float32. "
+                "Energies/forces will differ from mace-torch's float64 default at "
+                "the float32 precision level."
+            )
+            default_dtype = "float32"
+        if default_dtype != "float32":
+            raise NotImplementedError(f"default_dtype={default_dtype!r} is not supported (float32 only)")
+        super().__init__(**kwargs)
+        self._device = _resolve_device(device)
+        model_dir = self._resolve_model(str(model_path))
+        self.model = MACEModel(model_dir, device=self._device)
+        self._head = head
+        heads = self.model.config.get("heads")
+        if head is not None and heads and head not in heads:
+            raise ValueError(f"Head '{head}' not found in model heads: {heads}")
+        self.r_max = float(self.model.r_max)
+        self.z_table = self.model.z_table
+        self._skin = float(skin)
+        self._use_compile = use_compile
+        self._nl_cache: EdgeSet | None = None
+        self._cache_positions = None
+        self._cache_cell = None
+        self._cache_pbc = None
+        self._cache_natoms = 0
+        self._cached_numbers = None
+        self._species_dev = None
+        self._graph_ptr_dev = None
+        self._stress_always = False
+        self._out = None
+        self._host = None
+
+    # ------------------------------------------------------------------
+    @classmethod
+    def _resolve_model(cls, model_path: str) -> str:
+        is_named = model_path.startswith("off-") or model_path in _NAMED
+        if not is_named:
+            return model_path
+        if model_path in cls._converted_cache and Path(cls._converted_cache[model_path]).exists():
+            return cls._converted_cache[model_path]
+        target = _conversion_cache_root() / model_path / f"v{_CONVERTER_CACHE_VERSION}"
+        if (target / "config.json").exists() and (target / "weights.npz").exists():
+            cls._converted_cache[model_path] = str(target)
+            return str(target)
+        raise FileNotFoundError(
+            f"named model {model_path!r} is not in the converted-model cache ({target}). "
+            "Convert it once with the reference's converter (needs torch + mace-torch and a "
+            "download) or pass the path of a converted config.json + weights.npz directory."
+        )
+
+    # ------------------------------------------------------------------
+    def _needs_neighbor_update(self, atoms) -> bool:
+        if self._nl_cache is None:
+            return True
+        if len(atoms) != self._cache_natoms:
+            return True
+        if not np.array_equal(atoms.pbc, self._cache_pbc):
+            return True
+        if not np.allclose(np.array(atoms.cell), self._cache_cell, atol=1e-10):
+            return True
+        if self._skin <= 0:
+            return True
+        disp = np.linalg.norm(atoms.positions - self._cache_positions, axis=1)
+        return float(np.max(disp, initial=0.0)) > self._skin / 2
+
+    def _species(self, atoms):
+        numbers = atoms.get_atomic_numbers()
+        if self._species_dev is None or self._cached_numbers is None or not np.array_equal(numbers, self._cached_numbers):
+            idx = self.model.species_index(numbers)
+            self._species_dev = torch.as_tensor(idx, device=self._device)
+            self._cached_numbers = numbers.copy()
+            self._graph_ptr_dev = torch.tensor([0, len(numbers)], dtype=torch.int32, device=self._device)
+        return self._species_dev
+
+    def _buffers(self, n: int, stress: bool):
+        if self._out is None or self._out["node_energy"].shape[0] != n:
+            dev = self._device
+            self._out = {
+                "energy": torch.empty(1, dtype=torch.float64, device=dev),
+                "node_energy": torch.empty(n, dtype=torch.float32, device=dev),
+                "forces": torch.empty(n, 3, dtype=torch.float32, device=dev),
+                "virial": torch.empty(9, dtype=torch.float64, device=dev),
+                "pos": torch.empty(n, 3, dtype=torch.float32, device=dev),
+                "cell": torch.empty(3, 3, dtype=torch.float32, device=dev),
+            }
+            self._host = {
+                "pos": torch.empty(n, 3, dtype=torch.float32, pin_memory=True),
+                "cell": torch.empty(3, 3, dtype=torch.float32, pin_memory=True),
+                "energy": torch.empty(1, dtype=torch.float64, pin_memory=True),
+                "virial": torch.empty(9, dtype=torch.float64, pin_memory=True),
+                "forces": torch.empty(n, 3, dtype=torch.float32, pin_memory=True),
+                "node_energy": torch.empty(n, dtype=torch.float32, pin_memory=True),
+            }
+        return self._out, self._host
+
+    # ------------------------------------------------------------------
+    def calculate(self, atoms=None, properties=None, system_changes=all_changes):
+        super().calculate(atoms, properties, system_changes)
+        atoms = self.atoms if atoms is None else atoms
+        dev = self._device
+        n = len(atoms)
+        with torch.cuda.device(dev):
+            species = self._species(atoms)
+            has_cell = atoms.cell.rank > 0
+            out, host = self._buffers(n, False)
+            # host -> device: positions (float32) and cell
+            host["pos"].numpy()[:] = atoms.positions
+            pos = out["pos"]
+            pos.copy_(host["pos"], non_blocking=True)
+            cell = None
+            if has_cell:
+                host["cell"].numpy()[:] = np.array(atoms.cell)
+                cell = out["cell"]
+                cell.copy_(host["cell"], non_blocking=True)
+            if self._needs_neighbor_update(atoms):
+                pos64 = torch.as_tensor(atoms.positions, dtype=torch.float64).to(dev)
+                cell64 = torch.as_tensor(np.array(atoms.cell), dtype=torch.float64).to(dev) if has_cell else None
+                self._nl_cache = self.model.neighbour_list(pos64, cell64, atoms.pbc, self._graph_ptr_dev,
+                                                           self.r_max + self._skin, self._nl_cache)
+                self._cache_positions = atoms.positions.copy()
+                self._cache_cell = np.array(atoms.cell, dtype=np.float64)
+                self._cache_pbc = np.array(atoms.pbc).copy()
+                self._cache_natoms = n
+            if properties is not None and "stress" in properties and atoms.cell.rank == 3:
+                self._stress_always = True
+            compute_stress = "stress" in (properties or self.implemented_properties)
+            compute_stress = (compute_stress or self._stress_always) and atoms.cell.rank == 3
+            self.model.evaluate(pos, cell, species, self._graph_ptr_dev, self._nl_cache, forces=True,
+                                virial=compute_stress, out=out)
+            # device -> host
+            host["energy"].copy_(out["energy"], non_blocking=True)
+            host["forces"].copy_(out["forces"], non_blocking=True)
+            host["node_energy"].copy_(out["node_energy"], non_blocking=True)
+            if compute_stress:
+                host["virial"].copy_(out["virial"], non_blocking=True)
+            torch.cuda.current_stream(dev).synchronize()
+        energy = float(host["energy"][0])
+        self.results["energy"] = energy
+        self.results["free_energy"] = energy
+        self.results["forces"] = host["forces"].numpy().copy()
+        self.results["node_energy"] = host["node_energy"].numpy().copy()
+        self.results["energies"] = self.results["node_energy"]
+        if compute_stress:
+            g = host["virial"].numpy().reshape(3, 3).astype(np.float64)
+            s = 0.5 * (g + g.T) / abs(np.linalg.det(np.array(atoms.cell, dtype=np.float64)))
+            self.results["stress"] = s[[0, 1, 2, 1, 0, 0], [0, 1, 2, 2, 2, 1]]
+
+
+def mace_mp(model: str | None = None, device="cuda", default_dtype: str = "float32", head: str | None = None,
+            dispersion: bool = False, return_raw_model: bool = False, **kwargs) -> MACEMLXCalculator:
+    """MACE-MP foundation-model calculator (drop-in for ``mace.calculators.mace_mp``)."""
+    if return_raw_model:
+        raise NotImplementedError("return_raw_model is not supported")
+    if dispersion:
+        warnings.warn("D3 dispersion corrections are not supported. Ignoring dispersion=True.")
+    for key in ("damping", "dispersion_xc", "dispersion_cutoff"):
+        kwargs.pop(key, None)
+    return MACEMLXCalculator(model_path=model, device=device, default_dtype=default_dtype, head=head, **kwargs)
+
+
+def mace_off(model: str = "small", device="cuda", default_dtype: str = "float32", **kwargs) -> MACEMLXCalculator:
+    """MACE-OFF organic force-field calculator (drop-in for ``mace.calculators.mace_off``)."""
+    return MACEMLXCalculator(model_path=f"off-{model}", device=device, default_dtype=default_dtype, **kwargs)
+
+
+def mace_anicc(**kwargs):
+    raise NotImplementedError("mace_anicc is not supported. Use mace-torch for ANI models.")
+
+
+def mace_omol(**kwargs):
+    raise NotImplementedError("mace_omol is not supported. Use mace-torch for OMOL models.")
+
+
+MACECalculator = MACEMLXCalculator

@@ -89,6 +89,20 @@ struct mace_ctx {
   // bookkeeping
   int launches = 0;
   int64_t last_N = 0, last_E = 0;
+  // opt-in per-launch timing with CUDA events on the launching stream
+  static constexpr int PROF_MAX = 256;
+  bool prof_on = false;
+  int prof_n = 0;
+  cudaEvent_t ev[2 * PROF_MAX] = {};
+  const char* prof_name[PROF_MAX] = {};
+  int prof_layer[PROF_MAX] = {};
+  struct ProfAcc {
+    std::string name;
+    int layer;
+    int count;
+    double ms;
+  };
+  std::vector<ProfAcc> prof_acc;
 };
 
 namespace {
@@ -127,6 +141,45 @@ int alloc(mace_ctx* c, T** p, int64_t count) {
     int _rc = (x);          \
     if (_rc) return _rc;    \
   } while (0)
+
+// fold recorded event pairs into the per-(kernel, layer) totals
+int prof_fold(mace_ctx* c) {
+  if (c->prof_n == 0) return MACE_OK;
+  MACE_CUDA_TRY(cudaEventSynchronize(c->ev[2 * c->prof_n - 1]));
+  for (int i = 0; i < c->prof_n; ++i) {
+    float ms = 0.f;
+    MACE_CUDA_TRY(cudaEventElapsedTime(&ms, c->ev[2 * i], c->ev[2 * i + 1]));
+    bool found = false;
+    for (auto& a : c->prof_acc)
+      if (a.layer == c->prof_layer[i] && a.name == c->prof_name[i]) {
+        a.count += 1;
+        a.ms += ms;
+        found = true;
+        break;
+      }
+    if (!found) c->prof_acc.push_back({c->prof_name[i], c->prof_layer[i], 1, (double)ms});
+  }
+  c->prof_n = 0;
+  return MACE_OK;
+}
+
+// every kernel launch of the step goes through here: counted, and timed when profiling
+template <class Fn>
+int launch(mace_ctx* c, const char* name, int layer, cudaStream_t s, Fn&& fn) {
+  ++c->launches;
+  int slot = -1;
+  if (c->prof_on && c->prof_n < mace_ctx::PROF_MAX) {
+    slot = c->prof_n++;
+    c->prof_name[slot] = name;
+    c->prof_layer[slot] = layer;
+    MACE_CUDA_TRY(cudaEventRecord(c->ev[2 * slot], s));
+  }
+  int rc = fn();
+  if (slot >= 0) MACE_CUDA_TRY(cudaEventRecord(c->ev[2 * slot + 1], s));
+  return rc;
+}
+
+#define LAUNCH(name, layer, expr) TRY(launch(c, name, layer, s, [&]() { return (expr); }))
 
 int reserve(mace_ctx* c, int64_t N, int64_t E) {
   const mace_model_desc& d = c->desc;
@@ -201,8 +254,9 @@ LinJob make_job(int d, int n_k, const int* k_off, int out_off, const float* w, i
   return j;
 }
 
-int run_linear_slots(mace_ctx* c, int64_t N, const mace_slots& in_slots, const mace_slots& out_slots,
-                     const int64_t* f_w, const float* in, float* out, int accumulate, cudaStream_t s) {
+int run_linear_slots(mace_ctx* c, const char* name, int layer, int64_t N, const mace_slots& in_slots,
+                     const mace_slots& out_slots, const int64_t* f_w, const float* in, float* out,
+                     int accumulate, cudaStream_t s) {
   // 1-to-1 linears: slot q of `in_slots` -> slot q of `out_slots`
   LinParams p{};
   p.N = N;
@@ -216,8 +270,7 @@ int run_linear_slots(mace_ctx* c, int64_t N, const mace_slots& in_slots, const m
     int ko = in_slots.off[q];
     p.job[q] = make_job(2 * in_slots.l[q] + 1, 1, &ko, out_slots.off[q], F(c, f_w[q]), p.C, 1.f, accumulate);
   }
-  ++c->launches;
-  return launch_linear(p, s);
+  return launch(c, name, layer, s, [&]() { return launch_linear(p, s); });
 }
 
 ConvParams conv_params(mace_ctx* c, int t, int64_t N, const mace_system* sys) {
@@ -349,6 +402,7 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
   c->launches = 0;
   c->last_N = N;
   c->last_E = E;
+  if (c->prof_on) TRY(prof_fold(c));
   const bool want_grad = (flags & (MACE_WANT_FORCES | MACE_WANT_VIRIAL)) != 0;
 
   EdgeParams ep{};
@@ -371,14 +425,10 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
   ep.db = c->db;
   ep.dv = c->dv;
   ep.virial_part = (flags & MACE_WANT_VIRIAL) ? c->vir_part : nullptr;
-  if (E > 0) {
-    ++c->launches;
-    TRY(launch_edge_fwd(ep, s));
-  }
+  if (E > 0) LAUNCH("edge_fwd", -1, launch_edge_fwd(ep, s));
   {
     EmbedParams p{N, C, sys->species, F(c, d.f_emb), c->h[0]};
-    ++c->launches;
-    TRY(launch_embed(p, s));
+    LAUNCH("embed", -1, launch_embed(p, s));
   }
   const float dscale = d.scale_shift ? d.scale : 1.0f;
   for (int t = 0; t < T; ++t) {
@@ -388,18 +438,13 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
     MACE_CUDA_TRY(cudaMemsetAsync(c->h[t + 1], 0, sizeof(float) * N * L.hid.dim, s));
     if (L.residual) {
       SkipParams sp = skip_params(c, t, N, sys->species, false, L.in, L.hid, c->h[t], c->h[t + 1], 0);
-      ++c->launches;
-      TRY(launch_skip(sp, s));
+      LAUNCH("skip_fwd", t, launch_skip(sp, s));
     }
-    TRY(run_linear_slots(c, N, L.in, L.in, L.f_up, c->h[t], B.up, 0, s));
+    TRY(run_linear_slots(c, "linear_up", t, N, L.in, L.in, L.f_up, c->h[t], B.up, 0, s));
     MlpParams mp = mlp_params(c, t, E);
-    if (E > 0) {
-      ++c->launches;
-      TRY(launch_mlp_fwd(mp, s));
-    }
+    if (E > 0) LAUNCH("mlp_fwd", t, launch_mlp_fwd(mp, s));
     ConvParams cp = conv_params(c, t, N, sys);
-    ++c->launches;
-    TRY(launch_conv_fwd(cp, s));
+    LAUNCH("conv_fwd", t, launch_conv_fwd(cp, s));
     {
       LinParams lp{};
       lp.N = N;
@@ -415,21 +460,18 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
         for (int q = 0; q < g.n_src; ++q) ko[q] = L.conv[g.src[q]].off;
         lp.job[l] = make_job(2 * l + 1, g.n_src, ko, L.inter.off[l], F(c, g.f_w), C, d.inv_avg_num_neighbors, 0);
       }
-      ++c->launches;
-      TRY(launch_linear(lp, s));
+      LAUNCH("linear_msg", t, launch_linear(lp, s));
     }
     const float* sc_in = B.msg;
     if (!L.residual) {
       SkipParams sp = skip_params(c, t, N, sys->species, false, L.inter, L.inter, B.msg, B.msg2, 0);
       MACE_CUDA_TRY(cudaMemsetAsync(B.msg2, 0, sizeof(float) * N * L.inter.dim, s));
-      ++c->launches;
-      TRY(launch_skip(sp, s));
+      LAUNCH("skip_fwd", t, launch_skip(sp, s));
       sc_in = B.msg2;
     }
     ScParams scp = sc_params(c, t, N, sys->species, sc_in, B.B, nullptr, nullptr);
-    ++c->launches;
-    TRY(launch_sc_fwd(scp, s));
-    TRY(run_linear_slots(c, N, L.hid, L.hid, L.f_prod, B.B, c->h[t + 1], 1, s));
+    LAUNCH("sc_fwd", t, launch_sc_fwd(scp, s));
+    TRY(run_linear_slots(c, "linear_prod", t, N, L.hid, L.hid, L.f_prod, B.B, c->h[t + 1], 1, s));
     ReadoutParams rp{};
     rp.N = N;
     rp.C = C;
@@ -442,8 +484,7 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
     rp.e = c->e_layers + (int64_t)t * N;
     rp.dh = c->dh[t + 1];
     rp.dscale = dscale;
-    ++c->launches;
-    TRY(launch_readout(rp, s));
+    LAUNCH("readout", t, launch_readout(rp, s));
   }
   {
     EnergyParams p{};
@@ -459,8 +500,7 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
     p.shift = d.shift;
     p.node_energy = out ? out->node_energy : nullptr;
     p.energy = out ? out->energy : nullptr;
-    ++c->launches;
-    TRY(launch_energy(p, s));
+    LAUNCH("energy", -1, launch_energy(p, s));
   }
   if (!want_grad) return MACE_OK;
 
@@ -471,17 +511,15 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
   for (int t = T - 1; t >= 0; --t) {
     const mace_layer_desc& L = d.layers[t];
     LayerBufs& B = c->lb[t];
-    TRY(run_linear_slots(c, N, L.hid, L.hid, L.f_prod_t, c->dh[t + 1], B.dB, 0, s));
+    TRY(run_linear_slots(c, "linear_prod_bwd", t, N, L.hid, L.hid, L.f_prod_t, c->dh[t + 1], B.dB, 0, s));
     float* dsc_in = B.dmsg;
     ScParams scp = sc_params(c, t, N, sys->species, L.residual ? B.msg : B.msg2, nullptr, B.dB,
                              L.residual ? B.dmsg : B.dmsg2);
-    ++c->launches;
-    TRY(launch_sc_bwd(scp, s));
+    LAUNCH("sc_bwd", t, launch_sc_bwd(scp, s));
     if (!L.residual) {
       MACE_CUDA_TRY(cudaMemsetAsync(B.dmsg, 0, sizeof(float) * N * L.inter.dim, s));
       SkipParams sp = skip_params(c, t, N, sys->species, true, L.inter, L.inter, B.dmsg2, B.dmsg, 1);
-      ++c->launches;
-      TRY(launch_skip(sp, s));
+      LAUNCH("skip_bwd", t, launch_skip(sp, s));
     }
     {
       // dA[mid slot k] = inv_avg * dmsg[inter slot l_k] @ W_l^T (block q of the concat-K)
@@ -501,45 +539,34 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
                                          g.n_src * C, d.inv_avg_num_neighbors, 0);
         }
       }
-      ++c->launches;
-      TRY(launch_linear(lp, s));
+      LAUNCH("linear_msg_bwd", t, launch_linear(lp, s));
     }
     ConvParams cp = conv_params(c, t, N, sys);
-    ++c->launches;
-    TRY(launch_conv_bwd(cp, s));
+    LAUNCH("conv_bwd", t, launch_conv_bwd(cp, s));
     MlpParams mp = mlp_params(c, t, E);
-    if (E > 0) {
-      ++c->launches;
-      TRY(launch_mlp_bwd(mp, s));
-    }
+    if (E > 0) LAUNCH("mlp_bwd", t, launch_mlp_bwd(mp, s));
     if (t > 0) {
       // dh[t] holds the readout seed of layer t-1
-      TRY(run_linear_slots(c, N, L.in, L.in, L.f_up_t, B.dup, c->dh[t], 1, s));
+      TRY(run_linear_slots(c, "linear_up_bwd", t, N, L.in, L.in, L.f_up_t, B.dup, c->dh[t], 1, s));
       if (L.residual) {
         SkipParams sp = skip_params(c, t, N, sys->species, true, L.in, L.hid, c->dh[t + 1], c->dh[t], 1);
-        ++c->launches;
-        TRY(launch_skip(sp, s));
+        LAUNCH("skip_bwd", t, launch_skip(sp, s));
       }
     }
   }
-  int n_blocks = 0;
-  if (E > 0) {
-    ++c->launches;
-    TRY(launch_edge_bwd(ep, &n_blocks, s));
-  }
+  int n_blocks = (int)((E + 255) / 256);
+  if (E > 0) LAUNCH("edge_bwd", -1, launch_edge_bwd(ep, &n_blocks, s));
   if (out && out->forces) {
     if (E > 0) {
       ForceParams fp{N, sys->row_ptr, sys->sender, sys->receiver, sys->rev, c->dv, out->forces, c->d_err};
-      ++c->launches;
-      TRY(launch_forces(fp, s));
+      LAUNCH("forces", -1, launch_forces(fp, s));
     } else {
       MACE_CUDA_TRY(cudaMemsetAsync(out->forces, 0, sizeof(float) * 3 * N, s));
     }
   }
   if ((flags & MACE_WANT_VIRIAL) && out && out->virial) {
     if (E > 0) {
-      ++c->launches;
-      TRY(launch_virial_reduce(c->vir_part, n_blocks, out->virial, s));
+      LAUNCH("virial", -1, launch_virial_reduce(c->vir_part, n_blocks, out->virial, s));
     } else {
       MACE_CUDA_TRY(cudaMemsetAsync(out->virial, 0, sizeof(double) * 9, s));
     }
@@ -600,6 +627,8 @@ int mace_ctx_destroy(mace_ctx* c) {
   if (!c) return MACE_OK;
   DeviceGuard g(c->device);
   free_ws(c);
+  if (c->ev[0])
+    for (int i = 0; i < 2 * mace_ctx::PROF_MAX; ++i) cudaEventDestroy(c->ev[i]);
   cudaFree(c->d_floats);
   cudaFree(c->d_ints);
   delete c;
@@ -751,6 +780,38 @@ int mace_debug_buffer(mace_ctx* c, int32_t id, const float** ptr, int64_t* len) 
     case 13: *ptr = B.msg2; *len = B.msg2 ? N * L.inter.dim : 0; break;
     default: return fail(MACE_ERR_BAD_ARG, "unknown debug stage");
   }
+  return MACE_OK;
+}
+
+int mace_profile_enable(mace_ctx* c, int32_t enable) {
+  if (!c) return fail(MACE_ERR_BAD_ARG, "null argument");
+  DeviceGuard g(c->device);
+  if (enable && !c->ev[0]) {
+    for (int i = 0; i < 2 * mace_ctx::PROF_MAX; ++i) MACE_CUDA_TRY(cudaEventCreate(&c->ev[i]));
+  }
+  if (c->prof_on && c->prof_n) TRY(prof_fold(c));
+  c->prof_on = enable != 0;
+  c->prof_n = 0;
+  c->prof_acc.clear();
+  return MACE_OK;
+}
+
+int mace_profile_read(mace_ctx* c, int32_t max_entries, char* names, int32_t* layers, int32_t* counts,
+                      double* total_ms, int32_t* n_entries) {
+  if (!c || !n_entries) return fail(MACE_ERR_BAD_ARG, "null argument");
+  DeviceGuard g(c->device);
+  TRY(prof_fold(c));
+  int n = 0;
+  for (const auto& a : c->prof_acc) {
+    if (n >= max_entries) break;
+    if (names) std::snprintf(names + 32 * n, 32, "%s", a.name.c_str());
+    if (layers) layers[n] = a.layer;
+    if (counts) counts[n] = a.count;
+    if (total_ms) total_ms[n] = a.ms;
+    ++n;
+  }
+  *n_entries = n;
+  c->prof_acc.clear();
   return MACE_OK;
 }
 

@@ -187,6 +187,24 @@ class MACEModel:
         nv.check(self.lib.mace_last_launch_count(self.ctx, C.byref(c)), self.lib)
         return c.value
 
+    def profile_enable(self, enable: bool = True) -> None:
+        nv.check(self.lib.mace_profile_enable(self.ctx, int(enable)), self.lib)
+
+    def profile_read(self) -> list[dict]:
+        """Per (kernel, layer) launch counts and total event-timed milliseconds."""
+        mx = 128
+        names = C.create_string_buffer(32 * mx)
+        layers = (C.c_int32 * mx)()
+        counts = (C.c_int32 * mx)()
+        ms = (C.c_double * mx)()
+        n = C.c_int32()
+        nv.check(self.lib.mace_profile_read(self.ctx, mx, names, layers, counts, ms, C.byref(n)), self.lib)
+        out = []
+        for i in range(n.value):
+            nm = names.raw[32 * i: 32 * (i + 1)].split(b"\0", 1)[0].decode()
+            out.append({"name": nm, "layer": layers[i], "count": counts[i], "ms": ms[i]})
+        return out
+
     def error_flag(self) -> int:
         c = C.c_int32()
         nv.check(self.lib.mace_ctx_error_flag(self.ctx, C.byref(c)), self.lib)
