@@ -46,6 +46,51 @@ def species_of(numbers, z_table) -> np.ndarray:
     return np.array([lut[int(z)] for z in numbers], dtype=np.int32)
 
 
+def run_gpu(model, st: Structure, r_cut: float | None = None, virial: bool = True):
+    """Neighbour list + one evaluation through the C ABI; returns numpy results."""
+    import torch
+
+    dev = model.device
+    species = model.species_index(st.numbers)
+    gp = torch.as_tensor(graph_ptr_of(st), device=dev)
+    pos64 = torch.tensor(st.positions, dtype=torch.float64, device=dev)
+    periodic = bool(np.any(st.pbc))
+    cell64 = torch.tensor(st.cell, dtype=torch.float64, device=dev) if periodic else None
+    edges = model.neighbour_list(pos64, cell64, st.pbc, gp, r_cut or model.r_max)
+    out = model.evaluate(pos64.float(), cell64.float() if periodic else None, torch.as_tensor(species, device=dev),
+                         gp, edges, forces=True, virial=virial and periodic)
+    torch.cuda.synchronize(dev)
+    res = {
+        "energy": out["energy"].cpu().numpy(),
+        "node_energy": out["node_energy"].cpu().numpy(),
+        "forces": out["forces"].cpu().numpy().astype(np.float64),
+    }
+    if virial and periodic:
+        g = out["virial"].cpu().numpy().reshape(3, 3)
+        s = 0.5 * (g + g.T) / abs(np.linalg.det(st.cell))
+        res["stress"] = s[[0, 1, 2, 1, 0, 0], [0, 1, 2, 2, 2, 1]]
+    return res, edges, species
+
+
+def assert_parity(gpu: dict, ref: dict, n_atoms: int, stress: bool = False):
+    """BASELINE tolerances (absolute) plus relative bounds that keep them meaningful."""
+    de = np.abs(gpu["energy"] - ref["energy"]).max()
+    escale = max(np.abs(ref["node_energy"]).sum(), 1e-3)
+    assert de / n_atoms < 1e-5, f"energy/atom {de / n_atoms:.3e}"
+    assert de < 1e-5 * escale + 1e-7, f"energy rel {de / escale:.3e}"
+    df = np.abs(gpu["forces"] - ref["forces"]).max()
+    fscale = np.abs(ref["forces"]).max()
+    assert df < 1e-4, f"forces abs {df:.3e}"
+    assert df < 1e-4 * fscale + 1e-9, f"forces rel {df / fscale:.3e}"
+    dn = np.abs(gpu["node_energy"] - ref["node_energy"]).max()
+    assert dn < 1e-5 * max(np.abs(ref["node_energy"]).max(), 1e-3)
+    if stress:
+        ds = np.abs(gpu["stress"] - ref["stress"]).max()
+        sscale = np.abs(ref["stress"]).max()
+        assert ds < 1e-6, f"stress abs {ds:.3e}"
+        assert ds < 1e-4 * sscale + 1e-12, f"stress rel {ds / sscale:.3e}"
+
+
 def graph_ptr_of(st: Structure) -> np.ndarray:
     if st.batch is None:
         return np.array([0, len(st)], dtype=np.int32)

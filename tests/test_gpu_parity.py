@@ -1,0 +1,131 @@
+"""CUDA step (through the C ABI) against the float64 CPU oracle.
+
+Tolerances: energy 1e-5 eV/atom, forces 1e-4 eV/A max-abs,
+stress 1e-6 eV/A^3 -- plus relative bounds (1e-5 energy, 1e-4 forces/stress of
+their own scale) so that the checks stay meaningful at small magnitudes."""
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import assert_parity, irreps_to_channel_last, make_case, rel_err, run_gpu
+from mace_mlx_b200.model import MACEModel
+from mace_mlx_b200.spec import ModelSpec
+from mace_mlx_b200.structures import diamond_si, lipso_box, molecule_batch
+from mace_mlx_b200.weights import random_config, random_weights
+from oracle.model import OracleMACE
+
+pytestmark = pytest.mark.gpu
+torch.set_num_threads(min(16, torch.get_num_threads()))
+
+
+def oracle_of(config, weights, st, edges, species, stress):
+    s, r, S = edges.numpy()
+    orc = OracleMACE(config, weights)
+    return orc.compute(st.positions, species, s, r, S, st.cell if np.any(st.pbc) else None,
+                       stress=stress, batch=st.batch, num_graphs=st.num_graphs)
+
+
+def check(config, weights, st, stress=True):
+    m = MACEModel(config=config, weights=weights, device=0)
+    gpu, edges, species = run_gpu(m, st, virial=stress)
+    ref = oracle_of(config, weights, st, edges, species, stress and bool(np.any(st.pbc)))
+    assert_parity(gpu, ref, len(st), stress=stress and bool(np.any(st.pbc)))
+    return m, gpu, ref, edges
+
+
+@pytest.mark.parametrize("arch", ["small", "medium", "large"])
+def test_archs_on_si64(arch):
+    config, weights, st = make_case(arch, diamond_si(2, 0.05, 11), seed=11)
+    check(config, weights, st)
+
+
+def test_config0_small_si216():
+    config, weights, st = make_case("small", diamond_si(3, 0.01, 0), seed=0, avg_num_neighbors=46.0)
+    check(config, weights, st)
+
+
+def test_config1_medium_si1000_energy_forces():
+    config, weights, st = make_case("medium", diamond_si(5, 0.05, 1), seed=1, avg_num_neighbors=44.0)
+    check(config, weights, st, stress=False)
+
+
+def test_lipso_large_four_species_with_stress():
+    st = lipso_box(300, 2)
+    config, weights, _ = make_case("large", st, seed=2, z_table=[3, 8, 15, 16], avg_num_neighbors=50.0)
+    check(config, weights, st)
+
+
+def test_off_like_molecule_batch():
+    st = molecule_batch(8, 3)
+    config, weights, _ = make_case("medium", st, seed=3, z_table=[1, 6, 7, 8], r_max=5.0,
+                                   hidden_irreps="96x0e + 96x1o", avg_num_neighbors=12.0)
+    m, gpu, ref, _ = check(config, weights, st, stress=False)
+    assert gpu["energy"].shape == (8,)
+
+
+def test_non_residual_first_layer_and_scale_shift():
+    cfg = random_config("medium", z_table=[14, 6], avg_num_neighbors=30.0, first_interaction_nonresidual=True,
+                        atomic_energies=[-5.4, -8.1], model_type="ScaleShiftMACE")
+    cfg["scale"], cfg["shift"] = 1.3, -0.2
+    w = random_weights(ModelSpec.from_config(cfg), 4)
+    st = diamond_si(2, 0.05, 4)
+    st.numbers[::3] = 6
+    check(cfg, w, st)
+
+
+@pytest.mark.parametrize("max_ell,corr", [(2, 3), (3, 2), (1, 1)])
+def test_other_lmax_and_correlation(max_ell, corr):
+    cfg = random_config("medium", z_table=[14], avg_num_neighbors=40.0, max_ell=max_ell, correlation=corr)
+    w = random_weights(ModelSpec.from_config(cfg), 5)
+    check(cfg, w, diamond_si(2, 0.05, 5))
+
+
+def test_per_stage_buffers_medium():
+    config, weights, st = make_case("medium", diamond_si(2, 0.05, 1), seed=1)
+    m = MACEModel(config=config, weights=weights, device=0)
+    gpu, edges, species = run_gpu(m, st, virial=False)
+    s, r, S = edges.numpy()
+    trace = {}
+    OracleMACE(config, weights).compute(st.positions, species, s, r, S, st.cell, trace=trace)
+    spec = m.spec
+    N, E = len(st), edges.n_edges
+    assert rel_err(m.debug_buffer("Y").cpu().numpy().reshape(E, 16), trace["Y"].detach().numpy()) < 1e-5
+    assert rel_err(m.debug_buffer("b").cpu().numpy().reshape(E, -1), trace["b"].detach().numpy()) < 1e-5
+    for t, lay in enumerate(spec.layers):
+        def cmp(stage, key, irreps, grad=False, rows=N):
+            ref = trace[key].grad if grad else trace[key].detach()
+            ref = ref.numpy()
+            if irreps is not None:
+                ref = irreps_to_channel_last(ref, irreps)
+            got = m.debug_buffer(stage, t).cpu().numpy().reshape(rows, -1)
+            assert rel_err(got, ref) < 2e-5, (t, stage, rel_err(got, ref))
+
+        cmp("up", f"up{t}", lay.irreps_in)
+        cmp("w", f"w{t}", None, rows=E)
+        cmp("A", f"A{t}", lay.conv.irreps_mid)
+        cmp("msg", f"msg{t}", spec.interaction_irreps)
+        cmp("B", f"B{t}", lay.hidden)
+        cmp("h_out", f"h{t + 1}", lay.hidden)
+        cmp("dB", f"B{t}", lay.hidden, grad=True)
+        cmp("dmsg", f"msg{t}", spec.interaction_irreps, grad=True)
+        cmp("dA", f"A{t}", lay.conv.irreps_mid, grad=True)
+        if t > 0:
+            cmp("dup", f"up{t}", lay.irreps_in, grad=True)
+    assert rel_err(m.debug_buffer("dY").cpu().numpy().reshape(E, 16), trace["Y"].grad.numpy()) < 2e-5
+    assert rel_err(m.debug_buffer("dv").cpu().numpy().reshape(E, 3), trace["v"].grad.numpy()) < 2e-5
+    assert m.error_flag() == 0
+
+
+def test_bitwise_deterministic_and_translation_invariant():
+    config, weights, st = make_case("medium", diamond_si(3, 0.05, 8), seed=8)
+    m = MACEModel(config=config, weights=weights, device=0)
+    a, _, _ = run_gpu(m, st)
+    b, _, _ = run_gpu(m, st)
+    np.testing.assert_array_equal(a["forces"], b["forces"])
+    np.testing.assert_array_equal(a["energy"], b["energy"])
+    assert np.abs(a["forces"].sum(0)).max() < 1e-5 * max(1.0, np.abs(a["forces"]).max() * len(st))
+    st2 = diamond_si(3, 0.05, 8)
+    st2.positions = st2.positions + np.array([0.37, -0.21, 0.05])
+    c, _, _ = run_gpu(m, st2)
+    np.testing.assert_allclose(c["forces"], a["forces"], atol=1e-4 * np.abs(a["forces"]).max() + 1e-7)
