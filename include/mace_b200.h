@@ -215,6 +215,26 @@ int mace_nl_build(mace_ctx* ctx, const double* pos, const double* cell, const in
                   int32_t* rev, int64_t capacity, int64_t* n_edges, void* stream);
 
 /*
+ * Neighbour list for callers that cannot allocate device memory (no reference
+ * counterpart: the reference always builds its list on the host).  Same
+ * inputs, outputs, ordering and status codes as mace_nl_build, but no context:
+ * its scratch is a static __device__ array of MACE_NOALLOC_SCRATCH_BYTES that
+ * every GPU loading the library holds until exit, so it works for hosts that
+ * own all GPU memory or cannot afford cudaMalloc's implicit synchronisation.
+ * Calls nothing that allocates.  Limits: at most MACE_NOALLOC_MAX_ATOMS atoms
+ * (larger systems fail with MACE_ERR_BAD_ARG).  The first call on each device
+ * looks up the array's device address and should come before any stream
+ * capture.  All calls share the array: calls that overlap on the GPU race.
+ * Uses the caller's current device.
+ */
+#define MACE_NOALLOC_SCRATCH_BYTES (4u << 20)
+#define MACE_NOALLOC_MAX_ATOMS 131072
+int mace_nl_build_noalloc(const double* pos, const double* cell, const int32_t* pbc,
+                          const int32_t* graph_ptr, int32_t num_graphs, int64_t n, double r_cut,
+                          int32_t* sender, int32_t* receiver, int32_t* shifts, int32_t* row_ptr,
+                          int32_t* rev, int64_t capacity, int64_t* n_edges, void* stream);
+
+/*
  * One energy (+ forces, + virial) evaluation on `stream` (a cudaStream_t).
  * Asynchronous: results are valid once the stream reaches this point.  An
  * inconsistent reverse-edge index is recorded in the context's error flag

@@ -112,7 +112,9 @@ EXPORTED = (
     "mace_last_error", "mace_ctx_create", "mace_ctx_destroy", "mace_ctx_reserve",
     "mace_ctx_workspace_bytes", "mace_nl_build", "mace_forward_backward", "mace_debug_buffer",
     "mace_last_launch_count", "mace_ctx_error_flag", "mace_profile_enable", "mace_profile_read",
+    "mace_nl_build_noalloc",
 )
+NOALLOC_MAX_ATOMS = 131072
 
 _lib = None
 
@@ -142,6 +144,8 @@ def load_library(path: str | Path | None = None) -> C.CDLL:
         "mace_debug_buffer": ([vp, i32, C.POINTER(vp), C.POINTER(i64)], C.c_int),
         "mace_last_launch_count": ([vp, C.POINTER(i32)], C.c_int),
         "mace_ctx_error_flag": ([vp, C.POINTER(i32)], C.c_int),
+        "mace_nl_build_noalloc": ([vp, vp, C.POINTER(i32), vp, i32, i64, C.c_double, vp, vp, vp, vp, vp,
+                                  i64, C.POINTER(i64), vp], C.c_int),
         "mace_profile_enable": ([vp, i32], C.c_int),
         "mace_profile_read": ([vp, i32, C.c_char_p, C.POINTER(i32), C.POINTER(i32), C.POINTER(C.c_double),
                                C.POINTER(i32)], C.c_int),
