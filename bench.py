@@ -215,7 +215,7 @@ def b200_arm(args, rank: int, world: int, local_rank: int):
         torch.cuda.synchronize(dev)
 
     def step():
-        model.evaluate(pos, cell, species, gptr, edges, forces=True, virial=False, out=out)
+        model.evaluate(pos, cell, species, gptr, edges, forces=True, virial=False, out=out, graph=True)
 
     for _ in range(max(3, args.warmup)):
         step()

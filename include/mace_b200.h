@@ -51,7 +51,7 @@ extern "C" {
 #define MACE_ERR_UNSUPPORTED 6
 #define MACE_ERR_EDGES 7
 
-#define MACE_ABI_VERSION 1
+#define MACE_ABI_VERSION 2
 
 /* limits of the packed model description */
 #define MACE_MAX_LAYERS 4
@@ -63,6 +63,11 @@ extern "C" {
 /* flags of mace_forward_backward */
 #define MACE_WANT_FORCES 1
 #define MACE_WANT_VIRIAL 2
+/* Replay the step as a CUDA graph: captured on the first call (and whenever
+ * any pointer, size or flag of the call changes), then launched on `stream`.
+ * Buffers must keep their addresses between calls; mace_ctx_reserve drops
+ * the captured graph.  Ignored while profiling is enabled. */
+#define MACE_USE_GRAPH 4
 
 typedef struct mace_ctx mace_ctx;
 
@@ -93,14 +98,17 @@ typedef struct {
   int64_t f_wt;                   /* (C, n_src*C) transpose             */
 } mace_lin_group;
 
+/* Symmetric contraction of one output irrep, as a polynomial in the coupling
+ * features f[i] (i = l^2 + m): out[M][c] = sum_e G[z][e][c] * f[a_e] (* f[b_e] (* f[c_e]))
+ * over entries e with sorted indices a <= b <= c; G already contains the
+ * species weights contracted with the index-symmetrised U tensors. */
 typedef struct {
   int32_t L;                      /* output degree                      */
   int32_t corr;                   /* correlation order                  */
-  int32_t K[MACE_MAX_CORR];       /* number of paths for nu = 1..corr   */
-  int64_t f_w[MACE_MAX_CORR];     /* (num_elements, K, C) for nu = 1..corr */
-  int32_t nnz[MACE_MAX_CORR];     /* non-zeros of U_nu                  */
-  int64_t i_idx[MACE_MAX_CORR];   /* packed indices of the non-zeros    */
-  int64_t f_val[MACE_MAX_CORR];   /* values of the non-zeros            */
+  int32_t n_ent;                  /* number of entries                  */
+  int64_t i_ent;                  /* ints: (2L+2) segment starts by M, then n_ent packed
+                                     M | a<<4 | b<<8 | c<<12 | nu<<16 */
+  int64_t f_G;                    /* floats: (num_elements, n_ent, C)    */
 } mace_sc_out;
 
 typedef struct {

@@ -14,8 +14,8 @@ below refer to that file); the step itself runs on a B200 through
 
 Differences: ``device`` names a CUDA device ("cuda", "gpu", "cuda:1", or an
 index); "cpu" is rejected because this build has no CPU path.  ``use_compile``
-is accepted for compatibility and ignored (the step is a fixed kernel
-sequence).  Only float32 is computed.
+(the reference's ``mx.compile`` switch) selects CUDA-graph replay of the fixed
+kernel sequence.  Only float32 is computed.
 """
 
 from __future__ import annotations
@@ -97,6 +97,9 @@ class MACEMLXCalculator(Calculator):
         self.z_table = self.model.z_table
         self._skin = float(skin)
         self._use_compile = use_compile
+        # use_compile=True (the reference's default: mx.compile of the step) maps
+        # to CUDA-graph replay of the kernel sequence
+        self._use_graph = bool(use_compile)
         self._nl_cache: EdgeSet | None = None
         self._cache_positions = None
         self._cache_cell = None
@@ -204,8 +207,9 @@ class MACEMLXCalculator(Calculator):
                 self._stress_always = True
             compute_stress = "stress" in (properties or self.implemented_properties)
             compute_stress = (compute_stress or self._stress_always) and atoms.cell.rank == 3
+            # replayed as a CUDA graph: every buffer here keeps its address between steps
             self.model.evaluate(pos, cell, species, self._graph_ptr_dev, self._nl_cache, forces=True,
-                                virial=compute_stress, out=out)
+                                virial=compute_stress, out=out, graph=self._use_graph)
             # device -> host
             host["energy"].copy_(out["energy"], non_blocking=True)
             host["forces"].copy_(out["forces"], non_blocking=True)

@@ -110,6 +110,7 @@ struct ConvSlotDev {
   int src_ch;    // per-channel offset of x1 slot (sum of dims of earlier input slots)
   int off;       // offset of the slot inside a mid row
   int m_off;     // offset inside a per-edge M row
+  int h_off;     // offset (per channel) of the slot's (2l1+1)(2l2+1) H block
   const float* cg;  // (2l1+1)(2l2+1)(2l3+1)
 };
 struct ConvParams {
@@ -117,6 +118,7 @@ struct ConvParams {
   int C;
   int n_mid;
   int m_tot;
+  int h_tot;     // sum over slots of (2l1+1)(2l2+1)
   int wnumel;
   int in_dim;
   int in_ch;       // in_dim / C
@@ -179,14 +181,6 @@ struct SkipParams {
 };
 int launch_skip(const SkipParams& p, cudaStream_t s);
 
-struct ScTabDev {
-  int nnz;
-  const int32_t* seg;   // (2L+2) segment starts by M
-  const int32_t* idx;   // packed M | i1<<4 | i2<<8 | i3<<12 | k<<16
-  const float* val;
-  const float* w;       // (num_elements, K, C)
-  int K;
-};
 struct ScParams {
   int64_t N;
   int C;
@@ -195,9 +189,11 @@ struct ScParams {
   int ncoup;        // (max_ell+1)^2
   int n_out;
   int L[MACE_MAX_IN];
-  int corr[MACE_MAX_IN];
   int out_off[MACE_MAX_IN];
-  ScTabDev tab[MACE_MAX_IN][MACE_MAX_CORR];
+  int n_ent[MACE_MAX_IN];
+  const int32_t* seg[MACE_MAX_IN];  // (2L+2) entry segment starts by M
+  const int32_t* ent[MACE_MAX_IN];  // packed M | a<<4 | b<<8 | c<<12 | nu<<16
+  const float* G[MACE_MAX_IN];      // (num_elements, n_ent, C)
   float* out;       // (N, out_row)
   int out_row;
   // backward

@@ -156,10 +156,14 @@ __device__ __forceinline__ float warp_reduce16(float s[16]) {
   return s[0] + __shfl_xor_sync(FULL, s[0], 1);
 }
 
+// Per receiver n, slot k and channel u the receiver's gradient enters every edge
+// only through H[i][j] = sum_m pw CG[i, j, m] dA[n][k][m][u]; it is formed once
+// per CTA, so each edge needs (2l1+1)(2l2+1) multiply-adds per channel for
+//   dw_e[k, u] = sum_{i,j} x1[i] H[i][j] Y_e[j]     and     dY_e[j] += w sum_i x1[i] H[i][j].
 template <int L1, int L2, int L3>
 __device__ __forceinline__ void bwd_slot(const ConvParams& p, const ConvSlotDev& sl, int k,
-                                         int64_t e, int s, const float* Mk, const float* sG,
-                                         float* sDup, float sdy[16]) {
+                                         int64_t e, int s, const float* Mk, const float* Ye,
+                                         const float* sH, float* sDup, float sdy[16]) {
   constexpr int D1 = 2 * L1 + 1, D2 = 2 * L2 + 1, D3 = 2 * L3 + 1, YO = L2 * L2;
   constexpr float PAR = (L2 & 1) ? -1.f : 1.f;
   const int u = threadIdx.x;
@@ -169,38 +173,25 @@ __device__ __forceinline__ void bwd_slot(const ConvParams& p, const ConvSlotDev&
 #pragma unroll
   for (int i = 0; i < D1; ++i) x1[i] = __ldg(x + i * C);
   const float w = __ldg(p.w + e * p.wnumel + k * C + u);
-  float g[D3], gr[D3];
+  float gr[D3];
   const float* dAs = p.dA + (int64_t)s * p.mid_dim + sl.off + u;
 #pragma unroll
-  for (int m = 0; m < D3; ++m) {
-    g[m] = sG[sl.off + m * C + u];
-    gr[m] = __ldg(dAs + m * C);
-  }
-  // dw_e[k, u] = sum_m g[m] * sum_i x1[i] M[i][m]
-  float dw = 0.f;
+  for (int m = 0; m < D3; ++m) gr[m] = __ldg(dAs + m * C);
+  const float* H = sH + sl.h_off * C + u;
+  float xh[D2];
 #pragma unroll
-  for (int m = 0; m < D3; ++m) {
-    float t = 0.f;
-#pragma unroll
-    for (int i = 0; i < D1; ++i) t = fmaf(x1[i], Mk[i * D3 + m], t);
-    dw = fmaf(g[m], t, dw);
-  }
-  p.dw[e * p.wnumel + k * C + u] = dw;
-  // dY_e[j] += sum_{i,m} cgw[i][j][m] * w x1[i] g[m]
-  float q[D1][D3];
+  for (int jj = 0; jj < D2; ++jj) xh[jj] = 0.f;
 #pragma unroll
   for (int i = 0; i < D1; ++i)
 #pragma unroll
-    for (int m = 0; m < D3; ++m) q[i][m] = w * x1[i] * g[m];
+    for (int jj = 0; jj < D2; ++jj) xh[jj] = fmaf(x1[i], H[(i * D2 + jj) * C], xh[jj]);
+  float dw = 0.f;
 #pragma unroll
   for (int jj = 0; jj < D2; ++jj) {
-    float a = 0.f;
-#pragma unroll
-    for (int i = 0; i < D1; ++i)
-#pragma unroll
-      for (int m = 0; m < D3; ++m) a = fmaf(__ldg(sl.cg + (i * D2 + jj) * D3 + m), q[i][m], a);
-    sdy[YO + jj] += a;
+    dw = fmaf(xh[jj], Ye[YO + jj], dw);
+    sdy[YO + jj] = fmaf(w, xh[jj], sdy[YO + jj]);
   }
+  p.dw[e * p.wnumel + k * C + u] = dw;
   // sender side of node n through the reverse edge
 #pragma unroll
   for (int i = 0; i < D1; ++i) {
@@ -218,13 +209,32 @@ __global__ void k_conv_bwd(ConvParams p, int EC) {
   float* sY = sm + EC;
   float* sM = sY + EC * 16;
   float* sRed = sM + EC * p.m_tot;        // nw x EC x 16
-  float* sG = sRed + nw * EC * 16;         // mid_dim
-  float* sDup = sG + p.mid_dim;            // in_dim
+  float* sH = sRed + nw * EC * 16;         // h_tot x C
+  float* sDup = sH + p.h_tot * p.C;        // in_dim
   const int64_t n = blockIdx.x;
   const int tid = threadIdx.x;
+  const int C = p.C;
   const int64_t e_beg = p.row_ptr[n], e_end = p.row_ptr[n + 1];
-  for (int q = tid; q < p.mid_dim; q += blockDim.x) sG[q] = p.dA[n * p.mid_dim + q];
   for (int q = tid; q < p.in_dim; q += blockDim.x) sDup[q] = 0.f;
+  // H_k[i][j] = sum_m pw CG_k[i, j, m] dA[n][k][m][u] (thread u's own column)
+  {
+    const float* g = p.dA + n * p.mid_dim + tid;
+    for (int k = 0; k < p.n_mid; ++k) {
+      const ConvSlotDev& sl = p.slot[k];
+      const int D1 = cdim(sl.l1), D2 = cdim(sl.l2), D3 = cdim(sl.l3);
+      float gk[7];
+#pragma unroll
+      for (int m = 0; m < 7; ++m) gk[m] = (m < D3) ? g[sl.off + m * C] : 0.f;
+      for (int i = 0; i < D1; ++i)
+        for (int jj = 0; jj < D2; ++jj) {
+          float a = 0.f;
+#pragma unroll
+          for (int m = 0; m < 7; ++m)
+            if (m < D3) a = fmaf(__ldg(sl.cg + (i * D2 + jj) * D3 + m), gk[m], a);
+          sH[(sl.h_off + i * D2 + jj) * C + tid] = a;
+        }
+    }
+  }
   __syncthreads();
   const int warp = tid >> 5, lane = tid & 31;
   for (int64_t cb = e_beg; cb < e_end; cb += EC) {
@@ -237,12 +247,13 @@ __global__ void k_conv_bwd(ConvParams p, int EC) {
       const int s = sSnd[j];
       const int64_t e = cb + j;
       const float* Mrow = sM + j * p.m_tot;
+      const float* Ye = sY + j * 16;
       for (int k = 0; k < p.n_mid; ++k) {
         const ConvSlotDev& sl = p.slot[k];
         const float* Mk = Mrow + sl.m_off;
         switch (sl.combo) {
 #define BWD_CASE(a, b, c) \
-  case a * 16 + b * 4 + c: bwd_slot<a, b, c>(p, sl, k, e, s, Mk, sG, sDup, sdy); break;
+  case a * 16 + b * 4 + c: bwd_slot<a, b, c>(p, sl, k, e, s, Mk, Ye, sH, sDup, sdy); break;
           BWD_CASE(0, 0, 0) BWD_CASE(0, 1, 1) BWD_CASE(0, 2, 2) BWD_CASE(0, 3, 3)
           BWD_CASE(1, 0, 1) BWD_CASE(1, 1, 0) BWD_CASE(1, 1, 1) BWD_CASE(1, 1, 2)
           BWD_CASE(1, 2, 1) BWD_CASE(1, 2, 2) BWD_CASE(1, 2, 3) BWD_CASE(1, 3, 2)
@@ -300,7 +311,7 @@ int launch_conv_bwd(const ConvParams& p, cudaStream_t s) {
   if (rc) return rc;
   const int EC = 32;
   const int nw = p.C / 32;
-  size_t smem = (size_t)(EC + EC * 16 + EC * p.m_tot + nw * EC * 16 + p.mid_dim + p.in_dim) * sizeof(float);
+  size_t smem = (size_t)(EC + EC * 16 + EC * p.m_tot + nw * EC * 16 + p.h_tot * p.C + p.in_dim) * sizeof(float);
   if (smem > 227 * 1024) return fail(MACE_ERR_UNSUPPORTED, "conv backward tile exceeds shared memory");
   if (smem > 48 * 1024)
     MACE_CUDA_TRY(cudaFuncSetAttribute(k_conv_bwd, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));

@@ -19,9 +19,11 @@ namespace {
 
 // ---------------------------------------------------------------------------
 // o3.Linear: out[(n,m), c] (+)= alpha * sum_{ks,u} in[n, k_off[ks] + m*C + u] * W[ks*C+u][c]
-// 64 x 128 output tile per 256-thread CTA, 8 x 4 outputs per thread.
+// 32 x 128 output tile per 256-thread CTA, 4 x 4 outputs per thread (small
+// tiles: node counts of a few thousand must still fill 148 SMs).
 // ---------------------------------------------------------------------------
-constexpr int LR = 64;   // rows per tile
+constexpr int LR = 32;   // rows per tile
+constexpr int RPT = LR / 8;  // rows per thread
 constexpr int LK = 32;   // k chunk
 
 __global__ void __launch_bounds__(256) k_linear(LinParams p) {
@@ -34,9 +36,9 @@ __global__ void __launch_bounds__(256) k_linear(LinParams p) {
   if (r0 >= rows) return;
   const int tid = threadIdx.x;
   const int ty = tid >> 5, tx = tid & 31;
-  float acc[8][4];
+  float acc[RPT][4];
 #pragma unroll
-  for (int a = 0; a < 8; ++a)
+  for (int a = 0; a < RPT; ++a)
 #pragma unroll
     for (int b = 0; b < 4; ++b) acc[a][b] = 0.f;
   for (int ks = 0; ks < jb.n_k; ++ks) {
@@ -63,8 +65,8 @@ __global__ void __launch_bounds__(256) k_linear(LinParams p) {
       for (int kk = 0; kk < LK; ++kk) {
         float4 b4 = *reinterpret_cast<const float4*>(&sB[kk][tx * 4]);
 #pragma unroll
-        for (int a = 0; a < 8; ++a) {
-          float av = sA[kk][ty * 8 + a];
+        for (int a = 0; a < RPT; ++a) {
+          float av = sA[kk][ty * RPT + a];
           acc[a][0] = fmaf(av, b4.x, acc[a][0]);
           acc[a][1] = fmaf(av, b4.y, acc[a][1]);
           acc[a][2] = fmaf(av, b4.z, acc[a][2]);
@@ -75,8 +77,8 @@ __global__ void __launch_bounds__(256) k_linear(LinParams p) {
     }
   }
 #pragma unroll
-  for (int a = 0; a < 8; ++a) {
-    int64_t row = r0 + ty * 8 + a;
+  for (int a = 0; a < RPT; ++a) {
+    int64_t row = r0 + ty * RPT + a;
     if (row >= rows) continue;
     int64_t node = row / jb.d;
     int m = (int)(row % jb.d);
@@ -124,52 +126,56 @@ __global__ void k_skip(SkipParams p) {
 }
 
 // ---------------------------------------------------------------------------
-// symmetric contraction
-//   out[n][o][M][c] = sum_nu sum_{nz of U_nu with index M} U * W_nu[z_n][k][c] * prod f[n][c][i_a]
-// one CTA per node, one thread per channel; f and W staged per thread column.
+// symmetric contraction as a polynomial in the coupling features:
+//   out[n][o][M][c] = sum_{entries e of M} G[z_n][e][c] * f[a_e] (* f[b_e] (* f[c_e]))
+// (index-symmetrised U pre-contracted with the species weights at load time).
+// One CTA per node, one thread per channel; f (and df) live in the thread's
+// own shared-memory column, G is read coalesced over channels from L2.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ int ix(int v, int sh) { return (v >> sh) & 15; }
 
-__global__ void k_sc_fwd(ScParams p) {
-  extern __shared__ float sm[];
+__global__ void __launch_bounds__(128) k_sc_fwd(ScParams p) {
+  extern __shared__ float sf[];  // ncoup x C
   const int C = p.C, c = threadIdx.x;
   const int64_t n = blockIdx.x;
   const int z = p.species[n];
   const int nc = p.ncoup;
-  float* sf = sm;             // ncoup x C
-  float* sw = sm + 16 * C;    // sum_nu K_nu x C
   for (int i = 0; i < nc; ++i) sf[i * C + c] = p.f[n * nc * C + i * C + c];
+  const float* f = sf + c;
   for (int o = 0; o < p.n_out; ++o) {
-    const int L = p.L[o], corr = p.corr[o];
-    int kofs[MACE_MAX_CORR];
-    int tot = 0;
-    for (int nu = 0; nu < corr; ++nu) {
-      kofs[nu] = tot;
-      const ScTabDev& t = p.tab[o][nu];
-      for (int k = 0; k < t.K; ++k) sw[(tot + k) * C + c] = __ldg(t.w + ((int64_t)z * t.K + k) * C + c);
-      tot += t.K;
-    }
+    const int L = p.L[o];
+    const int32_t* __restrict__ ent = p.ent[o];
+    const float* __restrict__ G = p.G[o] + (int64_t)z * p.n_ent[o] * C + c;
     for (int M = 0; M < 2 * L + 1; ++M) {
-      float acc = 0.f;
-      for (int nu = 0; nu < corr; ++nu) {
-        const ScTabDev& t = p.tab[o][nu];
-        const float* swn = sw + kofs[nu] * C + c;
-        const int b = __ldg(t.seg + M), e = __ldg(t.seg + M + 1);
-        for (int q = b; q < e; ++q) {
-          const int id = __ldg(t.idx + q);
-          float v = __ldg(t.val + q) * swn[(id >> 16) * C];
-          v *= sf[ix(id, 4) * C + c];
-          if (nu >= 1) v *= sf[ix(id, 8) * C + c];
-          if (nu >= 2) v *= sf[ix(id, 12) * C + c];
-          acc += v;
-        }
+      const int b = __ldg(p.seg[o] + M), e = __ldg(p.seg[o] + M + 1);
+      float acc0 = 0.f, acc1 = 0.f;
+      int q = b;
+      for (; q + 1 < e; q += 2) {
+        const int i0 = __ldg(ent + q), i1 = __ldg(ent + q + 1);
+        const float g0 = __ldg(G + (int64_t)q * C), g1 = __ldg(G + (int64_t)(q + 1) * C);
+        float v0 = g0 * f[ix(i0, 4) * C], v1 = g1 * f[ix(i1, 4) * C];
+        const int n0 = i0 >> 16, n1 = i1 >> 16;
+        if (n0 >= 2) v0 *= f[ix(i0, 8) * C];
+        if (n0 >= 3) v0 *= f[ix(i0, 12) * C];
+        if (n1 >= 2) v1 *= f[ix(i1, 8) * C];
+        if (n1 >= 3) v1 *= f[ix(i1, 12) * C];
+        acc0 += v0;
+        acc1 += v1;
       }
-      p.out[n * p.out_row + p.out_off[o] + M * C + c] = acc;
+      if (q < e) {
+        const int i0 = __ldg(ent + q);
+        float v0 = __ldg(G + (int64_t)q * C) * f[ix(i0, 4) * C];
+        const int n0 = i0 >> 16;
+        if (n0 >= 2) v0 *= f[ix(i0, 8) * C];
+        if (n0 >= 3) v0 *= f[ix(i0, 12) * C];
+        acc0 += v0;
+      }
+      p.out[n * p.out_row + p.out_off[o] + M * C + c] = acc0 + acc1;
     }
   }
 }
 
-__global__ void k_sc_bwd(ScParams p) {
+__global__ void __launch_bounds__(128) k_sc_bwd(ScParams p) {
   extern __shared__ float sm[];
   const int C = p.C, c = threadIdx.x;
   const int64_t n = blockIdx.x;
@@ -177,45 +183,37 @@ __global__ void k_sc_bwd(ScParams p) {
   const int nc = p.ncoup;
   float* sf = sm;             // ncoup x C (16 rows reserved)
   float* sdf = sm + 16 * C;   // ncoup x C
-  float* sw = sdf + 16 * C;
   for (int i = 0; i < nc; ++i) {
     sf[i * C + c] = p.f[n * nc * C + i * C + c];
     sdf[i * C + c] = 0.f;
   }
+  const float* f = sf + c;
+  float* df = sdf + c;
   for (int o = 0; o < p.n_out; ++o) {
-    const int L = p.L[o], corr = p.corr[o];
-    int kofs[MACE_MAX_CORR];
-    int tot = 0;
-    for (int nu = 0; nu < corr; ++nu) {
-      kofs[nu] = tot;
-      const ScTabDev& t = p.tab[o][nu];
-      for (int k = 0; k < t.K; ++k) sw[(tot + k) * C + c] = __ldg(t.w + ((int64_t)z * t.K + k) * C + c);
-      tot += t.K;
-    }
+    const int L = p.L[o];
+    const int32_t* __restrict__ ent = p.ent[o];
+    const float* __restrict__ G = p.G[o] + (int64_t)z * p.n_ent[o] * C + c;
     for (int M = 0; M < 2 * L + 1; ++M) {
       const float g = p.dout[n * p.out_row + p.out_off[o] + M * C + c];
-      for (int nu = 0; nu < corr; ++nu) {
-        const ScTabDev& t = p.tab[o][nu];
-        const float* swn = sw + kofs[nu] * C + c;
-        const int b = __ldg(t.seg + M), e = __ldg(t.seg + M + 1);
-        for (int q = b; q < e; ++q) {
-          const int id = __ldg(t.idx + q);
-          const float v = __ldg(t.val + q) * swn[(id >> 16) * C] * g;
-          const int a0 = ix(id, 4);
-          if (nu == 0) {
-            sdf[a0 * C + c] += v;
-          } else if (nu == 1) {
-            const int a1 = ix(id, 8);
-            const float f0 = sf[a0 * C + c], f1 = sf[a1 * C + c];
-            sdf[a0 * C + c] += v * f1;
-            sdf[a1 * C + c] += v * f0;
-          } else {
-            const int a1 = ix(id, 8), a2 = ix(id, 12);
-            const float f0 = sf[a0 * C + c], f1 = sf[a1 * C + c], f2 = sf[a2 * C + c];
-            sdf[a0 * C + c] += v * f1 * f2;
-            sdf[a1 * C + c] += v * f0 * f2;
-            sdf[a2 * C + c] += v * f0 * f1;
-          }
+      const int b = __ldg(p.seg[o] + M), e = __ldg(p.seg[o] + M + 1);
+#pragma unroll 2
+      for (int q = b; q < e; ++q) {
+        const int id = __ldg(ent + q);
+        const float v = __ldg(G + (int64_t)q * C) * g;
+        const int a0 = ix(id, 4), nu = id >> 16;
+        if (nu == 1) {
+          df[a0 * C] += v;
+        } else if (nu == 2) {
+          const int a1 = ix(id, 8);
+          const float f0 = f[a0 * C], f1 = f[a1 * C];
+          df[a0 * C] += v * f1;
+          df[a1 * C] += v * f0;
+        } else {
+          const int a1 = ix(id, 8), a2 = ix(id, 12);
+          const float f0 = f[a0 * C], f1 = f[a1 * C], f2 = f[a2 * C];
+          df[a0 * C] += v * f1 * f2;
+          df[a1 * C] += v * f0 * f2;
+          df[a2 * C] += v * f0 * f1;
         }
       }
     }
@@ -318,21 +316,10 @@ int launch_skip(const SkipParams& p, cudaStream_t s) {
   return MACE_OK;
 }
 
-static size_t sc_smem(const ScParams& p, int extra) {
-  int kmax = 0;
-  for (int o = 0; o < p.n_out; ++o) {
-    int tot = 0;
-    for (int nu = 0; nu < p.corr[o]; ++nu) tot += p.tab[o][nu].K;
-    kmax = tot > kmax ? tot : kmax;
-  }
-  return (size_t)(16 * extra + kmax) * p.C * sizeof(float);
-}
-
 int launch_sc_fwd(const ScParams& p, cudaStream_t s) {
   if (p.N == 0) return MACE_OK;
-  size_t smem = sc_smem(p, 1);
-  if (smem > 48 * 1024)
-    MACE_CUDA_TRY(cudaFuncSetAttribute(k_sc_fwd, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  if (p.C > 128) return fail(MACE_ERR_UNSUPPORTED, "symmetric contraction: C must be <= 128");
+  size_t smem = (size_t)16 * p.C * sizeof(float);
   k_sc_fwd<<<(unsigned)p.N, p.C, smem, s>>>(p);
   MACE_LAUNCH_CHECK("sc_fwd");
   return MACE_OK;
@@ -340,9 +327,8 @@ int launch_sc_fwd(const ScParams& p, cudaStream_t s) {
 
 int launch_sc_bwd(const ScParams& p, cudaStream_t s) {
   if (p.N == 0) return MACE_OK;
-  size_t smem = sc_smem(p, 2);
-  if (smem > 48 * 1024)
-    MACE_CUDA_TRY(cudaFuncSetAttribute(k_sc_bwd, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  if (p.C > 128) return fail(MACE_ERR_UNSUPPORTED, "symmetric contraction: C must be <= 128");
+  size_t smem = (size_t)32 * p.C * sizeof(float);
   k_sc_bwd<<<(unsigned)p.N, p.C, smem, s>>>(p);
   MACE_LAUNCH_CHECK("sc_bwd");
   return MACE_OK;

@@ -103,6 +103,13 @@ struct mace_ctx {
     double ms;
   };
   std::vector<ProfAcc> prof_acc;
+  // CUDA-graph replay of the whole step, keyed on the exact call arguments
+  cudaStream_t cap_stream = nullptr;
+  cudaGraphExec_t gexec = nullptr;
+  mace_system g_sys{};
+  mace_outputs g_out{};
+  int g_flags = -1;
+  int g_launches = 0;
 };
 
 namespace {
@@ -117,6 +124,10 @@ int max_wnumel(const mace_model_desc& d) {
 }
 
 void free_ws(mace_ctx* c) {
+  if (c->gexec) {  // a captured step refers to the workspace being released
+    cudaGraphExecDestroy(c->gexec);
+    c->gexec = nullptr;
+  }
   for (void* p : c->allocs) cudaFree(p);
   c->allocs.clear();
   c->ws_bytes = 0;
@@ -284,9 +295,12 @@ ConvParams conv_params(mace_ctx* c, int t, int64_t N, const mace_system* sys) {
   p.in_dim = L.in.dim;
   p.in_ch = L.in.dim / L.C;
   p.mid_dim = L.mid.dim;
+  p.h_tot = 0;
   for (int k = 0; k < L.n_mid; ++k) {
     const mace_conv_slot& cs = L.conv[k];
     ConvSlotDev& d = p.slot[k];
+    d.h_off = p.h_tot;
+    p.h_tot += (2 * cs.l1 + 1) * (2 * cs.l2 + 1);
     d.l1 = cs.l1;
     d.l2 = cs.l2;
     d.l3 = cs.l3;
@@ -345,17 +359,11 @@ ScParams sc_params(mace_ctx* c, int t, int64_t N, const int32_t* species, const 
   for (int o = 0; o < L.hid.n; ++o) {
     const mace_sc_out& so = L.sc[o];
     p.L[o] = so.L;
-    p.corr[o] = so.corr;
     p.out_off[o] = L.hid.off[o];
-    for (int nu = 0; nu < so.corr; ++nu) {
-      ScTabDev& tb = p.tab[o][nu];
-      tb.nnz = so.nnz[nu];
-      tb.seg = I(c, so.i_idx[nu]);
-      tb.idx = I(c, so.i_idx[nu]) + (2 * so.L + 2);
-      tb.val = F(c, so.f_val[nu]);
-      tb.w = F(c, so.f_w[nu]);
-      tb.K = so.K[nu];
-    }
+    p.n_ent[o] = so.n_ent;
+    p.seg[o] = I(c, so.i_ent);
+    p.ent[o] = I(c, so.i_ent) + (2 * so.L + 2);
+    p.G[o] = F(c, so.f_G);
   }
   return p;
 }
@@ -629,6 +637,8 @@ int mace_ctx_destroy(mace_ctx* c) {
   free_ws(c);
   if (c->ev[0])
     for (int i = 0; i < 2 * mace_ctx::PROF_MAX; ++i) cudaEventDestroy(c->ev[i]);
+  if (c->gexec) cudaGraphExecDestroy(c->gexec);
+  if (c->cap_stream) cudaStreamDestroy(c->cap_stream);
   cudaFree(c->d_floats);
   cudaFree(c->d_ints);
   delete c;
@@ -737,7 +747,46 @@ int mace_forward_backward(mace_ctx* c, const mace_system* sys, const mace_output
   if (sys->n_edges > 0 && (!sys->sender || !sys->receiver || !sys->shifts || !sys->rev))
     return fail(MACE_ERR_BAD_ARG, "edges without sender/receiver/shift/rev arrays");
   DeviceGuard g(c->device);
-  return forward_backward(c, sys, out, flags, reinterpret_cast<cudaStream_t>(stream));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int base_flags = flags & ~MACE_USE_GRAPH;
+  if (!(flags & MACE_USE_GRAPH) || c->prof_on) return forward_backward(c, sys, out, base_flags, s);
+  mace_outputs o{};
+  if (out) o = *out;
+  const bool same = c->gexec && c->g_flags == base_flags && std::memcmp(&c->g_sys, sys, sizeof(mace_system)) == 0 &&
+                    std::memcmp(&c->g_out, &o, sizeof(mace_outputs)) == 0;
+  if (!same) {
+    if (c->gexec) {
+      MACE_CUDA_TRY(cudaGraphExecDestroy(c->gexec));
+      c->gexec = nullptr;
+    }
+    if (!c->cap_stream) MACE_CUDA_TRY(cudaStreamCreateWithFlags(&c->cap_stream, cudaStreamNonBlocking));
+    // order the capture after the caller's prior work (workspace reuse)
+    MACE_CUDA_TRY(cudaStreamSynchronize(s));
+    MACE_CUDA_TRY(cudaStreamBeginCapture(c->cap_stream, cudaStreamCaptureModeThreadLocal));
+    int rc = forward_backward(c, sys, out, base_flags, c->cap_stream);
+    cudaGraph_t graph = nullptr;
+    cudaError_t ce = cudaStreamEndCapture(c->cap_stream, &graph);
+    if (rc) {
+      if (graph) cudaGraphDestroy(graph);
+      return rc;
+    }
+    if (ce != cudaSuccess) return fail(MACE_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(ce));
+    ce = cudaGraphInstantiate(&c->gexec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (ce != cudaSuccess) {
+      c->gexec = nullptr;
+      return fail(MACE_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(ce));
+    }
+    c->g_sys = *sys;
+    c->g_out = o;
+    c->g_flags = base_flags;
+    c->g_launches = c->launches;
+  }
+  MACE_CUDA_TRY(cudaGraphLaunch(c->gexec, s));
+  c->launches = c->g_launches;
+  c->last_N = sys->n_nodes;
+  c->last_E = sys->n_edges;
+  return MACE_OK;
 }
 
 int mace_debug_buffer(mace_ctx* c, int32_t id, const float** ptr, int64_t* len) {

@@ -152,12 +152,13 @@ class MACEModel:
     # ------------------------------------------------------------------
     def evaluate(self, pos: torch.Tensor, cell: torch.Tensor | None, species: torch.Tensor,
                  graph_ptr: torch.Tensor, edges: EdgeSet, *, forces: bool = True, virial: bool = False,
-                 out: dict | None = None) -> dict:
+                 out: dict | None = None, graph: bool = False) -> dict:
         """Energy per graph (float64), node energies, forces and the raw virial.
 
         All inputs are device tensors: pos (N,3) float32, cell (3,3) float32 or
         None, species (N,) int32 model indices, graph_ptr (G+1,) int32.
-        Asynchronous on the current stream.
+        Asynchronous on the current stream.  ``graph=True`` replays the step as
+        a CUDA graph (re-captured whenever a buffer address or size changes).
         """
         N = pos.shape[0]
         E = edges.n_edges
@@ -177,7 +178,7 @@ class MACEModel:
             rev=edges.rev.data_ptr())
         outs = nv.Outputs(energy=_ptr(out["energy"]), node_energy=_ptr(out["node_energy"]),
                           forces=_ptr(out.get("forces")), virial=_ptr(out.get("virial")))
-        flags = (nv.WANT_FORCES if forces else 0) | (nv.WANT_VIRIAL if virial else 0)
+        flags = (nv.WANT_FORCES if forces else 0) | (nv.WANT_VIRIAL if virial else 0) | (nv.USE_GRAPH if graph else 0)
         stream = torch.cuda.current_stream(self.device).cuda_stream
         nv.check(self.lib.mace_forward_backward(self.ctx, C.byref(sysd), C.byref(outs), flags, stream), self.lib)
         return out

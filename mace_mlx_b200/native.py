@@ -19,7 +19,7 @@ MACE_ERR_TIMEOUT = 4
 MACE_ERR_NCCL = 5
 MACE_ERR_UNSUPPORTED = 6
 MACE_ERR_EDGES = 7
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 MAX_LAYERS = 4
 MAX_IN = 4
@@ -29,6 +29,7 @@ MAX_CORR = 3
 
 WANT_FORCES = 1
 WANT_VIRIAL = 2
+USE_GRAPH = 4
 
 # debug buffer ids: layer * 16 + stage; layer 15 holds per-edge / global buffers
 STAGES = {
@@ -54,8 +55,7 @@ class LinGroup(C.Structure):
 
 
 class ScOut(C.Structure):
-    _fields_ = [("L", i32), ("corr", i32), ("K", i32 * MAX_CORR), ("f_w", i64 * MAX_CORR),
-                ("nnz", i32 * MAX_CORR), ("i_idx", i64 * MAX_CORR), ("f_val", i64 * MAX_CORR)]
+    _fields_ = [("L", i32), ("corr", i32), ("n_ent", i32), ("i_ent", i64), ("f_G", i64)]
 
 
 class LayerDesc(C.Structure):

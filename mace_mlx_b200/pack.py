@@ -71,26 +71,53 @@ def _slots(irreps, C: int) -> nv.Slots:
     return s
 
 
-def _sc_tables(U: np.ndarray, L: int, nu: int, tb: _Tables) -> tuple[int, int, int]:
-    """Non-zeros of U_nu as (segment starts by M, packed indices, values)."""
-    if L == 0:
-        U = U[None]
-    dM = U.shape[0]
-    K = U.shape[-1]
-    if K >= (1 << 15) or U.shape[1] > 16:
-        raise UnsupportedModel("symmetric-contraction tensor too large to pack")
-    nz = np.argwhere(np.abs(U) > U_EPS)  # rows (M, a_1..a_nu, k), lexicographic
-    vals = U[tuple(nz.T)]
+def sc_polynomial(Us: list[np.ndarray], Ws: list[np.ndarray], L: int):
+    """Rewrite one output of the symmetric contraction as a polynomial in f.
+
+    The reference evaluates  out[M] = sum_nu sum U_nu[M, a_1..a_nu, k] W_nu[z, k, c] prod_q f[a_q]
+    (symmetric_contraction.py:95-121, 505-595).  The product of the f's is
+    symmetric in the a's, so U_nu is summed over index permutations onto
+    sorted tuples a_1 <= ... <= a_nu, and contracted with the (constant) species
+    weights once: G[z, e, c] = sum_k U_sym[e, k] W_nu[z, k, c].  Returns
+    (entries (n, 5): M, a, b, c, nu), G (num_elements, n, C) float64).
+    Us[nu-1] has shape ([2L+1,] d^nu, K_nu); Ws[nu-1] has shape (num_el, K_nu, C).
+    """
+    ents, Gs = [], []
+    for nu, (U, W) in enumerate(zip(Us, Ws), start=1):
+        if L == 0:
+            U = U[None]
+        if U.shape[1] > 16:
+            raise UnsupportedModel("symmetric-contraction coupling dimension above 16")
+        nz = np.argwhere(np.abs(U) > U_EPS)
+        vals = U[tuple(nz.T)]
+        keys = np.concatenate([nz[:, :1], np.sort(nz[:, 1:1 + nu], axis=1)], axis=1)
+        uniq, inv = np.unique(keys, axis=0, return_inverse=True)
+        inv = inv.reshape(-1)
+        Usym = np.zeros((len(uniq), U.shape[-1]))
+        np.add.at(Usym, (inv, nz[:, -1]), vals)
+        G = np.einsum("ek,zkc->zec", Usym, W.astype(np.float64))
+        e = np.zeros((len(uniq), 5), dtype=np.int64)
+        e[:, 0] = uniq[:, 0]
+        e[:, 1:1 + nu] = uniq[:, 1:]
+        e[:, 4] = nu
+        ents.append(e)
+        Gs.append(G)
+    ent = np.concatenate(ents)
+    G = np.concatenate(Gs, axis=1)
+    order = np.lexsort((ent[:, 3], ent[:, 2], ent[:, 1], ent[:, 4], ent[:, 0]))
+    return ent[order], G[:, order]
+
+
+def _sc_tables(Us, Ws, L: int, tb: _Tables) -> tuple[int, int, int]:
+    ent, G = sc_polynomial(Us, Ws, L)
+    dM = 2 * L + 1
     seg = np.zeros(dM + 1, dtype=np.int64)
     for M in range(dM):
-        seg[M + 1] = seg[M] + np.count_nonzero(nz[:, 0] == M)
-    packed = nz[:, 0].astype(np.int64)
-    for a in range(nu):
-        packed |= nz[:, 1 + a].astype(np.int64) << (4 + 4 * a)
-    packed |= nz[:, -1].astype(np.int64) << 16
+        seg[M + 1] = seg[M] + np.count_nonzero(ent[:, 0] == M)
+    packed = ent[:, 0] | (ent[:, 1] << 4) | (ent[:, 2] << 8) | (ent[:, 3] << 12) | (ent[:, 4] << 16)
     i_off = tb.addi(np.concatenate([seg, packed]).astype(np.int32))
-    f_off = tb.addf(vals)
-    return i_off, f_off, len(vals)
+    f_off = tb.addf(G)
+    return i_off, f_off, len(ent)
 
 
 def _layer(spec: ModelSpec, lay: LayerSpec, w: dict, tb: _Tables) -> nv.LayerDesc:
@@ -174,17 +201,13 @@ def _layer(spec: ModelSpec, lay: LayerSpec, w: dict, tb: _Tables) -> nv.LayerDes
         if out.correlation > nv.MAX_CORR:
             raise UnsupportedModel("correlation order above 3 is not supported")
         pre = f"products.{t}.symmetric_contractions.contractions.{o}"
+        Ws = []
         for nu in range(1, out.correlation + 1):
             if nu == out.correlation:
-                Wn = w[f"{pre}.weights_max"]
+                Ws.append(w[f"{pre}.weights_max"])
             else:
-                Wn = w[f"{pre}.weights.{out.correlation - 1 - nu}"]
-            so.K[nu - 1] = Wn.shape[1]
-            so.f_w[nu - 1] = tb.addf(Wn)
-            i_off, f_off, nnz = _sc_tables(out.U[nu - 1], so.L, nu, tb)
-            so.i_idx[nu - 1] = i_off
-            so.f_val[nu - 1] = f_off
-            so.nnz[nu - 1] = nnz
+                Ws.append(w[f"{pre}.weights.{out.correlation - 1 - nu}"])
+        so.i_ent, so.f_G, so.n_ent = _sc_tables(out.U, Ws, so.L, tb)
     # product linear (1-to-1)
     for q, ins in enumerate(lay.prod_linear.instrs):
         if ins.i_in != q or ins.i_out != q:

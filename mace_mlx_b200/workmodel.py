@@ -17,6 +17,19 @@ def _d(l: int) -> int:
     return 2 * l + 1
 
 
+def _sc_entry_counts(out) -> dict[int, int]:
+    """Entries per degree nu of the symmetrised polynomial of one SC output."""
+    import numpy as np
+
+    counts = {}
+    for nu, U in enumerate(out.U, start=1):
+        u = U[None] if out.ir_out.l == 0 else U
+        nz = np.argwhere(np.abs(u) > 1e-12)
+        keys = {(r[0],) + tuple(sorted(r[1:1 + nu])) for r in nz}
+        counts[nu] = len(keys)
+    return counts
+
+
 def kernel_work(spec: ModelSpec, N: int, E: int) -> dict[tuple[str, int], dict]:
     """{(kernel name, layer): {"flops": F, "bytes": B}} for one evaluation."""
     out: dict[tuple[str, int], dict] = {}
@@ -73,14 +86,13 @@ def kernel_work(spec: ModelSpec, N: int, E: int) -> dict[tuple[str, int], dict]:
               "bytes": N * (lay.skip.irreps_in1.dim + lay.skip.irreps_out.dim) * F32}
         out[("skip_fwd", t)] = sk
         out[("skip_bwd", t)] = sk
+        # symmetric contraction as the polynomial of pack.sc_polynomial: per entry of
+        # degree nu, nu multiplies + 1 add forward, 3*nu - 1 multiply-adds backward
         sc_f = sc_b = 0
         for o in lay.sc.outputs:
-            for nu, U in enumerate(o.U, start=1):
-                import numpy as np
-
-                nnz = int(np.count_nonzero(np.abs(U) > 1e-12))
-                sc_f += nnz * (nu + 2)
-                sc_b += nnz * (3 * nu + 3)
+            for nu, n_e in _sc_entry_counts(o).items():
+                sc_f += n_e * (nu + 1)
+                sc_b += n_e * (3 * nu + 1)
         out[("sc_fwd", t)] = {"flops": N * C * sc_f, "bytes": N * (inter_dim + hid_dim) * F32}
         out[("sc_bwd", t)] = {"flops": N * C * sc_b, "bytes": N * (2 * inter_dim + hid_dim) * F32}
         ro = 2 * N * C * (16 if lay.readout_nonlinear else 1) * (2 if lay.readout_nonlinear else 1)

@@ -117,6 +117,35 @@ def test_per_stage_buffers_medium():
     assert m.error_flag() == 0
 
 
+def test_cuda_graph_replay_matches_direct_launches():
+    config, weights, st = make_case("medium", diamond_si(2, 0.05, 9), seed=9)
+    m = MACEModel(config=config, weights=weights, device=0)
+    dev = m.device
+    species = torch.as_tensor(m.species_index(st.numbers), device=dev)
+    gp = torch.tensor([0, len(st)], dtype=torch.int32, device=dev)
+    pos64 = torch.tensor(st.positions, dtype=torch.float64, device=dev)
+    cell64 = torch.tensor(st.cell, dtype=torch.float64, device=dev)
+    edges = m.neighbour_list(pos64, cell64, st.pbc, gp, m.r_max + 0.5)
+    pos, cell = pos64.float(), cell64.float()
+    direct = m.evaluate(pos, cell, species, gp, edges, virial=True)
+    torch.cuda.synchronize()
+    ref = {k: v.clone() for k, v in direct.items()}
+    out = {k: torch.empty_like(v) for k, v in direct.items()}
+    with torch.cuda.stream(torch.cuda.Stream(dev)):
+        for step in range(3):
+            if step == 2:  # new positions in the same buffer: replay, not re-capture
+                pos.add_(1e-3)
+            m.evaluate(pos, cell, species, gp, edges, virial=True, out=out, graph=True)
+            torch.cuda.current_stream(dev).synchronize()
+            if step < 2:
+                for k in ref:
+                    torch.testing.assert_close(out[k], ref[k], rtol=0, atol=0)
+    again = m.evaluate(pos, cell, species, gp, edges, virial=True)
+    torch.cuda.synchronize()
+    for k in ref:
+        torch.testing.assert_close(out[k], again[k], rtol=0, atol=0)
+
+
 def test_bitwise_deterministic_and_translation_invariant():
     config, weights, st = make_case("medium", diamond_si(3, 0.05, 8), seed=8)
     m = MACEModel(config=config, weights=weights, device=0)

@@ -48,7 +48,7 @@ def test_struct_layout_matches_header(tmp_path):
     fields = [("ModelDesc", "mace_model_desc", "layers"), ("ModelDesc", "mace_model_desc", "floats"),
               ("ModelDesc", "mace_model_desc", "n_ints"), ("LayerDesc", "mace_layer_desc", "conv"),
               ("LayerDesc", "mace_layer_desc", "sc"), ("LayerDesc", "mace_layer_desc", "f_ro2"),
-              ("LayerDesc", "mace_layer_desc", "mlp_w"), ("ScOut", "mace_sc_out", "f_val"),
+              ("LayerDesc", "mace_layer_desc", "mlp_w"), ("ScOut", "mace_sc_out", "f_G"),
               ("System", "mace_system", "rev")]
     src = ["#include <stdio.h>", "#include <stddef.h>", '#include "mace_b200.h"', "int main(void){"]
     for py, c in structs.items():

@@ -1,0 +1,58 @@
+"""Host-side packing of the model tables (pack.py), checked on the CPU."""
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import make_case
+from mace_mlx_b200.pack import PackedModel, sc_polynomial
+from mace_mlx_b200.spec import ModelSpec
+from oracle.model import OracleMACE
+
+
+@pytest.mark.parametrize("arch", ["small", "medium", "large"])
+def test_symmetrised_sc_polynomial_equals_dense_contraction(arch):
+    """The entry/G tables reproduce the reference's dense einsum contraction."""
+    config, weights, _ = make_case(arch, seed=2, z_table=[14, 8])
+    spec = ModelSpec.from_config(config)
+    orc = OracleMACE(config, weights)
+    rng = np.random.default_rng(0)
+    lay = spec.layers[0]
+    C = spec.C
+    n = 6
+    species = torch.tensor([0, 1, 0, 1, 1, 0])
+    x = torch.tensor(rng.normal(size=(n, spec.interaction_irreps.dim)))
+    ref = orc.symmetric_contraction(x, species, 0).numpy()
+    # coupling-major features f[node, i, c] with i = l^2 + m
+    f = np.concatenate([b.permute(0, 2, 1).numpy() for b in orc._blocks(x, spec.interaction_irreps)], axis=1)
+    o_off = 0
+    for o, out in enumerate(lay.sc.outputs):
+        pre = f"products.0.symmetric_contractions.contractions.{o}"
+        Ws = [weights[f"{pre}.weights_max"] if nu == out.correlation else
+              weights[f"{pre}.weights.{out.correlation - 1 - nu}"] for nu in range(1, out.correlation + 1)]
+        ent, G = sc_polynomial(out.U, Ws, out.ir_out.l)
+        d = 2 * out.ir_out.l + 1
+        got = np.zeros((n, C, d))
+        for e_i, (M, a, b, c, nu) in enumerate(ent):
+            term = f[:, a, :].copy()
+            if nu >= 2:
+                term *= f[:, b, :]
+            if nu >= 3:
+                term *= f[:, c, :]
+            got[:, :, M] += G[species.numpy(), e_i, :] * term
+        want = ref[:, o_off:o_off + C * d].reshape(n, C, d)
+        np.testing.assert_allclose(got, want, rtol=1e-10, atol=1e-12)
+        o_off += C * d
+        assert len(ent) < sum(int(np.count_nonzero(np.abs(u) > 1e-12)) for u in out.U)
+
+
+def test_packed_tables_are_aligned_and_complete():
+    config, weights, _ = make_case("medium")
+    pm = PackedModel(ModelSpec.from_config(config), weights)
+    d = pm.desc
+    assert pm.floats.dtype == np.float32 and pm.ints.dtype == np.int32
+    assert d.f_emb % 4 == 0 and d.layers[1].f_mlp[3] % 4 == 0
+    assert d.layers[1].n_mid == 10 and d.layers[1].wnumel == 1280 and d.layers[1].mid.dim == 5120
+    assert [d.layers[1].lin[l].n_src for l in range(4)] == [2, 3, 3, 2]
+    assert d.layers[0].sc[1].L == 1 and d.layers[0].sc[1].n_ent == 328
+    assert np.all(np.isfinite(pm.floats))
