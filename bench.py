@@ -55,6 +55,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=20.0, help="budget of the CPU baseline sample")
+    ap.add_argument("--device-only", action="store_true",
+                    help="only W + K plain device steps, no JSON (the command the ncu captures profile)")
     return ap.parse_args()
 
 
@@ -217,6 +219,11 @@ def b200_arm(args, rank: int, world: int, local_rank: int):
     def step():
         model.evaluate(pos, cell, species, gptr, edges, forces=True, virial=False, out=out, graph=True)
 
+    if args.device_only:
+        for _ in range(args.warmup + args.steps):
+            model.evaluate(pos, cell, species, gptr, edges, forces=True, virial=False, out=out)
+        torch.cuda.synchronize(dev)
+        return 0
     for _ in range(max(3, args.warmup)):
         step()
     barrier()

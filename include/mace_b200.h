@@ -128,6 +128,12 @@ typedef struct {
   int32_t n_mlp;                  /* number of Linear layers            */
   int32_t mlp_w[8];               /* widths: in, hidden..., out         */
   int64_t f_mlp[7], f_mlp_t[7];   /* (in, out) and (out, in) per layer   */
+  /* MLP layers as tensor-core operand images (hidden width 64, <= 16 radial
+   * features; else -1), tf32 hi then lo, each 128B-swizzled K-major:
+   * last layer forward: per 64-output chunk the (64 x 64) slice of (out, in);
+   * last layer backward: per 32-output chunk the (64 x 32) slice of (in, out);
+   * hidden layers 1..: (out, in) for the forward, (in, out) for the backward. */
+  int64_t f_mlp_tc, f_mlp_tc_bwd, f_mlp_tc_trunk, f_mlp_tc_trunk_bwd;
   /* conv_tp */
   int32_t n_mid;
   int32_t m_tot;                  /* length of a per-edge M row          */

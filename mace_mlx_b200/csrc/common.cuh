@@ -97,9 +97,18 @@ struct MlpParams {
   // backward
   const float* dout;     // (E, widths[n_layers])
   float* db;             // (E, widths[0]) accumulated (+=)
+  // tensor-core path (hidden width 64): pre-split, pre-swizzled last-layer images
+  const float* tc_img;       // forward chunks (null: CUDA-core path)
+  const float* tc_img_bwd;   // backward chunks
+  const float* tc_trunk;     // hidden 64 x 64 layers 1.., forward operands
+  const float* tc_trunk_bwd; // the same, backward operands
+  int* err_flag;             // set to 2 when a bounded wait gives up
 };
 int launch_mlp_fwd(const MlpParams& p, cudaStream_t s);
 int launch_mlp_bwd(const MlpParams& p, cudaStream_t s);
+bool mlp_tc_supported(const MlpParams& p);
+int launch_mlp_fwd_tc(const MlpParams& p, cudaStream_t s);
+int launch_mlp_bwd_tc(const MlpParams& p, cudaStream_t s);
 
 // ---------------------------------------------------------------------------
 // conv tensor product + segmented scatter (receiver CSR)

@@ -217,6 +217,7 @@ int check_mlp(const MlpParams& p) {
 
 int launch_mlp_fwd(const MlpParams& p, cudaStream_t s) {
   if (p.E == 0) return MACE_OK;
+  if (mlp_tc_supported(p)) return launch_mlp_fwd_tc(p, s);
   int rc = check_mlp(p);
   if (rc) return rc;
   switch (p.widths[1]) {
@@ -228,6 +229,7 @@ int launch_mlp_fwd(const MlpParams& p, cudaStream_t s) {
 
 int launch_mlp_bwd(const MlpParams& p, cudaStream_t s) {
   if (p.E == 0) return MACE_OK;
+  if (mlp_tc_supported(p)) return launch_mlp_bwd_tc(p, s);
   int rc = check_mlp(p);
   if (rc) return rc;
   switch (p.widths[1]) {

@@ -9,6 +9,7 @@
 // 533-570) with explicit kernels; nothing is allocated on this path.
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <vector>
@@ -86,6 +87,8 @@ struct mace_ctx {
   void* scan_tmp = nullptr;
   size_t scan_bytes = 0;
   int* d_err = nullptr;
+  // MACE_B200_MLP_CUDA_CORES=1 at context creation selects the CUDA-core MLP kernels
+  bool mlp_cuda_cores = false;
   // bookkeeping
   int launches = 0;
   int64_t last_N = 0, last_E = 0;
@@ -339,6 +342,13 @@ MlpParams mlp_params(mace_ctx* c, int t, int64_t E) {
   p.out = c->lb[t].w;
   p.dout = c->dw;
   p.db = c->db;
+  const bool tc_ok = !c->mlp_cuda_cores && L.f_mlp_tc >= 0 && L.f_mlp_tc_bwd >= 0 && L.f_mlp_tc_trunk >= 0 &&
+                     L.f_mlp_tc_trunk_bwd >= 0;
+  p.tc_img = tc_ok ? F(c, L.f_mlp_tc) : nullptr;
+  p.tc_img_bwd = tc_ok ? F(c, L.f_mlp_tc_bwd) : nullptr;
+  p.tc_trunk = tc_ok ? F(c, L.f_mlp_tc_trunk) : nullptr;
+  p.tc_trunk_bwd = tc_ok ? F(c, L.f_mlp_tc_trunk_bwd) : nullptr;
+  p.err_flag = c->d_err;
   return p;
 }
 
@@ -627,6 +637,8 @@ int mace_ctx_create(const mace_model_desc* desc, int device, mace_ctx** out) {
   }
   c->desc.floats = nullptr;
   c->desc.ints = nullptr;
+  const char* env = std::getenv("MACE_B200_MLP_CUDA_CORES");
+  c->mlp_cuda_cores = env && env[0] == '1';
   *out = c;
   return MACE_OK;
 }

@@ -66,6 +66,7 @@ class LayerDesc(C.Structure):
         ("f_skip", i64 * MAX_IN), ("f_skip_t", i64 * MAX_IN),
         ("f_up", i64 * MAX_IN), ("f_up_t", i64 * MAX_IN),
         ("n_mlp", i32), ("mlp_w", i32 * 8), ("f_mlp", i64 * 7), ("f_mlp_t", i64 * 7),
+        ("f_mlp_tc", i64), ("f_mlp_tc_bwd", i64), ("f_mlp_tc_trunk", i64), ("f_mlp_tc_trunk_bwd", i64),
         ("n_mid", i32), ("m_tot", i32), ("wnumel", i32),
         ("conv", ConvSlot * MAX_MID),
         ("lin", LinGroup * MAX_IN),

@@ -31,8 +31,12 @@ class _Tables:
         self.i: list[np.ndarray] = []
         self.ni = 0
 
-    def addf(self, a) -> int:
+    def addf(self, a, align: int = 4) -> int:
         a = np.ascontiguousarray(np.asarray(a, dtype=np.float32).ravel())
+        lead = (-self.nf) % align
+        if lead:
+            self.f.append(np.zeros(lead, np.float32))
+            self.nf += lead
         off = self.nf
         # keep every table 16-byte aligned for vector loads
         pad = (-a.size) % 4
@@ -69,6 +73,71 @@ def _slots(irreps, C: int) -> nv.Slots:
         o += C * m.ir.dim
     s.dim = o
     return s
+
+
+def tf32_split(a: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    """fp32 -> (hi, lo): hi rounded to tf32 (nearest, ties away), lo = a - hi."""
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    u = a.view(np.uint32).astype(np.uint64)
+    hi = (((u + 0x1000) & 0xFFFFE000) & 0xFFFFFFFF).astype(np.uint32).view(np.float32)
+    return hi, (a - hi).astype(np.float32)
+
+
+def sw128_image(m: np.ndarray) -> np.ndarray:
+    """(rows, K) fp32 matrix in the 128B-swizzled K-major tensor-core layout.
+
+    K is split into 32-wide column panels (rows x 128 bytes each, rows
+    contiguous); the 16-byte chunk j of row r sits at chunk j ^ (r % 8).
+    Returns a flat float32 array of rows*K values.
+    """
+    rows, K = m.shape
+    assert K % 32 == 0 and rows % 8 == 0
+    r = np.arange(rows)[:, None]
+    k = np.arange(K)[None, :]
+    off = (k // 32) * rows * 32 + r * 32 + (((k % 32) // 4) ^ (r % 8)) * 4 + (k % 4)
+    out = np.zeros(rows * K, np.float32)
+    out[off.ravel()] = m.ravel()
+    return out
+
+
+def _hilo_image(m: np.ndarray) -> np.ndarray:
+    hi, lo = tf32_split(m)
+    return np.concatenate([sw128_image(hi), sw128_image(lo)])
+
+
+def mlp_tc_trunk_images(hidden_out_in: list[np.ndarray]) -> tuple[np.ndarray, np.ndarray]:
+    """Images of the 64 x 64 hidden layers 1.. for the tcgen05 kernels.
+
+    Forward operand B[o][i] is the (out, in) matrix; backward operand B[i][o]
+    is its transpose.  Each as tf32 hi then lo, 128B-swizzled K-major.
+    """
+    if not hidden_out_in:
+        return np.zeros(4, np.float32), np.zeros(4, np.float32)
+    fwd = np.concatenate([_hilo_image(np.asarray(w, np.float32)) for w in hidden_out_in])
+    bwd = np.concatenate([_hilo_image(np.ascontiguousarray(np.asarray(w, np.float32).T)) for w in hidden_out_in])
+    return fwd, bwd
+
+
+def mlp_tc_images(w_last_out_in: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    """Operand images of the last radial-MLP layer for the tcgen05 kernels.
+
+    ``w_last_out_in`` is the converted (out, in) weight with in = 64.  Forward:
+    per 64-output chunk the (64 x 64) slice, tf32 hi then lo.  Backward: per
+    32-output chunk the (64 x 32) slice of the transpose, hi then lo.
+    """
+    W = np.asarray(w_last_out_in, dtype=np.float32)
+    n_out, n_in = W.shape
+    pad_f = -(-n_out // 64) * 64
+    Wf = np.zeros((pad_f, n_in), np.float32)
+    Wf[:n_out] = W
+    fwd = np.concatenate([_hilo_image(Wf[c:c + 64]) for c in range(0, pad_f, 64)])
+    pad_b = -(-n_out // 32) * 32
+    Wb = np.zeros((n_in, pad_b), np.float32)
+    Wb[:, :n_out] = W.T
+    hi, lo = tf32_split(Wb)
+    bwd = np.concatenate([np.concatenate([sw128_image(hi[:, c:c + 32]), sw128_image(lo[:, c:c + 32])])
+                          for c in range(0, pad_b, 32)])
+    return fwd, bwd
 
 
 def sc_polynomial(Us: list[np.ndarray], Ws: list[np.ndarray], L: int):
@@ -158,6 +227,16 @@ def _layer(spec: ModelSpec, lay: LayerSpec, w: dict, tb: _Tables) -> nv.LayerDes
         Wm = w[f"interactions.{t}.conv_tp_weights.layers.{2 * j}.weight"].astype(np.float64)  # (out, in)
         d.f_mlp[j] = tb.addf(Wm.T)
         d.f_mlp_t[j] = tb.addf(Wm)
+    d.f_mlp_tc = d.f_mlp_tc_bwd = d.f_mlp_tc_trunk = d.f_mlp_tc_trunk_bwd = -1
+    if all(wd == 64 for wd in widths[1:-1]) and widths[0] <= 16:
+        last = w[f"interactions.{t}.conv_tp_weights.layers.{2 * (d.n_mlp - 1)}.weight"]
+        fwd_img, bwd_img = mlp_tc_images(last)
+        d.f_mlp_tc = tb.addf(fwd_img, align=32)
+        d.f_mlp_tc_bwd = tb.addf(bwd_img, align=32)
+        hidden = [w[f"interactions.{t}.conv_tp_weights.layers.{2 * j}.weight"] for j in range(1, d.n_mlp - 1)]
+        tf, tbw = mlp_tc_trunk_images(hidden)
+        d.f_mlp_tc_trunk = tb.addf(tf, align=32)
+        d.f_mlp_tc_trunk_bwd = tb.addf(tbw, align=32)
     # conv_tp slots
     cv = lay.conv
     if len(cv.instrs) > nv.MAX_MID:

@@ -158,3 +158,19 @@ def test_bitwise_deterministic_and_translation_invariant():
     st2.positions = st2.positions + np.array([0.37, -0.21, 0.05])
     c, _, _ = run_gpu(m, st2)
     np.testing.assert_allclose(c["forces"], a["forces"], atol=1e-4 * np.abs(a["forces"]).max() + 1e-7)
+
+
+def test_tensor_core_mlp_matches_cuda_core_mlp(monkeypatch):
+    """tcgen05 (3-term tf32) radial MLP vs the fp32 CUDA-core kernels."""
+    config, weights, st = make_case("medium", diamond_si(3, 0.05, 13), seed=13)
+    m_tc = MACEModel(config=config, weights=weights, device=0)
+    monkeypatch.setenv("MACE_B200_MLP_CUDA_CORES", "1")
+    m_cc = MACEModel(config=config, weights=weights, device=0)
+    a, _, _ = run_gpu(m_tc, st)
+    b, _, _ = run_gpu(m_cc, st)
+    for t in range(2):
+        wa = m_tc.debug_buffer("w", t).cpu().numpy()
+        wb = m_cc.debug_buffer("w", t).cpu().numpy()
+        assert rel_err(wa, wb) < 1e-5, rel_err(wa, wb)  # both fp32-accurate: ~2^-21 per product
+    assert rel_err(a["forces"], b["forces"]) < 2e-5
+    assert abs(a["energy"][0] - b["energy"][0]) < 1e-5 * max(1.0, abs(b["energy"][0]))

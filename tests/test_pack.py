@@ -56,3 +56,29 @@ def test_packed_tables_are_aligned_and_complete():
     assert [d.layers[1].lin[l].n_src for l in range(4)] == [2, 3, 3, 2]
     assert d.layers[0].sc[1].L == 1 and d.layers[0].sc[1].n_ent == 328
     assert np.all(np.isfinite(pm.floats))
+
+
+def test_tf32_split_and_swizzled_images_round_trip():
+    from mace_mlx_b200.pack import mlp_tc_images, sw128_image, tf32_split
+
+    rng = np.random.default_rng(1)
+    a = rng.normal(size=(64, 96)).astype(np.float32)
+    hi, lo = tf32_split(a)
+    assert np.all((hi.view(np.uint32) & 0x1FFF) == 0)
+    np.testing.assert_array_equal(hi + lo, a)
+    assert np.abs(lo).max() <= np.abs(a).max() * 2.0 ** -11
+    img = sw128_image(a)
+    r = np.arange(64)[:, None]
+    k = np.arange(96)[None, :]
+    off = (k // 32) * 64 * 32 + r * 32 + (((k % 32) // 4) ^ (r % 8)) * 4 + (k % 4)
+    np.testing.assert_array_equal(img[off], a)
+    assert len(set(off.ravel().tolist())) == a.size
+    w = rng.normal(size=(200, 64)).astype(np.float32)  # (out, in) with out not a multiple of 128
+    fwd, bwd = mlp_tc_images(w)
+    assert fwd.size == 4 * 2 * 64 * 64 and bwd.size == 7 * 2 * 64 * 32
+    # forward chunk 3 (outputs 192..255), hi part, row 7 (output 199) holds w[199] up to tf32 rounding
+    ch = fwd[3 * 2 * 64 * 64: 3 * 2 * 64 * 64 + 64 * 64]
+    rr = 7
+    kk = np.arange(64)
+    got = ch[(kk // 32) * 64 * 32 + rr * 32 + (((kk % 32) // 4) ^ (rr % 8)) * 4 + (kk % 4)]
+    np.testing.assert_allclose(got, w[199], rtol=2.0 ** -11)
