@@ -163,10 +163,9 @@ __device__ __forceinline__ float warp_reduce16(float s[16]) {
 template <int L1, int L2, int L3>
 __device__ __forceinline__ void bwd_slot(const ConvParams& p, const ConvSlotDev& sl, int k,
                                          int64_t e, int s, const float* Mk, const float* Ye,
-                                         const float* sH, float* sDup, float sdy[16]) {
+                                         const float* sH, float* sDup, float sdy[16], int u) {
   constexpr int D1 = 2 * L1 + 1, D2 = 2 * L2 + 1, D3 = 2 * L3 + 1, YO = L2 * L2;
   constexpr float PAR = (L2 & 1) ? -1.f : 1.f;
-  const int u = threadIdx.x;
   const int C = p.C;
   const float* x = p.up + (int64_t)s * p.in_dim + sl.src_off + u;
   float x1[D1];
@@ -202,24 +201,29 @@ __device__ __forceinline__ void bwd_slot(const ConvParams& p, const ConvSlotDev&
   }
 }
 
-__global__ void k_conv_bwd(ConvParams p, int EC) {
+// G groups of C threads share one receiver: group g takes edges j = g, g+G, ...
+// of every chunk, so the per-receiver tables (H, M rows) are staged once for
+// G times as many warps.
+__global__ void __launch_bounds__(512, 2) k_conv_bwd(ConvParams p, int EC, int G) {
   extern __shared__ float sm[];
-  const int nw = blockDim.x / 32;
+  const int C = p.C;
+  const int nw = C / 32;                   // warps per group
   int* sSnd = reinterpret_cast<int*>(sm);
   float* sY = sm + EC;
   float* sM = sY + EC * 16;
   float* sRed = sM + EC * p.m_tot;        // nw x EC x 16
   float* sH = sRed + nw * EC * 16;         // h_tot x C
-  float* sDup = sH + p.h_tot * p.C;        // in_dim
+  float* sDupAll = sH + p.h_tot * C;       // G x in_dim
   const int64_t n = blockIdx.x;
   const int tid = threadIdx.x;
-  const int C = p.C;
+  const int u = tid % C, grp = tid / C;
+  float* sDup = sDupAll + grp * p.in_dim;
   const int64_t e_beg = p.row_ptr[n], e_end = p.row_ptr[n + 1];
-  for (int q = tid; q < p.in_dim; q += blockDim.x) sDup[q] = 0.f;
-  // H_k[i][j] = sum_m pw CG_k[i, j, m] dA[n][k][m][u] (thread u's own column)
+  for (int q = tid; q < G * p.in_dim; q += blockDim.x) sDupAll[q] = 0.f;
+  // H_k[i][j] = sum_m pw CG_k[i, j, m] dA[n][k][m][u] (thread u's own column), slots split over groups
   {
-    const float* g = p.dA + n * p.mid_dim + tid;
-    for (int k = 0; k < p.n_mid; ++k) {
+    const float* g = p.dA + n * p.mid_dim + u;
+    for (int k = grp; k < p.n_mid; k += G) {
       const ConvSlotDev& sl = p.slot[k];
       const int D1 = cdim(sl.l1), D2 = cdim(sl.l2), D3 = cdim(sl.l3);
       float gk[7];
@@ -231,16 +235,16 @@ __global__ void k_conv_bwd(ConvParams p, int EC) {
 #pragma unroll
           for (int m = 0; m < 7; ++m)
             if (m < D3) a = fmaf(__ldg(sl.cg + (i * D2 + jj) * D3 + m), gk[m], a);
-          sH[(sl.h_off + i * D2 + jj) * C + tid] = a;
+          sH[(sl.h_off + i * D2 + jj) * C + u] = a;
         }
     }
   }
   __syncthreads();
-  const int warp = tid >> 5, lane = tid & 31;
+  const int warp = u >> 5, lane = tid & 31;
   for (int64_t cb = e_beg; cb < e_end; cb += EC) {
     const int ne = (int)imin64(EC, e_end - cb);
     stage_chunk(p, cb, ne, sSnd, sY, sM);
-    for (int j = 0; j < ne; ++j) {
+    for (int j = grp; j < ne; j += G) {
       float sdy[16];
 #pragma unroll
       for (int q = 0; q < 16; ++q) sdy[q] = 0.f;
@@ -253,7 +257,7 @@ __global__ void k_conv_bwd(ConvParams p, int EC) {
         const float* Mk = Mrow + sl.m_off;
         switch (sl.combo) {
 #define BWD_CASE(a, b, c) \
-  case a * 16 + b * 4 + c: bwd_slot<a, b, c>(p, sl, k, e, s, Mk, Ye, sH, sDup, sdy); break;
+  case a * 16 + b * 4 + c: bwd_slot<a, b, c>(p, sl, k, e, s, Mk, Ye, sH, sDup, sdy, u); break;
           BWD_CASE(0, 0, 0) BWD_CASE(0, 1, 1) BWD_CASE(0, 2, 2) BWD_CASE(0, 3, 3)
           BWD_CASE(1, 0, 1) BWD_CASE(1, 1, 0) BWD_CASE(1, 1, 1) BWD_CASE(1, 1, 2)
           BWD_CASE(1, 2, 1) BWD_CASE(1, 2, 2) BWD_CASE(1, 2, 3) BWD_CASE(1, 3, 2)
@@ -277,7 +281,11 @@ __global__ void k_conv_bwd(ConvParams p, int EC) {
     }
     __syncthreads();
   }
-  for (int q = tid; q < p.in_dim; q += blockDim.x) p.dup[n * p.in_dim + q] = sDup[q];
+  for (int q = tid; q < p.in_dim; q += blockDim.x) {
+    float v = 0.f;
+    for (int g = 0; g < G; ++g) v += sDupAll[g * p.in_dim + q];  // fixed order: deterministic
+    p.dup[n * p.in_dim + q] = v;
+  }
 }
 
 }  // namespace
@@ -311,11 +319,13 @@ int launch_conv_bwd(const ConvParams& p, cudaStream_t s) {
   if (rc) return rc;
   const int EC = 32;
   const int nw = p.C / 32;
-  size_t smem = (size_t)(EC + EC * 16 + EC * p.m_tot + nw * EC * 16 + p.h_tot * p.C + p.in_dim) * sizeof(float);
+  int G = 1024 / p.C;
+  if (G > 4) G = 4;
+  size_t smem = (size_t)(EC + EC * 16 + EC * p.m_tot + nw * EC * 16 + p.h_tot * p.C + G * p.in_dim) * sizeof(float);
   if (smem > 227 * 1024) return fail(MACE_ERR_UNSUPPORTED, "conv backward tile exceeds shared memory");
   if (smem > 48 * 1024)
     MACE_CUDA_TRY(cudaFuncSetAttribute(k_conv_bwd, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  k_conv_bwd<<<(unsigned)p.N, p.C, smem, s>>>(p, EC);
+  k_conv_bwd<<<(unsigned)p.N, p.C * G, smem, s>>>(p, EC, G);
   MACE_LAUNCH_CHECK("conv_bwd");
   return MACE_OK;
 }
