@@ -130,7 +130,7 @@ typedef struct {
   int64_t f_mlp[7], f_mlp_t[7];   /* (in, out) and (out, in) per layer   */
   /* MLP layers as tensor-core operand images (hidden width 64, <= 16 radial
    * features; else -1), tf32 hi then lo, each 128B-swizzled K-major:
-   * last layer forward: per 64-output chunk the (64 x 64) slice of (out, in);
+   * last layer forward: per 32-output chunk the (32 x 64) slice of (out, in);
    * last layer backward: per 32-output chunk the (64 x 32) slice of (in, out);
    * hidden layers 1..: (out, in) for the forward, (in, out) for the backward. */
   int64_t f_mlp_tc, f_mlp_tc_bwd, f_mlp_tc_trunk, f_mlp_tc_trunk_bwd;
@@ -260,7 +260,10 @@ int mace_forward_backward(mace_ctx* ctx, const mace_system* sys, const mace_outp
 /*
  * Debug/parity access to an internal per-stage buffer after the last call:
  * id = layer * 16 + stage (see mace_mlx_b200/native.py for the stage list).
- * Returns the device pointer and length in floats.
+ * Returns the device pointer and length in floats.  The radial weights
+ * (stage "w") are in 128-edge tiles: tile e / 128 holds ceil(W / 32) chunks
+ * of 128 rows x 32 floats; column c of edge e sits in chunk c / 32 at row
+ * e % 128, 16-byte group ((c % 32) / 4) XOR (e % 8), position c % 4.
  */
 int mace_debug_buffer(mace_ctx* ctx, int32_t id, const float** ptr, int64_t* len);
 

@@ -85,6 +85,24 @@ int launch_virial_reduce(const double* part, int n_part, double* out, cudaStream
 // ---------------------------------------------------------------------------
 // radial MLP
 // ---------------------------------------------------------------------------
+// Radial weights w and their gradient dw are stored in 128-edge tiles: tile
+// e >> 7 holds ceil(W / 32) chunks of 128 rows x 32 floats (16 KB each), and
+// inside a chunk row e & 127 fills 128 contiguous bytes whose 16-byte groups
+// are XOR-swizzled with (e & 7).  That is the tensor cores' 128B-swizzled
+// K-major operand layout, so one chunk moves between HBM and shared memory
+// in a single 1-D bulk copy, while a warp reading 32 consecutive columns of
+// one edge still reads one 128-byte line.  Rows of the last tile beyond E are
+// padding.
+constexpr int WT_TILE = 128;
+constexpr int WT_CHUNK = WT_TILE * 32;  // floats per chunk
+__host__ __device__ __forceinline__ int wt_nchunk(int W) { return (W + 31) / 32; }
+__host__ __device__ __forceinline__ int64_t wt_floats(int64_t E, int W) {
+  return ((E + WT_TILE - 1) / WT_TILE) * (int64_t)wt_nchunk(W) * WT_CHUNK;
+}
+__host__ __device__ __forceinline__ int64_t wt_index(int64_t e, int c, int nch) {
+  return (((e >> 7) * nch + (c >> 5)) << 12) + ((e & 127) << 5) + ((((c >> 2) & 7) ^ (int)(e & 7)) << 2) + (c & 3);
+}
+
 struct MlpParams {
   int64_t E;
   int n_layers;          // Linear layers (last has no activation)
@@ -93,9 +111,9 @@ struct MlpParams {
   const float* wt[7];    // (out, in) row-major
   const float* b;        // (E, widths[0])
   float* act;            // (E, sum hidden) pre-activations of hidden layers
-  float* out;            // (E, widths[n_layers])
+  float* out;            // (E, widths[n_layers]) in 128-edge tiles (wt_index)
   // backward
-  const float* dout;     // (E, widths[n_layers])
+  const float* dout;     // (E, widths[n_layers]) in 128-edge tiles (wt_index)
   float* db;             // (E, widths[0]) accumulated (+=)
   // tensor-core path (hidden width 64): pre-split, pre-swizzled last-layer images
   const float* tc_img;       // forward chunks (null: CUDA-core path)
@@ -129,6 +147,7 @@ struct ConvParams {
   int m_tot;
   int h_tot;     // sum over slots of (2l1+1)(2l2+1)
   int wnumel;
+  int wnch;      // wt_nchunk(wnumel)
   int in_dim;
   int in_ch;       // in_dim / C
   int mid_dim;
@@ -137,11 +156,11 @@ struct ConvParams {
   const int32_t* snd;
   const float* Y;        // (E,16)
   const float* up;       // (N,in_dim)
-  const float* w;        // (E,wnumel)
+  const float* w;        // (E,wnumel) in 128-edge tiles (wt_index)
   float* A;              // (N,mid_dim)
   // backward
   const float* dA;       // (N,mid_dim)
-  float* dw;             // (E,wnumel)
+  float* dw;             // (E,wnumel) in 128-edge tiles (wt_index)
   float* dY;             // (E,16) accumulated
   float* dup;            // (N,in_dim)
 };

@@ -74,7 +74,7 @@ __device__ __forceinline__ void fwd_slot(const ConvParams& p, const ConvSlotDev&
     float x1[D1];
 #pragma unroll
     for (int i = 0; i < D1; ++i) x1[i] = __ldg(x + i * C);
-    const float w = __ldg(p.w + (cb + j) * p.wnumel + k * C + u);
+    const float w = __ldg(p.w + wt_index(cb + j, k * C + u, p.wnch));
     const float* Mk = sM + j * p.m_tot + sl.m_off;
 #pragma unroll
     for (int m = 0; m < D3; ++m) {
@@ -171,7 +171,7 @@ __device__ __forceinline__ void bwd_slot(const ConvParams& p, const ConvSlotDev&
   float x1[D1];
 #pragma unroll
   for (int i = 0; i < D1; ++i) x1[i] = __ldg(x + i * C);
-  const float w = __ldg(p.w + e * p.wnumel + k * C + u);
+  const float w = __ldg(p.w + wt_index(e, k * C + u, p.wnch));
   float gr[D3];
   const float* dAs = p.dA + (int64_t)s * p.mid_dim + sl.off + u;
 #pragma unroll
@@ -190,7 +190,7 @@ __device__ __forceinline__ void bwd_slot(const ConvParams& p, const ConvSlotDev&
     dw = fmaf(xh[jj], Ye[YO + jj], dw);
     sdy[YO + jj] = fmaf(w, xh[jj], sdy[YO + jj]);
   }
-  p.dw[e * p.wnumel + k * C + u] = dw;
+  p.dw[wt_index(e, k * C + u, p.wnch)] = dw;
   // sender side of node n through the reverse edge
 #pragma unroll
   for (int i = 0; i < D1; ++i) {

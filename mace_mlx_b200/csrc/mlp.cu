@@ -97,7 +97,7 @@ __global__ void __launch_bounds__(NT) k_mlp_fwd(MlpParams p) {
     if (ok) {
 #pragma unroll
       for (int e = 0; e < TE; ++e)
-        if (e < ne) p.out[(e0 + e) * (int64_t)wout + c] = acc[e];
+        if (e < ne) p.out[wt_index(e0 + e, c, wt_nchunk(wout))] = acc[e];
     }
   }
 }
@@ -130,7 +130,7 @@ __global__ void __launch_bounds__(NT) k_mlp_bwd(MlpParams p) {
     const int kc = min(KC, wout - c0);
     for (int idx = threadIdx.x; idx < TE * KC; idx += NT) {
       int e = idx / KC, c = idx % KC;
-      sD[e * (KC + 1) + c] = (e < ne && c < kc) ? p.dout[(e0 + e) * (int64_t)wout + c0 + c] : 0.f;
+      sD[e * (KC + 1) + c] = (e < ne && c < kc) ? p.dout[wt_index(e0 + e, c0 + c, wt_nchunk(wout))] : 0.f;
     }
     for (int idx = threadIdx.x; idx < KC * H; idx += NT) {
       int c = idx / H, i = idx % H;

@@ -1,27 +1,34 @@
 // Radial MLP on the 5th-generation tensor cores (sm_100a tcgen05, kind::tf32
 // with a 3-term hi/lo split for fp32-level accuracy; see tc.cuh).
 //
-// One CTA of 128 threads owns a tile of 128 edges; thread t owns edge t, which
-// is also TMEM lane t of every 128-row accumulator.  About 100 KB of shared
-// memory, so two CTAs share an SM and overlap each other's phases.
+// One CTA owns a tile of 128 edges (TMEM lane t = edge t of the tile) and runs
+// five warps: warps 0-3 are the epilogue warps (thread t owns edge t), warp 4
+// is the control warp, whose lane 0 issues every bulk copy and every
+// tcgen05.mma.  The warps hand work to one another through mbarriers only, so
+// no warp waits for the slowest one at a block-wide barrier.  About 113 KB of
+// shared memory (forward) and 97 KB (backward): two CTAs per SM.
 //
 // Forward:
 //   layer 0 (radial features -> 64) on the CUDA cores; every 64 x 64 hidden
-//   layer and every 64-column chunk of the last layer as 8 K-blocks x 3
-//   tcgen05.mma (M = 128, N = 64, K = 8) from the swizzled hi/lo activation
-//   tile (A) and a pre-split, pre-swizzled weight image (B) brought in by a
-//   1-D bulk copy; epilogues read TMEM per edge (pre-activations stored for
-//   the backward, SiLU, split, back to A).  Two TMEM buffers alternate
-//   between chunks; the next image is fetched while an epilogue runs.
+//   layer as 8 K-blocks x 3 MMAs (M = 128, N = 64, K = 8) from the swizzled
+//   hi/lo activation tile (A) and a pre-split, pre-swizzled weight image (B);
+//   the last layer in 32-column chunks with two B stages and four TMEM
+//   buffers, so the control warp runs up to three chunks ahead of the
+//   epilogue.  Each epilogue warp moves its 32 rows of a finished chunk from
+//   TMEM through a 4 KB staging slice to HBM with one bulk store: the output
+//   is in the 128-edge tile layout (common.cuh), whose chunk rows are exactly
+//   the staging slice.
 // Backward:
-//   dH = dW (128 x W) . W_last^T with a 2-stage pipeline (the next dW chunk
-//   is prefetched into registers while the current one is split into A and
-//   its MMAs run), then for every hidden layer dH <- (dH * SiLU'(a)) . W_j^T
-//   on the tensor cores, and the last step to dL/db on the CUDA cores.
+//   dH = dW (128 x W) . W_last^T in 32-wide K chunks: the control warp copies
+//   a 16 KB dW chunk (already in operand layout) and the matching 16 KB weight
+//   image per stage, the epilogue warps split it into hi/lo in place, and the
+//   control warp accumulates 4 K-blocks x 3 MMAs into TMEM; then every hidden
+//   layer dH <- (dH * SiLU'(a)) . W_j^T on the tensor cores, and the last step
+//   to dL/db on the CUDA cores.
 //
-// Every mbarrier wait is bounded (tc::mbar_wait gives up after ~2 s); on a
-// timeout the kernel records MLP_TC_TIMEOUT in the error flag, frees its TMEM
-// and returns.
+// Every mbarrier wait is bounded (about 2 s).  A wait that gives up raises a
+// CTA-wide abort flag that ends every other wait, the kernel records
+// MLP_TC_TIMEOUT in the error flag, frees its TMEM and returns.
 #include "common.cuh"
 #include "tc.cuh"
 
@@ -29,12 +36,20 @@ namespace mace {
 
 namespace {
 
-constexpr int TM = 128;   // edges per tile (MMA M)
-constexpr int H = 64;     // hidden width
-constexpr int TN = 64;    // output columns per forward chunk (MMA N)
-constexpr int KC = 32;    // backward K chunk (one 128-byte panel)
+constexpr int TM = 128;           // edges per tile (MMA M)
+constexpr int H = 64;             // hidden width
+constexpr int TC32 = 32;          // output columns per forward chunk (MMA N)
+constexpr int KC = 32;            // backward K chunk (one 128-byte panel)
+constexpr int NEPI = 4;           // epilogue warps
+constexpr int NTHR = 32 * (NEPI + 1);
+constexpr int NBUF = 4;           // forward TMEM chunk buffers of 32 columns
+constexpr int TMEM_COLS = 128;
 constexpr int MLP_TC_TIMEOUT = 2;
-constexpr int IMG = 2 * 64 * 64;  // floats of one 64 x 64 hi/lo image
+constexpr int MLP_TC_ALIGN = 8;   // dynamic shared memory not 1024-byte aligned
+constexpr int IMG = 2 * H * H;    // floats of one 64 x 64 hi/lo image
+constexpr int CIMG = 2 * TC32 * H;  // floats of one forward chunk image (32 x 64, hi/lo)
+constexpr int BIMG = 2 * H * KC;    // floats of one backward chunk image (64 x 32, hi/lo)
+static_assert(WT_CHUNK * 4 == TM * 128, "a radial-weight chunk is one 128 x 128-byte operand panel");
 
 __device__ __forceinline__ void put_hilo(unsigned char* a_hi, unsigned char* a_lo, int row, int k0, float4 v) {
   float4 hi, lo;
@@ -71,356 +86,418 @@ __device__ __forceinline__ void tmem_row64(uint32_t tmem, int warp, int col0, fl
   tc::tmem_wait_ld();
 }
 
-struct FwdSmem {
-  static constexpr int A_HI = 0;                   // 128 x 64 fp32 = 32 KB
-  static constexpr int A_LO = A_HI + TM * H * 4;   // 32 KB
-  static constexpr int B = A_LO + TM * H * 4;      // hi/lo image, 32 KB
-  static constexpr int W0 = B + IMG * 4;           // layer 0 weights, <= 16 x 64
-  static constexpr int BARS = W0 + 16 * H * 4;
-  static constexpr int TOTAL = BARS + 64;
-};
-
+// layer 0 on the CUDA cores: y = b[e] . W0, W0 (NB, 64) read through L1 (one
+// address per warp instruction)
 template <int NB>
-__global__ void __launch_bounds__(128, 2) k_mlp_fwd_tc(MlpParams p) {
-  extern __shared__ unsigned char smem_raw[];
-  unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + FwdSmem::BARS);
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + FwdSmem::BARS + 32);
-  float* sW0 = reinterpret_cast<float*>(sm + FwdSmem::W0);
-  unsigned char* a_hi_p = sm + FwdSmem::A_HI;
-  unsigned char* a_lo_p = sm + FwdSmem::A_LO;
-  const uint32_t bar_b = tc::smem_u32(&bars[0]);
-  const uint32_t bar_m = tc::smem_u32(&bars[1]);
-  const uint32_t a_hi = tc::smem_u32(a_hi_p), a_lo = tc::smem_u32(a_lo_p);
-  const uint32_t b_hi = tc::smem_u32(sm + FwdSmem::B), b_lo = b_hi + IMG * 2;
-  const int t = threadIdx.x, warp = t >> 5;
-  const int64_t e = (int64_t)blockIdx.x * TM + t;
-  const bool valid = e < p.E;
-  const int nh = p.n_layers - 1;
-  const int wout = p.widths[p.n_layers];
-  const int nchunk = (wout + TN - 1) / TN;
-  const int n_img = (nh - 1) + nchunk;  // images in order: hidden 1.., then last-layer chunks
-  auto image = [&](int i) -> const float* {
-    return i < nh - 1 ? p.tc_trunk + (int64_t)i * IMG : p.tc_img + (int64_t)(i - (nh - 1)) * IMG;
-  };
-
-  if (warp == 0) {
-    tc::tmem_alloc(tc::smem_u32(tslot), 2 * TN);
-    tc::tmem_relinquish();
-  }
-  if (t == 0) {
-    tc::mbar_init(bar_b, 1);
-    tc::mbar_init(bar_m, 1);
-    tc::fence_barrier_init();
-  }
-  for (int q = t; q < NB * H; q += TM) sW0[q] = __ldg(p.w[0] + q);
-  __syncthreads();
-  if (t == 0) {  // first image in flight during layer 0
-    tc::mbar_expect_tx(bar_b, IMG * 4);
-    tc::bulk_g2s(b_hi, image(0), IMG * 4, bar_b);
-  }
-  // ---- layer 0 on the CUDA cores ----
-  float y[H];
-  {
-    float x[NB];
+__device__ __forceinline__ void layer0(const MlpParams& p, int64_t e, bool valid, float* y) {
+  float x[NB];
 #pragma unroll
-    for (int i = 0; i < NB; ++i) x[i] = valid ? p.b[e * NB + i] : 0.f;
+  for (int i = 0; i < NB; ++i) x[i] = valid ? __ldg(p.b + e * NB + i) : 0.f;
 #pragma unroll
-    for (int o = 0; o < H; ++o) y[o] = 0.f;
+  for (int o = 0; o < H; ++o) y[o] = 0.f;
 #pragma unroll
-    for (int i = 0; i < NB; ++i) {
-      const float4* w4 = reinterpret_cast<const float4*>(sW0 + i * H);
-#pragma unroll
-      for (int q = 0; q < H / 4; ++q) {
-        const float4 w = w4[q];
-        y[4 * q + 0] = fmaf(x[i], w.x, y[4 * q + 0]);
-        y[4 * q + 1] = fmaf(x[i], w.y, y[4 * q + 1]);
-        y[4 * q + 2] = fmaf(x[i], w.z, y[4 * q + 2]);
-        y[4 * q + 3] = fmaf(x[i], w.w, y[4 * q + 3]);
-      }
-    }
-  }
-  const uint32_t tmem = *tslot;
-  uint32_t pb = 0, pm = 0;
-  bool ok = true;
-  for (int j = 0; j < nh && ok; ++j) {
-    // epilogue of hidden layer j: store pre-activation, SiLU, split into A
-    if (valid) {
-      float4* act = reinterpret_cast<float4*>(p.act + e * (int64_t)(nh * H) + j * H);
-#pragma unroll
-      for (int q = 0; q < H / 4; ++q) act[q] = make_float4(y[4 * q], y[4 * q + 1], y[4 * q + 2], y[4 * q + 3]);
-    }
+  for (int i = 0; i < NB; ++i) {
+    const float4* w4 = reinterpret_cast<const float4*>(p.w[0] + i * H);
 #pragma unroll
     for (int q = 0; q < H / 4; ++q) {
-      float4 h = valid ? make_float4(silu_f(y[4 * q]), silu_f(y[4 * q + 1]), silu_f(y[4 * q + 2]), silu_f(y[4 * q + 3]))
-                       : make_float4(0.f, 0.f, 0.f, 0.f);
-      put_hilo(a_hi_p, a_lo_p, t, 4 * q, h);
+      const float4 w = __ldg(w4 + q);
+      y[4 * q + 0] = fmaf(x[i], w.x, y[4 * q + 0]);
+      y[4 * q + 1] = fmaf(x[i], w.y, y[4 * q + 1]);
+      y[4 * q + 2] = fmaf(x[i], w.z, y[4 * q + 2]);
+      y[4 * q + 3] = fmaf(x[i], w.w, y[4 * q + 3]);
     }
-    tc::fence_proxy_async();
-    tc::fence_before_sync();
-    __syncthreads();
-    if (j == nh - 1) break;  // the last hidden activation feeds the output chunks
-    // hidden layer j+1 on the tensor cores (TMEM buffer 0)
-    if (t == 0) {
-      ok = tc::mbar_wait(bar_b, pb);
-      if (ok) {
-        tc::fence_after_sync();
-        mma_k64<TN>(tmem, a_hi, a_lo, b_hi, b_lo);
-        tc::mma_commit(bar_m);
-      }
-    }
-    pb ^= 1;
-    ok = tc::mbar_wait(bar_m, pm) && ok;
-    pm ^= 1;
-    ok = __syncthreads_and(ok);
-    if (!ok) break;
-    tc::fence_after_sync();
-    if (t == 0) {  // B is free again: fetch the next image
-      tc::mbar_expect_tx(bar_b, IMG * 4);
-      tc::bulk_g2s(b_hi, image(j + 1), IMG * 4, bar_b);
-    }
-    tmem_row64(tmem, warp, 0, y);
   }
-  // ---- last layer: 64-column chunks, TMEM buffers alternate ----
-  for (int c = 0; c < nchunk && ok; ++c) {
-    const uint32_t buf = tmem + (c & 1) * TN;
-    if (t == 0) {
-      ok = tc::mbar_wait(bar_b, pb);
-      if (ok) {
-        tc::fence_after_sync();
-        mma_k64<TN>(buf, a_hi, a_lo, b_hi, b_lo);
-        tc::mma_commit(bar_m);
-      }
-    }
-    pb ^= 1;
-    ok = tc::mbar_wait(bar_m, pm) && ok;
-    pm ^= 1;
-    ok = __syncthreads_and(ok);
-    if (!ok) break;
-    tc::fence_after_sync();
-    const int next = (nh - 1) + c + 1;
-    if (t == 0 && next < n_img) {
-      tc::mbar_expect_tx(bar_b, IMG * 4);
-      tc::bulk_g2s(b_hi, image(next), IMG * 4, bar_b);
-    }
-    float v[TN];
-    tmem_row64(buf, warp, 0, v);
-    if (valid) {
-      float* dst = p.out + e * (int64_t)wout + c * TN;
-#pragma unroll
-      for (int q = 0; q < TN / 4; ++q)
-        if (c * TN + 4 * q < wout)
-          *reinterpret_cast<float4*>(dst + 4 * q) = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-    }
-    tc::fence_before_sync();
-  }
-  if (!ok && t == 0) atomicExch(p.err_flag, MLP_TC_TIMEOUT);
-  __syncthreads();
-  if (warp == 0) tc::tmem_dealloc(tmem, 2 * TN);
 }
 
-struct BwdSmem {
-  static constexpr int A = 0;                         // [2 stages][hi, lo] 128 x 32 = 16 KB each (64 KB)
-  static constexpr int B = A + 2 * 2 * TM * KC * 4;   // [2 stages][hi, lo] 64 x 32 = 8 KB each (32 KB)
-  static constexpr int W0 = B + 2 * 2 * H * KC * 4;   // layer 0 weights (in, out) <= 16 x 64
-  static constexpr int BARS = W0 + 16 * H * 4;
-  static constexpr int TOTAL = BARS + 128;
+struct FwdSmem {
+  static constexpr int A_HI = 0;       // 128 x 64 fp32, 32 KB
+  static constexpr int A_LO = 32768;   // 32 KB
+  static constexpr int B = 65536;      // 32 KB: one 64 x 64 hidden image, or two 32-row chunk images
+  static constexpr int OUT = 98304;    // 16 KB output staging; warp w owns rows 32w.. (4 KB)
+  static constexpr int BARS = 114688;
+  static constexpr int TOTAL = BARS + 256;
+  // barrier indices
+  static constexpr int TL = 0, A = 1, ACC = 2, BST = 3, FULL = 5, FREE = 9, NBARS = 13;
 };
 
 template <int NB>
-__global__ void __launch_bounds__(128, 2) k_mlp_bwd_tc(MlpParams p) {
-  extern __shared__ unsigned char smem_raw[];
-  unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + BwdSmem::BARS);
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + BwdSmem::BARS + 64);
-  float* sW0 = reinterpret_cast<float*>(sm + BwdSmem::W0);
-  const int t = threadIdx.x, warp = t >> 5;
-  const int64_t e = (int64_t)blockIdx.x * TM + t;
-  const bool valid = e < p.E;
+__global__ void __launch_bounds__(NTHR, 2) k_mlp_fwd_tc(MlpParams p) {
+  extern __shared__ __align__(1024) unsigned char sm[];
+  using S = FwdSmem;
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  if ((tc::smem_u32(sm) & 1023u) != 0) {
+    if (t == 0) atomicExch(p.err_flag, MLP_TC_ALIGN);
+    return;
+  }
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::BARS);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + S::BARS + 128);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + S::BARS + 136);
+  auto BAR = [&](int i) { return tc::smem_u32(&bars[i]); };
   const int nh = p.n_layers - 1;
   const int wout = p.widths[p.n_layers];
-  const uint32_t bar_b[2] = {tc::smem_u32(&bars[0]), tc::smem_u32(&bars[1])};
-  const uint32_t bar_m[2] = {tc::smem_u32(&bars[2]), tc::smem_u32(&bars[3])};
-  const uint32_t bar_tb = tc::smem_u32(&bars[4]), bar_tm = tc::smem_u32(&bars[5]);
-  if (warp == 0) {
-    tc::tmem_alloc(tc::smem_u32(tslot), H);
+  const int nch = wt_nchunk(wout);
+  const uint32_t a_hi = tc::smem_u32(sm + S::A_HI), a_lo = tc::smem_u32(sm + S::A_LO);
+  const uint32_t b_base = tc::smem_u32(sm + S::B);
+
+  if (warp == NEPI) {
+    tc::tmem_alloc(tc::smem_u32(tslot), TMEM_COLS);
     tc::tmem_relinquish();
   }
   if (t == 0) {
-    for (int i = 0; i < 2; ++i) {
-      tc::mbar_init(bar_b[i], 1);
-      tc::mbar_init(bar_m[i], 1);
+    for (int i = 0; i < S::NBARS; ++i) {
+      const bool by_warps = (i == S::A) || (i >= S::FREE && i < S::FREE + NBUF);
+      tc::mbar_init(BAR(i), by_warps ? NEPI : 1);
     }
-    tc::mbar_init(bar_tb, 1);
-    tc::mbar_init(bar_tm, 1);
+    *abort_flag = 0;
     tc::fence_barrier_init();
   }
-  for (int q = t; q < NB * H; q += TM) sW0[q] = __ldg(p.w[0] + q);  // (in = NB, out = 64)
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = *tslot;
-  constexpr uint32_t IDESC = tc::idesc_tf32(TM, H);
-  const int nchunk = (wout + KC - 1) / KC;
-  const float* row = p.dout + e * (int64_t)wout;
-  auto load_chunk = [&](int kc, float4* r) {
-#pragma unroll
-    for (int q = 0; q < KC / 4; ++q) {
-      const int c = kc * KC + 4 * q;
-      r[q] = (valid && c < wout) ? __ldg(reinterpret_cast<const float4*>(row + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-  };
-  float4 cur[KC / 4], nxt[KC / 4];
-  load_chunk(0, cur);
   bool ok = true;
-  for (int kc = 0; kc < nchunk; ++kc) {
-    const int s = kc & 1;
-    unsigned char* a_hi_p = sm + BwdSmem::A + (s * 2 + 0) * TM * KC * 4;
-    unsigned char* a_lo_p = sm + BwdSmem::A + (s * 2 + 1) * TM * KC * 4;
-    const uint32_t b_hi = tc::smem_u32(sm + BwdSmem::B + (s * 2 + 0) * H * KC * 4);
-    const uint32_t b_lo = b_hi + H * KC * 4;
-    if (kc >= 2) ok = tc::mbar_wait(bar_m[s], ((kc - 2) >> 1) & 1) && ok;  // stage s free again
-    if (t == 0 && ok) {
-      tc::mbar_expect_tx(bar_b[s], 2 * H * KC * 4);
-      tc::bulk_g2s(b_hi, p.tc_img_bwd + (int64_t)kc * 2 * H * KC, 2 * H * KC * 4, bar_b[s]);
-    }
-#pragma unroll
-    for (int q = 0; q < KC / 4; ++q) {
-      const float4 v = cur[q];
-      float4 hi, lo;
-      hi.x = tc::tf32_hi(v.x);
-      hi.y = tc::tf32_hi(v.y);
-      hi.z = tc::tf32_hi(v.z);
-      hi.w = tc::tf32_hi(v.w);
-      lo.x = v.x - hi.x;
-      lo.y = v.y - hi.y;
-      lo.z = v.z - hi.z;
-      lo.w = v.w - hi.w;
-      const uint32_t off = tc::sw128_offset(t, 4 * q, TM);
-      *reinterpret_cast<float4*>(a_hi_p + off) = hi;
-      *reinterpret_cast<float4*>(a_lo_p + off) = lo;
-    }
-    if (kc + 1 < nchunk) load_chunk(kc + 1, nxt);
-    tc::fence_proxy_async();
-    ok = __syncthreads_and(ok);
-    if (!ok) break;
-    if (t == 0) {
-      ok = tc::mbar_wait(bar_b[s], (kc >> 1) & 1);
-      if (ok) {
+
+  if (warp == NEPI) {
+    // ---------------- control warp: copies and MMAs from lane 0 ----------------
+    if (lane == 0) {
+      auto wait = [&](int i, uint32_t par) {
+        ok = ok && tc::mbar_wait_or_abort(BAR(i), par, abort_flag);
+        return ok;
+      };
+      auto copy_trunk = [&](int j) {
+        tc::mbar_expect_tx(BAR(S::TL), IMG * 4);
+        tc::bulk_g2s(b_base, p.tc_trunk + (int64_t)j * IMG, IMG * 4, BAR(S::TL));
+      };
+      auto copy_chunk = [&](int c) {
+        const int s = c & 1;
+        tc::mbar_expect_tx(BAR(S::BST + s), CIMG * 4);
+        tc::bulk_g2s(b_base + s * CIMG * 4, p.tc_img + (int64_t)c * CIMG, CIMG * 4, BAR(S::BST + s));
+      };
+      uint32_t pa = 0;
+      if (nh >= 2) copy_trunk(0);
+      for (int j = 1; j < nh; ++j) {  // hidden layer j reads A = SiLU(layer j-1)
+        if (!wait(S::TL, (j - 1) & 1) || !wait(S::A, pa)) break;
+        pa ^= 1;
         tc::fence_after_sync();
-        const uint32_t a_hi = tc::smem_u32(a_hi_p), a_lo = tc::smem_u32(a_lo_p);
-#pragma unroll
-        for (int kb = 0; kb < KC / 8; ++kb) {
-          const uint32_t off = kb * 32;
-          tc::mma_tf32(tmem, tc::sw128_desc(a_hi + off), tc::sw128_desc(b_hi + off), IDESC, (kc > 0 || kb > 0));
-          tc::mma_tf32(tmem, tc::sw128_desc(a_hi + off), tc::sw128_desc(b_lo + off), IDESC, 1);
-          tc::mma_tf32(tmem, tc::sw128_desc(a_lo + off), tc::sw128_desc(b_hi + off), IDESC, 1);
+        mma_k64<H>(tmem, a_hi, a_lo, b_base, b_base + IMG * 2);
+        tc::mma_commit(BAR(S::ACC));
+        if (!wait(S::ACC, (j - 1) & 1)) break;  // B is free again
+        if (j + 1 < nh) copy_trunk(j);
+      }
+      if (ok) {
+        copy_chunk(0);
+        if (nch > 1) copy_chunk(1);
+      }
+      if (ok && wait(S::A, pa)) {  // A = SiLU(last hidden layer)
+        for (int c = 0; c < nch; ++c) {
+          const int s = c & 1, buf = c % NBUF;
+          if (!wait(S::BST + s, (c >> 1) & 1)) break;
+          if (c >= NBUF && !wait(S::FREE + buf, ((c / NBUF) - 1) & 1)) break;
+          tc::fence_after_sync();
+          const uint32_t bs = b_base + s * CIMG * 4;
+          mma_k64<TC32>(tmem + buf * TC32, a_hi, a_lo, bs, bs + CIMG * 2);
+          tc::mma_commit(BAR(S::FULL + buf));
+          if (c >= 1 && c + 1 < nch) {  // stage (c+1)&1 is free once MMA(c-1) is done
+            if (!wait(S::FULL + (c - 1) % NBUF, ((c - 1) / NBUF) & 1)) break;
+            copy_chunk(c + 1);
+          }
         }
-        tc::mma_commit(bar_m[s]);
       }
     }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue warps: thread t owns edge t of the tile ----------------
+    const int64_t e = (int64_t)blockIdx.x * TM + t;
+    const bool valid = e < p.E;
+    auto wwait = [&](int i, uint32_t par) {
+      const bool r = ok && tc::mbar_wait_or_abort(BAR(i), par, abort_flag);
+      ok = __all_sync(0xffffffffu, r);
+      return ok;
+    };
+    unsigned char* a_hi_p = sm + S::A_HI;
+    unsigned char* a_lo_p = sm + S::A_LO;
+    float y[H];
+    layer0<NB>(p, e, valid, y);
+    uint32_t pacc = 0;
+    for (int j = 0; j < nh; ++j) {
+      if (valid) {
+        float4* act = reinterpret_cast<float4*>(p.act + e * (int64_t)(nh * H) + j * H);
 #pragma unroll
-    for (int q = 0; q < KC / 4; ++q) cur[q] = nxt[q];
-  }
-  float dh[H];
-  if (ok) {
-    const int last = nchunk - 1;
-    ok = tc::mbar_wait(bar_m[last & 1], (last >> 1) & 1);
-    ok = __syncthreads_and(ok);
-  }
-  if (ok) {
-    tc::fence_after_sync();
-    tmem_row64(tmem, warp, 0, dh);
-  }
-  // ---- hidden layers nh-1 .. 1 on the tensor cores ----
-  unsigned char* a_hi_p = sm + BwdSmem::A;               // 128 x 64 hi (32 KB)
-  unsigned char* a_lo_p = sm + BwdSmem::A + TM * H * 4;  // 128 x 64 lo (32 KB)
-  const uint32_t b_hi = tc::smem_u32(sm + BwdSmem::B), b_lo = b_hi + IMG * 2;
-  uint32_t ptb = 0, ptm = 0;
-  for (int j = nh - 1; j >= 1 && ok; --j) {
-    if (t == 0) {
-      tc::mbar_expect_tx(bar_tb, IMG * 4);
-      tc::bulk_g2s(b_hi, p.tc_trunk_bwd + (int64_t)(j - 1) * IMG, IMG * 4, bar_tb);
-    }
-    const float4* a4 = reinterpret_cast<const float4*>(p.act + e * (int64_t)(nh * H) + j * H);
+        for (int q = 0; q < H / 4; ++q) act[q] = make_float4(y[4 * q], y[4 * q + 1], y[4 * q + 2], y[4 * q + 3]);
+      }
 #pragma unroll
-    for (int q = 0; q < H / 4; ++q) {
-      float4 a = valid ? a4[q] : make_float4(0.f, 0.f, 0.f, 0.f);
-      float4 d = make_float4(dh[4 * q] * silu_grad_f(a.x), dh[4 * q + 1] * silu_grad_f(a.y),
-                             dh[4 * q + 2] * silu_grad_f(a.z), dh[4 * q + 3] * silu_grad_f(a.w));
-      if (!valid) d = make_float4(0.f, 0.f, 0.f, 0.f);
-      put_hilo(a_hi_p, a_lo_p, t, 4 * q, d);
-    }
-    tc::fence_proxy_async();
-    tc::fence_before_sync();
-    __syncthreads();
-    if (t == 0) {
-      ok = tc::mbar_wait(bar_tb, ptb);
-      if (ok) {
+      for (int q = 0; q < H / 4; ++q) {
+        const float4 h = valid ? make_float4(silu_f(y[4 * q]), silu_f(y[4 * q + 1]), silu_f(y[4 * q + 2]),
+                                             silu_f(y[4 * q + 3]))
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+        put_hilo(a_hi_p, a_lo_p, t, 4 * q, h);
+      }
+      tc::fence_proxy_async();
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(BAR(S::A));
+      if (j + 1 < nh) {
+        if (!wwait(S::ACC, pacc)) break;
+        pacc ^= 1;
         tc::fence_after_sync();
-        mma_k64<H>(tmem, tc::smem_u32(a_hi_p), tc::smem_u32(a_lo_p), b_hi, b_lo);
-        tc::mma_commit(bar_tm);
+        tmem_row64(tmem, warp, 0, y);
       }
     }
-    ptb ^= 1;
-    ok = tc::mbar_wait(bar_tm, ptm) && ok;
-    ptm ^= 1;
-    ok = __syncthreads_and(ok);
-    if (!ok) break;
-    tc::fence_after_sync();
-    tmem_row64(tmem, warp, 0, dh);
-    tc::fence_before_sync();
-    __syncthreads();
+    unsigned char* stg = sm + S::OUT + warp * 4096;
+    const uint32_t stg_u = tc::smem_u32(stg);
+    float* dst = p.out + (int64_t)blockIdx.x * nch * WT_CHUNK + warp * 32 * 32;
+    for (int c = 0; c < nch && ok; ++c) {
+      const int buf = c % NBUF;
+      if (!wwait(S::FULL + buf, (c / NBUF) & 1)) break;
+      tc::fence_after_sync();
+      float v[32];
+      tc::tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + buf * TC32, v);
+      tc::tmem_wait_ld();
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) {
+        tc::mbar_arrive(BAR(S::FREE + buf));
+        tc::bulk_wait_read_all();  // the staging slice is free again
+      }
+      __syncwarp();
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        *reinterpret_cast<float4*>(stg + lane * 128 + ((q ^ (lane & 7)) << 4)) =
+            make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+      tc::fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) {
+        tc::bulk_s2g(dst + (int64_t)c * WT_CHUNK, stg_u, 4096);
+        tc::bulk_commit();
+      }
+    }
+    if (lane == 0) tc::bulk_wait_all();
+    __syncwarp();
   }
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == 0) tc::tmem_dealloc(tmem, H);
-  if (!ok) {
-    if (t == 0) atomicExch(p.err_flag, MLP_TC_TIMEOUT);
+  if (!ok) atomicExch(p.err_flag, MLP_TC_TIMEOUT);
+  if (warp == NEPI) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+struct BwdSmem {
+  // stage s at s * STAGE: dW chunk hi (16 KB, written by the bulk copy and
+  // rounded in place), dW chunk lo (16 KB), weight chunk image (16 KB).
+  // After the K loop: trunk A hi [0, 32K), A lo [32K, 64K), B [64K, 96K).
+  static constexpr int STAGE = 49152;
+  static constexpr int BARS = 2 * STAGE;
+  static constexpr int TOTAL = BARS + 256;
+  static constexpr int LD = 0, SPLIT = 2, MMA = 4, TL = 6, A = 7, ACC = 8, NBARS = 9;
+};
+
+template <int NB>
+__global__ void __launch_bounds__(NTHR, 2) k_mlp_bwd_tc(MlpParams p) {
+  extern __shared__ __align__(1024) unsigned char sm[];
+  using S = BwdSmem;
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  if ((tc::smem_u32(sm) & 1023u) != 0) {
+    if (t == 0) atomicExch(p.err_flag, MLP_TC_ALIGN);
     return;
   }
-  // ---- layer 0 on the CUDA cores: dL/db[i] = sum_o dh[o] SiLU'(a0[o]) W0[i][o] ----
-  if (!valid) return;
-  float da[H];
-  const float4* a4 = reinterpret_cast<const float4*>(p.act + e * (int64_t)(nh * H));
-#pragma unroll
-  for (int q = 0; q < H / 4; ++q) {
-    const float4 a = a4[q];
-    da[4 * q + 0] = dh[4 * q + 0] * silu_grad_f(a.x);
-    da[4 * q + 1] = dh[4 * q + 1] * silu_grad_f(a.y);
-    da[4 * q + 2] = dh[4 * q + 2] * silu_grad_f(a.z);
-    da[4 * q + 3] = dh[4 * q + 3] * silu_grad_f(a.w);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::BARS);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + S::BARS + 128);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + S::BARS + 136);
+  auto BAR = [&](int i) { return tc::smem_u32(&bars[i]); };
+  const int nh = p.n_layers - 1;
+  const int wout = p.widths[p.n_layers];
+  const int nch = wt_nchunk(wout);
+  const int last = nch - 1;
+  const uint32_t base = tc::smem_u32(sm);
+
+  if (warp == NEPI) {
+    tc::tmem_alloc(tc::smem_u32(tslot), H);
+    tc::tmem_relinquish();
   }
-#pragma unroll
-  for (int i = 0; i < NB; ++i) {
-    const float4* w4 = reinterpret_cast<const float4*>(sW0 + i * H);
-    float acc = 0.f;
-#pragma unroll
-    for (int q = 0; q < H / 4; ++q) {
-      const float4 w = w4[q];
-      acc = fmaf(da[4 * q + 0], w.x, acc);
-      acc = fmaf(da[4 * q + 1], w.y, acc);
-      acc = fmaf(da[4 * q + 2], w.z, acc);
-      acc = fmaf(da[4 * q + 3], w.w, acc);
+  if (t == 0) {
+    for (int i = 0; i < S::NBARS; ++i) {
+      const bool by_warps = (i == S::SPLIT) || (i == S::SPLIT + 1) || (i == S::A);
+      tc::mbar_init(BAR(i), by_warps ? NEPI : 1);
     }
-    p.db[e * NB + i] += acc;
+    *abort_flag = 0;
+    tc::fence_barrier_init();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tslot;
+  bool ok = true;
+
+  if (warp == NEPI) {
+    if (lane == 0) {
+      auto wait = [&](int i, uint32_t par) {
+        ok = ok && tc::mbar_wait_or_abort(BAR(i), par, abort_flag);
+        return ok;
+      };
+      const float* dw_tile = p.dout + (int64_t)blockIdx.x * nch * WT_CHUNK;
+      auto copy_chunk = [&](int k) {
+        const int s = k & 1;
+        const uint32_t st = base + s * S::STAGE;
+        tc::mbar_expect_tx(BAR(S::LD + s), (WT_CHUNK + BIMG) * 4);
+        tc::bulk_g2s(st, dw_tile + (int64_t)k * WT_CHUNK, WT_CHUNK * 4, BAR(S::LD + s));
+        tc::bulk_g2s(st + 32768, p.tc_img_bwd + (int64_t)k * BIMG, BIMG * 4, BAR(S::LD + s));
+      };
+      constexpr uint32_t IDESC = tc::idesc_tf32(TM, H);
+      copy_chunk(0);
+      if (nch > 1) copy_chunk(1);
+      for (int kc = 0; kc < nch; ++kc) {
+        const int s = kc & 1;
+        if (!wait(S::SPLIT + s, (kc >> 1) & 1)) break;
+        tc::fence_after_sync();
+        const uint32_t ah = base + s * S::STAGE, al = ah + 16384, bh = ah + 32768, bl = bh + 8192;
+#pragma unroll
+        for (int kb = 0; kb < KC / 8; ++kb) {
+          const uint32_t off = kb * 32;
+          tc::mma_tf32(tmem, tc::sw128_desc(ah + off), tc::sw128_desc(bh + off), IDESC, (kc > 0 || kb > 0));
+          tc::mma_tf32(tmem, tc::sw128_desc(ah + off), tc::sw128_desc(bl + off), IDESC, 1);
+          tc::mma_tf32(tmem, tc::sw128_desc(al + off), tc::sw128_desc(bh + off), IDESC, 1);
+        }
+        tc::mma_commit(BAR(S::MMA + s));
+        if (kc + 2 < nch) {  // stage s is free once MMA(kc) is done
+          if (!wait(S::MMA + s, (kc >> 1) & 1)) break;
+          copy_chunk(kc + 2);
+        }
+      }
+      // every K-chunk MMA done before the trunk reuses the stages
+      wait(S::MMA + (last & 1), (last >> 1) & 1);
+      uint32_t pa = 0, pacc = 0, ptl = 0;
+      const uint32_t a_hi = base, a_lo = base + 32768, b_hi = base + 65536, b_lo = b_hi + 16384;
+      for (int j = nh - 1; j >= 1 && ok; --j) {
+        tc::mbar_expect_tx(BAR(S::TL), IMG * 4);
+        tc::bulk_g2s(b_hi, p.tc_trunk_bwd + (int64_t)(j - 1) * IMG, IMG * 4, BAR(S::TL));
+        if (!wait(S::A, pa) || !wait(S::TL, ptl)) break;
+        pa ^= 1;
+        ptl ^= 1;
+        tc::fence_after_sync();
+        mma_k64<H>(tmem, a_hi, a_lo, b_hi, b_lo);
+        tc::mma_commit(BAR(S::ACC));
+        if (!wait(S::ACC, pacc)) break;  // B is free again
+        pacc ^= 1;
+      }
+    }
+    __syncwarp();
+  } else {
+    const int64_t e = (int64_t)blockIdx.x * TM + t;
+    const bool valid = e < p.E;
+    auto wwait = [&](int i, uint32_t par) {
+      const bool r = ok && tc::mbar_wait_or_abort(BAR(i), par, abort_flag);
+      ok = __all_sync(0xffffffffu, r);
+      return ok;
+    };
+    // split each dW chunk into tf32 hi (in place) and lo
+    for (int kc = 0; kc < nch; ++kc) {
+      const int s = kc & 1;
+      if (!wwait(S::LD + s, (kc >> 1) & 1)) break;
+      unsigned char* ah = sm + s * S::STAGE;
+      unsigned char* al = ah + 16384;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const uint32_t off = t * 128 + ((q ^ (t & 7)) << 4);
+        const float4 v = *reinterpret_cast<const float4*>(ah + off);
+        float4 hi, lo;
+        hi.x = tc::tf32_hi(v.x);
+        hi.y = tc::tf32_hi(v.y);
+        hi.z = tc::tf32_hi(v.z);
+        hi.w = tc::tf32_hi(v.w);
+        lo.x = v.x - hi.x;
+        lo.y = v.y - hi.y;
+        lo.z = v.z - hi.z;
+        lo.w = v.w - hi.w;
+        *reinterpret_cast<float4*>(ah + off) = hi;
+        *reinterpret_cast<float4*>(al + off) = lo;
+      }
+      tc::fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(BAR(S::SPLIT + s));
+    }
+    float dh[H];
+    if (wwait(S::MMA + (last & 1), (last >> 1) & 1)) {
+      tc::fence_after_sync();
+      tmem_row64(tmem, warp, 0, dh);
+    }
+    // hidden layers nh-1 .. 1 on the tensor cores
+    unsigned char* a_hi_p = sm;
+    unsigned char* a_lo_p = sm + 32768;
+    uint32_t pacc = 0;
+    for (int j = nh - 1; j >= 1 && ok; --j) {
+      const float4* a4 = reinterpret_cast<const float4*>(p.act + e * (int64_t)(nh * H) + j * H);
+#pragma unroll
+      for (int q = 0; q < H / 4; ++q) {
+        float4 d = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (valid) {
+          const float4 a = a4[q];
+          d = make_float4(dh[4 * q] * silu_grad_f(a.x), dh[4 * q + 1] * silu_grad_f(a.y),
+                          dh[4 * q + 2] * silu_grad_f(a.z), dh[4 * q + 3] * silu_grad_f(a.w));
+        }
+        put_hilo(a_hi_p, a_lo_p, t, 4 * q, d);
+      }
+      tc::fence_proxy_async();
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(BAR(S::A));
+      if (!wwait(S::ACC, pacc)) break;
+      pacc ^= 1;
+      tc::fence_after_sync();
+      tmem_row64(tmem, warp, 0, dh);
+    }
+    // layer 0 on the CUDA cores: dL/db[i] = sum_o dh[o] SiLU'(a0[o]) W0[i][o]
+    if (ok && valid) {
+      float da[H];
+      const float4* a4 = reinterpret_cast<const float4*>(p.act + e * (int64_t)(nh * H));
+#pragma unroll
+      for (int q = 0; q < H / 4; ++q) {
+        const float4 a = a4[q];
+        da[4 * q + 0] = dh[4 * q + 0] * silu_grad_f(a.x);
+        da[4 * q + 1] = dh[4 * q + 1] * silu_grad_f(a.y);
+        da[4 * q + 2] = dh[4 * q + 2] * silu_grad_f(a.z);
+        da[4 * q + 3] = dh[4 * q + 3] * silu_grad_f(a.w);
+      }
+#pragma unroll
+      for (int i = 0; i < NB; ++i) {
+        const float4* w4 = reinterpret_cast<const float4*>(p.w[0] + i * H);
+        float acc = 0.f;
+#pragma unroll
+        for (int q = 0; q < H / 4; ++q) {
+          const float4 w = __ldg(w4 + q);
+          acc = fmaf(da[4 * q + 0], w.x, acc);
+          acc = fmaf(da[4 * q + 1], w.y, acc);
+          acc = fmaf(da[4 * q + 2], w.z, acc);
+          acc = fmaf(da[4 * q + 3], w.w, acc);
+        }
+        p.db[e * NB + i] += acc;
+      }
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (!ok) atomicExch(p.err_flag, MLP_TC_TIMEOUT);
+  if (warp == NEPI) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, H);
   }
 }
 
 template <int NB>
 int launch_fwd_nb(const MlpParams& p, cudaStream_t s) {
-  const size_t smem = FwdSmem::TOTAL + 1024;
+  const size_t smem = FwdSmem::TOTAL;
   MACE_CUDA_TRY(cudaFuncSetAttribute(k_mlp_fwd_tc<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  k_mlp_fwd_tc<NB><<<(unsigned)((p.E + TM - 1) / TM), TM, smem, s>>>(p);
+  k_mlp_fwd_tc<NB><<<(unsigned)((p.E + TM - 1) / TM), NTHR, smem, s>>>(p);
   MACE_LAUNCH_CHECK("mlp_fwd_tc");
   return MACE_OK;
 }
 
 template <int NB>
 int launch_bwd_nb(const MlpParams& p, cudaStream_t s) {
-  const size_t smem = BwdSmem::TOTAL + 1024;
+  const size_t smem = BwdSmem::TOTAL;
   MACE_CUDA_TRY(cudaFuncSetAttribute(k_mlp_bwd_tc<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  k_mlp_bwd_tc<NB><<<(unsigned)((p.E + TM - 1) / TM), TM, smem, s>>>(p);
+  k_mlp_bwd_tc<NB><<<(unsigned)((p.E + TM - 1) / TM), NTHR, smem, s>>>(p);
   MACE_LAUNCH_CHECK("mlp_bwd_tc");
   return MACE_OK;
 }

@@ -48,7 +48,7 @@ struct DeviceGuard {
 
 struct LayerBufs {
   float* up = nullptr;    // (N, in_dim)
-  float* w = nullptr;     // (E, wnumel)
+  float* w = nullptr;     // (E, wnumel) in 128-edge tiles
   float* act = nullptr;   // (E, nh*H)
   float* A = nullptr;     // (N, mid_dim)
   float* msg = nullptr;   // (N, 16C)
@@ -207,7 +207,11 @@ int reserve(mace_ctx* c, int64_t N, int64_t E) {
   TRY(alloc(c, &c->dY, E * 16));
   TRY(alloc(c, &c->db, E * d.num_bessel));
   TRY(alloc(c, &c->dv, E * 3));
-  TRY(alloc(c, &c->dw, E * wmax));
+  TRY(alloc(c, &c->dw, wt_floats(E, wmax)));
+  // padding rows of the last edge tile are read (never used) by the MLP backward
+  if (cudaMemset(c->dw, 0, (size_t)wt_floats(E, wmax) * sizeof(float)) != cudaSuccess ||
+      cudaDeviceSynchronize() != cudaSuccess)
+    return fail(MACE_ERR_CUDA, "workspace memset");
   TRY(alloc(c, &c->vir_part, ((E + 255) / 256 + 1) * 9));
   c->h.assign(T + 1, nullptr);
   c->dh.assign(T + 1, nullptr);
@@ -224,7 +228,7 @@ int reserve(mace_ctx* c, int64_t N, int64_t E) {
     LayerBufs& B = c->lb[t];
     int nh = L.n_mlp - 1, H = L.mlp_w[1];
     TRY(alloc(c, &B.up, N * L.in.dim));
-    TRY(alloc(c, &B.w, E * L.wnumel));
+    TRY(alloc(c, &B.w, wt_floats(E, L.wnumel)));
     TRY(alloc(c, &B.act, E * nh * H));
     TRY(alloc(c, &B.A, N * L.mid.dim));
     TRY(alloc(c, &B.msg, N * L.inter.dim));
@@ -295,6 +299,7 @@ ConvParams conv_params(mace_ctx* c, int t, int64_t N, const mace_system* sys) {
   p.n_mid = L.n_mid;
   p.m_tot = L.m_tot;
   p.wnumel = L.wnumel;
+  p.wnch = wt_nchunk(L.wnumel);
   p.in_dim = L.in.dim;
   p.in_ch = L.in.dim / L.C;
   p.mid_dim = L.mid.dim;
@@ -826,7 +831,7 @@ int mace_debug_buffer(mace_ctx* c, int32_t id, const float** ptr, int64_t* len) 
   const LayerBufs& B = c->lb[layer];
   switch (stage) {
     case 0: *ptr = B.up; *len = N * L.in.dim; break;
-    case 1: *ptr = B.w; *len = E * L.wnumel; break;
+    case 1: *ptr = B.w; *len = wt_floats(E, L.wnumel); break;
     case 2: *ptr = B.A; *len = N * L.mid.dim; break;
     case 3: *ptr = B.msg; *len = N * L.inter.dim; break;
     case 4: *ptr = B.B; *len = N * L.hid.dim; break;

@@ -109,6 +109,49 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t phase) {
   }
 }
 
+// As mbar_wait, for kernels whose warps wait on one another: a wait that gives
+// up raises the CTA-wide `abort` flag, and every later wait that sees the flag
+// returns false at once, so the whole CTA leaves its pipeline within one
+// timeout.
+__device__ __forceinline__ bool mbar_wait_or_abort(uint32_t bar, uint32_t phase, volatile int* abort) {
+  const uint64_t t0 = globaltimer();
+  for (uint32_t it = 0;; ++it) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(phase)
+        : "memory");
+    if (ok) return true;
+    if ((it & 63u) == 63u) {
+      if (*abort) return false;
+      if (globaltimer() - t0 > 2000000000ull) {
+        *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+// 1-D bulk store shared -> global, tracked per issuing thread by bulk groups
+__device__ __forceinline__ void bulk_s2g(void* dst, uint32_t src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// the source shared memory of every committed bulk store may be reused
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// every committed bulk store is complete
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 __device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
                : "memory");

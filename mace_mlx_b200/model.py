@@ -212,7 +212,11 @@ class MACEModel:
         return c.value
 
     def debug_buffer(self, stage: str, layer: int | None = None) -> torch.Tensor:
-        """Copy of an internal per-stage buffer of the last evaluation (parity tests)."""
+        """Copy of an internal per-stage buffer of the last evaluation (parity tests).
+
+        The radial weights (stage "w") come back in the kernels' 128-edge tile
+        layout; ``edge_tiles_to_rows`` turns them into an (E, W) matrix.
+        """
         bid = 15 * 16 + nv.EDGE_STAGES[stage] if layer is None else layer * 16 + nv.STAGES[stage]
         ptr, n = C.c_void_p(), C.c_int64()
         nv.check(self.lib.mace_debug_buffer(self.ctx, bid, C.byref(ptr), C.byref(n)), self.lib)
@@ -220,3 +224,21 @@ class MACEModel:
             return torch.empty(0, device=self.device)
         torch.cuda.synchronize(self.device)
         return torch.as_tensor(_CudaArray(ptr.value, n.value), device=self.device).clone()
+
+
+def edge_tiles_to_rows(buf: torch.Tensor, n_edges: int, width: int) -> torch.Tensor:
+    """(E, W) view of a per-edge matrix stored in 128-edge tiles.
+
+    Tile e // 128 holds ceil(W / 32) chunks of 128 rows x 32 floats; column c
+    of edge e is in chunk c // 32, row e % 128, at 16-byte group
+    ((c % 32) // 4) ^ (e % 8), position c % 4 (the 128B-swizzled operand
+    layout of the tensor-core MLP kernels).
+    """
+    nch = -(-width // 32)
+    nt = -(-n_edges // 128)
+    x = buf[: nt * nch * 4096].reshape(nt, nch, 128, 8, 4)
+    rows = torch.arange(128, device=buf.device)
+    groups = torch.arange(8, device=buf.device)
+    src = groups[None, :] ^ (rows[:, None] & 7)
+    x = x[:, :, rows[:, None], src, :]
+    return x.permute(0, 2, 1, 3, 4).reshape(nt * 128, nch * 32)[:n_edges, :width]

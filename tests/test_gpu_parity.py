@@ -9,7 +9,7 @@ import pytest
 import torch
 
 from helpers import assert_parity, irreps_to_channel_last, make_case, rel_err, run_gpu
-from mace_mlx_b200.model import MACEModel
+from mace_mlx_b200.model import MACEModel, edge_tiles_to_rows
 from mace_mlx_b200.spec import ModelSpec
 from mace_mlx_b200.structures import diamond_si, lipso_box, molecule_batch
 from mace_mlx_b200.weights import random_config, random_weights
@@ -98,7 +98,10 @@ def test_per_stage_buffers_medium():
             ref = ref.numpy()
             if irreps is not None:
                 ref = irreps_to_channel_last(ref, irreps)
-            got = m.debug_buffer(stage, t).cpu().numpy().reshape(rows, -1)
+            got = m.debug_buffer(stage, t)
+            if stage == "w":
+                got = edge_tiles_to_rows(got, E, ref.shape[1])
+            got = got.cpu().numpy().reshape(rows, -1)
             assert rel_err(got, ref) < 2e-5, (t, stage, rel_err(got, ref))
 
         cmp("up", f"up{t}", lay.irreps_in)
@@ -166,11 +169,12 @@ def test_tensor_core_mlp_matches_cuda_core_mlp(monkeypatch):
     m_tc = MACEModel(config=config, weights=weights, device=0)
     monkeypatch.setenv("MACE_B200_MLP_CUDA_CORES", "1")
     m_cc = MACEModel(config=config, weights=weights, device=0)
-    a, _, _ = run_gpu(m_tc, st)
+    a, edges, _ = run_gpu(m_tc, st)
     b, _, _ = run_gpu(m_cc, st)
     for t in range(2):
-        wa = m_tc.debug_buffer("w", t).cpu().numpy()
-        wb = m_cc.debug_buffer("w", t).cpu().numpy()
+        E, W = edges.n_edges, m_tc.spec.layers[t].mlp_widths[-1]
+        wa = edge_tiles_to_rows(m_tc.debug_buffer("w", t), E, W).cpu().numpy()
+        wb = edge_tiles_to_rows(m_cc.debug_buffer("w", t), E, W).cpu().numpy()
         assert rel_err(wa, wb) < 1e-5, rel_err(wa, wb)  # both fp32-accurate: ~2^-21 per product
     assert rel_err(a["forces"], b["forces"]) < 2e-5
     assert abs(a["energy"][0] - b["energy"][0]) < 1e-5 * max(1.0, abs(b["energy"][0]))

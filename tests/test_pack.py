@@ -75,10 +75,29 @@ def test_tf32_split_and_swizzled_images_round_trip():
     assert len(set(off.ravel().tolist())) == a.size
     w = rng.normal(size=(200, 64)).astype(np.float32)  # (out, in) with out not a multiple of 128
     fwd, bwd = mlp_tc_images(w)
-    assert fwd.size == 4 * 2 * 64 * 64 and bwd.size == 7 * 2 * 64 * 32
-    # forward chunk 3 (outputs 192..255), hi part, row 7 (output 199) holds w[199] up to tf32 rounding
-    ch = fwd[3 * 2 * 64 * 64: 3 * 2 * 64 * 64 + 64 * 64]
+    assert fwd.size == 7 * 2 * 32 * 64 and bwd.size == 7 * 2 * 64 * 32
+    # forward chunk 6 (outputs 192..223), hi part, row 7 (output 199) holds w[199] up to tf32 rounding
+    ch = fwd[6 * 2 * 32 * 64: 6 * 2 * 32 * 64 + 32 * 64]
     rr = 7
     kk = np.arange(64)
-    got = ch[(kk // 32) * 64 * 32 + rr * 32 + (((kk % 32) // 4) ^ (rr % 8)) * 4 + (kk % 4)]
+    got = ch[(kk // 32) * 32 * 32 + rr * 32 + (((kk % 32) // 4) ^ (rr % 8)) * 4 + (kk % 4)]
     np.testing.assert_allclose(got, w[199], rtol=2.0 ** -11)
+
+
+def test_edge_tile_layout_round_trip():
+    """edge_tiles_to_rows inverts the kernels' 128-edge tile index (common.cuh wt_index)."""
+    import torch
+
+    from mace_mlx_b200.model import edge_tiles_to_rows
+
+    E, W = 300, 80
+    nch, nt = -(-W // 32), -(-E // 128)
+    buf = np.full(nt * nch * 4096, np.nan, np.float32)
+    M = np.random.default_rng(0).normal(size=(E, W)).astype(np.float32)
+    e = np.arange(E)[:, None]
+    c = np.arange(W)[None, :]
+    idx = (((e >> 7) * nch + (c >> 5)) << 12) + ((e & 127) << 5) + ((((c >> 2) & 7) ^ (e & 7)) << 2) + (c & 3)
+    assert len(np.unique(idx)) == E * W
+    buf[idx.ravel()] = M.ravel()
+    got = edge_tiles_to_rows(torch.from_numpy(buf), E, W).numpy()
+    np.testing.assert_array_equal(got, M)
