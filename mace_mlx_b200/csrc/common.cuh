@@ -35,9 +35,11 @@ int fail(int code, const std::string& msg);
 
 __host__ __device__ __forceinline__ int64_t imin64(int64_t a, int64_t b) { return a < b ? a : b; }
 
-__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
+// SiLU with the hardware exponential and reciprocal (__expf, __fdividef):
+// a few ulp, about 1e-6 relative at worst for the MLP's pre-activations.
+__device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 __device__ __forceinline__ float silu_grad_f(float x) {
-  float s = 1.0f / (1.0f + expf(-x));
+  const float s = __fdividef(1.0f, 1.0f + __expf(-x));
   return s * (1.0f + x * (1.0f - s));
 }
 

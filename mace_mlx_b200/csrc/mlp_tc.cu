@@ -86,10 +86,17 @@ __device__ __forceinline__ void tmem_row64(uint32_t tmem, int warp, int col0, fl
   tc::tmem_wait_ld();
 }
 
-// layer 0 on the CUDA cores: y = b[e] . W0, W0 (NB, 64) read through L1 (one
-// address per warp instruction)
+// the (NB, 64) layer-0 weights into shared memory by the 128 epilogue threads
 template <int NB>
-__device__ __forceinline__ void layer0(const MlpParams& p, int64_t e, bool valid, float* y) {
+__device__ __forceinline__ void load_w0(const MlpParams& p, float* sW0, int t) {
+  for (int q = t; q < NB * H / 4; q += TM)
+    reinterpret_cast<float4*>(sW0)[q] = __ldg(reinterpret_cast<const float4*>(p.w[0]) + q);
+  tc::named_sync(1, TM);
+}
+
+// layer 0 on the CUDA cores: y = b[e] . W0 (shared-memory broadcast reads)
+template <int NB>
+__device__ __forceinline__ void layer0(const MlpParams& p, const float* sW0, int64_t e, bool valid, float* y) {
   float x[NB];
 #pragma unroll
   for (int i = 0; i < NB; ++i) x[i] = valid ? __ldg(p.b + e * NB + i) : 0.f;
@@ -97,10 +104,10 @@ __device__ __forceinline__ void layer0(const MlpParams& p, int64_t e, bool valid
   for (int o = 0; o < H; ++o) y[o] = 0.f;
 #pragma unroll
   for (int i = 0; i < NB; ++i) {
-    const float4* w4 = reinterpret_cast<const float4*>(p.w[0] + i * H);
+    const float4* w4 = reinterpret_cast<const float4*>(sW0 + i * H);
 #pragma unroll
     for (int q = 0; q < H / 4; ++q) {
-      const float4 w = __ldg(w4 + q);
+      const float4 w = w4[q];
       y[4 * q + 0] = fmaf(x[i], w.x, y[4 * q + 0]);
       y[4 * q + 1] = fmaf(x[i], w.y, y[4 * q + 1]);
       y[4 * q + 2] = fmaf(x[i], w.z, y[4 * q + 2]);
@@ -113,7 +120,8 @@ struct FwdSmem {
   static constexpr int A_HI = 0;       // 128 x 64 fp32, 32 KB
   static constexpr int A_LO = 32768;   // 32 KB
   static constexpr int B = 65536;      // 32 KB: one 64 x 64 hidden image, or two 32-row chunk images
-  static constexpr int OUT = 98304;    // 16 KB output staging; warp w owns rows 32w.. (4 KB)
+  static constexpr int OUT = 98304;    // 16 KB output staging; warp w owns rows 32w.. (4 KB);
+                                       // holds the layer-0 weights until the first chunk
   static constexpr int BARS = 114688;
   static constexpr int TOTAL = BARS + 256;
   // barrier indices
@@ -217,7 +225,8 @@ __global__ void __launch_bounds__(NTHR, 2) k_mlp_fwd_tc(MlpParams p) {
     unsigned char* a_hi_p = sm + S::A_HI;
     unsigned char* a_lo_p = sm + S::A_LO;
     float y[H];
-    layer0<NB>(p, e, valid, y);
+    load_w0<NB>(p, reinterpret_cast<float*>(sm + S::OUT), t);
+    layer0<NB>(p, reinterpret_cast<const float*>(sm + S::OUT), e, valid, y);
     uint32_t pacc = 0;
     for (int j = 0; j < nh; ++j) {
       if (valid) {
@@ -288,7 +297,8 @@ struct BwdSmem {
   // rounded in place), dW chunk lo (16 KB), weight chunk image (16 KB).
   // After the K loop: trunk A hi [0, 32K), A lo [32K, 64K), B [64K, 96K).
   static constexpr int STAGE = 49152;
-  static constexpr int BARS = 2 * STAGE;
+  static constexpr int W0 = 2 * STAGE;  // layer-0 weights (NB, 64), <= 4 KB
+  static constexpr int BARS = W0 + 4096;
   static constexpr int TOTAL = BARS + 256;
   static constexpr int LD = 0, SPLIT = 2, MMA = 4, TL = 6, A = 7, ACC = 8, NBARS = 9;
 };
@@ -391,6 +401,8 @@ __global__ void __launch_bounds__(NTHR, 2) k_mlp_bwd_tc(MlpParams p) {
       ok = __all_sync(0xffffffffu, r);
       return ok;
     };
+    float* sW0 = reinterpret_cast<float*>(sm + S::W0);
+    load_w0<NB>(p, sW0, t);
     // split each dW chunk into tf32 hi (in place) and lo
     for (int kc = 0; kc < nch; ++kc) {
       const int s = kc & 1;
@@ -461,11 +473,11 @@ __global__ void __launch_bounds__(NTHR, 2) k_mlp_bwd_tc(MlpParams p) {
       }
 #pragma unroll
       for (int i = 0; i < NB; ++i) {
-        const float4* w4 = reinterpret_cast<const float4*>(p.w[0] + i * H);
+        const float4* w4 = reinterpret_cast<const float4*>(sW0 + i * H);
         float acc = 0.f;
 #pragma unroll
         for (int q = 0; q < H / 4; ++q) {
-          const float4 w = __ldg(w4 + q);
+          const float4 w = w4[q];
           acc = fmaf(da[4 * q + 0], w.x, acc);
           acc = fmaf(da[4 * q + 1], w.y, acc);
           acc = fmaf(da[4 * q + 2], w.z, acc);

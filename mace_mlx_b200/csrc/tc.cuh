@@ -92,6 +92,10 @@ __device__ __forceinline__ uint64_t globaltimer() {
   return t;
 }
 
+// A waiting thread sleeps until the phase completes or this many nanoseconds
+// pass, instead of spinning on the issue slots.
+constexpr uint32_t WAIT_SUSPEND_NS = 10000;
+
 // Wait for `phase` of the barrier; gives up after ~2 s (returns false).
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t phase) {
   const uint64_t t0 = globaltimer();
@@ -99,10 +103,10 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t phase) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(bar), "r"(phase)
+        : "r"(bar), "r"(phase), "r"(WAIT_SUSPEND_NS)
         : "memory");
     if (ok) return true;
     if ((it & 255u) == 255u && globaltimer() - t0 > 2000000000ull) return false;
@@ -114,15 +118,16 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t phase) {
 // returns false at once, so the whole CTA leaves its pipeline within one
 // timeout.
 __device__ __forceinline__ bool mbar_wait_or_abort(uint32_t bar, uint32_t phase, volatile int* abort) {
+  if (*abort) return false;
   const uint64_t t0 = globaltimer();
   for (uint32_t it = 0;; ++it) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(bar), "r"(phase)
+        : "r"(bar), "r"(phase), "r"(WAIT_SUSPEND_NS)
         : "memory");
     if (ok) return true;
     if ((it & 63u) == 63u) {
@@ -133,6 +138,11 @@ __device__ __forceinline__ bool mbar_wait_or_abort(uint32_t bar, uint32_t phase,
       }
     }
   }
+}
+
+// barrier `id` (1..15) among `n` threads (a multiple of 32)
+__device__ __forceinline__ void named_sync(uint32_t id, uint32_t n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
 
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
