@@ -78,24 +78,69 @@ def make_model_dir(tmp: str) -> str:
 # clocks sampling during the timed region
 # ---------------------------------------------------------------------------
 class ClockSampler:
+    """SM clock, power and clock-event reasons sampled every 10 ms (NVML, read-only).
+
+    Falls back to ``nvidia-smi -lms 100`` when the NVML binding is missing.
+    """
+
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40, "sw_power_cap": 0x4}
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int):
-        self.index = index
+    def __init__(self, cuda_index: int):
+        self.cuda_index = cuda_index
+        self.samples: list[tuple[float, int]] = []
+        self.max_mhz = None
+        self.stop = threading.Event()
         self.proc = None
         self.lines: list[str] = []
+        self.nvml = None
+
+    def _handle(self):
+        import pynvml as nv
+        import torch
+
+        nv.nvmlInit()
+        props = torch.cuda.get_device_properties(self.cuda_index)
+        bus = getattr(props, "pci_bus_id", None)
+        if bus is not None:
+            pci = f"{getattr(props, 'pci_domain_id', 0):08X}:{bus:02X}:{getattr(props, 'pci_device_id', 0):02X}.0"
+            try:
+                return nv, nv.nvmlDeviceGetHandleByPciBusId(pci)
+            except Exception:  # noqa: BLE001
+                pass
+        return nv, nv.nvmlDeviceGetHandleByIndex(self.cuda_index)
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
+            nv, h = self._handle()
+            self.nvml = (nv, h)
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+            get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                nv.nvmlDeviceGetCurrentClocksThrottleReasons
+
+            def run():
+                while not self.stop.is_set():
+                    try:
+                        self.samples.append((float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)), int(get_reasons(h))))
+                    except Exception:  # noqa: BLE001
+                        pass
+                    self.stop.wait(0.01)
+
+            self.t = threading.Thread(target=run, daemon=True)
             self.t.start()
         except Exception:  # noqa: BLE001
-            self.proc = None
+            self.nvml = None
+            try:
+                self.proc = subprocess.Popen(
+                    ["nvidia-smi", f"--id={self.cuda_index}", f"--query-gpu={self.Q}",
+                     "--format=csv,noheader,nounits", "-lms", "100"],
+                    stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                self.t = threading.Thread(target=self._read, daemon=True)
+                self.t.start()
+            except Exception:  # noqa: BLE001
+                self.proc = None
         return self
 
     def _read(self):
@@ -103,6 +148,9 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def __exit__(self, *exc):
+        self.stop.set()
+        if self.nvml is not None:
+            self.t.join(timeout=1)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -111,22 +159,29 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self) -> dict:
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
-            except ValueError:
-                continue
-            for nm, val in zip(names, parts[5:9]):
-                if val.lower().startswith("active"):
-                    reasons.add(nm)
+        sm, mx, reasons = [], self.max_mhz, set()
+        if self.nvml is not None:
+            for mhz, bits in self.samples:
+                sm.append(mhz)
+                reasons.update(nm for nm, bit in self.REASONS.items() if bits & bit)
+            src = "nvml 10 ms"
+        else:
+            names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+            for ln in self.lines:
+                parts = [p.strip() for p in ln.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    mx = float(parts[2])
+                except ValueError:
+                    continue
+                for nm, val in zip(names, parts[5:9]):
+                    if val.lower().startswith("active"):
+                        reasons.add(nm)
+            src = "nvidia-smi 100 ms"
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": src}
 
 
 # ---------------------------------------------------------------------------
@@ -280,14 +335,24 @@ def b200_arm(args, rank: int, world: int, local_rank: int):
     top = prof[0]
     avg_ms = top["ms"] / top["count"]
     wk = work.get((top["name"], top["layer"]), {"flops": 0, "bytes": 0})
+    # Tensor-core kernels (radial MLP, o3 linears) are compared with the tensor
+    # pipe when their arithmetic intensity is high; the CUDA-core kernels
+    # (conv, symmetric contraction, edge, forces) with HBM, plus their fp32
+    # issue rate against the FMA peak at the sampled SM clock.
+    tensor_kernel = top["name"].startswith(("mlp", "linear"))
     intensity = wk["flops"] / max(wk["bytes"], 1)
     ridge = bf16 * 1e12 / (hbm * 1e9)
-    if intensity > ridge * 0.05:  # compute-heavy: compare with the tensor pipe
+    if tensor_kernel and intensity > ridge * 0.05:
         ach = wk["flops"] / (avg_ms * 1e-3) / 1e12
         roof = {"bound": "tensor", "achieved": ach, "peak": bf16, "unit": "TFLOP/s", "frac": ach / bf16}
     else:
         ach = wk["bytes"] / (avg_ms * 1e-3) / 1e9
         roof = {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm}
+        clk_mhz = clk.summary().get("sm_mhz") or 1965.0
+        fma_peak = 148 * 128 * 2 * clk_mhz * 1e6 / 1e12
+        fl = wk["flops"] / (avg_ms * 1e-3) / 1e12
+        roof["fp32"] = {"achieved_tflops": fl, "peak_tflops": fma_peak, "frac": fl / fma_peak,
+                        "peak_source": "148 SMs x 128 FMA/clk x sampled SM clock (derived, not measured)"}
     traffic = None
     tp = ROOT / "profiles" / "ncu_traffic.json"
     if tp.exists():
