@@ -168,6 +168,9 @@ struct ConvParams {
 };
 int launch_conv_fwd(const ConvParams& p, cudaStream_t s);
 int launch_conv_bwd(const ConvParams& p, cudaStream_t s);
+// layer-signature specialisations (conv_sig.cu); *used = false: not instantiated
+int launch_conv_fwd_sig(const ConvParams& p, cudaStream_t s, bool* used);
+int launch_conv_bwd_sig(const ConvParams& p, cudaStream_t s, bool* used);
 
 // ---------------------------------------------------------------------------
 // node-level ops

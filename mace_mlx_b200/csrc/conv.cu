@@ -304,6 +304,9 @@ int launch_conv_fwd(const ConvParams& p, cudaStream_t s) {
   if (p.N == 0) return MACE_OK;
   int rc = conv_check(p);
   if (rc) return rc;
+  bool used = false;
+  rc = launch_conv_fwd_sig(p, s, &used);
+  if (rc || used) return rc;
   const int EC = 64;
   size_t smem = (size_t)(EC + EC * 16 + EC * p.m_tot) * sizeof(float);
   if (smem > 48 * 1024)
@@ -317,6 +320,9 @@ int launch_conv_bwd(const ConvParams& p, cudaStream_t s) {
   if (p.N == 0) return MACE_OK;
   int rc = conv_check(p);
   if (rc) return rc;
+  bool used = false;
+  rc = launch_conv_bwd_sig(p, s, &used);
+  if (rc || used) return rc;
   const int EC = 32;
   const int nw = p.C / 32;
   int G = 1024 / p.C;
