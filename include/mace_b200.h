@@ -51,7 +51,7 @@ extern "C" {
 #define MACE_ERR_UNSUPPORTED 6
 #define MACE_ERR_EDGES 7
 
-#define MACE_ABI_VERSION 2
+#define MACE_ABI_VERSION 3
 
 /* limits of the packed model description */
 #define MACE_MAX_LAYERS 4
@@ -143,6 +143,14 @@ typedef struct {
   mace_lin_group lin[MACE_MAX_IN];
   /* symmetric contraction: one entry per hidden slot */
   mace_sc_out sc[MACE_MAX_IN];
+  /* symmetric-contraction backward as one polynomial per coupling index k:
+   *   df[k][c] = sum_e G'[z][e][c] * g[r_e][c] (* f[b_e] (* f[c_e]))
+   * where g is the product-output gradient, r = (slot offset / C) + M its row,
+   * and G' = (multiplicity of k in the forward entry) x G. */
+  int32_t sc_n_bwd;               /* number of backward entries         */
+  int64_t i_sc_bwd;               /* ints: (ncoup+1) segment starts by k, then packed
+                                     b | c<<4 | nu'<<8 | r<<10 (nu' = degree - 1) */
+  int64_t f_sc_bwd;               /* floats: (num_elements, sc_n_bwd, C) */
   /* product linear: one (C, C) block per hidden slot */
   int64_t f_prod[MACE_MAX_IN], f_prod_t[MACE_MAX_IN];
   /* readout */

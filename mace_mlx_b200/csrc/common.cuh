@@ -232,6 +232,11 @@ struct ScParams {
   // backward
   const float* dout;
   float* df;        // (N, ncoup*C)
+  int n_bwd;                 // backward polynomial, one segment per coupling index
+  const int32_t* bwd_seg;    // (ncoup + 1)
+  const int32_t* bwd_ent;    // packed b | c<<4 | nu'<<8 | r<<10
+  const float* Gb;           // (num_elements, n_bwd, C)
+  int n_rows;                // rows of the product output (hid.dim / C)
 };
 int launch_sc_fwd(const ScParams& p, cudaStream_t s);
 int launch_sc_bwd(const ScParams& p, cudaStream_t s);

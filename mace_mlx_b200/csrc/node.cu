@@ -128,11 +128,56 @@ __global__ void k_skip(SkipParams p) {
 // ---------------------------------------------------------------------------
 // symmetric contraction as a polynomial in the coupling features:
 //   out[n][o][M][c] = sum_{entries e of M} G[z_n][e][c] * f[a_e] (* f[b_e] (* f[c_e]))
-// (index-symmetrised U pre-contracted with the species weights at load time).
-// One CTA per node, one thread per channel; f (and df) live in the thread's
-// own shared-memory column, G is read coalesced over channels from L2.
+// (index-symmetrised U pre-contracted with the species weights at load time),
+// and its gradient as one polynomial per coupling index k:
+//   df[k][c] = sum_e G'[z_n][e][c] * g[r_e][c] (* f[b_e] (* f[c_e])).
+// Generic form for any coupling table: one CTA per node, one thread per
+// channel, f and g in the thread's own shared-memory column, entries decoded
+// at run time, eight independent G loads in flight.  The standard tables
+// (16 coupling features, correlation 3) use the generated kernels of
+// sc_gen.cu instead.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ int ix(int v, int sh) { return (v >> sh) & 15; }
+
+constexpr int SC_UNROLL = 8;
+
+// sum over entries [b, e) of G[q] * f[a] (* f[b] (* f[c])), packed M | a<<4 | b<<8 | c<<12 | nu<<16
+__device__ __forceinline__ float sc_poly(const int32_t* __restrict__ ent, const float* __restrict__ G, int C,
+                                         const float* f, int b, int e) {
+  float acc[SC_UNROLL];
+#pragma unroll
+  for (int k = 0; k < SC_UNROLL; ++k) acc[k] = 0.f;
+  int q = b;
+  for (; q + SC_UNROLL <= e; q += SC_UNROLL) {
+    int id[SC_UNROLL];
+    float g[SC_UNROLL];
+#pragma unroll
+    for (int k = 0; k < SC_UNROLL; ++k) {
+      id[k] = __ldg(ent + q + k);
+      g[k] = __ldg(G + (int64_t)(q + k) * C);
+    }
+#pragma unroll
+    for (int k = 0; k < SC_UNROLL; ++k) {
+      const int nu = (id[k] >> 16) & 3;
+      float v = g[k] * f[ix(id[k], 4) * C];
+      if (nu >= 2) v *= f[ix(id[k], 8) * C];
+      if (nu >= 3) v *= f[ix(id[k], 12) * C];
+      acc[k] += v;
+    }
+  }
+  for (; q < e; ++q) {
+    const int id = __ldg(ent + q);
+    const int nu = (id >> 16) & 3;
+    float v = __ldg(G + (int64_t)q * C) * f[ix(id, 4) * C];
+    if (nu >= 2) v *= f[ix(id, 8) * C];
+    if (nu >= 3) v *= f[ix(id, 12) * C];
+    acc[0] += v;
+  }
+  float t = 0.f;
+#pragma unroll
+  for (int k = 0; k < SC_UNROLL; ++k) t += acc[k];
+  return t;
+}
 
 __global__ void __launch_bounds__(128) k_sc_fwd(ScParams p) {
   extern __shared__ float sf[];  // ncoup x C
@@ -144,33 +189,10 @@ __global__ void __launch_bounds__(128) k_sc_fwd(ScParams p) {
   const float* f = sf + c;
   for (int o = 0; o < p.n_out; ++o) {
     const int L = p.L[o];
-    const int32_t* __restrict__ ent = p.ent[o];
     const float* __restrict__ G = p.G[o] + (int64_t)z * p.n_ent[o] * C + c;
     for (int M = 0; M < 2 * L + 1; ++M) {
       const int b = __ldg(p.seg[o] + M), e = __ldg(p.seg[o] + M + 1);
-      float acc0 = 0.f, acc1 = 0.f;
-      int q = b;
-      for (; q + 1 < e; q += 2) {
-        const int i0 = __ldg(ent + q), i1 = __ldg(ent + q + 1);
-        const float g0 = __ldg(G + (int64_t)q * C), g1 = __ldg(G + (int64_t)(q + 1) * C);
-        float v0 = g0 * f[ix(i0, 4) * C], v1 = g1 * f[ix(i1, 4) * C];
-        const int n0 = i0 >> 16, n1 = i1 >> 16;
-        if (n0 >= 2) v0 *= f[ix(i0, 8) * C];
-        if (n0 >= 3) v0 *= f[ix(i0, 12) * C];
-        if (n1 >= 2) v1 *= f[ix(i1, 8) * C];
-        if (n1 >= 3) v1 *= f[ix(i1, 12) * C];
-        acc0 += v0;
-        acc1 += v1;
-      }
-      if (q < e) {
-        const int i0 = __ldg(ent + q);
-        float v0 = __ldg(G + (int64_t)q * C) * f[ix(i0, 4) * C];
-        const int n0 = i0 >> 16;
-        if (n0 >= 2) v0 *= f[ix(i0, 8) * C];
-        if (n0 >= 3) v0 *= f[ix(i0, 12) * C];
-        acc0 += v0;
-      }
-      p.out[n * p.out_row + p.out_off[o] + M * C + c] = acc0 + acc1;
+      p.out[n * p.out_row + p.out_off[o] + M * C + c] = sc_poly(p.ent[o], G, C, f, b, e);
     }
   }
 }
@@ -182,43 +204,49 @@ __global__ void __launch_bounds__(128) k_sc_bwd(ScParams p) {
   const int z = p.species[n];
   const int nc = p.ncoup;
   float* sf = sm;             // ncoup x C (16 rows reserved)
-  float* sdf = sm + 16 * C;   // ncoup x C
-  for (int i = 0; i < nc; ++i) {
-    sf[i * C + c] = p.f[n * nc * C + i * C + c];
-    sdf[i * C + c] = 0.f;
-  }
+  float* sg = sm + 16 * C;    // product-output gradient rows x C
+  for (int i = 0; i < nc; ++i) sf[i * C + c] = p.f[n * nc * C + i * C + c];
+  for (int r = 0; r < p.n_rows; ++r) sg[r * C + c] = p.dout[n * p.out_row + r * C + c];
   const float* f = sf + c;
-  float* df = sdf + c;
-  for (int o = 0; o < p.n_out; ++o) {
-    const int L = p.L[o];
-    const int32_t* __restrict__ ent = p.ent[o];
-    const float* __restrict__ G = p.G[o] + (int64_t)z * p.n_ent[o] * C + c;
-    for (int M = 0; M < 2 * L + 1; ++M) {
-      const float g = p.dout[n * p.out_row + p.out_off[o] + M * C + c];
-      const int b = __ldg(p.seg[o] + M), e = __ldg(p.seg[o] + M + 1);
-#pragma unroll 2
-      for (int q = b; q < e; ++q) {
-        const int id = __ldg(ent + q);
-        const float v = __ldg(G + (int64_t)q * C) * g;
-        const int a0 = ix(id, 4), nu = id >> 16;
-        if (nu == 1) {
-          df[a0 * C] += v;
-        } else if (nu == 2) {
-          const int a1 = ix(id, 8);
-          const float f0 = f[a0 * C], f1 = f[a1 * C];
-          df[a0 * C] += v * f1;
-          df[a1 * C] += v * f0;
-        } else {
-          const int a1 = ix(id, 8), a2 = ix(id, 12);
-          const float f0 = f[a0 * C], f1 = f[a1 * C], f2 = f[a2 * C];
-          df[a0 * C] += v * f1 * f2;
-          df[a1 * C] += v * f0 * f2;
-          df[a2 * C] += v * f0 * f1;
-        }
+  const float* g = sg + c;
+  const float* __restrict__ G = p.Gb + (int64_t)z * p.n_bwd * C + c;
+  const int32_t* __restrict__ ent = p.bwd_ent;
+  for (int k = 0; k < nc; ++k) {
+    const int b = __ldg(p.bwd_seg + k), e = __ldg(p.bwd_seg + k + 1);
+    float acc[SC_UNROLL];
+#pragma unroll
+    for (int u = 0; u < SC_UNROLL; ++u) acc[u] = 0.f;
+    int q = b;
+    for (; q + SC_UNROLL <= e; q += SC_UNROLL) {
+      int id[SC_UNROLL];
+      float gw[SC_UNROLL];
+#pragma unroll
+      for (int u = 0; u < SC_UNROLL; ++u) {
+        id[u] = __ldg(ent + q + u);
+        gw[u] = __ldg(G + (int64_t)(q + u) * C);
+      }
+#pragma unroll
+      for (int u = 0; u < SC_UNROLL; ++u) {
+        const int nu1 = (id[u] >> 8) & 3;
+        float v = gw[u] * g[(id[u] >> 10) * C];
+        if (nu1 >= 1) v *= f[ix(id[u], 0) * C];
+        if (nu1 >= 2) v *= f[ix(id[u], 4) * C];
+        acc[u] += v;
       }
     }
+    for (; q < e; ++q) {
+      const int id = __ldg(ent + q);
+      const int nu1 = (id >> 8) & 3;
+      float v = __ldg(G + (int64_t)q * C) * g[(id >> 10) * C];
+      if (nu1 >= 1) v *= f[ix(id, 0) * C];
+      if (nu1 >= 2) v *= f[ix(id, 4) * C];
+      acc[0] += v;
+    }
+    float t = 0.f;
+#pragma unroll
+    for (int u = 0; u < SC_UNROLL; ++u) t += acc[u];
+    p.df[n * nc * C + k * C + c] = t;
   }
-  for (int i = 0; i < nc; ++i) p.df[n * nc * C + i * C + c] = sdf[i * C + c];
 }
 
 // ---------------------------------------------------------------------------
@@ -328,7 +356,8 @@ int launch_sc_fwd(const ScParams& p, cudaStream_t s) {
 int launch_sc_bwd(const ScParams& p, cudaStream_t s) {
   if (p.N == 0) return MACE_OK;
   if (p.C > 128) return fail(MACE_ERR_UNSUPPORTED, "symmetric contraction: C must be <= 128");
-  size_t smem = (size_t)32 * p.C * sizeof(float);
+  if (p.n_rows > 48) return fail(MACE_ERR_UNSUPPORTED, "symmetric contraction: product output too wide");
+  size_t smem = (size_t)(16 + p.n_rows) * p.C * sizeof(float);
   k_sc_bwd<<<(unsigned)p.N, p.C, smem, s>>>(p);
   MACE_LAUNCH_CHECK("sc_bwd");
   return MACE_OK;

@@ -380,6 +380,11 @@ ScParams sc_params(mace_ctx* c, int t, int64_t N, const int32_t* species, const 
     p.ent[o] = I(c, so.i_ent) + (2 * so.L + 2);
     p.G[o] = F(c, so.f_G);
   }
+  p.n_bwd = L.sc_n_bwd;
+  p.bwd_seg = I(c, L.i_sc_bwd);
+  p.bwd_ent = I(c, L.i_sc_bwd) + p.ncoup + 1;
+  p.Gb = F(c, L.f_sc_bwd);
+  p.n_rows = L.hid.dim / L.C;
   return p;
 }
 

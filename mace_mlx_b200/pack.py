@@ -189,6 +189,37 @@ def _sc_tables(Us, Ws, L: int, tb: _Tables) -> tuple[int, int, int]:
     return i_off, f_off, len(ent)
 
 
+def sc_backward_polynomial(outs: list[tuple[np.ndarray, np.ndarray, int]], ncoup: int):
+    """Gradient of the symmetric-contraction polynomials w.r.t. the coupling features.
+
+    ``outs`` holds, per product output slot, (entries, G, row0) from
+    ``sc_polynomial`` and the slot's first row (offset / C) in the product
+    output.  For out[r][c] = sum_e G[z,e,c] prod_q f[a_q], the derivative is
+      df[k][c] = sum_r g[r][c] sum_{e of r, k in e} mult_k(e) G[z,e,c] prod_{q != one k} f[a_q],
+    returned as entries (k, b, c, nu', r) sorted by k (nu' = degree - 1, b <= c
+    the remaining indices) and G' = mult_k x G, shape (num_elements, n, C).
+    """
+    rows, Gs = [], []
+    for ent, G, row0 in outs:
+        for e in range(len(ent)):
+            M, nu = int(ent[e, 0]), int(ent[e, 4])
+            idx = [int(v) for v in ent[e, 1:1 + nu]]
+            for k in sorted(set(idx)):
+                rem = list(idx)
+                rem.remove(k)
+                rem += [0] * (2 - len(rem))
+                rows.append((k, rem[0], rem[1], nu - 1, row0 + M))
+                Gs.append(idx.count(k) * G[:, e, :])
+    ent_b = np.array(rows, dtype=np.int64).reshape(-1, 5)
+    G_b = np.stack(Gs, axis=1) if Gs else np.zeros((0, 0, 0))
+    order = np.lexsort((ent_b[:, 2], ent_b[:, 1], ent_b[:, 3], ent_b[:, 4], ent_b[:, 0]))
+    ent_b, G_b = ent_b[order], G_b[:, order]
+    seg = np.zeros(ncoup + 1, dtype=np.int64)
+    for k in range(ncoup):
+        seg[k + 1] = seg[k] + np.count_nonzero(ent_b[:, 0] == k)
+    return ent_b, G_b, seg
+
+
 def _layer(spec: ModelSpec, lay: LayerSpec, w: dict, tb: _Tables) -> nv.LayerDesc:
     C = spec.C
     t = lay.index
@@ -273,6 +304,7 @@ def _layer(spec: ModelSpec, lay: LayerSpec, w: dict, tb: _Tables) -> nv.LayerDes
         lg.f_w = tb.addf(Wc)
         lg.f_wt = tb.addf(Wc.T)
     # symmetric contraction
+    sc_outs = []
     for o, out in enumerate(lay.sc.outputs):
         so = d.sc[o]
         so.L = out.ir_out.l
@@ -287,6 +319,14 @@ def _layer(spec: ModelSpec, lay: LayerSpec, w: dict, tb: _Tables) -> nv.LayerDes
             else:
                 Ws.append(w[f"{pre}.weights.{out.correlation - 1 - nu}"])
         so.i_ent, so.f_G, so.n_ent = _sc_tables(out.U, Ws, so.L, tb)
+        ent, G = sc_polynomial(out.U, Ws, so.L)
+        sc_outs.append((ent, G, d.hid.off[o] // C))
+    ncoup = spec.interaction_irreps.dim // C
+    ent_b, G_b, seg_b = sc_backward_polynomial(sc_outs, ncoup)
+    packed = ent_b[:, 1] | (ent_b[:, 2] << 4) | (ent_b[:, 3] << 8) | (ent_b[:, 4] << 10)
+    d.sc_n_bwd = len(ent_b)
+    d.i_sc_bwd = tb.addi(np.concatenate([seg_b, packed]).astype(np.int32))
+    d.f_sc_bwd = tb.addf(G_b)
     # product linear (1-to-1)
     for q, ins in enumerate(lay.prod_linear.instrs):
         if ins.i_in != q or ins.i_out != q:

@@ -5,7 +5,7 @@ import pytest
 import torch
 
 from helpers import make_case
-from mace_mlx_b200.pack import PackedModel, sc_polynomial
+from mace_mlx_b200.pack import PackedModel, sc_backward_polynomial, sc_polynomial
 from mace_mlx_b200.spec import ModelSpec
 from oracle.model import OracleMACE
 
@@ -44,6 +44,54 @@ def test_symmetrised_sc_polynomial_equals_dense_contraction(arch):
         np.testing.assert_allclose(got, want, rtol=1e-10, atol=1e-12)
         o_off += C * d
         assert len(ent) < sum(int(np.count_nonzero(np.abs(u) > 1e-12)) for u in out.U)
+
+
+@pytest.mark.parametrize("arch", ["medium", "large"])
+def test_sc_backward_polynomial_is_the_gradient(arch):
+    """Per-index backward entries reproduce d/df of g . (forward polynomial), by autograd."""
+    config, weights, _ = make_case(arch, seed=4, z_table=[14, 8])
+    spec = ModelSpec.from_config(config)
+    lay = spec.layers[0]
+    C = spec.C
+    ncoup = spec.interaction_irreps.dim // C
+    rng = np.random.default_rng(1)
+    n = 3
+    species = np.array([0, 1, 1])
+    f = torch.tensor(rng.normal(size=(n, ncoup, C)), requires_grad=True)
+    outs, total, row0 = [], 0.0, 0
+    rows = sum(2 * o.ir_out.l + 1 for o in lay.sc.outputs)
+    g = torch.tensor(rng.normal(size=(n, rows, C)))
+    for o, out in enumerate(lay.sc.outputs):
+        pre = f"products.0.symmetric_contractions.contractions.{o}"
+        Ws = [weights[f"{pre}.weights_max"] if nu == out.correlation else
+              weights[f"{pre}.weights.{out.correlation - 1 - nu}"] for nu in range(1, out.correlation + 1)]
+        ent, G = sc_polynomial(out.U, Ws, out.ir_out.l)
+        outs.append((ent, G, row0))
+        Gt = torch.tensor(G[species])  # (n, e, C)
+        for e_i, (M, a, b, c, nu) in enumerate(ent):
+            term = f[:, a, :]
+            if nu >= 2:
+                term = term * f[:, b, :]
+            if nu >= 3:
+                term = term * f[:, c, :]
+            total = total + (Gt[:, e_i, :] * term * g[:, row0 + M, :]).sum()
+        row0 += 2 * out.ir_out.l + 1
+    total.backward()
+    ent_b, G_b, seg = sc_backward_polynomial(outs, ncoup)
+    assert seg[-1] == len(ent_b)
+    got = np.zeros((n, ncoup, C))
+    fn = f.detach().numpy()
+    gn = g.numpy()
+    for e_i, (k, b, c, nu1, r) in enumerate(ent_b):
+        term = gn[:, r, :].copy()
+        if nu1 >= 1:
+            term *= fn[:, b, :]
+        if nu1 >= 2:
+            term *= fn[:, c, :]
+        got[:, k, :] += G_b[species, e_i, :] * term
+    np.testing.assert_allclose(got, f.grad.numpy(), rtol=1e-9, atol=1e-9)
+    for k in range(ncoup):
+        assert np.all(ent_b[seg[k]:seg[k + 1], 0] == k)
 
 
 def test_packed_tables_are_aligned_and_complete():
