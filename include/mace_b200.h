@@ -51,7 +51,7 @@ extern "C" {
 #define MACE_ERR_UNSUPPORTED 6
 #define MACE_ERR_EDGES 7
 
-#define MACE_ABI_VERSION 3
+#define MACE_ABI_VERSION 4
 
 /* limits of the packed model description */
 #define MACE_MAX_LAYERS 4
@@ -151,6 +151,10 @@ typedef struct {
   int64_t i_sc_bwd;               /* ints: (ncoup+1) segment starts by k, then packed
                                      b | c<<4 | nu'<<8 | r<<10 (nu' = degree - 1) */
   int64_t f_sc_bwd;               /* floats: (num_elements, sc_n_bwd, C) */
+  /* 1, 2, 3: the product outputs are (0e), (0e, 1o), (0e, 1o, 2e) with the
+   * standard entry lists (16 coupling features, correlation 3), served by the
+   * generated straight-line kernels; 0: table-driven kernels */
+  int32_t sc_gen;
   /* product linear: one (C, C) block per hidden slot */
   int64_t f_prod[MACE_MAX_IN], f_prod_t[MACE_MAX_IN];
   /* readout */

@@ -237,7 +237,10 @@ struct ScParams {
   const int32_t* bwd_ent;    // packed b | c<<4 | nu'<<8 | r<<10
   const float* Gb;           // (num_elements, n_bwd, C)
   int n_rows;                // rows of the product output (hid.dim / C)
+  int gen_sig;               // > 0: generated kernels of sc_gen.cu apply (signature id)
 };
+// generated straight-line kernels (sc_gen.cu); *used = false: not available for p.C
+int launch_sc_gen(const ScParams& p, int sig, bool bwd, cudaStream_t s, bool* used);
 int launch_sc_fwd(const ScParams& p, cudaStream_t s);
 int launch_sc_bwd(const ScParams& p, cudaStream_t s);
 

@@ -346,6 +346,11 @@ int launch_skip(const SkipParams& p, cudaStream_t s) {
 
 int launch_sc_fwd(const ScParams& p, cudaStream_t s) {
   if (p.N == 0) return MACE_OK;
+  if (p.gen_sig > 0) {
+    bool used = false;
+    const int rc = launch_sc_gen(p, p.gen_sig, false, s, &used);
+    if (rc || used) return rc;
+  }
   if (p.C > 128) return fail(MACE_ERR_UNSUPPORTED, "symmetric contraction: C must be <= 128");
   size_t smem = (size_t)16 * p.C * sizeof(float);
   k_sc_fwd<<<(unsigned)p.N, p.C, smem, s>>>(p);
@@ -355,6 +360,11 @@ int launch_sc_fwd(const ScParams& p, cudaStream_t s) {
 
 int launch_sc_bwd(const ScParams& p, cudaStream_t s) {
   if (p.N == 0) return MACE_OK;
+  if (p.gen_sig > 0) {
+    bool used = false;
+    const int rc = launch_sc_gen(p, p.gen_sig, true, s, &used);
+    if (rc || used) return rc;
+  }
   if (p.C > 128) return fail(MACE_ERR_UNSUPPORTED, "symmetric contraction: C must be <= 128");
   if (p.n_rows > 48) return fail(MACE_ERR_UNSUPPORTED, "symmetric contraction: product output too wide");
   size_t smem = (size_t)(16 + p.n_rows) * p.C * sizeof(float);

@@ -385,6 +385,7 @@ ScParams sc_params(mace_ctx* c, int t, int64_t N, const int32_t* species, const 
   p.bwd_ent = I(c, L.i_sc_bwd) + p.ncoup + 1;
   p.Gb = F(c, L.f_sc_bwd);
   p.n_rows = L.hid.dim / L.C;
+  p.gen_sig = L.sc_gen;
   return p;
 }
 

@@ -19,7 +19,7 @@ MACE_ERR_TIMEOUT = 4
 MACE_ERR_NCCL = 5
 MACE_ERR_UNSUPPORTED = 6
 MACE_ERR_EDGES = 7
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 MAX_LAYERS = 4
 MAX_IN = 4
@@ -71,7 +71,7 @@ class LayerDesc(C.Structure):
         ("conv", ConvSlot * MAX_MID),
         ("lin", LinGroup * MAX_IN),
         ("sc", ScOut * MAX_IN),
-        ("sc_n_bwd", i32), ("i_sc_bwd", i64), ("f_sc_bwd", i64),
+        ("sc_n_bwd", i32), ("i_sc_bwd", i64), ("f_sc_bwd", i64), ("sc_gen", i32),
         ("f_prod", i64 * MAX_IN), ("f_prod_t", i64 * MAX_IN),
         ("readout_nonlinear", i32), ("readout_hidden", i32),
         ("f_ro1", i64), ("f_ro2", i64),

@@ -220,6 +220,22 @@ def sc_backward_polynomial(outs: list[tuple[np.ndarray, np.ndarray, int]], ncoup
     return ent_b, G_b, seg
 
 
+def _sc_generated_signature(lay: LayerSpec, spec: ModelSpec, ents: list[np.ndarray]) -> int:
+    """Id of the generated SC kernels (sc_gen.cu) serving this layer, or 0."""
+    from . import sc_codegen as gen
+
+    if lay.sc.coupling != gen.COUPLING or spec.interaction_irreps.dim != 16 * spec.C:
+        return 0
+    names = tuple(str(out.ir_out) for out in lay.sc.outputs)
+    if names not in gen.SIGNATURES or any(out.correlation != gen.CORRELATION for out in lay.sc.outputs):
+        return 0
+    for name, ent in zip(names, ents):
+        ref = gen.standard_entries(name)
+        if ref.shape != ent.shape or not np.array_equal(ref, ent):
+            return 0
+    return gen.SIGNATURES.index(names) + 1
+
+
 def _layer(spec: ModelSpec, lay: LayerSpec, w: dict, tb: _Tables) -> nv.LayerDesc:
     C = spec.C
     t = lay.index
@@ -327,6 +343,7 @@ def _layer(spec: ModelSpec, lay: LayerSpec, w: dict, tb: _Tables) -> nv.LayerDes
     d.sc_n_bwd = len(ent_b)
     d.i_sc_bwd = tb.addi(np.concatenate([seg_b, packed]).astype(np.int32))
     d.f_sc_bwd = tb.addf(G_b)
+    d.sc_gen = _sc_generated_signature(lay, spec, [e for e, _, _ in sc_outs])
     # product linear (1-to-1)
     for q, ins in enumerate(lay.prod_linear.instrs):
         if ins.i_in != q or ins.i_out != q:

@@ -149,3 +149,42 @@ def test_edge_tile_layout_round_trip():
     buf[idx.ravel()] = M.ravel()
     got = edge_tiles_to_rows(torch.from_numpy(buf), E, W).numpy()
     np.testing.assert_array_equal(got, M)
+
+
+def test_generated_sc_source_is_current():
+    """csrc/sc_gen.cu is what sc_codegen.py writes today."""
+    from mace_mlx_b200 import sc_codegen
+
+    assert sc_codegen.OUT.read_text() == sc_codegen.generate()
+
+
+@pytest.mark.parametrize("name", ["0e", "1o", "2e"])
+def test_generated_sc_terms_match_the_polynomial_and_its_gradient(name):
+    """The generated forward terms and per-index backward terms equal the table-driven forms."""
+    from mace_mlx_b200 import sc_codegen
+
+    ent = sc_codegen.standard_entries(name)
+    rng = np.random.default_rng(3)
+    G = rng.normal(size=(len(ent), 5))
+    f = rng.normal(size=(16, 5))
+    dM = 2 * sc_codegen.VARIANTS[name].l + 1
+    g = rng.normal(size=(dM, 5))
+    ft = torch.tensor(f, requires_grad=True)
+    out = torch.zeros(dM, 5, dtype=torch.float64)
+    for q, (M, a, b, c, nu) in enumerate(ent.tolist()):
+        term = ft[a]
+        if nu >= 2:
+            term = term * ft[b]
+        if nu >= 3:
+            term = term * ft[c]
+        out[M] = out[M] + torch.tensor(G[q]) * term
+    np.testing.assert_allclose(sc_codegen.eval_forward(ent, G, f), out.detach().numpy(), rtol=1e-12, atol=1e-12)
+    (out * torch.tensor(g)).sum().backward()
+    np.testing.assert_allclose(sc_codegen.eval_backward(ent, G, f, g), ft.grad.numpy(), rtol=1e-10, atol=1e-10)
+
+
+def test_standard_models_use_the_generated_sc_kernels():
+    for arch, sig in [("small", [1, 1]), ("medium", [2, 1]), ("large", [3, 1])]:
+        config, weights, _ = make_case(arch, seed=1, z_table=[14])
+        pm = PackedModel(ModelSpec.from_config(config), weights)
+        assert [pm.desc.layers[t].sc_gen for t in range(2)] == sig, arch
