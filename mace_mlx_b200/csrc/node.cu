@@ -19,78 +19,106 @@ namespace {
 
 // ---------------------------------------------------------------------------
 // o3.Linear: out[(n,m), c] (+)= alpha * sum_{ks,u} in[n, k_off[ks] + m*C + u] * W[ks*C+u][c]
-// 32 x 128 output tile per 256-thread CTA, 4 x 4 outputs per thread (small
-// tiles: node counts of a few thousand must still fill 148 SMs).
+// 64 x 128 output tile per 256-thread CTA, 8 x 4 outputs per thread; K in
+// chunks of 32 through shared memory, the next chunk's loads in flight in
+// registers while the current one is multiplied.  Inner step per thread: two
+// broadcast 128-bit loads of A, one 128-bit load of B, 32 FMAs.
 // ---------------------------------------------------------------------------
-constexpr int LR = 32;   // rows per tile
-constexpr int RPT = LR / 8;  // rows per thread
-constexpr int LK = 32;   // k chunk
+constexpr int LR = 64;        // rows per tile
+constexpr int RPT = LR / 8;   // rows per thread
+constexpr int LK = 32;        // k chunk
+constexpr int LAP = LR + 4;   // pitch of the transposed A tile (16-byte rows, no bank conflicts on the stores)
 
 __global__ void __launch_bounds__(256) k_linear(LinParams p) {
-  __shared__ float sA[LK][LR + 1];
+  __shared__ __align__(16) float sA[LK][LAP];
   __shared__ __align__(16) float sB[LK][128];
   const LinJob& jb = p.job[blockIdx.y];
   const int C = p.C;
-  const int64_t rows = p.N * jb.d;
-  const int64_t r0 = (int64_t)blockIdx.x * LR;
+  const int rows = (int)(p.N * jb.d);
+  const int r0 = blockIdx.x * LR;
   if (r0 >= rows) return;
   const int tid = threadIdx.x;
   const int ty = tid >> 5, tx = tid & 31;
+  // this thread's A row for the loads (fixed across K)
+  const int lr = tid & (LR - 1), lq = tid >> 6;  // row, first 4-wide k group (and lq + 4)
+  const int arow = r0 + lr;
+  const bool arow_ok = arow < rows;
+  const float* abase = p.in;
+  if (arow_ok) {
+    const int node = arow / jb.d, m = arow - node * jb.d;
+    abase = p.in + (int64_t)node * p.in_row + m * C;
+  }
+  const int nck = C / LK;
+  const int nchunks = jb.n_k * nck;
+  auto load = [&](int t, float4* ra, float4* rb) {
+    const int ks = t / nck, kc = (t - ks * nck) * LK;
+    const float* ap = abase + jb.k_off[ks] + kc;
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+      ra[h] = arow_ok ? __ldg(reinterpret_cast<const float4*>(ap + 4 * (lq + 4 * h))) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int idx = tid + 256 * q;
+      const int kk = idx >> 5, c4 = (idx & 31) * 4;
+      rb[q] = (c4 < C) ? __ldg(reinterpret_cast<const float4*>(jb.w + (int64_t)(ks * C + kc + kk) * jb.ldb + c4))
+                       : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
   float acc[RPT][4];
 #pragma unroll
   for (int a = 0; a < RPT; ++a)
 #pragma unroll
     for (int b = 0; b < 4; ++b) acc[a][b] = 0.f;
-  for (int ks = 0; ks < jb.n_k; ++ks) {
-    for (int kc = 0; kc < C; kc += LK) {
+  float4 ra[2], rb[4];
+  load(0, ra, rb);
+  for (int t = 0; t < nchunks; ++t) {
 #pragma unroll
-      for (int q = 0; q < (LR * LK) / 256; ++q) {
-        int idx = tid + 256 * q;
-        int r = idx / LK, kk = idx % LK;
-        int64_t row = r0 + r;
-        float v = 0.f;
-        if (row < rows) {
-          int64_t node = row / jb.d;
-          int m = (int)(row % jb.d);
-          v = p.in[node * p.in_row + jb.k_off[ks] + m * C + kc + kk];
-        }
-        sA[kk][r] = v;
-      }
-      for (int idx = tid; idx < LK * 128; idx += 256) {
-        int kk = idx >> 7, c = idx & 127;
-        sB[kk][c] = (c < C) ? __ldg(jb.w + (int64_t)(ks * C + kc + kk) * jb.ldb + c) : 0.f;
-      }
-      __syncthreads();
-#pragma unroll 8
-      for (int kk = 0; kk < LK; ++kk) {
-        float4 b4 = *reinterpret_cast<const float4*>(&sB[kk][tx * 4]);
-#pragma unroll
-        for (int a = 0; a < RPT; ++a) {
-          float av = sA[kk][ty * RPT + a];
-          acc[a][0] = fmaf(av, b4.x, acc[a][0]);
-          acc[a][1] = fmaf(av, b4.y, acc[a][1]);
-          acc[a][2] = fmaf(av, b4.z, acc[a][2]);
-          acc[a][3] = fmaf(av, b4.w, acc[a][3]);
-        }
-      }
-      __syncthreads();
+    for (int h = 0; h < 2; ++h) {
+      const int k0 = 4 * (lq + 4 * h);
+      sA[k0 + 0][lr] = ra[h].x;
+      sA[k0 + 1][lr] = ra[h].y;
+      sA[k0 + 2][lr] = ra[h].z;
+      sA[k0 + 3][lr] = ra[h].w;
     }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int idx = tid + 256 * q;
+      *reinterpret_cast<float4*>(&sB[idx >> 5][(idx & 31) * 4]) = rb[q];
+    }
+    __syncthreads();
+    if (t + 1 < nchunks) load(t + 1, ra, rb);
+#pragma unroll 8
+    for (int kk = 0; kk < LK; ++kk) {
+      const float4 b4 = *reinterpret_cast<const float4*>(&sB[kk][tx * 4]);
+      const float4 a0 = *reinterpret_cast<const float4*>(&sA[kk][ty * RPT]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&sA[kk][ty * RPT + 4]);
+      const float av[RPT] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+#pragma unroll
+      for (int a = 0; a < RPT; ++a) {
+        acc[a][0] = fmaf(av[a], b4.x, acc[a][0]);
+        acc[a][1] = fmaf(av[a], b4.y, acc[a][1]);
+        acc[a][2] = fmaf(av[a], b4.z, acc[a][2]);
+        acc[a][3] = fmaf(av[a], b4.w, acc[a][3]);
+      }
+    }
+    __syncthreads();
   }
+  if (tx * 4 >= C) return;
 #pragma unroll
   for (int a = 0; a < RPT; ++a) {
-    int64_t row = r0 + ty * RPT + a;
+    const int row = r0 + ty * RPT + a;
     if (row >= rows) continue;
-    int64_t node = row / jb.d;
-    int m = (int)(row % jb.d);
-    float* o = p.out + node * p.out_row + jb.out_off + m * C;
-#pragma unroll
-    for (int b = 0; b < 4; ++b) {
-      int c = tx * 4 + b;
-      if (c < C) {
-        float v = jb.alpha * acc[a][b];
-        o[c] = jb.accumulate ? o[c] + v : v;
-      }
+    const int node = row / jb.d, m = row - node * jb.d;
+    float4* o = reinterpret_cast<float4*>(p.out + (int64_t)node * p.out_row + jb.out_off + m * C + tx * 4);
+    float4 v = make_float4(jb.alpha * acc[a][0], jb.alpha * acc[a][1], jb.alpha * acc[a][2], jb.alpha * acc[a][3]);
+    if (jb.accumulate) {
+      const float4 w = *o;
+      v.x += w.x;
+      v.y += w.y;
+      v.z += w.z;
+      v.w += w.w;
     }
+    *o = v;
   }
 }
 
@@ -326,6 +354,7 @@ __global__ void k_energy(EnergyParams p) {
 int launch_linear(const LinParams& p, cudaStream_t s) {
   if (p.N == 0 || p.n_jobs == 0) return MACE_OK;
   if (p.C > 128 || p.C % 32 != 0) return fail(MACE_ERR_UNSUPPORTED, "linear: C must be a multiple of 32, <= 128");
+  if (p.N * 7 >= (int64_t)1 << 31) return fail(MACE_ERR_UNSUPPORTED, "linear: too many rows");
   int dmax = 1;
   for (int j = 0; j < p.n_jobs; ++j) dmax = p.job[j].d > dmax ? p.job[j].d : dmax;
   dim3 grid((unsigned)((p.N * dmax + LR - 1) / LR), (unsigned)p.n_jobs);
