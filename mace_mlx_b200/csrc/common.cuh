@@ -305,7 +305,24 @@ struct NlParams {
   int32_t* shifts;
   int32_t* rev;
   int* err_flag;
+  // cell lists (mode 1: periodic along all axes, bins in wrapped fractional
+  // coordinates; mode 2: open along all axes, bins over the Cartesian box);
+  // mode 0 tests every pair of a graph
+  int mode;
+  int nbin[3];
+  double origin[3], inv_binw[3];
+  int32_t* atom_bin;   // (n)
+  int32_t* bin_start;  // (nbins + 1)
+  int32_t* bin_fill;   // (nbins)
+  int32_t* bin_atoms;  // (n) atom ids ordered by bin
+  unsigned long long* keys;  // (capacity) unsorted (sender, S) keys of the fill pass
 };
+constexpr int NL_SHIFT_RANGE = 511;  // cell-list keys hold |S| <= 511 per axis
+constexpr int NL_ERR_SHIFT = 2;      // err_flag value: a cell-list shift out of range
+int launch_nl_bins(const NlParams& p, void* tmp, size_t tmp_bytes, cudaStream_t s);
+int launch_nl_cl_count(const NlParams& p, cudaStream_t s);
+int launch_nl_cl_fill(const NlParams& p, cudaStream_t s);
+int launch_nl_bbox(const NlParams& p, double* out6, cudaStream_t s);
 int launch_nl_prep(const NlParams& p, int32_t* node_graph, int32_t* wrap, cudaStream_t s);
 int launch_nl_count(const NlParams& p, cudaStream_t s);
 int launch_nl_fill(const NlParams& p, cudaStream_t s);

@@ -177,7 +177,197 @@ __global__ void k_nl_rev(NlParams p, int64_t E) {
   if (found < 0) atomicExch(p.err_flag, 1);
 }
 
+// ---------------------------------------------------------------------------
+// cell lists (one graph): atoms binned with bins at least the cutoff wide, so
+// every neighbour of an atom lies in the 27 bins around its own; the same
+// float64 distance test decides, so the edge set equals the all-pairs one.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ double frac_wrapped(const NlParams& p, int64_t i, int d) {
+  return p.pos[3 * i + 0] * p.inv_cell[0 * 3 + d] + p.pos[3 * i + 1] * p.inv_cell[1 * 3 + d] +
+         p.pos[3 * i + 2] * p.inv_cell[2 * 3 + d] - p.wrap[3 * i + d];
+}
+
+__device__ __forceinline__ int bin_coord(const NlParams& p, int64_t i, int d) {
+  double t = (p.mode == 1) ? frac_wrapped(p, i, d) * p.nbin[d] : (p.pos[3 * i + d] - p.origin[d]) * p.inv_binw[d];
+  int b = (int)floor(t);
+  return b < 0 ? 0 : (b >= p.nbin[d] ? p.nbin[d] - 1 : b);
+}
+
+__global__ void k_nl_bin(NlParams p) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= p.n) return;
+  const int b = (bin_coord(p, i, 2) * p.nbin[1] + bin_coord(p, i, 1)) * p.nbin[0] + bin_coord(p, i, 0);
+  p.atom_bin[i] = b;
+  atomicAdd(p.bin_fill + b, 1);
+}
+
+__global__ void k_nl_scatter(NlParams p) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= p.n) return;
+  const int b = p.atom_bin[i];
+  const int slot = atomicAdd(p.bin_fill + b, 1);
+  p.bin_atoms[p.bin_start[b] + slot] = (int32_t)i;
+}
+
+// Visit every candidate sender of receiver j (lanes of one warp in parallel,
+// all 32 lanes in every step): f(valid, i, S) for each (i, S) in the 27
+// surrounding bins, S the integer shift of the all-pairs test (image k of the
+// bin: S = wrap_i - wrap_j - k); lanes past the end of a bin get valid = false.
+template <class F>
+__device__ __forceinline__ void cl_candidates(const NlParams& p, int64_t j, int lane, F&& f) {
+  int bj[3];
+  for (int d = 0; d < 3; ++d) bj[d] = bin_coord(p, j, d);
+  for (int dz = -1; dz <= 1; ++dz)
+    for (int dy = -1; dy <= 1; ++dy)
+      for (int dx = -1; dx <= 1; ++dx) {
+        const int dd[3] = {dx, dy, dz};
+        int b[3], k[3];
+        bool ok = true;
+        for (int d = 0; d < 3; ++d) {
+          int v = bj[d] + dd[d];
+          k[d] = 0;
+          if (p.mode == 1) {
+            if (v < 0) { v += p.nbin[d]; k[d] = -1; }
+            else if (v >= p.nbin[d]) { v -= p.nbin[d]; k[d] = 1; }
+          } else if (v < 0 || v >= p.nbin[d]) {
+            ok = false;
+          }
+          b[d] = v;
+        }
+        if (!ok) continue;
+        const int bin = (b[2] * p.nbin[1] + b[1]) * p.nbin[0] + b[0];
+        const int s0 = p.bin_start[bin], s1 = p.bin_start[bin + 1];
+        for (int q0 = s0; q0 < s1; q0 += 32) {
+          const int q = q0 + lane;
+          const bool valid = q < s1;
+          const int64_t i = valid ? p.bin_atoms[q] : j;
+          int S[3];
+          for (int d = 0; d < 3; ++d) S[d] = (p.mode == 1) ? p.wrap[3 * i + d] - p.wrap[3 * j + d] - k[d] : 0;
+          f(valid, i, S);
+        }
+      }
+}
+
+__global__ void __launch_bounds__(256) k_nl_cl_count(NlParams p) {
+  const int64_t j = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (j >= p.n) return;
+  int cnt = 0;
+  cl_candidates(p, j, lane, [&](bool valid, int64_t i, const int S[3]) { cnt += (valid && hit(p, i, j, S)) ? 1 : 0; });
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+  if (lane == 0) p.count[j] = cnt;
+}
+
+__device__ __forceinline__ unsigned long long edge_key(int64_t i, const int S[3]) {
+  return ((unsigned long long)i << 30) | ((unsigned long long)(S[0] + 512) << 20) |
+         ((unsigned long long)(S[1] + 512) << 10) | (unsigned long long)(S[2] + 512);
+}
+
+// hits of receiver j appended unsorted to keys[row_ptr[j]..], then placed in
+// (sender, S) order by rank (keys are unique within a receiver)
+__global__ void __launch_bounds__(256) k_nl_cl_fill(NlParams p) {
+  const int64_t j = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (j >= p.n) return;
+  const int64_t base = p.row_ptr[j], end = p.row_ptr[j + 1];
+  int64_t cursor = base;
+  cl_candidates(p, j, lane, [&](bool valid, int64_t i, const int S[3]) {
+    const bool h = valid && hit(p, i, j, S);
+    bool in_range = true;
+    for (int d = 0; d < 3; ++d) in_range &= (S[d] >= -NL_SHIFT_RANGE && S[d] <= NL_SHIFT_RANGE);
+    if (h && !in_range) atomicExch(p.err_flag, NL_ERR_SHIFT);
+    const unsigned hits = __ballot_sync(0xffffffffu, h && in_range);
+    if (h && in_range) {
+      const int64_t o = cursor + __popc(hits & ((1u << lane) - 1));
+      if (o < end) p.keys[o] = edge_key(i, S);
+    }
+    cursor += __popc(hits);
+  });
+  __syncwarp();
+  const int64_t n = end - base;
+  for (int64_t a = lane; a < n; a += 32) {
+    const unsigned long long ka = p.keys[base + a];
+    int64_t rank = 0;
+    for (int64_t b = 0; b < n; ++b) rank += p.keys[base + b] < ka ? 1 : 0;
+    const int64_t o = base + rank;
+    p.snd[o] = (int32_t)(ka >> 30);
+    p.rcv[o] = (int32_t)j;
+    p.shifts[3 * o + 0] = (int)((ka >> 20) & 1023) - 512;
+    p.shifts[3 * o + 1] = (int)((ka >> 10) & 1023) - 512;
+    p.shifts[3 * o + 2] = (int)(ka & 1023) - 512;
+  }
+}
+
+// bounding box of the positions: out6 = (min x, min y, min z, max x, max y, max z)
+__global__ void __launch_bounds__(1024) k_nl_bbox(NlParams p, double* out6) {
+  __shared__ double red[6][32];
+  double lo[3] = {1e300, 1e300, 1e300}, hi[3] = {-1e300, -1e300, -1e300};
+  for (int64_t i = threadIdx.x; i < p.n; i += blockDim.x)
+    for (int d = 0; d < 3; ++d) {
+      const double x = p.pos[3 * i + d];
+      lo[d] = fmin(lo[d], x);
+      hi[d] = fmax(hi[d], x);
+    }
+  for (int o = 16; o > 0; o >>= 1)
+    for (int d = 0; d < 3; ++d) {
+      lo[d] = fmin(lo[d], __shfl_xor_sync(0xffffffffu, lo[d], o));
+      hi[d] = fmax(hi[d], __shfl_xor_sync(0xffffffffu, hi[d], o));
+    }
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0)
+    for (int d = 0; d < 3; ++d) {
+      red[d][w] = lo[d];
+      red[3 + d][w] = hi[d];
+    }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int d = 0; d < 3; ++d) {
+      double a = red[d][0], b = red[3 + d][0];
+      for (int q = 1; q < (int)(blockDim.x >> 5); ++q) {
+        a = fmin(a, red[d][q]);
+        b = fmax(b, red[3 + d][q]);
+      }
+      out6[d] = a;
+      out6[3 + d] = b;
+    }
+  }
+}
+
 }  // namespace
+
+int launch_nl_bins(const NlParams& p, void* tmp, size_t tmp_bytes, cudaStream_t s) {
+  const int nb = p.nbin[0] * p.nbin[1] * p.nbin[2];
+  MACE_CUDA_TRY(cudaMemsetAsync(p.bin_fill, 0, sizeof(int32_t) * (nb + 1), s));
+  const unsigned g = (unsigned)((p.n + 255) / 256);
+  k_nl_bin<<<g, 256, 0, s>>>(p);
+  MACE_LAUNCH_CHECK("nl_bin");
+  MACE_CUDA_TRY(cub::DeviceScan::ExclusiveSum(tmp, tmp_bytes, p.bin_fill, p.bin_start, nb + 1, s));
+  MACE_CUDA_TRY(cudaMemsetAsync(p.bin_fill, 0, sizeof(int32_t) * nb, s));
+  k_nl_scatter<<<g, 256, 0, s>>>(p);
+  MACE_LAUNCH_CHECK("nl_scatter");
+  return MACE_OK;
+}
+
+int launch_nl_cl_count(const NlParams& p, cudaStream_t s) {
+  if (p.n == 0) return MACE_OK;
+  k_nl_cl_count<<<(unsigned)((p.n * 32 + 255) / 256), 256, 0, s>>>(p);
+  MACE_LAUNCH_CHECK("nl_cl_count");
+  return MACE_OK;
+}
+
+int launch_nl_cl_fill(const NlParams& p, cudaStream_t s) {
+  if (p.n == 0) return MACE_OK;
+  k_nl_cl_fill<<<(unsigned)((p.n * 32 + 255) / 256), 256, 0, s>>>(p);
+  MACE_LAUNCH_CHECK("nl_cl_fill");
+  return MACE_OK;
+}
+
+int launch_nl_bbox(const NlParams& p, double* out6, cudaStream_t s) {
+  k_nl_bbox<<<1, 1024, 0, s>>>(p, out6);
+  MACE_LAUNCH_CHECK("nl_bbox");
+  return MACE_OK;
+}
 
 int launch_nl_prep(const NlParams& p, int32_t* node_graph, int32_t* wrap, cudaStream_t s) {
   if (p.n == 0) return MACE_OK;

@@ -84,6 +84,12 @@ struct mace_ctx {
   // neighbour-list scratch
   int32_t *nl_count = nullptr, *nl_graph = nullptr, *nl_wrap = nullptr;
   double* nl_inv = nullptr;
+  // cell-list scratch: bins for up to nl_bin_cap bins, unsorted edge keys
+  int32_t *nl_atom_bin = nullptr, *nl_bin_start = nullptr, *nl_bin_fill = nullptr, *nl_bin_atoms = nullptr;
+  int64_t nl_bin_cap = 0;
+  double* nl_bbox = nullptr;
+  unsigned long long* nl_keys = nullptr;
+  int64_t nl_keys_cap = 0;
   void* scan_tmp = nullptr;
   size_t scan_bytes = 0;
   int* d_err = nullptr;
@@ -133,6 +139,9 @@ void free_ws(mace_ctx* c) {
   }
   for (void* p : c->allocs) cudaFree(p);
   c->allocs.clear();
+  if (c->nl_keys) cudaFree(c->nl_keys);
+  c->nl_keys = nullptr;
+  c->nl_keys_cap = 0;
   c->ws_bytes = 0;
   c->cap_nodes = c->cap_edges = 0;
 }
@@ -246,7 +255,13 @@ int reserve(mace_ctx* c, int64_t N, int64_t E) {
   TRY(alloc(c, &c->nl_graph, N));
   TRY(alloc(c, &c->nl_wrap, N * 3));
   TRY(alloc(c, &c->nl_inv, 9));
-  c->scan_bytes = scan_tmp_bytes(N);
+  c->nl_bin_cap = 2 * N + 64;
+  TRY(alloc(c, &c->nl_atom_bin, N));
+  TRY(alloc(c, &c->nl_bin_atoms, N));
+  TRY(alloc(c, &c->nl_bin_start, c->nl_bin_cap + 1));
+  TRY(alloc(c, &c->nl_bin_fill, c->nl_bin_cap + 1));
+  TRY(alloc(c, &c->nl_bbox, 6));
+  c->scan_bytes = scan_tmp_bytes(c->nl_bin_cap + 1 > N + 1 ? c->nl_bin_cap : N);
   TRY(alloc(c, reinterpret_cast<char**>(&c->scan_tmp), (int64_t)c->scan_bytes));
   TRY(alloc(c, &c->d_err, 1));
   MACE_CUDA_TRY(cudaMemset(c->d_err, 0, sizeof(int)));
@@ -608,6 +623,163 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
 // ===========================================================================
 // C ABI
 // ===========================================================================
+namespace {
+
+// Cell-list geometry for one graph of n atoms (p.reach set for periodic
+// axes): mode 1 when every axis is periodic and at least 3 bins of one reach
+// fit per axis, mode 2 when no axis is periodic (bins over the bounding box,
+// read back from the device); otherwise 0 (all pairs).
+int nl_choose_mode(mace_ctx* c, NlParams& p, bool any_pbc, int32_t num_graphs, int64_t n, cudaStream_t s) {
+  // all pairs are cheaper for small graphs; MACE_B200_NL_CELL_MIN overrides the 2048-atom threshold
+  const char* env = std::getenv("MACE_B200_NL_CELL_MIN");
+  const int64_t cl_min = env ? std::atoll(env) : 2048;
+  p.mode = 0;
+  if (num_graphs != 1 || n < cl_min) return MACE_OK;
+  const bool all_pbc = p.pbc[0] && p.pbc[1] && p.pbc[2];
+  int64_t nb[3] = {1, 1, 1};
+  if (all_pbc) {
+    for (int d = 0; d < 3; ++d) {
+      nb[d] = (int64_t)std::floor(1.0 / p.reach[d]);
+      if (nb[d] < 3) return MACE_OK;
+    }
+  } else if (!any_pbc) {
+    TRY(launch_nl_bbox(p, c->nl_bbox, s));
+    double bb[6];
+    MACE_CUDA_TRY(cudaMemcpyAsync(bb, c->nl_bbox, sizeof(bb), cudaMemcpyDeviceToHost, s));
+    MACE_CUDA_TRY(cudaStreamSynchronize(s));
+    for (int d = 0; d < 3; ++d) {
+      const double ext = bb[3 + d] - bb[d];
+      nb[d] = (int64_t)std::floor(ext / p.r_cut);
+      if (nb[d] < 1) nb[d] = 1;
+      p.origin[d] = bb[d];
+    }
+  } else {
+    return MACE_OK;
+  }
+  // at most nl_bin_cap bins: merge bins along the longest axis (bins only widen)
+  const int64_t floor_nb = all_pbc ? 3 : 1;
+  while (nb[0] * nb[1] * nb[2] > c->nl_bin_cap) {
+    int d = 0;
+    for (int q = 1; q < 3; ++q) d = nb[q] > nb[d] ? q : d;
+    if (nb[d] <= floor_nb) return MACE_OK;
+    nb[d] = nb[d] - 1 > floor_nb ? (nb[d] * 3) / 4 : floor_nb;
+  }
+  for (int d = 0; d < 3; ++d) p.nbin[d] = (int)nb[d];
+  if (!all_pbc) {
+    double bb[6];
+    MACE_CUDA_TRY(cudaMemcpyAsync(bb, c->nl_bbox, sizeof(bb), cudaMemcpyDeviceToHost, s));
+    MACE_CUDA_TRY(cudaStreamSynchronize(s));
+    for (int d = 0; d < 3; ++d) {
+      const double ext = bb[3 + d] - bb[d];
+      p.inv_binw[d] = ext > 0.0 ? (double)nb[d] / ext : 0.0;
+    }
+  }
+  p.mode = all_pbc ? 1 : 2;
+  p.atom_bin = c->nl_atom_bin;
+  p.bin_start = c->nl_bin_start;
+  p.bin_fill = c->nl_bin_fill;
+  p.bin_atoms = c->nl_bin_atoms;
+  return MACE_OK;
+}
+
+int nl_build(mace_ctx* c, const double* pos, const double* cell, const int32_t* pbc, const int32_t* graph_ptr,
+             int32_t num_graphs, int64_t n, double r_cut, int32_t* sender, int32_t* receiver, int32_t* shifts,
+             int32_t* row_ptr, int32_t* rev, int64_t capacity, int64_t* n_edges, bool allow_cells,
+             cudaStream_t s) {
+  NlParams p{};
+  p.n = n;
+  p.pos = pos;
+  p.cell = cell;
+  p.r_cut = r_cut;
+  p.graph_ptr = graph_ptr;
+  p.num_graphs = num_graphs;
+  bool any_pbc = false;
+  for (int d = 0; d < 3; ++d) {
+    p.pbc[d] = pbc[d] ? 1 : 0;
+    any_pbc |= pbc[d] != 0;
+  }
+  double hc[9] = {0}, inv[9] = {0};
+  if (any_pbc) {
+    if (!cell) return fail(MACE_ERR_BAD_ARG, "periodic system without a cell");
+    MACE_CUDA_TRY(cudaMemcpyAsync(hc, cell, sizeof(hc), cudaMemcpyDeviceToHost, s));
+    MACE_CUDA_TRY(cudaStreamSynchronize(s));
+    double det = hc[0] * (hc[4] * hc[8] - hc[5] * hc[7]) - hc[1] * (hc[3] * hc[8] - hc[5] * hc[6]) +
+                 hc[2] * (hc[3] * hc[7] - hc[4] * hc[6]);
+    if (!(std::fabs(det) > 1e-12)) return fail(MACE_ERR_BAD_ARG, "periodic cell is singular");
+    inv[0] = (hc[4] * hc[8] - hc[5] * hc[7]) / det;
+    inv[1] = (hc[2] * hc[7] - hc[1] * hc[8]) / det;
+    inv[2] = (hc[1] * hc[5] - hc[2] * hc[4]) / det;
+    inv[3] = (hc[5] * hc[6] - hc[3] * hc[8]) / det;
+    inv[4] = (hc[0] * hc[8] - hc[2] * hc[6]) / det;
+    inv[5] = (hc[2] * hc[3] - hc[0] * hc[5]) / det;
+    inv[6] = (hc[3] * hc[7] - hc[4] * hc[6]) / det;
+    inv[7] = (hc[1] * hc[6] - hc[0] * hc[7]) / det;
+    inv[8] = (hc[0] * hc[4] - hc[1] * hc[3]) / det;
+    const double vol = std::fabs(det);
+    for (int d = 0; d < 3; ++d) {
+      const double* a = hc + 3 * ((d + 1) % 3);
+      const double* b = hc + 3 * ((d + 2) % 3);
+      double cx = a[1] * b[2] - a[2] * b[1], cy = a[2] * b[0] - a[0] * b[2], cz = a[0] * b[1] - a[1] * b[0];
+      double h = vol / std::sqrt(cx * cx + cy * cy + cz * cz);
+      p.reach[d] = r_cut / h * (1.0 + 1e-9) + 1e-9;
+    }
+  }
+  MACE_CUDA_TRY(cudaMemcpyAsync(c->nl_inv, inv, sizeof(inv), cudaMemcpyHostToDevice, s));
+  p.inv_cell = c->nl_inv;
+  p.count = c->nl_count;
+  p.row_ptr = row_ptr;
+  p.snd = sender;
+  p.rcv = receiver;
+  p.shifts = shifts;
+  p.rev = rev;
+  p.err_flag = c->d_err;
+  p.node_graph = c->nl_graph;
+  p.wrap = c->nl_wrap;
+  if (allow_cells) TRY(nl_choose_mode(c, p, any_pbc, num_graphs, n, s));
+  TRY(launch_nl_prep(p, c->nl_graph, c->nl_wrap, s));
+  if (p.mode) {
+    TRY(launch_nl_bins(p, c->scan_tmp, c->scan_bytes, s));
+    TRY(launch_nl_cl_count(p, s));
+  } else {
+    TRY(launch_nl_count(p, s));
+  }
+  MACE_CUDA_TRY(cudaMemsetAsync(c->nl_count + n, 0, sizeof(int32_t), s));
+  TRY(scan_counts(c->nl_count, row_ptr, n, c->scan_tmp, c->scan_bytes, s));
+  int32_t total = 0;
+  MACE_CUDA_TRY(cudaMemcpyAsync(&total, row_ptr + n, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+  MACE_CUDA_TRY(cudaStreamSynchronize(s));
+  *n_edges = total;
+  if (total > capacity) return fail(MACE_ERR_NL_OVERFLOW, "edge capacity too small");
+  if (total > 0 && (!sender || !receiver || !shifts || !rev)) return fail(MACE_ERR_BAD_ARG, "null edge output");
+  MACE_CUDA_TRY(cudaMemsetAsync(c->d_err, 0, sizeof(int), s));
+  if (p.mode) {
+    if (total > c->nl_keys_cap) {
+      if (c->nl_keys) cudaFree(c->nl_keys);
+      c->nl_keys = nullptr;
+      c->nl_keys_cap = 0;
+      MACE_CUDA_TRY(cudaMalloc(&c->nl_keys, sizeof(unsigned long long) * (size_t)(total > 0 ? total : 1)));
+      c->nl_keys_cap = total;
+    }
+    p.keys = c->nl_keys;
+    TRY(launch_nl_cl_fill(p, s));
+  } else {
+    TRY(launch_nl_fill(p, s));
+  }
+  int err = 0;
+  MACE_CUDA_TRY(cudaMemcpyAsync(&err, c->d_err, sizeof(int), cudaMemcpyDeviceToHost, s));
+  MACE_CUDA_TRY(cudaStreamSynchronize(s));
+  if (err == NL_ERR_SHIFT)  // a shift beyond the cell-list key range: all pairs instead
+    return nl_build(c, pos, cell, pbc, graph_ptr, num_graphs, n, r_cut, sender, receiver, shifts, row_ptr, rev,
+                    capacity, n_edges, false, s);
+  TRY(launch_nl_rev(p, total, s));
+  MACE_CUDA_TRY(cudaMemcpyAsync(&err, c->d_err, sizeof(int), cudaMemcpyDeviceToHost, s));
+  MACE_CUDA_TRY(cudaStreamSynchronize(s));
+  if (err) return fail(MACE_ERR_EDGES, "neighbour list is not closed under edge reversal");
+  return MACE_OK;
+}
+
+}  // namespace
+
 extern "C" {
 
 int mace_last_error(char* buf, size_t len) {
@@ -692,74 +864,10 @@ int mace_nl_build(mace_ctx* c, const double* pos, const double* cell, const int3
   if (n <= 0 || num_graphs <= 0 || !(r_cut > 0)) return fail(MACE_ERR_BAD_ARG, "bad sizes or cutoff");
   if (n > c->cap_nodes) return fail(MACE_ERR_BAD_ARG, "more atoms than reserved (call mace_ctx_reserve)");
   DeviceGuard g(c->device);
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  NlParams p{};
-  p.n = n;
-  p.pos = pos;
-  p.cell = cell;
-  p.r_cut = r_cut;
-  p.graph_ptr = graph_ptr;
-  p.num_graphs = num_graphs;
-  bool any_pbc = false;
-  for (int d = 0; d < 3; ++d) {
-    p.pbc[d] = pbc[d] ? 1 : 0;
-    any_pbc |= pbc[d] != 0;
-  }
-  double hc[9] = {0}, inv[9] = {0};
-  if (any_pbc) {
-    if (!cell) return fail(MACE_ERR_BAD_ARG, "periodic system without a cell");
-    MACE_CUDA_TRY(cudaMemcpyAsync(hc, cell, sizeof(hc), cudaMemcpyDeviceToHost, s));
-    MACE_CUDA_TRY(cudaStreamSynchronize(s));
-    double det = hc[0] * (hc[4] * hc[8] - hc[5] * hc[7]) - hc[1] * (hc[3] * hc[8] - hc[5] * hc[6]) +
-                 hc[2] * (hc[3] * hc[7] - hc[4] * hc[6]);
-    if (!(std::fabs(det) > 1e-12)) return fail(MACE_ERR_BAD_ARG, "periodic cell is singular");
-    inv[0] = (hc[4] * hc[8] - hc[5] * hc[7]) / det;
-    inv[1] = (hc[2] * hc[7] - hc[1] * hc[8]) / det;
-    inv[2] = (hc[1] * hc[5] - hc[2] * hc[4]) / det;
-    inv[3] = (hc[5] * hc[6] - hc[3] * hc[8]) / det;
-    inv[4] = (hc[0] * hc[8] - hc[2] * hc[6]) / det;
-    inv[5] = (hc[2] * hc[3] - hc[0] * hc[5]) / det;
-    inv[6] = (hc[3] * hc[7] - hc[4] * hc[6]) / det;
-    inv[7] = (hc[1] * hc[6] - hc[0] * hc[7]) / det;
-    inv[8] = (hc[0] * hc[4] - hc[1] * hc[3]) / det;
-    const double vol = std::fabs(det);
-    for (int d = 0; d < 3; ++d) {
-      const double* a = hc + 3 * ((d + 1) % 3);
-      const double* b = hc + 3 * ((d + 2) % 3);
-      double cx = a[1] * b[2] - a[2] * b[1], cy = a[2] * b[0] - a[0] * b[2], cz = a[0] * b[1] - a[1] * b[0];
-      double h = vol / std::sqrt(cx * cx + cy * cy + cz * cz);
-      p.reach[d] = r_cut / h * (1.0 + 1e-9) + 1e-9;
-    }
-  }
-  MACE_CUDA_TRY(cudaMemcpyAsync(c->nl_inv, inv, sizeof(inv), cudaMemcpyHostToDevice, s));
-  p.inv_cell = c->nl_inv;
-  p.count = c->nl_count;
-  p.row_ptr = row_ptr;
-  p.snd = sender;
-  p.rcv = receiver;
-  p.shifts = shifts;
-  p.rev = rev;
-  p.err_flag = c->d_err;
-  p.node_graph = c->nl_graph;
-  p.wrap = c->nl_wrap;
-  TRY(launch_nl_prep(p, c->nl_graph, c->nl_wrap, s));
-  TRY(launch_nl_count(p, s));
-  MACE_CUDA_TRY(cudaMemsetAsync(c->nl_count + n, 0, sizeof(int32_t), s));
-  TRY(scan_counts(c->nl_count, row_ptr, n, c->scan_tmp, c->scan_bytes, s));
-  int32_t total = 0;
-  MACE_CUDA_TRY(cudaMemcpyAsync(&total, row_ptr + n, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
-  MACE_CUDA_TRY(cudaStreamSynchronize(s));
-  *n_edges = total;
-  if (total > capacity) return fail(MACE_ERR_NL_OVERFLOW, "edge capacity too small");
-  if (total > 0 && (!sender || !receiver || !shifts || !rev)) return fail(MACE_ERR_BAD_ARG, "null edge output");
-  MACE_CUDA_TRY(cudaMemsetAsync(c->d_err, 0, sizeof(int), s));
-  TRY(launch_nl_fill(p, s));
-  TRY(launch_nl_rev(p, total, s));
-  int err = 0;
-  MACE_CUDA_TRY(cudaMemcpyAsync(&err, c->d_err, sizeof(int), cudaMemcpyDeviceToHost, s));
-  MACE_CUDA_TRY(cudaStreamSynchronize(s));
-  if (err) return fail(MACE_ERR_EDGES, "neighbour list is not closed under edge reversal");
-  return MACE_OK;
+  const char* env = std::getenv("MACE_B200_NL_ALL_PAIRS");
+  const bool allow_cells = !(env && env[0] == '1');
+  return nl_build(c, pos, cell, pbc, graph_ptr, num_graphs, n, r_cut, sender, receiver, shifts, row_ptr, rev,
+                  capacity, n_edges, allow_cells, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int mace_forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* out, int32_t flags,

@@ -2,6 +2,8 @@
 (as sets of (sender, receiver, shift)), sorted by (receiver, sender, S), with a
 consistent CSR row pointer and reverse-edge map."""
 
+import dataclasses
+
 import numpy as np
 import pytest
 import torch
@@ -112,3 +114,42 @@ def test_capacity_overflow_is_retried(model):
     e = model.neighbour_list(pos, cell, st.pbc, gp, 6.0, tiny)
     i, _, _ = neighbour_list(st.positions, st.cell, st.pbc, 6.0)
     assert e.n_edges == len(i)
+
+
+def _sheared(st: Structure, shear: float) -> Structure:
+    M = np.eye(3)
+    M[1, 0] = shear
+    M[2, 1] = 0.5 * shear
+    return dataclasses.replace(st, positions=st.positions @ M, cell=st.cell @ M)
+
+
+@pytest.mark.parametrize("case", ["periodic", "periodic_r65", "triclinic", "wrapped", "open_cluster"])
+def test_cell_list_against_oracle(model, monkeypatch, case):
+    """Cell lists forced on (threshold 1 atom): bit-exact edge set against the oracle."""
+    monkeypatch.setenv("MACE_B200_NL_CELL_MIN", "1")
+    st, r = diamond_si(5, 0.05, 11), 6.0
+    if case == "periodic_r65":
+        r = 6.5
+    elif case == "triclinic":
+        st = _sheared(st, 0.3)
+    elif case == "wrapped":
+        rng = np.random.default_rng(5)
+        k = rng.integers(-2, 3, size=(len(st), 3))
+        st = dataclasses.replace(st, positions=st.positions + k @ st.cell)
+    elif case == "open_cluster":
+        st = dataclasses.replace(st, pbc=np.zeros(3, dtype=bool))
+    check_edges(model, st, r)
+
+
+@pytest.mark.parametrize("pbc", [(True, True, True), (False, False, False)])
+def test_cell_list_equals_all_pairs_on_large_systems(model, monkeypatch, pbc):
+    """4096 atoms (cell lists by default) against the all-pairs kernels, array for array."""
+    st = dataclasses.replace(diamond_si(8, 0.05, 12), pbc=np.array(pbc))
+    a = gpu_nl(model, st, 6.0)
+    monkeypatch.setenv("MACE_B200_NL_ALL_PAIRS", "1")
+    b = gpu_nl(model, st, 6.0)
+    assert a.n_edges == b.n_edges > 30 * len(st) * (1 if pbc[0] else 0.5)
+    for x, y in zip(a.numpy(), b.numpy()):
+        np.testing.assert_array_equal(x, y)
+    np.testing.assert_array_equal(a.row_ptr.cpu().numpy(), b.row_ptr.cpu().numpy())
+    np.testing.assert_array_equal(a.rev[: a.n_edges].cpu().numpy(), b.rev[: b.n_edges].cpu().numpy())
