@@ -51,7 +51,7 @@ extern "C" {
 #define MACE_ERR_UNSUPPORTED 6
 #define MACE_ERR_EDGES 7
 
-#define MACE_ABI_VERSION 4
+#define MACE_ABI_VERSION 5
 
 /* limits of the packed model description */
 #define MACE_MAX_LAYERS 4
@@ -199,6 +199,18 @@ typedef struct {
   const int32_t* shifts;          /* (n_edges, 3) integer lattice shifts */
   const int32_t* row_ptr;         /* (n_nodes + 1) CSR over receivers    */
   const int32_t* rev;             /* (n_edges) index of the reverse edge */
+  /* (n_nodes) weight of each node's energy in the graph energies and hence in
+   * every gradient, or NULL for all 1.  Spatial domain decomposition gives
+   * owned atoms 1 and ghost atoms 0. */
+  const float* energy_weight;
+  /* The per-edge radial work runs in n_chunks consecutive receiver ranges
+   * (0 or 1: one range), so the per-edge weight buffers only hold one chunk
+   * (mace_ctx_reserve_chunked); with several chunks the backward recomputes
+   * the radial MLP of each chunk.  Host arrays of n_chunks + 1 entries:
+   * receiver boundaries (0 .. n_nodes) and row_ptr at those receivers. */
+  int32_t n_chunks;
+  const int64_t* chunk_nodes;
+  const int64_t* chunk_edges;
 } mace_system;
 
 /* Device pointers receiving the results (NULL = not wanted). */
@@ -218,6 +230,10 @@ int mace_ctx_destroy(mace_ctx* ctx);
 
 /* Size the workspace for systems up to max_nodes / max_edges (allocates; not a hot call). */
 int mace_ctx_reserve(mace_ctx* ctx, int64_t max_nodes, int64_t max_edges);
+
+/* As mace_ctx_reserve, with the per-edge radial-weight buffers sized for
+ * edge chunks of at most max_chunk_edges edges (see mace_system.n_chunks). */
+int mace_ctx_reserve_chunked(mace_ctx* ctx, int64_t max_nodes, int64_t max_edges, int64_t max_chunk_edges);
 
 /* Bytes of device workspace the context currently holds. */
 int mace_ctx_workspace_bytes(const mace_ctx* ctx, int64_t* bytes);

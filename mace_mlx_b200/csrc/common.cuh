@@ -150,6 +150,8 @@ struct ConvParams {
   int h_tot;     // sum over slots of (2l1+1)(2l2+1)
   int wnumel;
   int wnch;      // wt_nchunk(wnumel)
+  int64_t n0;    // first receiver of this launch (blockIdx.x = receiver - n0)
+  int64_t e0;    // first edge of the chunk: w / dw hold edges e0.. (tile index of e - e0)
   int in_dim;
   int in_ch;       // in_dim / C
   int mid_dim;
@@ -256,6 +258,7 @@ struct ReadoutParams {
   float* e;       // (N) readout energy of this layer
   float* dh;      // (N, h_row) gradient seed (overwritten; zero outside the 0e slot)
   float dscale;   // dE/d e
+  const float* weight;  // (N) energy weight per node, or null (1)
 };
 int launch_readout(const ReadoutParams& p, cudaStream_t s);
 
@@ -280,6 +283,7 @@ struct EnergyParams {
   float scale, shift;
   float* node_energy;
   double* energy;
+  const float* weight;  // (N) energy weight per node, or null (1)
 };
 int launch_energy(const EnergyParams& p, cudaStream_t s);
 

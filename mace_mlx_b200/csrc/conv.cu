@@ -74,7 +74,7 @@ __device__ __forceinline__ void fwd_slot(const ConvParams& p, const ConvSlotDev&
     float x1[D1];
 #pragma unroll
     for (int i = 0; i < D1; ++i) x1[i] = __ldg(x + i * C);
-    const float w = __ldg(p.w + wt_index(cb + j, k * C + u, p.wnch));
+    const float w = __ldg(p.w + wt_index(cb + j - p.e0, k * C + u, p.wnch));
     const float* Mk = sM + j * p.m_tot + sl.m_off;
 #pragma unroll
     for (int m = 0; m < D3; ++m) {
@@ -93,7 +93,7 @@ __global__ void k_conv_fwd(ConvParams p, int EC) {
   int* sSnd = reinterpret_cast<int*>(sm);
   float* sY = sm + EC;
   float* sM = sY + EC * 16;
-  const int64_t n = blockIdx.x;
+  const int64_t n = p.n0 + blockIdx.x;
   const int64_t e_beg = p.row_ptr[n], e_end = p.row_ptr[n + 1];
   if (e_beg == e_end) {
     for (int q = threadIdx.x; q < p.mid_dim; q += blockDim.x) p.A[n * p.mid_dim + q] = 0.f;
@@ -171,7 +171,7 @@ __device__ __forceinline__ void bwd_slot(const ConvParams& p, const ConvSlotDev&
   float x1[D1];
 #pragma unroll
   for (int i = 0; i < D1; ++i) x1[i] = __ldg(x + i * C);
-  const float w = __ldg(p.w + wt_index(e, k * C + u, p.wnch));
+  const float w = __ldg(p.w + wt_index(e - p.e0, k * C + u, p.wnch));
   float gr[D3];
   const float* dAs = p.dA + (int64_t)s * p.mid_dim + sl.off + u;
 #pragma unroll
@@ -190,7 +190,7 @@ __device__ __forceinline__ void bwd_slot(const ConvParams& p, const ConvSlotDev&
     dw = fmaf(xh[jj], Ye[YO + jj], dw);
     sdy[YO + jj] = fmaf(w, xh[jj], sdy[YO + jj]);
   }
-  p.dw[wt_index(e, k * C + u, p.wnch)] = dw;
+  p.dw[wt_index(e - p.e0, k * C + u, p.wnch)] = dw;
   // sender side of node n through the reverse edge
 #pragma unroll
   for (int i = 0; i < D1; ++i) {
@@ -214,7 +214,7 @@ __global__ void __launch_bounds__(512, 2) k_conv_bwd(ConvParams p, int EC, int G
   float* sRed = sM + EC * p.m_tot;        // nw x EC x 16
   float* sH = sRed + nw * EC * 16;         // h_tot x C
   float* sDupAll = sH + p.h_tot * C;       // G x in_dim
-  const int64_t n = blockIdx.x;
+  const int64_t n = p.n0 + blockIdx.x;
   const int tid = threadIdx.x;
   const int u = tid % C, grp = tid / C;
   float* sDup = sDupAll + grp * p.in_dim;
@@ -300,8 +300,9 @@ static int conv_check(const ConvParams& p) {
   return MACE_OK;
 }
 
+// receivers n0 .. N-1 (p.N is the end of the range)
 int launch_conv_fwd(const ConvParams& p, cudaStream_t s) {
-  if (p.N == 0) return MACE_OK;
+  if (p.N <= p.n0) return MACE_OK;
   int rc = conv_check(p);
   if (rc) return rc;
   bool used = false;
@@ -311,13 +312,13 @@ int launch_conv_fwd(const ConvParams& p, cudaStream_t s) {
   size_t smem = (size_t)(EC + EC * 16 + EC * p.m_tot) * sizeof(float);
   if (smem > 48 * 1024)
     MACE_CUDA_TRY(cudaFuncSetAttribute(k_conv_fwd, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  k_conv_fwd<<<(unsigned)p.N, p.C, smem, s>>>(p, EC);
+  k_conv_fwd<<<(unsigned)(p.N - p.n0), p.C, smem, s>>>(p, EC);
   MACE_LAUNCH_CHECK("conv_fwd");
   return MACE_OK;
 }
 
 int launch_conv_bwd(const ConvParams& p, cudaStream_t s) {
-  if (p.N == 0) return MACE_OK;
+  if (p.N <= p.n0) return MACE_OK;
   int rc = conv_check(p);
   if (rc) return rc;
   bool used = false;
@@ -331,7 +332,7 @@ int launch_conv_bwd(const ConvParams& p, cudaStream_t s) {
   if (smem > 227 * 1024) return fail(MACE_ERR_UNSUPPORTED, "conv backward tile exceeds shared memory");
   if (smem > 48 * 1024)
     MACE_CUDA_TRY(cudaFuncSetAttribute(k_conv_bwd, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  k_conv_bwd<<<(unsigned)p.N, p.C * G, smem, s>>>(p, EC, G);
+  k_conv_bwd<<<(unsigned)(p.N - p.n0), p.C * G, smem, s>>>(p, EC, G);
   MACE_LAUNCH_CHECK("conv_bwd");
   return MACE_OK;
 }

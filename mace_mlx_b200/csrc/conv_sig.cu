@@ -130,7 +130,7 @@ __global__ void __launch_bounds__(C) k_conv_fwd_sig(ConvParams p) {
   int* sSnd = reinterpret_cast<int*>(sm);
   float* sY = sm + EC;
   float* sM = sY + EC * 16;
-  const int64_t n = blockIdx.x;
+  const int64_t n = p.n0 + blockIdx.x;
   const int u = threadIdx.x;
   const int64_t e_beg = p.row_ptr[n], e_end = p.row_ptr[n + 1];
   float acc[S::atot()];
@@ -145,7 +145,7 @@ __global__ void __launch_bounds__(C) k_conv_fwd_sig(ConvParams p) {
       const int64_t e = cb + j;
       float x[S::in_ch()];
       load_sender<S, C>(p, sSnd[j], u, x);
-      const float* wp = p.w + wt_index(e, u, nch);
+      const float* wp = p.w + wt_index(e - p.e0, u, nch);
       const float* Mrow = sM + j * MT;
       each_path<S>([&](auto kc) {
         constexpr int K = decltype(kc)::value;
@@ -251,7 +251,7 @@ __global__ void __launch_bounds__(C * G, 2) k_conv_bwd_sig(ConvParams p) {
   float* sRed = sm + Lay::RED;
   float* sH = sm + Lay::H;
   float* sDup = sm + Lay::DUP;
-  const int64_t n = blockIdx.x;
+  const int64_t n = p.n0 + blockIdx.x;
   const int tid = threadIdx.x;
   const int u = tid % C, grp = tid / C;
   const int warp = u >> 5, lane = tid & 31;
@@ -305,7 +305,7 @@ __global__ void __launch_bounds__(C * G, 2) k_conv_bwd_sig(ConvParams p) {
       }
       float x[IC];
       load_sender<S, C>(p, s, u, x);
-      const int64_t wi = wt_index(e, u, nch);
+      const int64_t wi = wt_index(e - p.e0, u, nch);
       const float* wp = p.w + wi;
       float* dwp = p.dw + wi;
       const float* dAs = p.dA + s * p.mid_dim + u;
@@ -404,7 +404,7 @@ template <int C, class S>
 int run_fwd(const ConvParams& p, cudaStream_t s) {
   const size_t smem = (size_t)(64 + 64 * 16 + 64 * S::mtot()) * sizeof(float);
   MACE_CUDA_TRY(cudaFuncSetAttribute(k_conv_fwd_sig<C, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  k_conv_fwd_sig<C, S><<<(unsigned)p.N, C, smem, s>>>(p);
+  k_conv_fwd_sig<C, S><<<(unsigned)(p.N - p.n0), C, smem, s>>>(p);
   MACE_LAUNCH_CHECK("conv_fwd_sig");
   return MACE_OK;
 }
@@ -414,7 +414,7 @@ int run_bwd(const ConvParams& p, cudaStream_t s) {
   const size_t smem = (size_t)BwdLayout<C, G, S>::TOTAL * sizeof(float);
   if (smem > 227 * 1024) return fail(MACE_ERR_UNSUPPORTED, "conv backward tile exceeds shared memory");
   MACE_CUDA_TRY(cudaFuncSetAttribute(k_conv_bwd_sig<C, G, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  k_conv_bwd_sig<C, G, S><<<(unsigned)p.N, C * G, smem, s>>>(p);
+  k_conv_bwd_sig<C, G, S><<<(unsigned)(p.N - p.n0), C * G, smem, s>>>(p);
   MACE_LAUNCH_CHECK("conv_bwd_sig");
   return MACE_OK;
 }

@@ -286,12 +286,13 @@ __global__ void k_readout(ReadoutParams p) {
   if (n >= p.N) return;
   const float* h = p.h + n * p.h_row;
   float* dh = p.dh + n * p.h_row;
+  const float dscale = p.weight ? p.dscale * p.weight[n] : p.dscale;
   for (int q = p.C + lane; q < p.h_row; q += 32) dh[q] = 0.f;
   if (!p.nonlinear) {
     float a = 0.f;
     for (int c = lane; c < p.C; c += 32) {
       a = fmaf(h[c], __ldg(p.w1 + c), a);
-      dh[c] = p.dscale * __ldg(p.w1 + c);
+      dh[c] = dscale * __ldg(p.w1 + c);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
@@ -309,7 +310,7 @@ __global__ void k_readout(ReadoutParams p) {
   if (lane < H) {
     float w2 = __ldg(p.w2 + lane);
     e = silu_f(z) * w2;
-    dz = p.dscale * w2 * silu_grad_f(z);
+    dz = dscale * w2 * silu_grad_f(z);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) e += __shfl_xor_sync(0xffffffffu, e, o);
@@ -338,7 +339,7 @@ __global__ void k_energy(EnergyParams p) {
     float e0 = __ldg(p.e0 + p.species[n]);
     float ne = p.scale_shift ? e0 + (p.scale * inter + p.shift) : e0 + inter;
     if (p.node_energy) p.node_energy[n] = ne;
-    acc += (double)ne;
+    acc += p.weight ? (double)p.weight[n] * (double)ne : (double)ne;
   }
   red[threadIdx.x] = acc;
   __syncthreads();

@@ -69,6 +69,7 @@ struct mace_ctx {
   float* d_floats = nullptr;
   int32_t* d_ints = nullptr;
   int64_t cap_nodes = 0, cap_edges = 0;
+  int64_t cap_chunk_edges = 0;  // edges of one receiver chunk the radial-weight buffers hold
   std::vector<void*> allocs;
   int64_t ws_bytes = 0;
   // edge buffers
@@ -118,6 +119,7 @@ struct mace_ctx {
   mace_system g_sys{};
   mace_outputs g_out{};
   int g_flags = -1;
+  std::vector<int64_t> g_chunks;  // chunk boundaries of the captured call (host arrays)
   int g_launches = 0;
 };
 
@@ -204,7 +206,7 @@ int launch(mace_ctx* c, const char* name, int layer, cudaStream_t s, Fn&& fn) {
 
 #define LAUNCH(name, layer, expr) TRY(launch(c, name, layer, s, [&]() { return (expr); }))
 
-int reserve(mace_ctx* c, int64_t N, int64_t E) {
+int reserve(mace_ctx* c, int64_t N, int64_t E, int64_t EC) {
   const mace_model_desc& d = c->desc;
   free_ws(c);
   const int C = d.C;
@@ -216,9 +218,9 @@ int reserve(mace_ctx* c, int64_t N, int64_t E) {
   TRY(alloc(c, &c->dY, E * 16));
   TRY(alloc(c, &c->db, E * d.num_bessel));
   TRY(alloc(c, &c->dv, E * 3));
-  TRY(alloc(c, &c->dw, wt_floats(E, wmax)));
+  TRY(alloc(c, &c->dw, wt_floats(EC, wmax)));
   // padding rows of the last edge tile are read (never used) by the MLP backward
-  if (cudaMemset(c->dw, 0, (size_t)wt_floats(E, wmax) * sizeof(float)) != cudaSuccess ||
+  if (cudaMemset(c->dw, 0, (size_t)wt_floats(EC, wmax) * sizeof(float)) != cudaSuccess ||
       cudaDeviceSynchronize() != cudaSuccess)
     return fail(MACE_ERR_CUDA, "workspace memset");
   TRY(alloc(c, &c->vir_part, ((E + 255) / 256 + 1) * 9));
@@ -237,8 +239,8 @@ int reserve(mace_ctx* c, int64_t N, int64_t E) {
     LayerBufs& B = c->lb[t];
     int nh = L.n_mlp - 1, H = L.mlp_w[1];
     TRY(alloc(c, &B.up, N * L.in.dim));
-    TRY(alloc(c, &B.w, wt_floats(E, L.wnumel)));
-    TRY(alloc(c, &B.act, E * nh * H));
+    TRY(alloc(c, &B.w, wt_floats(EC, L.wnumel)));
+    TRY(alloc(c, &B.act, EC * nh * H));
     TRY(alloc(c, &B.A, N * L.mid.dim));
     TRY(alloc(c, &B.msg, N * L.inter.dim));
     TRY(alloc(c, &B.B, N * L.hid.dim));
@@ -267,6 +269,7 @@ int reserve(mace_ctx* c, int64_t N, int64_t E) {
   MACE_CUDA_TRY(cudaMemset(c->d_err, 0, sizeof(int)));
   c->cap_nodes = N;
   c->cap_edges = E;
+  c->cap_chunk_edges = EC;
   return MACE_OK;
 }
 
@@ -347,21 +350,22 @@ ConvParams conv_params(mace_ctx* c, int t, int64_t N, const mace_system* sys) {
   return p;
 }
 
-MlpParams mlp_params(mace_ctx* c, int t, int64_t E) {
+// radial MLP over edges e0 .. e0 + ne (the chunk's weights are in the layer buffers)
+MlpParams mlp_params(mace_ctx* c, int t, int64_t e0, int64_t ne) {
   const mace_layer_desc& L = c->desc.layers[t];
   MlpParams p{};
-  p.E = E;
+  p.E = ne;
   p.n_layers = L.n_mlp;
   for (int j = 0; j <= L.n_mlp; ++j) p.widths[j] = L.mlp_w[j];
   for (int j = 0; j < L.n_mlp; ++j) {
     p.w[j] = F(c, L.f_mlp[j]);
     p.wt[j] = F(c, L.f_mlp_t[j]);
   }
-  p.b = c->b;
+  p.b = c->b + e0 * c->desc.num_bessel;
   p.act = c->lb[t].act;
   p.out = c->lb[t].w;
   p.dout = c->dw;
-  p.db = c->db;
+  p.db = c->db + e0 * c->desc.num_bessel;
   const bool tc_ok = !c->mlp_cuda_cores && L.f_mlp_tc >= 0 && L.f_mlp_tc_bwd >= 0 && L.f_mlp_tc_trunk >= 0 &&
                      L.f_mlp_tc_trunk_bwd >= 0;
   p.tc_img = tc_ok ? F(c, L.f_mlp_tc) : nullptr;
@@ -441,6 +445,27 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
   if (N > c->cap_nodes || E > c->cap_edges)
     return fail(MACE_ERR_BAD_ARG, "system larger than the reserved workspace (call mace_ctx_reserve)");
   if (N <= 0) return fail(MACE_ERR_BAD_ARG, "empty system");
+  struct Chunk {
+    int64_t n0, n1, e0, e1;
+  };
+  std::vector<Chunk> chunks;
+  if (sys->n_chunks <= 1) {
+    chunks.push_back({0, N, 0, E});
+  } else {
+    if (!sys->chunk_nodes || !sys->chunk_edges) return fail(MACE_ERR_BAD_ARG, "chunks without boundary arrays");
+    const int64_t* cn = sys->chunk_nodes;
+    const int64_t* ce = sys->chunk_edges;
+    if (cn[0] != 0 || ce[0] != 0 || cn[sys->n_chunks] != N || ce[sys->n_chunks] != E)
+      return fail(MACE_ERR_BAD_ARG, "chunk boundaries must run from 0 to n_nodes / n_edges");
+    for (int k = 0; k < sys->n_chunks; ++k) {
+      if (cn[k + 1] < cn[k] || ce[k + 1] < ce[k]) return fail(MACE_ERR_BAD_ARG, "chunk boundaries must not decrease");
+      chunks.push_back({cn[k], cn[k + 1], ce[k], ce[k + 1]});
+    }
+  }
+  for (const Chunk& ch : chunks)
+    if (ch.e1 - ch.e0 > c->cap_chunk_edges)
+      return fail(MACE_ERR_BAD_ARG, "an edge chunk exceeds the reserved chunk capacity (mace_ctx_reserve_chunked)");
+  const bool recompute = chunks.size() > 1;
   const int T = d.num_layers;
   const int C = d.C;
   c->launches = 0;
@@ -485,10 +510,14 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
       LAUNCH("skip_fwd", t, launch_skip(sp, s));
     }
     TRY(run_linear_slots(c, "linear_up", t, N, L.in, L.in, L.f_up, c->h[t], B.up, 0, s));
-    MlpParams mp = mlp_params(c, t, E);
-    if (E > 0) LAUNCH("mlp_fwd", t, launch_mlp_fwd(mp, s));
-    ConvParams cp = conv_params(c, t, N, sys);
-    LAUNCH("conv_fwd", t, launch_conv_fwd(cp, s));
+    for (const Chunk& ch : chunks) {
+      MlpParams mp = mlp_params(c, t, ch.e0, ch.e1 - ch.e0);
+      if (ch.e1 > ch.e0) LAUNCH("mlp_fwd", t, launch_mlp_fwd(mp, s));
+      ConvParams cp = conv_params(c, t, ch.n1, sys);
+      cp.n0 = ch.n0;
+      cp.e0 = ch.e0;
+      LAUNCH("conv_fwd", t, launch_conv_fwd(cp, s));
+    }
     {
       LinParams lp{};
       lp.N = N;
@@ -528,6 +557,7 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
     rp.e = c->e_layers + (int64_t)t * N;
     rp.dh = c->dh[t + 1];
     rp.dscale = dscale;
+    rp.weight = sys->energy_weight;
     LAUNCH("readout", t, launch_readout(rp, s));
   }
   {
@@ -544,6 +574,7 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
     p.shift = d.shift;
     p.node_energy = out ? out->node_energy : nullptr;
     p.energy = out ? out->energy : nullptr;
+    p.weight = sys->energy_weight;
     LAUNCH("energy", -1, launch_energy(p, s));
   }
   if (!want_grad) return MACE_OK;
@@ -585,10 +616,16 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
       }
       LAUNCH("linear_msg_bwd", t, launch_linear(lp, s));
     }
-    ConvParams cp = conv_params(c, t, N, sys);
-    LAUNCH("conv_bwd", t, launch_conv_bwd(cp, s));
-    MlpParams mp = mlp_params(c, t, E);
-    if (E > 0) LAUNCH("mlp_bwd", t, launch_mlp_bwd(mp, s));
+    for (const Chunk& ch : chunks) {
+      MlpParams mp = mlp_params(c, t, ch.e0, ch.e1 - ch.e0);
+      // several chunks share the weight buffers: recompute this chunk's radial weights
+      if (recompute && ch.e1 > ch.e0) LAUNCH("mlp_fwd", t, launch_mlp_fwd(mp, s));
+      ConvParams cp = conv_params(c, t, ch.n1, sys);
+      cp.n0 = ch.n0;
+      cp.e0 = ch.e0;
+      LAUNCH("conv_bwd", t, launch_conv_bwd(cp, s));
+      if (ch.e1 > ch.e0) LAUNCH("mlp_bwd", t, launch_mlp_bwd(mp, s));
+    }
     if (t > 0) {
       // dh[t] holds the readout seed of layer t-1
       TRY(run_linear_slots(c, "linear_up_bwd", t, N, L.in, L.in, L.f_up_t, B.dup, c->dh[t], 1, s));
@@ -840,14 +877,23 @@ int mace_ctx_destroy(mace_ctx* c) {
   return MACE_OK;
 }
 
-int mace_ctx_reserve(mace_ctx* c, int64_t max_nodes, int64_t max_edges) {
-  if (!c || max_nodes < 0 || max_edges < 0) return fail(MACE_ERR_BAD_ARG, "bad reserve arguments");
-  if (max_nodes <= c->cap_nodes && max_edges <= c->cap_edges && c->cap_nodes > 0) return MACE_OK;
+int mace_ctx_reserve_chunked(mace_ctx* c, int64_t max_nodes, int64_t max_edges, int64_t max_chunk_edges) {
+  if (!c || max_nodes < 0 || max_edges < 0 || max_chunk_edges < 0)
+    return fail(MACE_ERR_BAD_ARG, "bad reserve arguments");
+  if (max_chunk_edges > max_edges) max_chunk_edges = max_edges;
+  if (max_nodes <= c->cap_nodes && max_edges <= c->cap_edges && max_chunk_edges <= c->cap_chunk_edges &&
+      c->cap_nodes > 0)
+    return MACE_OK;
   DeviceGuard g(c->device);
-  int64_t N = max_nodes > c->cap_nodes ? max_nodes : c->cap_nodes;
-  int64_t E = max_edges > c->cap_edges ? max_edges : c->cap_edges;
+  const int64_t N = max_nodes > c->cap_nodes ? max_nodes : c->cap_nodes;
+  const int64_t E = max_edges > c->cap_edges ? max_edges : c->cap_edges;
+  const int64_t EC = max_chunk_edges > c->cap_chunk_edges ? max_chunk_edges : c->cap_chunk_edges;
   MACE_CUDA_TRY(cudaDeviceSynchronize());
-  return reserve(c, N < 1 ? 1 : N, E < 1 ? 1 : E);
+  return reserve(c, N < 1 ? 1 : N, E < 1 ? 1 : E, EC < 1 ? 1 : EC);
+}
+
+int mace_ctx_reserve(mace_ctx* c, int64_t max_nodes, int64_t max_edges) {
+  return mace_ctx_reserve_chunked(c, max_nodes, max_edges, max_edges);
 }
 
 int mace_ctx_workspace_bytes(const mace_ctx* c, int64_t* bytes) {
@@ -883,8 +929,13 @@ int mace_forward_backward(mace_ctx* c, const mace_system* sys, const mace_output
   if (!(flags & MACE_USE_GRAPH) || c->prof_on) return forward_backward(c, sys, out, base_flags, s);
   mace_outputs o{};
   if (out) o = *out;
+  std::vector<int64_t> chunk_key;
+  if (sys->n_chunks > 1 && sys->chunk_nodes && sys->chunk_edges) {
+    chunk_key.assign(sys->chunk_nodes, sys->chunk_nodes + sys->n_chunks + 1);
+    chunk_key.insert(chunk_key.end(), sys->chunk_edges, sys->chunk_edges + sys->n_chunks + 1);
+  }
   const bool same = c->gexec && c->g_flags == base_flags && std::memcmp(&c->g_sys, sys, sizeof(mace_system)) == 0 &&
-                    std::memcmp(&c->g_out, &o, sizeof(mace_outputs)) == 0;
+                    std::memcmp(&c->g_out, &o, sizeof(mace_outputs)) == 0 && c->g_chunks == chunk_key;
   if (!same) {
     if (c->gexec) {
       MACE_CUDA_TRY(cudaGraphExecDestroy(c->gexec));
@@ -911,6 +962,7 @@ int mace_forward_backward(mace_ctx* c, const mace_system* sys, const mace_output
     c->g_sys = *sys;
     c->g_out = o;
     c->g_flags = base_flags;
+    c->g_chunks = chunk_key;
     c->g_launches = c->launches;
   }
   MACE_CUDA_TRY(cudaGraphLaunch(c->gexec, s));
@@ -945,7 +997,7 @@ int mace_debug_buffer(mace_ctx* c, int32_t id, const float** ptr, int64_t* len) 
   const LayerBufs& B = c->lb[layer];
   switch (stage) {
     case 0: *ptr = B.up; *len = N * L.in.dim; break;
-    case 1: *ptr = B.w; *len = wt_floats(E, L.wnumel); break;
+    case 1: *ptr = B.w; *len = wt_floats(E < c->cap_chunk_edges ? E : c->cap_chunk_edges, L.wnumel); break;
     case 2: *ptr = B.A; *len = N * L.mid.dim; break;
     case 3: *ptr = B.msg; *len = N * L.inter.dim; break;
     case 4: *ptr = B.B; *len = N * L.hid.dim; break;

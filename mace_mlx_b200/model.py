@@ -9,6 +9,8 @@ kernels.
 
 from __future__ import annotations
 
+import dataclasses
+
 import ctypes as C
 import os
 from dataclasses import dataclass
@@ -41,6 +43,29 @@ class EdgeSet:
     row_ptr: torch.Tensor  # (N+1,) int32
     rev: torch.Tensor  # (cap,) int32
     n_edges: int
+    _chunks: dict = dataclasses.field(default_factory=dict, repr=False)
+
+    def receiver_chunks(self, max_edges: int) -> tuple[np.ndarray, np.ndarray]:
+        """Receiver ranges whose edge counts stay <= max_edges (host int64 arrays).
+
+        Returns (nodes, edges): boundaries 0 .. N and row_ptr at them.  Cached,
+        so the arrays (and the pointers the library sees) stay the same while
+        the list is unchanged.
+        """
+        if max_edges not in self._chunks:
+            rp = self.row_ptr.cpu().numpy().astype(np.int64)
+            n = rp.shape[0] - 1
+            nodes = [0]
+            while nodes[-1] < n:
+                start = nodes[-1]
+                # last receiver boundary with row_ptr <= row_ptr[start] + max_edges
+                end = int(np.searchsorted(rp, rp[start] + max_edges, side="right")) - 1
+                if end <= start:
+                    raise ValueError(f"receiver {start} alone has more than {max_edges} edges")
+                nodes.append(min(end, n))
+            nodes_a = np.asarray(nodes, dtype=np.int64)
+            self._chunks[max_edges] = (nodes_a, np.ascontiguousarray(rp[nodes_a]))
+        return self._chunks[max_edges]
 
     def numpy(self):
         e = self.n_edges
@@ -75,8 +100,17 @@ class MACEModel:
         self.ctx = ctx
         self.z_table = self.spec.z_table
         self.r_max = self.spec.r_max
-        self._cap = (0, 0)
+        self._cap = (0, 0, 0)
         self._edge_cap = 0
+        # per-edge radial-weight buffers (all layers' w and MLP activations, one dw)
+        per_edge = 0
+        for lay in self.spec.layers:
+            w = lay.mlp_widths
+            per_edge += w[-1] + sum(w[1:-1])
+        per_edge += max(lay.mlp_widths[-1] for lay in self.spec.layers)
+        self.bytes_per_chunk_edge = 4 * per_edge
+        budget = float(os.environ.get("MACE_B200_CHUNK_BYTES", 24e9))
+        self.max_chunk_edges = max(4096, int(budget // self.bytes_per_chunk_edge))
 
     def close(self):
         if getattr(self, "ctx", None) is not None and self.ctx.value:
@@ -108,11 +142,14 @@ class MACEModel:
         return idx.astype(np.int32)
 
     def reserve(self, n_nodes: int, n_edges: int) -> None:
-        if n_nodes > self._cap[0] or n_edges > self._cap[1]:
+        """Workspace for n_nodes / n_edges; radial-weight buffers for at most max_chunk_edges."""
+        chunk = min(n_edges, self.max_chunk_edges)
+        if n_nodes > self._cap[0] or n_edges > self._cap[1] or chunk > self._cap[2]:
             N = max(n_nodes, self._cap[0])
             E = max(n_edges, self._cap[1])
-            nv.check(self.lib.mace_ctx_reserve(self.ctx, N, E), self.lib)
-            self._cap = (N, E)
+            EC = max(chunk, self._cap[2])
+            nv.check(self.lib.mace_ctx_reserve_chunked(self.ctx, N, E, EC), self.lib)
+            self._cap = (N, E, EC)
 
     def workspace_bytes(self) -> int:
         b = C.c_int64()
@@ -146,19 +183,24 @@ class MACEModel:
                 continue
             nv.check(rc, self.lib)
             edges.n_edges = int(ne.value)
+            edges._chunks.clear()
             return edges
         raise RuntimeError("neighbour list did not fit after resizing")
 
     # ------------------------------------------------------------------
     def evaluate(self, pos: torch.Tensor, cell: torch.Tensor | None, species: torch.Tensor,
                  graph_ptr: torch.Tensor, edges: EdgeSet, *, forces: bool = True, virial: bool = False,
-                 out: dict | None = None, graph: bool = False) -> dict:
+                 out: dict | None = None, graph: bool = False, energy_weight: torch.Tensor | None = None) -> dict:
         """Energy per graph (float64), node energies, forces and the raw virial.
 
         All inputs are device tensors: pos (N,3) float32, cell (3,3) float32 or
         None, species (N,) int32 model indices, graph_ptr (G+1,) int32.
         Asynchronous on the current stream.  ``graph=True`` replays the step as
         a CUDA graph (re-captured whenever a buffer address or size changes).
+        ``energy_weight`` (N,) float32 weighs each node's energy in the graph
+        energies and all gradients (owned 1 / ghost 0 under domain decomposition).
+        Lists with more than ``max_chunk_edges`` edges run the radial work in
+        receiver chunks (the MLP of each chunk is recomputed in the backward).
         """
         N = pos.shape[0]
         E = edges.n_edges
@@ -175,7 +217,12 @@ class MACEModel:
             n_nodes=N, n_edges=E, num_graphs=G, pos=pos.data_ptr(), cell=_ptr(cell),
             species=species.data_ptr(), graph_ptr=graph_ptr.data_ptr(), sender=edges.sender.data_ptr(),
             receiver=edges.receiver.data_ptr(), shifts=edges.shifts.data_ptr(), row_ptr=edges.row_ptr.data_ptr(),
-            rev=edges.rev.data_ptr())
+            rev=edges.rev.data_ptr(), energy_weight=_ptr(energy_weight))
+        if E > self.max_chunk_edges:
+            nodes, ebounds = edges.receiver_chunks(self.max_chunk_edges)
+            sysd.n_chunks = len(nodes) - 1
+            sysd.chunk_nodes = nodes.ctypes.data
+            sysd.chunk_edges = ebounds.ctypes.data
         outs = nv.Outputs(energy=_ptr(out["energy"]), node_energy=_ptr(out["node_energy"]),
                           forces=_ptr(out.get("forces")), virial=_ptr(out.get("virial")))
         flags = (nv.WANT_FORCES if forces else 0) | (nv.WANT_VIRIAL if virial else 0) | (nv.USE_GRAPH if graph else 0)

@@ -19,7 +19,7 @@ MACE_ERR_TIMEOUT = 4
 MACE_ERR_NCCL = 5
 MACE_ERR_UNSUPPORTED = 6
 MACE_ERR_EDGES = 7
-ABI_VERSION = 4
+ABI_VERSION = 5
 
 MAX_LAYERS = 4
 MAX_IN = 4
@@ -96,6 +96,8 @@ class System(C.Structure):
         ("pos", C.c_void_p), ("cell", C.c_void_p), ("species", C.c_void_p),
         ("graph_ptr", C.c_void_p), ("sender", C.c_void_p), ("receiver", C.c_void_p),
         ("shifts", C.c_void_p), ("row_ptr", C.c_void_p), ("rev", C.c_void_p),
+        ("energy_weight", C.c_void_p), ("n_chunks", i32), ("chunk_nodes", C.c_void_p),
+        ("chunk_edges", C.c_void_p),
     ]
 
 
@@ -111,7 +113,7 @@ class NativeError(RuntimeError):
 
 
 EXPORTED = (
-    "mace_last_error", "mace_ctx_create", "mace_ctx_destroy", "mace_ctx_reserve",
+    "mace_last_error", "mace_ctx_create", "mace_ctx_destroy", "mace_ctx_reserve", "mace_ctx_reserve_chunked",
     "mace_ctx_workspace_bytes", "mace_nl_build", "mace_forward_backward", "mace_debug_buffer",
     "mace_last_launch_count", "mace_ctx_error_flag", "mace_profile_enable", "mace_profile_read",
     "mace_nl_build_noalloc",
@@ -139,6 +141,7 @@ def load_library(path: str | Path | None = None) -> C.CDLL:
         "mace_ctx_create": ([C.POINTER(ModelDesc), C.c_int, C.POINTER(vp)], C.c_int),
         "mace_ctx_destroy": ([vp], C.c_int),
         "mace_ctx_reserve": ([vp, i64, i64], C.c_int),
+        "mace_ctx_reserve_chunked": ([vp, i64, i64, i64], C.c_int),
         "mace_ctx_workspace_bytes": ([vp, C.POINTER(i64)], C.c_int),
         "mace_nl_build": ([vp, vp, vp, C.POINTER(i32), vp, i32, i64, C.c_double, vp, vp, vp, vp, vp,
                            i64, C.POINTER(i64), vp], C.c_int),

@@ -8,7 +8,7 @@ import numpy as np
 import pytest
 import torch
 
-from helpers import assert_parity, irreps_to_channel_last, make_case, rel_err, run_gpu
+from helpers import assert_parity, graph_ptr_of, irreps_to_channel_last, make_case, rel_err, run_gpu
 from mace_mlx_b200.model import MACEModel, edge_tiles_to_rows
 from mace_mlx_b200.spec import ModelSpec
 from mace_mlx_b200.structures import diamond_si, lipso_box, molecule_batch
@@ -178,3 +178,46 @@ def test_tensor_core_mlp_matches_cuda_core_mlp(monkeypatch):
         assert rel_err(wa, wb) < 1e-5, rel_err(wa, wb)  # both fp32-accurate: ~2^-21 per product
     assert rel_err(a["forces"], b["forces"]) < 2e-5
     assert abs(a["energy"][0] - b["energy"][0]) < 1e-5 * max(1.0, abs(b["energy"][0]))
+
+
+def _eval(m, st, edges, species, weight=None):
+    dev = m.device
+    gp = torch.as_tensor(graph_ptr_of(st), device=dev)
+    cell = torch.tensor(st.cell, dtype=torch.float32, device=dev)
+    w = None if weight is None else torch.as_tensor(weight, dtype=torch.float32, device=dev)
+    out = m.evaluate(torch.tensor(st.positions, dtype=torch.float32, device=dev), cell,
+                     torch.as_tensor(species, device=dev), gp, edges, forces=True, virial=True, energy_weight=w)
+    torch.cuda.synchronize(dev)
+    return {k: v.cpu().numpy().astype(np.float64) for k, v in out.items()}
+
+
+def test_receiver_chunks_give_identical_results():
+    """Radial work in receiver chunks (MLP recomputed in the backward) equals the one-pass step bitwise."""
+    config, weights, st = make_case("medium", diamond_si(3, 0.05, 21), seed=21)
+    m = MACEModel(config=config, weights=weights, device=0)
+    _, edges, species = run_gpu(m, st)
+    a = _eval(m, st, edges, species)
+    m.max_chunk_edges = edges.n_edges // 5 + 1
+    nodes, ebounds = edges.receiver_chunks(m.max_chunk_edges)
+    assert len(nodes) - 1 >= 5 and np.all(np.diff(ebounds) <= m.max_chunk_edges)
+    b = _eval(m, st, edges, species)
+    for k in ("energy", "node_energy", "forces", "virial"):
+        np.testing.assert_array_equal(a[k], b[k])
+    assert m.error_flag() == 0
+
+
+def test_energy_weights_are_linear():
+    """E and forces with node weights w plus those with 1 - w equal the unweighted step."""
+    config, weights, st = make_case("medium", diamond_si(2, 0.05, 22), seed=22)
+    m = MACEModel(config=config, weights=weights, device=0)
+    _, edges, species = run_gpu(m, st)
+    w = (np.random.default_rng(0).random(len(st)) < 0.4).astype(np.float32)
+    full = _eval(m, st, edges, species)
+    a = _eval(m, st, edges, species, w)
+    b = _eval(m, st, edges, species, 1.0 - w)
+    np.testing.assert_allclose(a["node_energy"], full["node_energy"], rtol=0, atol=0)
+    np.testing.assert_allclose(a["energy"], (w * full["node_energy"]).sum(), rtol=1e-6)
+    np.testing.assert_allclose(a["energy"] + b["energy"], full["energy"], rtol=1e-6)
+    scale = np.abs(full["forces"]).max()
+    np.testing.assert_allclose(a["forces"] + b["forces"], full["forces"], atol=2e-5 * scale)
+    np.testing.assert_allclose(a["virial"] + b["virial"], full["virial"], atol=2e-5 * np.abs(full["virial"]).max())
