@@ -57,6 +57,9 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=20.0, help="budget of the CPU baseline sample")
     ap.add_argument("--device-only", action="store_true",
                     help="only W + K plain device steps, no JSON (the command the ncu captures profile)")
+    ap.add_argument("--config", default="c1", choices=["c1", "c3", "c4"],
+                    help="c1: the headline Si1000 (default); c3: 512 OFF-like molecules sharded by structure; "
+                         "c4: 1M-atom Si, spatially domain-decomposed over the ranks")
     return ap.parse_args()
 
 
@@ -237,6 +240,54 @@ def reference_arm(args, rank: int, world: int):
     return 0
 
 
+
+# ---------------------------------------------------------------------------
+# roofline of the dominant kernel of a profiled step
+# ---------------------------------------------------------------------------
+def roofline_of(work: dict, prof: list[dict], clk) -> dict:
+    peaks = {}
+    pp = ROOT / "MEASURED_PEAKS.json"
+    if pp.exists():
+        peaks = json.loads(pp.read_text())
+    hbm = float(peaks.get("hbm_gbs", 6650.0))
+    bf16 = float(peaks.get("bf16_tflops", 1590.0))
+    peak_src = "measured" if pp.exists() else "fallback"
+    prof = sorted(prof, key=lambda r: -r["ms"])
+    tot_prof = sum(r["ms"] for r in prof)
+    top = prof[0]
+    avg_ms = top["ms"] / top["count"]
+    wk = work.get((top["name"], top["layer"]), {"flops": 0, "bytes": 0})
+    # Tensor-core kernels (radial MLP, o3 linears) are compared with the tensor
+    # pipe when their arithmetic intensity is high; the CUDA-core kernels
+    # (conv, symmetric contraction, edge, forces) with HBM, plus their fp32
+    # issue rate against the FMA peak at the sampled SM clock.
+    tensor_kernel = top["name"].startswith(("mlp", "linear"))
+    intensity = wk["flops"] / max(wk["bytes"], 1)
+    ridge = bf16 * 1e12 / (hbm * 1e9)
+    if tensor_kernel and intensity > ridge * 0.05:
+        ach = wk["flops"] / (avg_ms * 1e-3) / 1e12
+        roof = {"bound": "tensor", "achieved": ach, "peak": bf16, "unit": "TFLOP/s", "frac": ach / bf16}
+    else:
+        ach = wk["bytes"] / (avg_ms * 1e-3) / 1e9
+        roof = {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm}
+        clk_mhz = clk.summary().get("sm_mhz") or 1965.0
+        fma_peak = 148 * 128 * 2 * clk_mhz * 1e6 / 1e12
+        fl = wk["flops"] / (avg_ms * 1e-3) / 1e12
+        roof["fp32"] = {"achieved_tflops": fl, "peak_tflops": fma_peak, "frac": fl / fma_peak,
+                        "peak_source": "148 SMs x 128 FMA/clk x sampled SM clock (derived, not measured)"}
+    traffic = None
+    tp = ROOT / "profiles" / "ncu_traffic.json"
+    if tp.exists():
+        tr = json.loads(tp.read_text())
+        traffic = tr.get(f"{top['name']}/{top['layer']}")
+    roof.update({
+        "traffic": traffic, "kernel": f"{top['name']} layer {top['layer']}",
+        "kernel_share": top["ms"] / tot_prof, "avg_launch_ms": avg_ms,
+        "algorithmic_flops": wk["flops"], "algorithmic_bytes": wk["bytes"], "peak_source": peak_src,
+        "all_kernels_ms_per_step": {f"{r['name']}/{r['layer']}": r["ms"] / max(1, r["count"]) for r in prof},
+    })
+    return roof
+
 # ---------------------------------------------------------------------------
 # B200 arm
 # ---------------------------------------------------------------------------
@@ -321,49 +372,7 @@ def b200_arm(args, rank: int, world: int, local_rank: int):
         return 0
     value = world * N * args.steps / (total_ms / 1e3)
     e2e_value = world * N * args.steps / e2e_s
-    # roofline of the dominant kernel
-    work = kernel_work(model.spec, N, E)
-    peaks = {}
-    pp = ROOT / "MEASURED_PEAKS.json"
-    if pp.exists():
-        peaks = json.loads(pp.read_text())
-    hbm = float(peaks.get("hbm_gbs", 6650.0))
-    bf16 = float(peaks.get("bf16_tflops", 1590.0))
-    peak_src = "measured" if pp.exists() else "fallback"
-    prof.sort(key=lambda r: -r["ms"])
-    tot_prof = sum(r["ms"] for r in prof)
-    top = prof[0]
-    avg_ms = top["ms"] / top["count"]
-    wk = work.get((top["name"], top["layer"]), {"flops": 0, "bytes": 0})
-    # Tensor-core kernels (radial MLP, o3 linears) are compared with the tensor
-    # pipe when their arithmetic intensity is high; the CUDA-core kernels
-    # (conv, symmetric contraction, edge, forces) with HBM, plus their fp32
-    # issue rate against the FMA peak at the sampled SM clock.
-    tensor_kernel = top["name"].startswith(("mlp", "linear"))
-    intensity = wk["flops"] / max(wk["bytes"], 1)
-    ridge = bf16 * 1e12 / (hbm * 1e9)
-    if tensor_kernel and intensity > ridge * 0.05:
-        ach = wk["flops"] / (avg_ms * 1e-3) / 1e12
-        roof = {"bound": "tensor", "achieved": ach, "peak": bf16, "unit": "TFLOP/s", "frac": ach / bf16}
-    else:
-        ach = wk["bytes"] / (avg_ms * 1e-3) / 1e9
-        roof = {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm}
-        clk_mhz = clk.summary().get("sm_mhz") or 1965.0
-        fma_peak = 148 * 128 * 2 * clk_mhz * 1e6 / 1e12
-        fl = wk["flops"] / (avg_ms * 1e-3) / 1e12
-        roof["fp32"] = {"achieved_tflops": fl, "peak_tflops": fma_peak, "frac": fl / fma_peak,
-                        "peak_source": "148 SMs x 128 FMA/clk x sampled SM clock (derived, not measured)"}
-    traffic = None
-    tp = ROOT / "profiles" / "ncu_traffic.json"
-    if tp.exists():
-        tr = json.loads(tp.read_text())
-        traffic = tr.get(f"{top['name']}/{top['layer']}")
-    roof.update({
-        "traffic": traffic, "kernel": f"{top['name']} layer {top['layer']}",
-        "kernel_share": top["ms"] / tot_prof, "avg_launch_ms": avg_ms,
-        "algorithmic_flops": wk["flops"], "algorithmic_bytes": wk["bytes"], "peak_source": peak_src,
-        "all_kernels_ms_per_step": {f"{r['name']}/{r['layer']}": r["ms"] / max(1, r["count"]) for r in prof},
-    })
+    roof = roofline_of(kernel_work(model.spec, N, E), prof, clk)
     cpu = None
     if world == 1:
         try:
@@ -390,6 +399,181 @@ def b200_arm(args, rank: int, world: int, local_rank: int):
     return 0
 
 
+# ---------------------------------------------------------------------------
+# partitioned configurations: c3 (structure sharding), c4 (spatial domains)
+# ---------------------------------------------------------------------------
+C3_WORKLOAD = ("config3: MACE-OFF-medium-like (96x0e+96x1o, lmax3, corr3, 2 layers, r_max 5.0, H/C/N/O) random-init "
+               "seed 3; 512 random-walk molecules of 20-60 atoms (seed 3), non-periodic; energy+forces; molecules "
+               "sharded over the ranks by atom count")
+C4_WORKLOAD = ("config4: medium MACE as config 1 (seed 1); diamond Si 50x50x50 = 1,000,000 atoms rattled 0.05 A "
+               "(seed 4); energy+forces+stress; spatial domains (grid 1x1xN..2x2x2) with 2 r_max + skin = 12.5 A "
+               "ghost shells; positions all-gathered, forces/energy/virial all-reduced (NCCL)")
+
+
+def partition_arm(args, rank: int, world: int, local_rank: int):
+    import torch
+    import torch.distributed as dist
+
+    from mace_mlx_b200.distributed import PositionExchange, SpatialRunner, plan_domain, shard_structures
+    from mace_mlx_b200.model import MACEModel
+    from mace_mlx_b200.spec import ModelSpec
+    from mace_mlx_b200.structures import diamond_si, molecule_batch
+    from mace_mlx_b200.weights import random_config, random_weights
+    from mace_mlx_b200.workmodel import kernel_work
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    if args.config == "c4":
+        st = diamond_si(50, 0.05, 4)
+        config = random_config("medium", z_table=list(range(1, 90)), avg_num_neighbors=AVG_NUM_NEIGHBORS)
+        model = MACEModel(config=config, weights=random_weights(ModelSpec.from_config(config), seed=1), device=dev)
+        runner = SpatialRunner(model, st.numbers, st.cell, world, rank, skin=0.5)
+        pos_global = torch.tensor(st.positions, dtype=torch.float64, device=dev)
+        n_total = len(st)
+        virial = True
+        runner.evaluate(pos_global, virial=True)
+        owned = [plan_domain(st.positions, st.cell, runner.grid, r, runner.ghost_width).owned_index
+                 for r in range(world)] if world > 1 else [np.arange(n_total)]
+        exch = PositionExchange(owned, dev) if world > 1 else None
+        own_idx = torch.as_tensor(owned[rank], device=dev)
+        own_pos = pos_global[own_idx].clone()
+
+        def step():
+            if exch is not None:
+                exch(own_pos, pos_global)
+            out = runner.evaluate(pos_global, virial=True)
+            return runner.reduce(out, n_total, virial=True)
+
+        host_pos = torch.empty(len(owned[rank]), 3, dtype=torch.float64, pin_memory=True)
+        host_pos.copy_(own_pos)
+        host_f = torch.empty(len(owned[rank]), 3, dtype=torch.float32, pin_memory=True)
+
+        def step_e2e():
+            own_pos.copy_(host_pos, non_blocking=True)
+            if exch is None:
+                pos_global.copy_(own_pos)
+            res = step()
+            host_f.copy_(res["forces"][own_idx], non_blocking=True)
+            e = res["energy"].item()  # synchronises
+            return e
+
+        h2d, d2h = len(owned[rank]) * 24, len(owned[rank]) * 12 + 8
+        n_local, e_local = runner.plan.n_local, runner.edges.n_edges
+        workload, scaling = C4_WORKLOAD, "strong"
+        parallel = f"spatial domains {runner.grid[0]}x{runner.grid[1]}x{runner.grid[2]}"
+        prof_model, prof_n, prof_e = model, n_local, e_local
+    else:
+        st_all = molecule_batch(512, 3)
+        config = random_config("medium", hidden_irreps="96x0e + 96x1o", r_max=5.0, z_table=[1, 6, 7, 8],
+                               avg_num_neighbors=12.0)
+        model = MACEModel(config=config, weights=random_weights(ModelSpec.from_config(config), seed=3), device=dev)
+        sizes = np.bincount(st_all.batch)
+        mine = shard_structures(sizes, world)[rank]
+        sel = np.isin(st_all.batch, mine)
+        remap = {g: k for k, g in enumerate(mine)}
+        batch = np.array([remap[g] for g in st_all.batch[sel]], dtype=np.int64)
+        gp = torch.as_tensor(np.concatenate([[0], np.cumsum(np.bincount(batch, minlength=len(mine)))]).astype(np.int32),
+                             device=dev)
+        pos64 = torch.tensor(st_all.positions[sel], dtype=torch.float64, device=dev)
+        edges = model.neighbour_list(pos64, None, (False, False, False), gp, model.r_max + 0.5)
+        species = torch.as_tensor(model.species_index(st_all.numbers[sel]), device=dev)
+        pos32 = pos64.float()
+        n_total = len(st_all)
+        virial = False
+        state = {"out": None}
+
+        def step():
+            state["out"] = model.evaluate(pos32, None, species, gp, edges, forces=True, out=state["out"], graph=True)
+            return state["out"]
+
+        host_pos = torch.empty(pos32.shape, dtype=torch.float32, pin_memory=True)
+        host_pos.copy_(pos32)
+        host_f = torch.empty(pos32.shape, dtype=torch.float32, pin_memory=True)
+        host_e = torch.empty(len(mine), dtype=torch.float64, pin_memory=True)
+
+        def step_e2e():
+            pos32.copy_(host_pos, non_blocking=True)
+            out = step()
+            host_f.copy_(out["forces"], non_blocking=True)
+            host_e.copy_(out["energy"], non_blocking=True)
+            torch.cuda.current_stream(dev).synchronize()
+            return float(host_e.sum())
+
+        h2d, d2h = pos32.numel() * 4, pos32.numel() * 4 + len(mine) * 8
+        workload, scaling = C3_WORKLOAD, "strong"
+        parallel = f"structure-sharded over {world} ranks ({len(mine)} molecules, {int(sel.sum())} atoms on rank 0)"
+        prof_model, prof_n, prof_e = model, int(sel.sum()), edges.n_edges
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    barrier()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with ClockSampler(local_rank) as clk:
+        barrier()
+        for k in range(args.steps):
+            ev[k][0].record()
+            step()
+            ev[k][1].record()
+        barrier()
+    total_ms = float(sum(a.elapsed_time(b) for a, b in ev))
+    launches = prof_model.last_launch_count()
+    for _ in range(max(1, args.warmup // 2)):
+        step_e2e()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step_e2e()
+    barrier()
+    e2e_s = time.perf_counter() - t0
+    prof_model.profile_enable(True)
+    for _ in range(min(args.steps, 3)):
+        step()
+    torch.cuda.synchronize(dev)
+    prof = prof_model.profile_read()
+    prof_model.profile_enable(False)
+    if world > 1:
+        tt = torch.tensor([total_ms, e2e_s], dtype=torch.float64, device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        total_ms, e2e_s = float(tt[0]), float(tt[1])
+    if rank != 0:
+        return 0
+    value = n_total * args.steps / (total_ms / 1e3)
+    roof = roofline_of(kernel_work(prof_model.spec, prof_n, prof_e), prof, clk)
+    cpu = None
+    if world == 1:
+        try:
+            with tempfile.TemporaryDirectory() as tmp:
+                md = make_model_dir(tmp)
+                v, threads, n, t = time_cpu_port(make_structure(0), md, args.cpu_seconds, 3)
+            cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
+                   "sample": f"{n} full 1000-atom Si steps of the medium model (median {t:.2f} s) of the torch-CPU "
+                             f"fp32 oracle port; the per-atom rate stands in for this workload"}
+        except Exception as e:  # noqa: BLE001
+            cpu = {"value": None, "unit": UNIT, "cores": os.cpu_count(), "kind": "port", "sample": f"failed: {e}"}
+    line = {
+        "metric": f"energy+forces atom-steps/s, {args.config}", "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+        "scaling": scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": workload, "n_atoms_total": n_total, "n_local_atoms_rank0": prof_n,
+                   "n_edges_rank0": prof_e, "parallelism": parallel,
+                   "l2": "inputs larger than L2 (c4)" if args.config == "c4" else "no flush (sub-L2 shards)"},
+        "e2e": {"value": n_total * args.steps / e2e_s, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_s * 1e3 / args.steps},
+        "gpu_launches": launches * args.steps,
+        "clocks": clk.summary(),
+        "roofline": roof,
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -404,9 +588,11 @@ def main():
         import torch.distributed as dist
 
         torch.cuda.set_device(local_rank)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
     try:
+        if args.config in ("c3", "c4"):
+            return partition_arm(args, rank, world, local_rank)
         return b200_arm(args, rank, world, local_rank)
     finally:
         if world > 1:
