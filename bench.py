@@ -244,7 +244,15 @@ def reference_arm(args, rank: int, world: int):
 # ---------------------------------------------------------------------------
 # roofline of the dominant kernel of a profiled step
 # ---------------------------------------------------------------------------
-def roofline_of(work: dict, prof: list[dict], clk) -> dict:
+def roofline_of(work: dict, prof: list[dict], clk, steps: int, traffic_file: bool = True) -> dict:
+    """Roofline of the kernel with the largest share of `steps` profiled steps.
+
+    ``work`` holds one step's algorithmic FLOPs and bytes per (kernel, layer);
+    the kernel's time per step is its event-timed total over the steps, so a
+    kernel launched once per receiver chunk is compared with its whole work.
+    ``traffic`` (ncu DRAM bytes per launch) is filled from
+    profiles/ncu_traffic.json, which was captured on the headline workload.
+    """
     peaks = {}
     pp = ROOT / "MEASURED_PEAKS.json"
     if pp.exists():
@@ -255,7 +263,7 @@ def roofline_of(work: dict, prof: list[dict], clk) -> dict:
     prof = sorted(prof, key=lambda r: -r["ms"])
     tot_prof = sum(r["ms"] for r in prof)
     top = prof[0]
-    avg_ms = top["ms"] / top["count"]
+    avg_ms = top["ms"] / max(1, steps)
     wk = work.get((top["name"], top["layer"]), {"flops": 0, "bytes": 0})
     # Tensor-core kernels (radial MLP, o3 linears) are compared with the tensor
     # pipe when their arithmetic intensity is high; the CUDA-core kernels
@@ -277,14 +285,15 @@ def roofline_of(work: dict, prof: list[dict], clk) -> dict:
                         "peak_source": "148 SMs x 128 FMA/clk x sampled SM clock (derived, not measured)"}
     traffic = None
     tp = ROOT / "profiles" / "ncu_traffic.json"
-    if tp.exists():
+    if traffic_file and tp.exists():
         tr = json.loads(tp.read_text())
         traffic = tr.get(f"{top['name']}/{top['layer']}")
     roof.update({
         "traffic": traffic, "kernel": f"{top['name']} layer {top['layer']}",
-        "kernel_share": top["ms"] / tot_prof, "avg_launch_ms": avg_ms,
+        "kernel_share": top["ms"] / tot_prof, "avg_launch_ms": top["ms"] / top["count"],
+        "kernel_ms_per_step": avg_ms,
         "algorithmic_flops": wk["flops"], "algorithmic_bytes": wk["bytes"], "peak_source": peak_src,
-        "all_kernels_ms_per_step": {f"{r['name']}/{r['layer']}": r["ms"] / max(1, r["count"]) for r in prof},
+        "all_kernels_ms_per_step": {f"{r['name']}/{r['layer']}": r["ms"] / max(1, steps) for r in prof},
     })
     return roof
 
@@ -372,7 +381,7 @@ def b200_arm(args, rank: int, world: int, local_rank: int):
         return 0
     value = world * N * args.steps / (total_ms / 1e3)
     e2e_value = world * N * args.steps / e2e_s
-    roof = roofline_of(kernel_work(model.spec, N, E), prof, clk)
+    roof = roofline_of(kernel_work(model.spec, N, E), prof, clk, args.steps)
     cpu = None
     if world == 1:
         try:
@@ -532,7 +541,8 @@ def partition_arm(args, rank: int, world: int, local_rank: int):
     barrier()
     e2e_s = time.perf_counter() - t0
     prof_model.profile_enable(True)
-    for _ in range(min(args.steps, 3)):
+    prof_steps = min(args.steps, 3)
+    for _ in range(prof_steps):
         step()
     torch.cuda.synchronize(dev)
     prof = prof_model.profile_read()
@@ -544,7 +554,7 @@ def partition_arm(args, rank: int, world: int, local_rank: int):
     if rank != 0:
         return 0
     value = n_total * args.steps / (total_ms / 1e3)
-    roof = roofline_of(kernel_work(prof_model.spec, prof_n, prof_e), prof, clk)
+    roof = roofline_of(kernel_work(prof_model.spec, prof_n, prof_e), prof, clk, prof_steps, traffic_file=False)
     cpu = None
     if world == 1:
         try:
