@@ -309,10 +309,12 @@ struct NlParams {
   int32_t* shifts;
   int32_t* rev;
   int* err_flag;
-  // cell lists (mode 1: periodic along all axes, bins in wrapped fractional
-  // coordinates; mode 2: open along all axes, bins over the Cartesian box);
-  // mode 0 tests every pair of a graph
+  // cell lists (mode 1) or every pair of a graph (mode 0).  Bin coordinates
+  // are fractional when the system has a cell (use_frac), else Cartesian;
+  // periodic axes bin the wrapped coordinate in [0, 1) and wrap around, open
+  // axes bin [origin, origin + nbin / inv_binw) and end there.
   int mode;
+  int use_frac;
   int nbin[3];
   double origin[3], inv_binw[3];
   int32_t* atom_bin;   // (n)

@@ -178,8 +178,9 @@ __global__ void k_nl_rev(NlParams p, int64_t E) {
 }
 
 // ---------------------------------------------------------------------------
-// cell lists (one graph): atoms binned with bins at least the cutoff wide, so
-// every neighbour of an atom lies in the 27 bins around its own; the same
+// cell lists (one graph): atoms binned with bins at least one cutoff wide (in
+// fractional units, r_cut / plane spacing), so every neighbour of an atom lies
+// in the 27 bins around its own; periodic axes wrap, open axes end.  The same
 // float64 distance test decides, so the edge set equals the all-pairs one.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ double frac_wrapped(const NlParams& p, int64_t i, int d) {
@@ -187,9 +188,14 @@ __device__ __forceinline__ double frac_wrapped(const NlParams& p, int64_t i, int
          p.pos[3 * i + 2] * p.inv_cell[2 * 3 + d] - p.wrap[3 * i + d];
 }
 
+__device__ __forceinline__ double bin_space(const NlParams& p, int64_t i, int d) {
+  return p.use_frac ? frac_wrapped(p, i, d) : p.pos[3 * i + d];
+}
+
 __device__ __forceinline__ int bin_coord(const NlParams& p, int64_t i, int d) {
-  double t = (p.mode == 1) ? frac_wrapped(p, i, d) * p.nbin[d] : (p.pos[3 * i + d] - p.origin[d]) * p.inv_binw[d];
-  int b = (int)floor(t);
+  const double x = bin_space(p, i, d);
+  const double t = p.pbc[d] ? x * p.nbin[d] : (x - p.origin[d]) * p.inv_binw[d];
+  const int b = (int)floor(t);
   return b < 0 ? 0 : (b >= p.nbin[d] ? p.nbin[d] - 1 : b);
 }
 
@@ -226,7 +232,7 @@ __device__ __forceinline__ void cl_candidates(const NlParams& p, int64_t j, int 
         for (int d = 0; d < 3; ++d) {
           int v = bj[d] + dd[d];
           k[d] = 0;
-          if (p.mode == 1) {
+          if (p.pbc[d]) {
             if (v < 0) { v += p.nbin[d]; k[d] = -1; }
             else if (v >= p.nbin[d]) { v -= p.nbin[d]; k[d] = 1; }
           } else if (v < 0 || v >= p.nbin[d]) {
@@ -242,7 +248,7 @@ __device__ __forceinline__ void cl_candidates(const NlParams& p, int64_t j, int 
           const bool valid = q < s1;
           const int64_t i = valid ? p.bin_atoms[q] : j;
           int S[3];
-          for (int d = 0; d < 3; ++d) S[d] = (p.mode == 1) ? p.wrap[3 * i + d] - p.wrap[3 * j + d] - k[d] : 0;
+          for (int d = 0; d < 3; ++d) S[d] = p.pbc[d] ? p.wrap[3 * i + d] - p.wrap[3 * j + d] - k[d] : 0;
           f(valid, i, S);
         }
       }
@@ -299,13 +305,14 @@ __global__ void __launch_bounds__(256) k_nl_cl_fill(NlParams p) {
   }
 }
 
-// bounding box of the positions: out6 = (min x, min y, min z, max x, max y, max z)
+// bounding box of the bin coordinates (fractional with a cell, else Cartesian):
+// out6 = (min 0, min 1, min 2, max 0, max 1, max 2)
 __global__ void __launch_bounds__(1024) k_nl_bbox(NlParams p, double* out6) {
   __shared__ double red[6][32];
   double lo[3] = {1e300, 1e300, 1e300}, hi[3] = {-1e300, -1e300, -1e300};
   for (int64_t i = threadIdx.x; i < p.n; i += blockDim.x)
     for (int d = 0; d < 3; ++d) {
-      const double x = p.pos[3 * i + d];
+      const double x = bin_space(p, i, d);
       lo[d] = fmin(lo[d], x);
       hi[d] = fmax(hi[d], x);
     }

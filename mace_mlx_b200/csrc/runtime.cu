@@ -662,56 +662,52 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
 // ===========================================================================
 namespace {
 
-// Cell-list geometry for one graph of n atoms (p.reach set for periodic
-// axes): mode 1 when every axis is periodic and at least 3 bins of one reach
-// fit per axis, mode 2 when no axis is periodic (bins over the bounding box,
-// read back from the device); otherwise 0 (all pairs).
+// Cell-list geometry for one graph of n atoms (p.reach and the inverse cell set
+// when any axis is periodic; wraps computed): bins per axis at least one reach
+// wide, at least 3 along periodic axes (else all pairs), over the wrapped
+// [0, 1) range along periodic axes and the atoms' range along open ones
+// (fractional with a cell, Cartesian without).
 int nl_choose_mode(mace_ctx* c, NlParams& p, bool any_pbc, int32_t num_graphs, int64_t n, cudaStream_t s) {
   // all pairs are cheaper for small graphs; MACE_B200_NL_CELL_MIN overrides the 2048-atom threshold
   const char* env = std::getenv("MACE_B200_NL_CELL_MIN");
   const int64_t cl_min = env ? std::atoll(env) : 2048;
   p.mode = 0;
   if (num_graphs != 1 || n < cl_min) return MACE_OK;
-  const bool all_pbc = p.pbc[0] && p.pbc[1] && p.pbc[2];
-  int64_t nb[3] = {1, 1, 1};
-  if (all_pbc) {
-    for (int d = 0; d < 3; ++d) {
-      nb[d] = (int64_t)std::floor(1.0 / p.reach[d]);
+  p.use_frac = any_pbc ? 1 : 0;
+  p.mode = 1;  // bin_space reads use_frac; set before the bounding box
+  TRY(launch_nl_bbox(p, c->nl_bbox, s));
+  double bb[6];
+  MACE_CUDA_TRY(cudaMemcpyAsync(bb, c->nl_bbox, sizeof(bb), cudaMemcpyDeviceToHost, s));
+  MACE_CUDA_TRY(cudaStreamSynchronize(s));
+  p.mode = 0;
+  int64_t nb[3];
+  double ext[3];
+  for (int d = 0; d < 3; ++d) {
+    const double unit = any_pbc ? p.reach[d] : p.r_cut;  // one cutoff in bin coordinates
+    if (p.pbc[d]) {
+      nb[d] = (int64_t)std::floor(1.0 / unit);
       if (nb[d] < 3) return MACE_OK;
-    }
-  } else if (!any_pbc) {
-    TRY(launch_nl_bbox(p, c->nl_bbox, s));
-    double bb[6];
-    MACE_CUDA_TRY(cudaMemcpyAsync(bb, c->nl_bbox, sizeof(bb), cudaMemcpyDeviceToHost, s));
-    MACE_CUDA_TRY(cudaStreamSynchronize(s));
-    for (int d = 0; d < 3; ++d) {
-      const double ext = bb[3 + d] - bb[d];
-      nb[d] = (int64_t)std::floor(ext / p.r_cut);
+      ext[d] = 1.0;
+    } else {
+      ext[d] = bb[3 + d] - bb[d];
+      nb[d] = (int64_t)std::floor(ext[d] / unit);
       if (nb[d] < 1) nb[d] = 1;
       p.origin[d] = bb[d];
     }
-  } else {
-    return MACE_OK;
   }
   // at most nl_bin_cap bins: merge bins along the longest axis (bins only widen)
-  const int64_t floor_nb = all_pbc ? 3 : 1;
   while (nb[0] * nb[1] * nb[2] > c->nl_bin_cap) {
     int d = 0;
     for (int q = 1; q < 3; ++q) d = nb[q] > nb[d] ? q : d;
+    const int64_t floor_nb = p.pbc[d] ? 3 : 1;
     if (nb[d] <= floor_nb) return MACE_OK;
-    nb[d] = nb[d] - 1 > floor_nb ? (nb[d] * 3) / 4 : floor_nb;
+    nb[d] = (nb[d] * 3) / 4 > floor_nb ? (nb[d] * 3) / 4 : floor_nb;
   }
-  for (int d = 0; d < 3; ++d) p.nbin[d] = (int)nb[d];
-  if (!all_pbc) {
-    double bb[6];
-    MACE_CUDA_TRY(cudaMemcpyAsync(bb, c->nl_bbox, sizeof(bb), cudaMemcpyDeviceToHost, s));
-    MACE_CUDA_TRY(cudaStreamSynchronize(s));
-    for (int d = 0; d < 3; ++d) {
-      const double ext = bb[3 + d] - bb[d];
-      p.inv_binw[d] = ext > 0.0 ? (double)nb[d] / ext : 0.0;
-    }
+  for (int d = 0; d < 3; ++d) {
+    p.nbin[d] = (int)nb[d];
+    p.inv_binw[d] = (!p.pbc[d] && ext[d] > 0.0) ? (double)nb[d] / ext[d] : 0.0;
   }
-  p.mode = all_pbc ? 1 : 2;
+  p.mode = 1;
   p.atom_bin = c->nl_atom_bin;
   p.bin_start = c->nl_bin_start;
   p.bin_fill = c->nl_bin_fill;
@@ -772,8 +768,8 @@ int nl_build(mace_ctx* c, const double* pos, const double* cell, const int32_t* 
   p.err_flag = c->d_err;
   p.node_graph = c->nl_graph;
   p.wrap = c->nl_wrap;
-  if (allow_cells) TRY(nl_choose_mode(c, p, any_pbc, num_graphs, n, s));
   TRY(launch_nl_prep(p, c->nl_graph, c->nl_wrap, s));
+  if (allow_cells) TRY(nl_choose_mode(c, p, any_pbc, num_graphs, n, s));
   if (p.mode) {
     TRY(launch_nl_bins(p, c->scan_tmp, c->scan_bytes, s));
     TRY(launch_nl_cl_count(p, s));

@@ -72,13 +72,18 @@ def shard_structures(sizes, world: int) -> list[list[int]]:
 
 @dataclass
 class DomainPlan:
-    """Local atoms of one rank: owned first (ascending global index), then ghosts."""
+    """Local atoms of one rank: owned first (ascending global index), then ghosts.
+
+    The local system stays periodic along the axes the grid does not split
+    (``pbc``) and is open along the split ones, where the ghosts are.
+    """
 
     rank: int
     grid: tuple[int, int, int]
     local_index: np.ndarray  # (n_local,) int64 global atom of each local atom
     local_shift: np.ndarray  # (n_local, 3) int64: local position = pos[g] + shift @ cell
     n_owned: int
+    pbc: tuple[bool, bool, bool] = (False, False, False)
 
     @property
     def n_local(self) -> int:
@@ -101,10 +106,11 @@ def plan_domain(positions: np.ndarray, cell: np.ndarray, grid: tuple[int, int, i
     """Owned atoms and ghost images of domain `rank` of a fully periodic cell.
 
     Domain (ix, iy, iz) with rank = (ix * py + iy) * pz + iz covers fractional
-    coordinates [i_d / p_d, (i_d + 1) / p_d) of the wrapped positions; ghosts
-    are the images (shift k in {-1, 0, 1}^3) of all atoms whose wrapped
-    fractional coordinates fall within ghost_width / spacing_d of it along
-    every axis and are not owned copies.
+    coordinates [i_d / p_d, (i_d + 1) / p_d) of the wrapped positions.  Along
+    the split axes (p_d > 1) the ghosts are the images (shift k_d in
+    {-1, 0, 1}) of all atoms whose wrapped fractional coordinate falls within
+    ghost_width / spacing_d of the domain, owned copies excluded; the unsplit
+    axes stay periodic in the local system and need no ghosts.
     """
     pos = np.asarray(positions, dtype=np.float64)
     cell = np.asarray(cell, dtype=np.float64)
@@ -120,15 +126,17 @@ def plan_domain(positions: np.ndarray, cell: np.ndarray, grid: tuple[int, int, i
     owned_mask = np.all(idx3 == me, axis=1)
     lo = me / p
     hi = (me + 1) / p
+    split = p > 1
     gw = ghost_width / plane_spacings(cell)
-    if np.any(gw >= 1.0):
+    if np.any(gw[split] >= 1.0):
         # images with |k| > 1 would be needed
         raise ValueError(f"cell thinner than the {ghost_width:.2f} A ghost shell")
     owned = np.nonzero(owned_mask)[0]
     ghosts, shifts = [], []
-    for k in np.array(np.meshgrid([-1, 0, 1], [-1, 0, 1], [-1, 0, 1], indexing="ij")).reshape(3, -1).T:
+    ks = [[-1, 0, 1] if split[d] else [0] for d in range(3)]
+    for k in np.array(np.meshgrid(*ks, indexing="ij")).reshape(3, -1).T:
         uk = u + k
-        inside = np.all((uk >= lo - gw) & (uk < hi + gw), axis=1)
+        inside = np.all(((uk >= lo - gw) & (uk < hi + gw)) | ~split, axis=1)
         if not np.any(k):
             inside &= ~owned_mask
         sel = np.nonzero(inside)[0]
@@ -141,7 +149,8 @@ def plan_domain(positions: np.ndarray, cell: np.ndarray, grid: tuple[int, int, i
     local_index = np.concatenate([owned, ghosts_a]).astype(np.int64)
     # local position = pos[g] + (k - w_g) @ cell  (the image of the wrapped atom)
     local_shift = np.concatenate([-w[owned], shifts_a - w[ghosts_a]]).astype(np.int64)
-    return DomainPlan(rank, tuple(int(x) for x in p), local_index, local_shift, len(owned))
+    return DomainPlan(rank, tuple(int(x) for x in p), local_index, local_shift, len(owned),
+                      tuple(bool(not x) for x in split))
 
 
 class SpatialRunner:
@@ -155,7 +164,6 @@ class SpatialRunner:
 
     def __init__(self, model, numbers, cell, world: int, rank: int, *, skin: float = 0.5, group=None,
                  ghost_width: float | None = None):
-        # world == 1 evaluates the periodic cell directly (owned = all, no ghosts)
         import torch
 
         self.model = model
@@ -178,25 +186,22 @@ class SpatialRunner:
     def _rebuild(self, pos_global64):
         torch = self.torch
         dev = self.dev
-        n = pos_global64.shape[0]
-        if self.world == 1:
-            # one domain: the periodic structure itself, no ghosts
-            self.plan = DomainPlan(0, (1, 1, 1), np.arange(n, dtype=np.int64), np.zeros((n, 3), np.int64), n)
-            self.weight = None
-            pbc, cell = (True, True, True), self.cell_dev
-        else:
-            self.plan = plan_domain(pos_global64.cpu().numpy(), self.cell, self.grid, self.rank, self.ghost_width)
-            self.weight = torch.zeros(self.plan.n_local, dtype=torch.float32, device=dev)
-            self.weight[: self.plan.n_owned] = 1.0
-            pbc, cell = (False, False, False), None
+        self.plan = plan_domain(pos_global64.cpu().numpy(), self.cell, self.grid, self.rank, self.ghost_width)
         pl = self.plan
+        if pl.n_local == pl.n_owned:  # one domain: the periodic structure itself
+            self.weight = None
+        else:
+            self.weight = torch.zeros(pl.n_local, dtype=torch.float32, device=dev)
+            self.weight[: pl.n_owned] = 1.0
+        pbc = pl.pbc
+        cell = self.cell_dev if any(pbc) else None
         self.li = torch.as_tensor(pl.local_index, device=dev)
         self.ls = torch.as_tensor(pl.local_shift, dtype=torch.float64, device=dev)
         self.species = torch.as_tensor(self.species_all[pl.local_index], device=dev)
         self.graph_ptr = torch.tensor([0, pl.n_local], dtype=torch.int32, device=dev)
         loc = self._local(pos_global64)
         self.edges = self.model.neighbour_list(loc, cell, pbc, self.graph_ptr, self.r_cut, edges=self.edges)
-        self.cell32 = self.cell_dev.float() if self.world == 1 else None
+        self.cell32 = self.cell_dev.float() if any(pbc) else None
         self.ref_pos = loc.clone()
         self.out = None
 

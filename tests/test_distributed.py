@@ -47,21 +47,25 @@ def test_plan_partitions_atoms_and_covers_the_receptive_field(world):
     # every image within gw of an owned atom is local, at the right shift
     i, j, S = neighbour_list(pos, st.cell, st.pbc, gw)
     for p in plans:
-        local = {(int(g), tuple(s)) for g, s in zip(p.local_index, p.local_shift)}
+        split = ~np.asarray(p.pbc)
+        assert split.sum() == sum(g > 1 for g in p.grid)
+        full = {(int(g), tuple(s)) for g, s in zip(p.local_index, p.local_shift)}
+        assert len(full) == p.n_local  # no image twice
+        # periodic (unsplit) axes wrap in the local system: only split-axis shifts must match
+        local = {(int(g), tuple(s[split])) for g, s in zip(p.local_index, p.local_shift)}
         own_shift = {int(g): s for g, s in zip(p.owned_index, p.local_shift[: p.n_owned])}
         for a, b, s in zip(i, j, S):
             if int(b) in own_shift:  # receiver b owned: the sender's image pos_a - S @ cell, in b's frame
-                need = tuple((own_shift[int(b)] - s).tolist())
+                need = tuple((own_shift[int(b)] - s)[split].tolist())
                 assert (int(a), need) in local
-        assert len(local) == p.n_local  # no image twice
     assert np.all(gw / plane_spacings(st.cell) < 1)
 
 
-def _weighted_oracle(orc, pos, species, weight, r_cut):
-    i, j, S = neighbour_list(pos, np.zeros((3, 3)), np.zeros(3, dtype=bool), r_cut)
+def _weighted_oracle(orc, pos, cell, pbc, species, weight, r_cut):
+    i, j, S = neighbour_list(pos, cell, np.asarray(pbc), r_cut)
     p = torch.tensor(pos, dtype=torch.float64, requires_grad=True)
     snd, rcv = torch.as_tensor(i), torch.as_tensor(j)
-    v = p[rcv] - p[snd]
+    v = p[rcv] - p[snd] + torch.as_tensor(S, dtype=torch.float64) @ torch.as_tensor(cell, dtype=torch.float64)
     r = torch.sqrt(torch.clamp((v * v).sum(-1, keepdim=True), min=1e-24))
     _, node_e = orc.energy_from_vectors(v, r, torch.as_tensor(species, dtype=torch.long), snd, rcv, None, 1)
     e = (node_e * torch.as_tensor(weight, dtype=torch.float64)).sum()
@@ -90,7 +94,7 @@ def _rank_main(rank, world, port, path, case):
         species = np.zeros(plan.n_local, dtype=np.int64)  # z_table [14]
         weight = np.zeros(plan.n_local)
         weight[: plan.n_owned] = 1.0
-        e, f, vir = _weighted_oracle(orc, loc, species, weight, config["r_max"])
+        e, f, vir = _weighted_oracle(orc, loc, st.cell, plan.pbc, species, weight, config["r_max"])
         out = {"energy": e.reshape(1), "forces": f, "virial": vir.reshape(9)}
         res = reduce_local(plan.local_index, out, len(st), world, virial=True)
         if rank == 0:

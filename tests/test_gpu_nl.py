@@ -123,7 +123,8 @@ def _sheared(st: Structure, shear: float) -> Structure:
     return dataclasses.replace(st, positions=st.positions @ M, cell=st.cell @ M)
 
 
-@pytest.mark.parametrize("case", ["periodic", "periodic_r65", "triclinic", "wrapped", "open_cluster"])
+@pytest.mark.parametrize("case", ["periodic", "periodic_r65", "triclinic", "wrapped", "open_cluster", "slab",
+                                  "wire"])
 def test_cell_list_against_oracle(model, monkeypatch, case):
     """Cell lists forced on (threshold 1 atom): bit-exact edge set against the oracle."""
     monkeypatch.setenv("MACE_B200_NL_CELL_MIN", "1")
@@ -138,10 +139,14 @@ def test_cell_list_against_oracle(model, monkeypatch, case):
         st = dataclasses.replace(st, positions=st.positions + k @ st.cell)
     elif case == "open_cluster":
         st = dataclasses.replace(st, pbc=np.zeros(3, dtype=bool))
+    elif case == "slab":  # periodic in x, y; open in z (a domain of a split along z)
+        st = dataclasses.replace(_sheared(st, 0.2), pbc=np.array([True, True, False]))
+    elif case == "wire":
+        st = dataclasses.replace(st, pbc=np.array([True, False, False]))
     check_edges(model, st, r)
 
 
-@pytest.mark.parametrize("pbc", [(True, True, True), (False, False, False)])
+@pytest.mark.parametrize("pbc", [(True, True, True), (False, False, False), (True, True, False)])
 def test_cell_list_equals_all_pairs_on_large_systems(model, monkeypatch, pbc):
     """4096 atoms (cell lists by default) against the all-pairs kernels, array for array."""
     st = dataclasses.replace(diamond_si(8, 0.05, 12), pbc=np.array(pbc))
