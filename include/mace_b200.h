@@ -51,7 +51,7 @@ extern "C" {
 #define MACE_ERR_UNSUPPORTED 6
 #define MACE_ERR_EDGES 7
 
-#define MACE_ABI_VERSION 5
+#define MACE_ABI_VERSION 6
 
 /* limits of the packed model description */
 #define MACE_MAX_LAYERS 4
@@ -185,6 +185,23 @@ typedef struct {
   const int32_t* ints; int64_t n_ints;
 } mace_model_desc;
 
+/*
+ * Halo exchange between interaction layers (spatial domain decomposition).
+ * Called on the host, in stream order, with the device rows of all nodes
+ * (row_len floats per node, node-major) and the stream of the step:
+ *   phase MACE_HALO_FEATURES:  after layer `layer` produced its node features;
+ *     the callee overwrites the ghost rows with their owners' rows.
+ *   phase MACE_HALO_GRADIENTS: after the backward produced the gradient of the
+ *     energy w.r.t. the input features of layer `layer` + 1; the callee adds
+ *     the ghost rows into their owners' rows (on the owning ranks) and zeroes
+ *     the ghost rows.
+ * Return 0, or non-zero to abort the step (reported as MACE_ERR_NCCL).
+ * Not used under MACE_USE_GRAPH.
+ */
+#define MACE_HALO_FEATURES 0
+#define MACE_HALO_GRADIENTS 1
+typedef int (*mace_halo_fn)(void* user, int32_t phase, int32_t layer, float* rows, int64_t row_len, void* stream);
+
 /* Device pointers describing one (batch of) structure(s). */
 typedef struct {
   int64_t n_nodes;
@@ -211,6 +228,9 @@ typedef struct {
   int32_t n_chunks;
   const int64_t* chunk_nodes;
   const int64_t* chunk_edges;
+  /* halo exchange between layers, or NULL (see mace_halo_fn) */
+  mace_halo_fn halo;
+  void* halo_user;
 } mace_system;
 
 /* Device pointers receiving the results (NULL = not wanted). */

@@ -559,6 +559,10 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
     rp.dscale = dscale;
     rp.weight = sys->energy_weight;
     LAUNCH("readout", t, launch_readout(rp, s));
+    if (sys->halo && t + 1 < T) {
+      if (sys->halo(sys->halo_user, MACE_HALO_FEATURES, t, c->h[t + 1], L.hid.dim, s) != 0)
+        return fail(MACE_ERR_NCCL, "halo exchange of node features failed");
+    }
   }
   {
     EnergyParams p{};
@@ -633,6 +637,9 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
         SkipParams sp = skip_params(c, t, N, sys->species, true, L.in, L.hid, c->dh[t + 1], c->dh[t], 1);
         LAUNCH("skip_bwd", t, launch_skip(sp, s));
       }
+      // dh[t]: gradient w.r.t. the features layer t - 1 produced
+      if (sys->halo && sys->halo(sys->halo_user, MACE_HALO_GRADIENTS, t - 1, c->dh[t], L.in.dim, s) != 0)
+        return fail(MACE_ERR_NCCL, "halo reduction of feature gradients failed");
     }
   }
   int n_blocks = (int)((E + 255) / 256);
@@ -922,7 +929,7 @@ int mace_forward_backward(mace_ctx* c, const mace_system* sys, const mace_output
   DeviceGuard g(c->device);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int base_flags = flags & ~MACE_USE_GRAPH;
-  if (!(flags & MACE_USE_GRAPH) || c->prof_on) return forward_backward(c, sys, out, base_flags, s);
+  if (!(flags & MACE_USE_GRAPH) || c->prof_on || sys->halo) return forward_backward(c, sys, out, base_flags, s);
   mace_outputs o{};
   if (out) o = *out;
   std::vector<int64_t> chunk_key;

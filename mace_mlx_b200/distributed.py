@@ -101,6 +101,16 @@ def plane_spacings(cell: np.ndarray) -> np.ndarray:
     return np.array([vol / np.linalg.norm(np.cross(cell[(d + 1) % 3], cell[(d + 2) % 3])) for d in range(3)])
 
 
+def domain_of(positions: np.ndarray, cell: np.ndarray, grid: tuple[int, int, int]) -> np.ndarray:
+    """Owning rank of every atom: (ix * py + iy) * pz + iz of its wrapped fractional position."""
+    f = np.asarray(positions, dtype=np.float64) @ np.linalg.inv(np.asarray(cell, dtype=np.float64))
+    u = f - np.floor(f)
+    u = np.where(u >= 1.0, 0.0, u)
+    p = np.asarray(grid)
+    idx3 = np.minimum((u * p).astype(np.int64), p - 1)
+    return (idx3[:, 0] * p[1] + idx3[:, 1]) * p[2] + idx3[:, 2]
+
+
 def plan_domain(positions: np.ndarray, cell: np.ndarray, grid: tuple[int, int, int], rank: int,
                 ghost_width: float) -> DomainPlan:
     """Owned atoms and ghost images of domain `rank` of a fully periodic cell.
@@ -163,7 +173,10 @@ class SpatialRunner:
     """
 
     def __init__(self, model, numbers, cell, world: int, rank: int, *, skin: float = 0.5, group=None,
-                 ghost_width: float | None = None):
+                 ghost_width: float | None = None, halo: bool = True):
+        """halo=True: ghost shell r_max + skin and node features exchanged between
+        layers (HaloExchange); halo=False: ghost shell 2 r_max + skin, no exchange
+        between layers (each rank recomputes its ghosts' first layer)."""
         import torch
 
         self.model = model
@@ -174,7 +187,10 @@ class SpatialRunner:
         self.numbers = np.asarray(numbers)
         self.species_all = model.species_index(self.numbers)
         self.skin = float(skin)
-        self.ghost_width = float(ghost_width if ghost_width is not None else 2 * model.r_max + self.skin)
+        self.use_halo = bool(halo) and world > 1 and model.spec.num_interactions > 1
+        layers = 1 if self.use_halo else model.spec.num_interactions
+        self.ghost_width = float(ghost_width if ghost_width is not None else layers * model.r_max + self.skin)
+        self.halo = None
         self.r_cut = model.r_max + self.skin
         self.plan: DomainPlan | None = None
         self.edges = None
@@ -186,8 +202,11 @@ class SpatialRunner:
     def _rebuild(self, pos_global64):
         torch = self.torch
         dev = self.dev
-        self.plan = plan_domain(pos_global64.cpu().numpy(), self.cell, self.grid, self.rank, self.ghost_width)
+        pos_host = pos_global64.cpu().numpy()
+        self.plan = plan_domain(pos_host, self.cell, self.grid, self.rank, self.ghost_width)
         pl = self.plan
+        if self.use_halo:
+            self.halo = HaloExchange(pl, domain_of(pos_host, self.cell, self.grid), self.world, dev, self.group)
         if pl.n_local == pl.n_owned:  # one domain: the periodic structure itself
             self.weight = None
         else:
@@ -230,7 +249,8 @@ class SpatialRunner:
                 self._rebuild(pos_global64)
         loc = self._local(pos_global64)
         self.out = self.model.evaluate(loc.float(), self.cell32, self.species, self.graph_ptr, self.edges,
-                                       forces=True, virial=virial, out=self.out, energy_weight=self.weight)
+                                       forces=True, virial=virial, out=self.out, energy_weight=self.weight,
+                                       halo=self.halo)
         return self.out
 
     def reduce(self, out: dict, n_atoms: int, *, virial: bool = False) -> dict:
@@ -265,6 +285,64 @@ def reduce_local(local_index, out: dict, n_atoms: int, world: int, *, virial: bo
     return res
 
 
+class HaloExchange:
+    """Ghost rows of node features (forward) and their gradients (backward) over NCCL.
+
+    Built from a rank's plan: its ghosts, grouped by owning rank, are
+    requested from their owners once per neighbour-list rebuild (an
+    ``all_to_all`` of global atom ids); then per step
+      features:  owners send the rows of the requested atoms, ghosts take them;
+      gradients: ghosts send their rows back, owners add them, ghosts are zeroed.
+    Both are one ``all_to_all_single`` with uneven splits.  Images of a rank's
+    own atoms go through the same path as a copy to itself.
+    """
+
+    def __init__(self, plan: DomainPlan, owner_of: np.ndarray, world: int, device, group=None):
+        import torch
+        import torch.distributed as dist
+
+        self.torch, self.dist, self.group = torch, dist, group
+        gid = plan.local_index[plan.n_owned:]
+        own = owner_of[gid]
+        order = np.argsort(own, kind="stable")
+        self.ghost_rows = torch.as_tensor(plan.n_owned + order, device=device)
+        self.recv_counts = np.bincount(own, minlength=world).tolist()
+        rc = torch.tensor(self.recv_counts, dtype=torch.int64, device=device)
+        sc = torch.empty_like(rc)
+        dist.all_to_all_single(sc, rc, group=group)
+        self.send_counts = sc.cpu().tolist()
+        ids_out = torch.as_tensor(np.ascontiguousarray(gid[order]), device=device)
+        ids_in = torch.empty(sum(self.send_counts), dtype=torch.int64, device=device)
+        dist.all_to_all_single(ids_in, ids_out, output_split_sizes=self.send_counts,
+                               input_split_sizes=self.recv_counts, group=group)
+        owned = plan.local_index[: plan.n_owned]  # ascending global ids
+        want = ids_in.cpu().numpy()
+        rows = np.searchsorted(owned, want)
+        if np.any(rows >= len(owned)) or np.any(owned[np.minimum(rows, len(owned) - 1)] != want):
+            raise RuntimeError("halo request for an atom this rank does not own")
+        self.send_rows = torch.as_tensor(rows, device=device)
+
+    def features(self, rows):
+        torch = self.torch
+        send = rows.index_select(0, self.send_rows)
+        recv = torch.empty(len(self.ghost_rows), rows.shape[1], dtype=rows.dtype, device=rows.device)
+        self.dist.all_to_all_single(recv, send, output_split_sizes=self.recv_counts,
+                                    input_split_sizes=self.send_counts, group=self.group)
+        rows.index_copy_(0, self.ghost_rows, recv)
+
+    def gradients(self, rows):
+        torch = self.torch
+        send = rows.index_select(0, self.ghost_rows)
+        recv = torch.empty(len(self.send_rows), rows.shape[1], dtype=rows.dtype, device=rows.device)
+        self.dist.all_to_all_single(recv, send, output_split_sizes=self.send_counts,
+                                    input_split_sizes=self.recv_counts, group=self.group)
+        rows.index_add_(0, self.send_rows, recv)
+        rows.index_fill_(0, self.ghost_rows, 0.0)
+
+    def __call__(self, phase: int, layer: int, rows):
+        (self.features if phase == 0 else self.gradients)(rows)
+
+
 class PositionExchange:
     """All-gather of owned positions into the global array (ranks own different counts)."""
 
@@ -291,5 +369,5 @@ class PositionExchange:
         return out64
 
 
-__all__ = ["grid_for", "shard_structures", "DomainPlan", "plan_domain", "plane_spacings", "SpatialRunner",
-           "PositionExchange", "reduce_local"]
+__all__ = ["grid_for", "shard_structures", "DomainPlan", "domain_of", "plan_domain", "plane_spacings",
+           "SpatialRunner", "HaloExchange", "PositionExchange", "reduce_local"]

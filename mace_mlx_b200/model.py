@@ -190,7 +190,8 @@ class MACEModel:
     # ------------------------------------------------------------------
     def evaluate(self, pos: torch.Tensor, cell: torch.Tensor | None, species: torch.Tensor,
                  graph_ptr: torch.Tensor, edges: EdgeSet, *, forces: bool = True, virial: bool = False,
-                 out: dict | None = None, graph: bool = False, energy_weight: torch.Tensor | None = None) -> dict:
+                 out: dict | None = None, graph: bool = False, energy_weight: torch.Tensor | None = None,
+                 halo=None) -> dict:
         """Energy per graph (float64), node energies, forces and the raw virial.
 
         All inputs are device tensors: pos (N,3) float32, cell (3,3) float32 or
@@ -201,6 +202,9 @@ class MACEModel:
         energies and all gradients (owned 1 / ghost 0 under domain decomposition).
         Lists with more than ``max_chunk_edges`` edges run the radial work in
         receiver chunks (the MLP of each chunk is recomputed in the backward).
+        ``halo(phase, layer, rows)`` is called between layers with the (N, row)
+        node-feature (phase 0) or feature-gradient (phase 1) rows, on the step's
+        stream (domain decomposition; see mace_halo_fn in include/mace_b200.h).
         """
         N = pos.shape[0]
         E = edges.n_edges
@@ -218,6 +222,22 @@ class MACEModel:
             species=species.data_ptr(), graph_ptr=graph_ptr.data_ptr(), sender=edges.sender.data_ptr(),
             receiver=edges.receiver.data_ptr(), shifts=edges.shifts.data_ptr(), row_ptr=edges.row_ptr.data_ptr(),
             rev=edges.rev.data_ptr(), energy_weight=_ptr(energy_weight))
+        if halo is not None:
+            dev = self.device
+
+            def _cb(user, phase, layer, ptr, row_len, stream):
+                try:
+                    rows = torch.as_tensor(_CudaArray(ptr, N * row_len), device=dev).view(N, row_len)
+                    with torch.cuda.stream(torch.cuda.ExternalStream(stream, device=dev)):
+                        halo(int(phase), int(layer), rows)
+                    return 0
+                except Exception as e:  # noqa: BLE001  (reported through the status code)
+                    self.halo_error = e
+                    return 1
+
+            self._halo_fn = nv.HaloFn(_cb)  # kept alive for the duration of the call
+            sysd.halo = C.cast(self._halo_fn, C.c_void_p)
+            graph = False
         if E > self.max_chunk_edges:
             nodes, ebounds = edges.receiver_chunks(self.max_chunk_edges)
             sysd.n_chunks = len(nodes) - 1

@@ -19,7 +19,7 @@ MACE_ERR_TIMEOUT = 4
 MACE_ERR_NCCL = 5
 MACE_ERR_UNSUPPORTED = 6
 MACE_ERR_EDGES = 7
-ABI_VERSION = 5
+ABI_VERSION = 6
 
 MAX_LAYERS = 4
 MAX_IN = 4
@@ -90,6 +90,12 @@ class ModelDesc(C.Structure):
     ]
 
 
+HALO_FEATURES = 0
+HALO_GRADIENTS = 1
+# int (*)(void* user, int32 phase, int32 layer, float* rows, int64 row_len, void* stream)
+HaloFn = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.c_int64, C.c_void_p)
+
+
 class System(C.Structure):
     _fields_ = [
         ("n_nodes", i64), ("n_edges", i64), ("num_graphs", i32),
@@ -97,7 +103,7 @@ class System(C.Structure):
         ("graph_ptr", C.c_void_p), ("sender", C.c_void_p), ("receiver", C.c_void_p),
         ("shifts", C.c_void_p), ("row_ptr", C.c_void_p), ("rev", C.c_void_p),
         ("energy_weight", C.c_void_p), ("n_chunks", i32), ("chunk_nodes", C.c_void_p),
-        ("chunk_edges", C.c_void_p),
+        ("chunk_edges", C.c_void_p), ("halo", C.c_void_p), ("halo_user", C.c_void_p),
     ]
 
 

@@ -144,3 +144,49 @@ def test_two_gloo_ranks_reproduce_the_periodic_oracle():
     s = 0.5 * (g + g.T) / vol
     voigt = s[[0, 1, 2, 1, 0, 0], [0, 1, 2, 2, 2, 1]]
     np.testing.assert_allclose(voigt, ref["stress"], rtol=1e-8, atol=1e-12)
+
+
+def _halo_rank(rank, world, port, path, pos, cell):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.set_num_threads(1)
+    torch.distributed.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from mace_mlx_b200.distributed import HaloExchange, domain_of
+
+        grid = grid_for(world)
+        plan = plan_domain(pos, cell, grid, rank, 3.5)
+        hx = HaloExchange(plan, domain_of(pos, cell, grid), world, "cpu")
+        gid = torch.as_tensor(plan.local_index, dtype=torch.float64)
+        rows = torch.stack([gid, 2 * gid + 1, -gid], dim=1)
+        rows[plan.n_owned:] = -7.0
+        hx(0, 0, rows)  # features: ghosts take their owners' rows
+        ok_fwd = bool(torch.equal(rows, torch.stack([gid, 2 * gid + 1, -gid], dim=1)))
+        g = torch.zeros(plan.n_local, 2, dtype=torch.float64)
+        g[plan.n_owned:] = 1.0
+        hx(1, 0, g)  # gradients: ghosts' rows go to their owners
+        ok_zero = bool(torch.all(g[plan.n_owned:] == 0))
+        counts = np.zeros(len(pos))
+        np.add.at(counts, plan.local_index[: plan.n_owned], g[: plan.n_owned, 0].numpy())
+        ghosts = [None] * world
+        torch.distributed.all_gather_object(ghosts, plan.local_index[plan.n_owned:])
+        c = torch.as_tensor(counts)
+        torch.distributed.all_reduce(c)
+        want = np.bincount(np.concatenate(ghosts), minlength=len(pos)).astype(np.float64)
+        if rank == 0:
+            np.savez(path, ok_fwd=ok_fwd, ok_zero=ok_zero, counts=c.numpy(), want=want,
+                     n_ghost=plan.n_local - plan.n_owned)
+    finally:
+        torch.distributed.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_halo_exchange_moves_ghost_rows_and_reduces_gradients(world):
+    st = diamond_si(4, 0.05, 33)
+    with tempfile.TemporaryDirectory() as tmp, _single_threaded_children():
+        path = os.path.join(tmp, "r0.npz")
+        torch.multiprocessing.spawn(_halo_rank, args=(world, _free_port(), path, st.positions, st.cell),
+                                    nprocs=world, join=True)
+        got = np.load(path)
+    assert got["n_ghost"] > 0 and got["ok_fwd"] and got["ok_zero"]
+    np.testing.assert_array_equal(got["counts"], got["want"])

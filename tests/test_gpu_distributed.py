@@ -27,8 +27,8 @@ def _case():
     return st, config, weights
 
 
-def _run(model, st, world, rank):
-    runner = SpatialRunner(model, st.numbers, st.cell, world, rank, skin=0.5)
+def _run(model, st, world, rank, halo=True):
+    runner = SpatialRunner(model, st.numbers, st.cell, world, rank, skin=0.5, halo=halo)
     pos = torch.tensor(st.positions, dtype=torch.float64, device=model.device)
     out = runner.evaluate(pos, virial=True)
     res = runner.reduce(out, len(st), virial=True)
@@ -36,7 +36,7 @@ def _run(model, st, world, rank):
     return {k: v.cpu().numpy().astype(np.float64) for k, v in res.items()}, runner.plan
 
 
-def _rank_main(rank, world, port, path):
+def _rank_main(rank, world, port, path, halo):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     torch.cuda.set_device(rank)
@@ -44,7 +44,7 @@ def _rank_main(rank, world, port, path):
     try:
         st, config, weights = _case()
         model = MACEModel(config=config, weights=weights, device=rank)
-        res, plan = _run(model, st, world, rank)
+        res, plan = _run(model, st, world, rank, halo)
         if rank == 0:
             np.savez(path, n_local=plan.n_local, n_owned=plan.n_owned, **res)
         torch.distributed.barrier()
@@ -52,13 +52,15 @@ def _rank_main(rank, world, port, path):
         torch.distributed.destroy_process_group()
 
 
-def test_two_gpu_domains_match_one_gpu():
+@pytest.mark.parametrize("halo", [True, False])
+def test_two_gpu_domains_match_one_gpu(halo):
+    """halo: r_max ghost shell with layer features exchanged over NCCL; else a 2 r_max shell."""
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
     with tempfile.TemporaryDirectory() as tmp:
         path = os.path.join(tmp, "rank0.npz")
-        torch.multiprocessing.spawn(_rank_main, args=(2, port, path), nprocs=2, join=True)
+        torch.multiprocessing.spawn(_rank_main, args=(2, port, path, halo), nprocs=2, join=True)
         got = dict(np.load(path))
     st, config, weights = _case()
     ref, _ = _run(MACEModel(config=config, weights=weights, device=0), st, 1, 0)
