@@ -228,7 +228,9 @@ class MACEModel:
             def _cb(user, phase, layer, ptr, row_len, stream):
                 try:
                     rows = torch.as_tensor(_CudaArray(ptr, N * row_len), device=dev).view(N, row_len)
-                    with torch.cuda.stream(torch.cuda.ExternalStream(stream, device=dev)):
+                    # a NULL stream (the legacy default stream) arrives as None
+                    st = torch.cuda.ExternalStream(stream, device=dev) if stream else torch.cuda.default_stream(dev)
+                    with torch.cuda.stream(st):
                         halo(int(phase), int(layer), rows)
                     return 0
                 except Exception as e:  # noqa: BLE001  (reported through the status code)
@@ -247,7 +249,11 @@ class MACEModel:
                           forces=_ptr(out.get("forces")), virial=_ptr(out.get("virial")))
         flags = (nv.WANT_FORCES if forces else 0) | (nv.WANT_VIRIAL if virial else 0) | (nv.USE_GRAPH if graph else 0)
         stream = torch.cuda.current_stream(self.device).cuda_stream
-        nv.check(self.lib.mace_forward_backward(self.ctx, C.byref(sysd), C.byref(outs), flags, stream), self.lib)
+        self.halo_error = None
+        rc = self.lib.mace_forward_backward(self.ctx, C.byref(sysd), C.byref(outs), flags, stream)
+        if rc and self.halo_error is not None:
+            raise RuntimeError("halo exchange callback failed") from self.halo_error
+        nv.check(rc, self.lib)
         return out
 
     def last_launch_count(self) -> int:
