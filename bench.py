@@ -415,8 +415,10 @@ C3_WORKLOAD = ("config3: MACE-OFF-medium-like (96x0e+96x1o, lmax3, corr3, 2 laye
                "seed 3; 512 random-walk molecules of 20-60 atoms (seed 3), non-periodic; energy+forces; molecules "
                "sharded over the ranks by atom count")
 C4_WORKLOAD = ("config4: medium MACE as config 1 (seed 1); diamond Si 50x50x50 = 1,000,000 atoms rattled 0.05 A "
-               "(seed 4); energy+forces+stress; spatial domains (grid 1x1xN..2x2x2) with 2 r_max + skin = 12.5 A "
-               "ghost shells; positions all-gathered, forces/energy/virial all-reduced (NCCL)")
+               "(seed 4); energy+forces+stress; spatial domains (grid 1x1x2, 1x2x2, 2x2x2) periodic along unsplit "
+               "axes, r_max + skin = 6.5 A ghost shells across split axes; layer-1 node features halo-exchanged and "
+               "their gradients halo-reduced (NCCL all-to-all); positions all-gathered, forces/energy/virial "
+               "all-reduced")
 
 
 def partition_arm(args, rank: int, world: int, local_rank: int):

@@ -109,8 +109,11 @@ class MACEModel:
             per_edge += w[-1] + sum(w[1:-1])
         per_edge += max(lay.mlp_widths[-1] for lay in self.spec.layers)
         self.bytes_per_chunk_edge = 4 * per_edge
-        budget = float(os.environ.get("MACE_B200_CHUNK_BYTES", 24e9))
-        self.max_chunk_edges = max(4096, int(budget // self.bytes_per_chunk_edge))
+        # MACE_B200_CHUNK_BYTES caps the radial-weight buffers; by default they
+        # take up to 80% of the device memory left after the rest of the workspace
+        env = os.environ.get("MACE_B200_CHUNK_BYTES")
+        self._chunk_budget = float(env) if env else None
+        self.max_chunk_edges = max(4096, int(self._chunk_budget // self.bytes_per_chunk_edge)) if env else 1 << 40
 
     def close(self):
         if getattr(self, "ctx", None) is not None and self.ctx.value:
@@ -143,13 +146,20 @@ class MACEModel:
 
     def reserve(self, n_nodes: int, n_edges: int) -> None:
         """Workspace for n_nodes / n_edges; radial-weight buffers for at most max_chunk_edges."""
-        chunk = min(n_edges, self.max_chunk_edges)
-        if n_nodes > self._cap[0] or n_edges > self._cap[1] or chunk > self._cap[2]:
-            N = max(n_nodes, self._cap[0])
-            E = max(n_edges, self._cap[1])
-            EC = max(chunk, self._cap[2])
-            nv.check(self.lib.mace_ctx_reserve_chunked(self.ctx, N, E, EC), self.lib)
-            self._cap = (N, E, EC)
+        if n_nodes <= self._cap[0] and n_edges <= self._cap[1] and min(n_edges, self.max_chunk_edges) <= self._cap[2]:
+            return
+        N = max(n_nodes, self._cap[0])
+        E = max(n_edges, self._cap[1])
+        if self._chunk_budget is None:
+            # size the rest of the workspace first, then give the radial buffers what is left
+            small = min(E, 4096)
+            nv.check(self.lib.mace_ctx_reserve_chunked(self.ctx, N, E, small), self.lib)
+            self._cap = (N, E, small)
+            free, _ = torch.cuda.mem_get_info(self.device)
+            self.max_chunk_edges = max(4096, int(0.8 * free // self.bytes_per_chunk_edge))
+        EC = max(min(E, self.max_chunk_edges), self._cap[2])
+        nv.check(self.lib.mace_ctx_reserve_chunked(self.ctx, N, E, EC), self.lib)
+        self._cap = (N, E, EC)
 
     def workspace_bytes(self) -> int:
         b = C.c_int64()
