@@ -186,6 +186,9 @@ struct LinJob {
   const float* w;   // (n_k*C, ldb) row-major, first C columns used
   float alpha;
   int accumulate;
+  // species-indexed weights (skip_tp): row (n, m) uses w + species[n] * zstride
+  const int32_t* species;
+  int64_t zstride;
 };
 struct LinParams {
   int64_t N;

@@ -218,13 +218,17 @@ __global__ void k_edge_bwd(EdgeParams p) {
   if (threadIdx.x < 9) p.virial_part[9 * (int64_t)blockIdx.x + threadIdx.x] = red[threadIdx.x][0];
 }
 
+// one warp per node: lanes take the node's incoming edges, then a fixed
+// shuffle tree sums them (deterministic)
 __global__ void k_forces(ForceParams p) {
-  int64_t n = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t n = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
   if (n >= p.N) return;
   float f0 = 0.f, f1 = 0.f, f2 = 0.f;
   int bad = 0;
-  for (int e = p.row_ptr[n]; e < p.row_ptr[n + 1]; ++e) {
-    int r = p.rev[e];
+  const int e1 = p.row_ptr[n + 1];
+  for (int e = p.row_ptr[n] + lane; e < e1; e += 32) {
+    const int r = p.rev[e];
     if (r < 0 || p.snd[r] != (int)n || p.rcv[r] != p.snd[e]) {
       bad = 1;
       continue;
@@ -233,6 +237,14 @@ __global__ void k_forces(ForceParams p) {
     f1 += p.dv[3 * (int64_t)r + 1] - p.dv[3 * (int64_t)e + 1];
     f2 += p.dv[3 * (int64_t)r + 2] - p.dv[3 * (int64_t)e + 2];
   }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    f0 += __shfl_xor_sync(0xffffffffu, f0, o);
+    f1 += __shfl_xor_sync(0xffffffffu, f1, o);
+    f2 += __shfl_xor_sync(0xffffffffu, f2, o);
+    bad |= __shfl_xor_sync(0xffffffffu, bad, o);
+  }
+  if (lane != 0) return;
   if (bad) atomicExch(p.err_flag, 1);
   p.forces[3 * n + 0] = f0;
   p.forces[3 * n + 1] = f1;
@@ -280,7 +292,7 @@ int launch_edge_bwd(const EdgeParams& p, int* n_blocks, cudaStream_t s) {
 
 int launch_forces(const ForceParams& p, cudaStream_t s) {
   if (p.N == 0) return MACE_OK;
-  k_forces<<<(unsigned)((p.N + 127) / 128), 128, 0, s>>>(p);
+  k_forces<<<(unsigned)((p.N * 32 + 255) / 256), 256, 0, s>>>(p);
   MACE_LAUNCH_CHECK("forces");
   return MACE_OK;
 }

@@ -23,6 +23,10 @@ namespace {
 // chunks of 32 through shared memory, the next chunk's loads in flight in
 // registers while the current one is multiplied.  Inner step per thread: two
 // broadcast 128-bit loads of A, one 128-bit load of B, 32 FMAs.
+// With species-indexed weights (the skip tensor product with a one-hot
+// species input) the tile runs one pass per distinct species among its rows,
+// each with the other rows' A masked to zero: a single pass when the tile's
+// nodes share one element.
 // ---------------------------------------------------------------------------
 constexpr int LR = 64;        // rows per tile
 constexpr int RPT = LR / 8;   // rows per thread
@@ -32,6 +36,7 @@ constexpr int LAP = LR + 4;   // pitch of the transposed A tile (16-byte rows, n
 __global__ void __launch_bounds__(256) k_linear(LinParams p) {
   __shared__ __align__(16) float sA[LK][LAP];
   __shared__ __align__(16) float sB[LK][128];
+  __shared__ int sZ[LR + 1];  // distinct species of the tile's rows, count in sZ[LR]
   const LinJob& jb = p.job[blockIdx.y];
   const int C = p.C;
   const int rows = (int)(p.N * jb.d);
@@ -42,14 +47,35 @@ __global__ void __launch_bounds__(256) k_linear(LinParams p) {
   // this thread's A row for the loads (fixed across K)
   const int lr = tid & (LR - 1), lq = tid >> 6;  // row, first 4-wide k group (and lq + 4)
   const int arow = r0 + lr;
-  const bool arow_ok = arow < rows;
+  const bool arow_in = arow < rows;
   const float* abase = p.in;
-  if (arow_ok) {
+  int arow_z = -1;
+  if (arow_in) {
     const int node = arow / jb.d, m = arow - node * jb.d;
     abase = p.in + (int64_t)node * p.in_row + m * C;
+    if (jb.species) arow_z = jb.species[node];
+  }
+  int n_pass = 1;
+  if (jb.species) {
+    if (tid < LR) sZ[tid] = arow_z;
+    __syncthreads();
+    if (tid == 0) {  // compact the distinct species in place (at most LR)
+      int nd = 0;
+      for (int q = 0; q < LR; ++q) {
+        const int z = sZ[q];
+        bool seen = z < 0;
+        for (int k = 0; k < nd && !seen; ++k) seen = sZ[k] == z;
+        if (!seen) sZ[nd++] = z;
+      }
+      sZ[LR] = nd;
+    }
+    __syncthreads();
+    n_pass = sZ[LR];
   }
   const int nck = C / LK;
   const int nchunks = jb.n_k * nck;
+  bool arow_ok = arow_in;
+  const float* wbase = jb.w;
   auto load = [&](int t, float4* ra, float4* rb) {
     const int ks = t / nck, kc = (t - ks * nck) * LK;
     const float* ap = abase + jb.k_off[ks] + kc;
@@ -60,7 +86,7 @@ __global__ void __launch_bounds__(256) k_linear(LinParams p) {
     for (int q = 0; q < 4; ++q) {
       const int idx = tid + 256 * q;
       const int kk = idx >> 5, c4 = (idx & 31) * 4;
-      rb[q] = (c4 < C) ? __ldg(reinterpret_cast<const float4*>(jb.w + (int64_t)(ks * C + kc + kk) * jb.ldb + c4))
+      rb[q] = (c4 < C) ? __ldg(reinterpret_cast<const float4*>(wbase + (int64_t)(ks * C + kc + kk) * jb.ldb + c4))
                        : make_float4(0.f, 0.f, 0.f, 0.f);
     }
   };
@@ -70,6 +96,12 @@ __global__ void __launch_bounds__(256) k_linear(LinParams p) {
 #pragma unroll
     for (int b = 0; b < 4; ++b) acc[a][b] = 0.f;
   float4 ra[2], rb[4];
+  for (int pass = 0; pass < n_pass; ++pass) {
+  if (jb.species) {
+    const int z = sZ[pass];
+    arow_ok = arow_in && arow_z == z;
+    wbase = jb.w + (int64_t)z * jb.zstride;
+  }
   load(0, ra, rb);
   for (int t = 0; t < nchunks; ++t) {
 #pragma unroll
@@ -103,6 +135,7 @@ __global__ void __launch_bounds__(256) k_linear(LinParams p) {
     }
     __syncthreads();
   }
+  }  // species passes
   if (tx * 4 >= C) return;
 #pragma unroll
   for (int a = 0; a < RPT; ++a) {
@@ -119,37 +152,6 @@ __global__ void __launch_bounds__(256) k_linear(LinParams p) {
       v.w += w.w;
     }
     *o = v;
-  }
-}
-
-// ---------------------------------------------------------------------------
-// skip_tp: out[n, out_off + m*C + w] (+)= sum_u in[n, in_off + m*C + u] * W[z_n][u][w]
-// one CTA per node, one thread per output channel
-// ---------------------------------------------------------------------------
-__global__ void k_skip(SkipParams p) {
-  extern __shared__ float sIn[];
-  const int64_t n = blockIdx.x;
-  const int C = p.C, w = threadIdx.x;
-  const int z = p.species[n];
-  for (int jb = 0; jb < p.n_jobs; ++jb) {
-    const int d = p.d[jb];
-    for (int q = w; q < d * C; q += blockDim.x) sIn[q] = p.in[n * p.in_row + p.in_off[jb] + q];
-    __syncthreads();
-    const float* W = p.w[jb] + (int64_t)z * C * C;
-    float acc[7];
-#pragma unroll
-    for (int m = 0; m < 7; ++m) acc[m] = 0.f;
-    for (int u = 0; u < C; ++u) {
-      float wv = __ldg(W + (int64_t)u * C + w);
-#pragma unroll
-      for (int m = 0; m < 7; ++m)
-        if (m < d) acc[m] = fmaf(sIn[m * C + u], wv, acc[m]);
-    }
-    float* o = p.out + n * p.out_row + p.out_off[jb] + w;
-#pragma unroll
-    for (int m = 0; m < 7; ++m)
-      if (m < d) o[m * C] = p.accumulate ? o[m * C] + acc[m] : acc[m];
-    __syncthreads();
   }
 }
 
@@ -364,14 +366,32 @@ int launch_linear(const LinParams& p, cudaStream_t s) {
   return MACE_OK;
 }
 
+// skip_tp with a one-hot species input = per-species (C, C) weights: run as
+// species-indexed linear jobs
 int launch_skip(const SkipParams& p, cudaStream_t s) {
   if (p.N == 0 || p.n_jobs == 0) return MACE_OK;
-  int dmax = 1;
-  for (int j = 0; j < p.n_jobs; ++j) dmax = p.d[j] > dmax ? p.d[j] : dmax;
-  size_t smem = (size_t)dmax * p.C * sizeof(float);
-  k_skip<<<(unsigned)p.N, p.C, smem, s>>>(p);
-  MACE_LAUNCH_CHECK("skip");
-  return MACE_OK;
+  LinParams lp{};
+  lp.N = p.N;
+  lp.C = p.C;
+  lp.in = p.in;
+  lp.in_row = p.in_row;
+  lp.out = p.out;
+  lp.out_row = p.out_row;
+  lp.n_jobs = p.n_jobs;
+  for (int q = 0; q < p.n_jobs; ++q) {
+    LinJob& j = lp.job[q];
+    j.d = p.d[q];
+    j.n_k = 1;
+    j.k_off[0] = p.in_off[q];
+    j.out_off = p.out_off[q];
+    j.ldb = p.C;
+    j.w = p.w[q];
+    j.alpha = 1.f;
+    j.accumulate = p.accumulate;
+    j.species = p.species;
+    j.zstride = (int64_t)p.C * p.C;
+  }
+  return launch_linear(lp, s);
 }
 
 int launch_sc_fwd(const ScParams& p, cudaStream_t s) {
