@@ -43,7 +43,6 @@ constexpr int KC = 32;            // backward K chunk (one 128-byte panel)
 constexpr int NEPI = 4;           // epilogue warps
 constexpr int NTHR = 32 * (NEPI + 1);
 constexpr int NBUF = 4;           // forward TMEM chunk buffers of 32 columns
-constexpr int TMEM_COLS = 128;
 constexpr int MLP_TC_TIMEOUT = 2;
 constexpr int MLP_TC_ALIGN = 8;   // dynamic shared memory not 1024-byte aligned
 constexpr int IMG = 2 * H * H;    // floats of one 64 x 64 hi/lo image
@@ -116,20 +115,46 @@ __device__ __forceinline__ void layer0(const MlpParams& p, const float* sW0, int
   }
 }
 
+// ---------------------------------------------------------------------------
+// forward
+// ---------------------------------------------------------------------------
+constexpr int F_NEPI = 8;                 // epilogue warps: quadrant q = warp & 3, group g = warp >> 2
+constexpr int F_NTHR = 32 * (F_NEPI + 1); // + control warp
+constexpr int F_TMEM = 256;               // [0, 128) accumulators, [128, 192) A hi, [192, 256) A lo
+constexpr uint32_t F_AHI = 128, F_ALO = 192;
+
 struct FwdSmem {
-  static constexpr int A_HI = 0;       // 128 x 64 fp32, 32 KB
-  static constexpr int A_LO = 32768;   // 32 KB
-  static constexpr int B = 65536;      // 32 KB: one 64 x 64 hidden image, or two 32-row chunk images
-  static constexpr int OUT = 98304;    // 16 KB output staging; warp w owns rows 32w.. (4 KB);
-                                       // holds the layer-0 weights until the first chunk
-  static constexpr int BARS = 114688;
+  static constexpr int B = 0;          // 32 KB: one 64 x 64 hidden image, or two 32-row chunk images
+  static constexpr int STG = 32768;    // 8 warps x 2 x 4 KB output staging; holds the layer-0 weights first
+  static constexpr int BARS = STG + F_NEPI * 2 * 4096;
   static constexpr int TOTAL = BARS + 256;
-  // barrier indices
+  // request enough to keep two CTAs per SM (each holds 256 of the SM's 512 TMEM columns)
+  static constexpr int REQUEST = 100 * 1024;
   static constexpr int TL = 0, A = 1, ACC = 2, BST = 3, FULL = 5, FREE = 9, NBARS = 13;
 };
+static_assert(FwdSmem::TOTAL <= FwdSmem::REQUEST, "forward shared memory");
 
+// D (128 x N) = A (TMEM, 128 x 64, hi/lo) . B (N x 64, hi/lo)^T, issued by one thread
+template <int N>
+__device__ __forceinline__ void mma_k64_ta(uint32_t tmem_d, uint32_t a_hi, uint32_t a_lo, uint32_t b_hi,
+                                           uint32_t b_lo) {
+  constexpr uint32_t IDESC = tc::idesc_tf32(TM, N);
+#pragma unroll
+  for (int kb = 0; kb < H / 8; ++kb) {
+    const uint32_t ob = (kb >> 2) * (N * 128) + (kb & 3) * 32;
+    tc::mma_tf32_ta(tmem_d, a_hi + kb * 8, tc::sw128_desc(b_hi + ob), IDESC, kb > 0);
+    tc::mma_tf32_ta(tmem_d, a_hi + kb * 8, tc::sw128_desc(b_lo + ob), IDESC, 1);
+    tc::mma_tf32_ta(tmem_d, a_lo + kb * 8, tc::sw128_desc(b_hi + ob), IDESC, 1);
+  }
+}
+
+// One CTA per 128-edge tile, 8 epilogue warps + 1 control warp, two CTAs per SM.
+// The activation operand A lives in TMEM (written with tcgen05.st), so shared
+// memory only holds the weight images and the output staging, which each
+// epilogue warp double-buffers: a chunk's bulk store drains while the warp
+// prepares the next one.  The epilogue warp groups take alternate chunks.
 template <int NB>
-__global__ void __launch_bounds__(NTHR, 2) k_mlp_fwd_tc(MlpParams p) {
+__global__ void __maxnreg__(96) k_mlp_fwd_tc(MlpParams p) {
   extern __shared__ __align__(1024) unsigned char sm[];
   using S = FwdSmem;
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
@@ -144,17 +169,18 @@ __global__ void __launch_bounds__(NTHR, 2) k_mlp_fwd_tc(MlpParams p) {
   const int nh = p.n_layers - 1;
   const int wout = p.widths[p.n_layers];
   const int nch = wt_nchunk(wout);
-  const uint32_t a_hi = tc::smem_u32(sm + S::A_HI), a_lo = tc::smem_u32(sm + S::A_LO);
   const uint32_t b_base = tc::smem_u32(sm + S::B);
 
-  if (warp == NEPI) {
-    tc::tmem_alloc(tc::smem_u32(tslot), TMEM_COLS);
+  if (warp == F_NEPI) {
+    tc::tmem_alloc(tc::smem_u32(tslot), F_TMEM);
     tc::tmem_relinquish();
   }
   if (t == 0) {
     for (int i = 0; i < S::NBARS; ++i) {
-      const bool by_warps = (i == S::A) || (i >= S::FREE && i < S::FREE + NBUF);
-      tc::mbar_init(BAR(i), by_warps ? NEPI : 1);
+      int count = 1;
+      if (i == S::A) count = F_NEPI;
+      if (i >= S::FREE && i < S::FREE + NBUF) count = F_NEPI / 2;  // one group drains a buffer
+      tc::mbar_init(BAR(i), count);
     }
     *abort_flag = 0;
     tc::fence_barrier_init();
@@ -165,7 +191,7 @@ __global__ void __launch_bounds__(NTHR, 2) k_mlp_fwd_tc(MlpParams p) {
   const uint32_t tmem = *tslot;
   bool ok = true;
 
-  if (warp == NEPI) {
+  if (warp == F_NEPI) {
     // ---------------- control warp: copies and MMAs from lane 0 ----------------
     if (lane == 0) {
       auto wait = [&](int i, uint32_t par) {
@@ -181,13 +207,14 @@ __global__ void __launch_bounds__(NTHR, 2) k_mlp_fwd_tc(MlpParams p) {
         tc::mbar_expect_tx(BAR(S::BST + s), CIMG * 4);
         tc::bulk_g2s(b_base + s * CIMG * 4, p.tc_img + (int64_t)c * CIMG, CIMG * 4, BAR(S::BST + s));
       };
+      const uint32_t a_hi = tmem + F_AHI, a_lo = tmem + F_ALO;
       uint32_t pa = 0;
       if (nh >= 2) copy_trunk(0);
       for (int j = 1; j < nh; ++j) {  // hidden layer j reads A = SiLU(layer j-1)
         if (!wait(S::TL, (j - 1) & 1) || !wait(S::A, pa)) break;
         pa ^= 1;
         tc::fence_after_sync();
-        mma_k64<H>(tmem, a_hi, a_lo, b_base, b_base + IMG * 2);
+        mma_k64_ta<H>(tmem, a_hi, a_lo, b_base, b_base + IMG * 2);
         tc::mma_commit(BAR(S::ACC));
         if (!wait(S::ACC, (j - 1) & 1)) break;  // B is free again
         if (j + 1 < nh) copy_trunk(j);
@@ -203,7 +230,7 @@ __global__ void __launch_bounds__(NTHR, 2) k_mlp_fwd_tc(MlpParams p) {
           if (c >= NBUF && !wait(S::FREE + buf, ((c / NBUF) - 1) & 1)) break;
           tc::fence_after_sync();
           const uint32_t bs = b_base + s * CIMG * 4;
-          mma_k64<TC32>(tmem + buf * TC32, a_hi, a_lo, bs, bs + CIMG * 2);
+          mma_k64_ta<TC32>(tmem + buf * TC32, a_hi, a_lo, bs, bs + CIMG * 2);
           tc::mma_commit(BAR(S::FULL + buf));
           if (c >= 1 && c + 1 < nch) {  // stage (c+1)&1 is free once MMA(c-1) is done
             if (!wait(S::FULL + (c - 1) % NBUF, ((c - 1) / NBUF) & 1)) break;
@@ -214,34 +241,62 @@ __global__ void __launch_bounds__(NTHR, 2) k_mlp_fwd_tc(MlpParams p) {
     }
     __syncwarp();
   } else {
-    // ---------------- epilogue warps: thread t owns edge t of the tile ----------------
-    const int64_t e = (int64_t)blockIdx.x * TM + t;
+    // ---------------- epilogue warps: row = TMEM lane, columns split by group ----------------
+    const int q = warp & 3, g = warp >> 2;
+    const int row = q * 32 + lane;
+    const int64_t e = (int64_t)blockIdx.x * TM + row;
     const bool valid = e < p.E;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     auto wwait = [&](int i, uint32_t par) {
       const bool r = ok && tc::mbar_wait_or_abort(BAR(i), par, abort_flag);
       ok = __all_sync(0xffffffffu, r);
       return ok;
     };
-    unsigned char* a_hi_p = sm + S::A_HI;
-    unsigned char* a_lo_p = sm + S::A_LO;
-    float y[H];
-    load_w0<NB>(p, reinterpret_cast<float*>(sm + S::OUT), t);
-    layer0<NB>(p, reinterpret_cast<const float*>(sm + S::OUT), e, valid, y);
+    // layer 0 on the CUDA cores for this group's 32 hidden columns
+    float* sW0 = reinterpret_cast<float*>(sm + S::STG);
+    for (int i = t; i < NB * H / 4; i += 32 * F_NEPI)
+      reinterpret_cast<float4*>(sW0)[i] = __ldg(reinterpret_cast<const float4*>(p.w[0]) + i);
+    tc::named_sync(1, 32 * F_NEPI);
+    float y[32];
+    {
+      float x[NB];
+#pragma unroll
+      for (int i = 0; i < NB; ++i) x[i] = valid ? __ldg(p.b + e * NB + i) : 0.f;
+#pragma unroll
+      for (int o = 0; o < 32; ++o) y[o] = 0.f;
+#pragma unroll
+      for (int i = 0; i < NB; ++i) {
+        const float4* w4 = reinterpret_cast<const float4*>(sW0 + i * H + 32 * g);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float4 w = w4[k];
+          y[4 * k + 0] = fmaf(x[i], w.x, y[4 * k + 0]);
+          y[4 * k + 1] = fmaf(x[i], w.y, y[4 * k + 1]);
+          y[4 * k + 2] = fmaf(x[i], w.z, y[4 * k + 2]);
+          y[4 * k + 3] = fmaf(x[i], w.w, y[4 * k + 3]);
+        }
+      }
+    }
     uint32_t pacc = 0;
     for (int j = 0; j < nh; ++j) {
       if (valid) {
-        float4* act = reinterpret_cast<float4*>(p.act + e * (int64_t)(nh * H) + j * H);
+        float4* act = reinterpret_cast<float4*>(p.act + e * (int64_t)(nh * H) + j * H + 32 * g);
 #pragma unroll
-        for (int q = 0; q < H / 4; ++q) act[q] = make_float4(y[4 * q], y[4 * q + 1], y[4 * q + 2], y[4 * q + 3]);
+        for (int k = 0; k < 8; ++k) act[k] = make_float4(y[4 * k], y[4 * k + 1], y[4 * k + 2], y[4 * k + 3]);
       }
 #pragma unroll
-      for (int q = 0; q < H / 4; ++q) {
-        const float4 h = valid ? make_float4(silu_f(y[4 * q]), silu_f(y[4 * q + 1]), silu_f(y[4 * q + 2]),
-                                             silu_f(y[4 * q + 3]))
-                               : make_float4(0.f, 0.f, 0.f, 0.f);
-        put_hilo(a_hi_p, a_lo_p, t, 4 * q, h);
+      for (int o = 0; o < 32; ++o) y[o] = valid ? silu_f(y[o]) : 0.f;
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {  // 16 columns at a time keeps the temporaries small
+        float part[16];
+#pragma unroll
+        for (int o = 0; o < 16; ++o) part[o] = tc::tf32_hi(y[16 * hf + o]);
+        tc::tmem_st16(tmem + lane_base + F_AHI + 32 * g + 16 * hf, part);
+#pragma unroll
+        for (int o = 0; o < 16; ++o) part[o] = y[16 * hf + o] - tc::tf32_hi(y[16 * hf + o]);
+        tc::tmem_st16(tmem + lane_base + F_ALO + 32 * g + 16 * hf, part);
       }
-      tc::fence_proxy_async();
+      tc::tmem_wait_st();
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(BAR(S::A));
@@ -249,34 +304,36 @@ __global__ void __launch_bounds__(NTHR, 2) k_mlp_fwd_tc(MlpParams p) {
         if (!wwait(S::ACC, pacc)) break;
         pacc ^= 1;
         tc::fence_after_sync();
-        tmem_row64(tmem, warp, 0, y);
+        tc::tmem_ld32(tmem + lane_base + 32 * g, y);
+        tc::tmem_wait_ld();
       }
     }
-    unsigned char* stg = sm + S::OUT + warp * 4096;
-    const uint32_t stg_u = tc::smem_u32(stg);
-    float* dst = p.out + (int64_t)blockIdx.x * nch * WT_CHUNK + warp * 32 * 32;
-    for (int c = 0; c < nch && ok; ++c) {
+    // output chunks c = g, g + 2, ...: TMEM -> registers -> staging -> bulk store
+    float* dst = p.out + (int64_t)blockIdx.x * nch * WT_CHUNK + q * 32 * 32;
+    int k = 0;
+    for (int c = g; c < nch && ok; c += 2, ++k) {
       const int buf = c % NBUF;
       if (!wwait(S::FULL + buf, (c / NBUF) & 1)) break;
       tc::fence_after_sync();
       float v[32];
-      tc::tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + buf * TC32, v);
+      tc::tmem_ld32(tmem + lane_base + buf * TC32, v);
       tc::tmem_wait_ld();
       tc::fence_before_sync();
       __syncwarp();
+      unsigned char* stg = sm + S::STG + (warp * 2 + (k & 1)) * 4096;
       if (lane == 0) {
         tc::mbar_arrive(BAR(S::FREE + buf));
-        tc::bulk_wait_read_all();  // the staging slice is free again
+        tc::bulk_wait_read_but_one();  // the store issued from this buffer two chunks ago has read it
       }
       __syncwarp();
 #pragma unroll
-      for (int q = 0; q < 8; ++q)
-        *reinterpret_cast<float4*>(stg + lane * 128 + ((q ^ (lane & 7)) << 4)) =
-            make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+      for (int u = 0; u < 8; ++u)
+        *reinterpret_cast<float4*>(stg + lane * 128 + ((u ^ (lane & 7)) << 4)) =
+            make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
       tc::fence_proxy_async();
       __syncwarp();
       if (lane == 0) {
-        tc::bulk_s2g(dst + (int64_t)c * WT_CHUNK, stg_u, 4096);
+        tc::bulk_s2g(dst + (int64_t)c * WT_CHUNK, tc::smem_u32(stg), 4096);
         tc::bulk_commit();
       }
     }
@@ -286,9 +343,9 @@ __global__ void __launch_bounds__(NTHR, 2) k_mlp_fwd_tc(MlpParams p) {
   tc::fence_before_sync();
   __syncthreads();
   if (!ok) atomicExch(p.err_flag, MLP_TC_TIMEOUT);
-  if (warp == NEPI) {
+  if (warp == F_NEPI) {
     tc::fence_after_sync();
-    tc::tmem_dealloc(tmem, TMEM_COLS);
+    tc::tmem_dealloc(tmem, F_TMEM);
   }
 }
 
@@ -498,9 +555,12 @@ __global__ void __launch_bounds__(NTHR, 2) k_mlp_bwd_tc(MlpParams p) {
 
 template <int NB>
 int launch_fwd_nb(const MlpParams& p, cudaStream_t s) {
-  const size_t smem = FwdSmem::TOTAL;
+  const size_t smem = FwdSmem::REQUEST;
   MACE_CUDA_TRY(cudaFuncSetAttribute(k_mlp_fwd_tc<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  k_mlp_fwd_tc<NB><<<(unsigned)((p.E + TM - 1) / TM), NTHR, smem, s>>>(p);
+  // all of the SM's unified memory as shared memory: two CTAs per SM
+  MACE_CUDA_TRY(cudaFuncSetAttribute(k_mlp_fwd_tc<NB>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                     (int)cudaSharedmemCarveoutMaxShared));
+  k_mlp_fwd_tc<NB><<<(unsigned)((p.E + TM - 1) / TM), F_NTHR, smem, s>>>(p);
   MACE_LAUNCH_CHECK("mlp_fwd_tc");
   return MACE_OK;
 }
@@ -509,6 +569,8 @@ template <int NB>
 int launch_bwd_nb(const MlpParams& p, cudaStream_t s) {
   const size_t smem = BwdSmem::TOTAL;
   MACE_CUDA_TRY(cudaFuncSetAttribute(k_mlp_bwd_tc<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  MACE_CUDA_TRY(cudaFuncSetAttribute(k_mlp_bwd_tc<NB>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                     (int)cudaSharedmemCarveoutMaxShared));
   k_mlp_bwd_tc<NB><<<(unsigned)((p.E + TM - 1) / TM), NTHR, smem, s>>>(p);
   MACE_LAUNCH_CHECK("mlp_bwd_tc");
   return MACE_OK;
