@@ -115,6 +115,13 @@ struct mace_ctx {
   std::vector<ProfAcc> prof_acc;
   // CUDA-graph replay of the whole step, keyed on the exact call arguments
   cudaStream_t cap_stream = nullptr;
+  // second stream for the radial-MLP chain (forked from and joined into the step's stream)
+  cudaStream_t aux = nullptr;
+  static constexpr int NEV = 2 * MACE_MAX_LAYERS + 4;
+  cudaEvent_t fork_ev[NEV] = {};
+  // per-layer dW buffers (when the whole list fits one chunk), so that one
+  // layer's MLP backward can overlap the next layer's conv backward
+  float* dw_layer[MACE_MAX_LAYERS] = {};
   cudaGraphExec_t gexec = nullptr;
   mace_system g_sys{};
   mace_outputs g_out{};
@@ -205,6 +212,7 @@ int launch(mace_ctx* c, const char* name, int layer, cudaStream_t s, Fn&& fn) {
 }
 
 #define LAUNCH(name, layer, expr) TRY(launch(c, name, layer, s, [&]() { return (expr); }))
+#define LAUNCH_ON(st, name, layer, expr) TRY(launch(c, name, layer, st, [&]() { return (expr); }))
 
 int reserve(mace_ctx* c, int64_t N, int64_t E, int64_t EC) {
   const mace_model_desc& d = c->desc;
@@ -223,6 +231,15 @@ int reserve(mace_ctx* c, int64_t N, int64_t E, int64_t EC) {
   if (cudaMemset(c->dw, 0, (size_t)wt_floats(EC, wmax) * sizeof(float)) != cudaSuccess ||
       cudaDeviceSynchronize() != cudaSuccess)
     return fail(MACE_ERR_CUDA, "workspace memset");
+  for (int t = 0; t < T; ++t) c->dw_layer[t] = nullptr;
+  if (EC >= E && T > 1) {
+    for (int t = 0; t < T; ++t) {
+      const int64_t n = wt_floats(EC, d.layers[t].wnumel);
+      TRY(alloc(c, &c->dw_layer[t], n));
+      if (cudaMemset(c->dw_layer[t], 0, (size_t)n * sizeof(float)) != cudaSuccess)
+        return fail(MACE_ERR_CUDA, "workspace memset");
+    }
+  }
   TRY(alloc(c, &c->vir_part, ((E + 255) / 256 + 1) * 9));
   c->h.assign(T + 1, nullptr);
   c->dh.assign(T + 1, nullptr);
@@ -344,7 +361,7 @@ ConvParams conv_params(mace_ctx* c, int t, int64_t N, const mace_system* sys) {
   p.w = c->lb[t].w;
   p.A = c->lb[t].A;
   p.dA = c->lb[t].dA;
-  p.dw = c->dw;
+  p.dw = c->dw_layer[t] ? c->dw_layer[t] : c->dw;
   p.dY = c->dY;
   p.dup = c->lb[t].dup;
   return p;
@@ -364,7 +381,7 @@ MlpParams mlp_params(mace_ctx* c, int t, int64_t e0, int64_t ne) {
   p.b = c->b + e0 * c->desc.num_bessel;
   p.act = c->lb[t].act;
   p.out = c->lb[t].w;
-  p.dout = c->dw;
+  p.dout = c->dw_layer[t] ? c->dw_layer[t] : c->dw;
   p.db = c->db + e0 * c->desc.num_bessel;
   const bool tc_ok = !c->mlp_cuda_cores && L.f_mlp_tc >= 0 && L.f_mlp_tc_bwd >= 0 && L.f_mlp_tc_trunk >= 0 &&
                      L.f_mlp_tc_trunk_bwd >= 0;
@@ -466,6 +483,19 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
     if (ch.e1 - ch.e0 > c->cap_chunk_edges)
       return fail(MACE_ERR_BAD_ARG, "an edge chunk exceeds the reserved chunk capacity (mace_ctx_reserve_chunked)");
   const bool recompute = chunks.size() > 1;
+  // When the list is one chunk, the radial-MLP chain (both layers' forwards,
+  // each layer's backward once its conv backward is done) runs on a second
+  // stream forked from and joined back into `s` with events, so the
+  // latency-bound node kernels overlap it (inside a captured graph the fork
+  // and join become graph edges).
+  const bool fork = !recompute && E > 0 && !sys->halo && c->dw_layer[0] != nullptr;
+  if (fork) {
+    if (!c->aux) MACE_CUDA_TRY(cudaStreamCreateWithFlags(&c->aux, cudaStreamNonBlocking));
+    for (cudaEvent_t& e : c->fork_ev)
+      if (!e) MACE_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  }
+  cudaStream_t sa = fork ? c->aux : s;
+  cudaEvent_t* ev = c->fork_ev;  // 0: edges ready; 1+t: mlp_fwd(t); 1+T+t: conv_bwd(t); 1+2T: last mlp_bwd
   const int T = d.num_layers;
   const int C = d.C;
   c->launches = 0;
@@ -495,6 +525,15 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
   ep.dv = c->dv;
   ep.virial_part = (flags & MACE_WANT_VIRIAL) ? c->vir_part : nullptr;
   if (E > 0) LAUNCH("edge_fwd", -1, launch_edge_fwd(ep, s));
+  if (fork) {
+    MACE_CUDA_TRY(cudaEventRecord(ev[0], s));
+    MACE_CUDA_TRY(cudaStreamWaitEvent(sa, ev[0], 0));
+    for (int t = 0; t < T; ++t) {
+      MlpParams mp = mlp_params(c, t, 0, E);
+      LAUNCH_ON(sa, "mlp_fwd", t, launch_mlp_fwd(mp, sa));
+      MACE_CUDA_TRY(cudaEventRecord(ev[1 + t], sa));
+    }
+  }
   {
     EmbedParams p{N, C, sys->species, F(c, d.f_emb), c->h[0]};
     LAUNCH("embed", -1, launch_embed(p, s));
@@ -510,9 +549,10 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
       LAUNCH("skip_fwd", t, launch_skip(sp, s));
     }
     TRY(run_linear_slots(c, "linear_up", t, N, L.in, L.in, L.f_up, c->h[t], B.up, 0, s));
+    if (fork) MACE_CUDA_TRY(cudaStreamWaitEvent(s, ev[1 + t], 0));
     for (const Chunk& ch : chunks) {
       MlpParams mp = mlp_params(c, t, ch.e0, ch.e1 - ch.e0);
-      if (ch.e1 > ch.e0) LAUNCH("mlp_fwd", t, launch_mlp_fwd(mp, s));
+      if (!fork && ch.e1 > ch.e0) LAUNCH("mlp_fwd", t, launch_mlp_fwd(mp, s));
       ConvParams cp = conv_params(c, t, ch.n1, sys);
       cp.n0 = ch.n0;
       cp.e0 = ch.e0;
@@ -628,7 +668,13 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
       cp.n0 = ch.n0;
       cp.e0 = ch.e0;
       LAUNCH("conv_bwd", t, launch_conv_bwd(cp, s));
-      if (ch.e1 > ch.e0) LAUNCH("mlp_bwd", t, launch_mlp_bwd(mp, s));
+      if (fork) {
+        MACE_CUDA_TRY(cudaEventRecord(ev[1 + T + t], s));
+        MACE_CUDA_TRY(cudaStreamWaitEvent(sa, ev[1 + T + t], 0));
+        LAUNCH_ON(sa, "mlp_bwd", t, launch_mlp_bwd(mp, sa));
+      } else if (ch.e1 > ch.e0) {
+        LAUNCH("mlp_bwd", t, launch_mlp_bwd(mp, s));
+      }
     }
     if (t > 0) {
       // dh[t] holds the readout seed of layer t-1
@@ -641,6 +687,10 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
       if (sys->halo && sys->halo(sys->halo_user, MACE_HALO_GRADIENTS, t - 1, c->dh[t], L.in.dim, s) != 0)
         return fail(MACE_ERR_NCCL, "halo reduction of feature gradients failed");
     }
+  }
+  if (fork) {  // join: every MLP backward has accumulated into db
+    MACE_CUDA_TRY(cudaEventRecord(ev[1 + 2 * T], sa));
+    MACE_CUDA_TRY(cudaStreamWaitEvent(s, ev[1 + 2 * T], 0));
   }
   int n_blocks = (int)((E + 255) / 256);
   if (E > 0) LAUNCH("edge_bwd", -1, launch_edge_bwd(ep, &n_blocks, s));
@@ -874,6 +924,9 @@ int mace_ctx_destroy(mace_ctx* c) {
     for (int i = 0; i < 2 * mace_ctx::PROF_MAX; ++i) cudaEventDestroy(c->ev[i]);
   if (c->gexec) cudaGraphExecDestroy(c->gexec);
   if (c->cap_stream) cudaStreamDestroy(c->cap_stream);
+  if (c->aux) cudaStreamDestroy(c->aux);
+  for (cudaEvent_t e : c->fork_ev)
+    if (e) cudaEventDestroy(e);
   cudaFree(c->d_floats);
   cudaFree(c->d_ints);
   delete c;
