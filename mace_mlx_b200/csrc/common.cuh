@@ -167,12 +167,18 @@ struct ConvParams {
   float* dw;             // (E,wnumel) in 128-edge tiles (wt_index)
   float* dY;             // (E,16) accumulated
   float* dup;            // (N,in_dim)
+  int need_dup;          // 0: the input gradient is not needed (first layer)
+  const int32_t* rev;    // (E) reverse edge
+  float* tq;             // (E, in_dim) per-edge sender-side terms, or null (then gathered from dA)
 };
 int launch_conv_fwd(const ConvParams& p, cudaStream_t s);
-int launch_conv_bwd(const ConvParams& p, cudaStream_t s);
+// *need_gather: the kernel wrote per-edge sender-side terms to p.tq and
+// launch_dup_gather must sum them into p.dup
+int launch_conv_bwd(const ConvParams& p, cudaStream_t s, bool* need_gather);
+int launch_dup_gather(const ConvParams& p, cudaStream_t s);
 // layer-signature specialisations (conv_sig.cu); *used = false: not instantiated
 int launch_conv_fwd_sig(const ConvParams& p, cudaStream_t s, bool* used);
-int launch_conv_bwd_sig(const ConvParams& p, cudaStream_t s, bool* used);
+int launch_conv_bwd_sig(const ConvParams& p, cudaStream_t s, bool* used, bool* need_gather);
 
 // ---------------------------------------------------------------------------
 // node-level ops

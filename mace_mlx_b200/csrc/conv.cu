@@ -317,12 +317,13 @@ int launch_conv_fwd(const ConvParams& p, cudaStream_t s) {
   return MACE_OK;
 }
 
-int launch_conv_bwd(const ConvParams& p, cudaStream_t s) {
+int launch_conv_bwd(const ConvParams& p, cudaStream_t s, bool* need_gather) {
+  *need_gather = false;
   if (p.N <= p.n0) return MACE_OK;
   int rc = conv_check(p);
   if (rc) return rc;
   bool used = false;
-  rc = launch_conv_bwd_sig(p, s, &used);
+  rc = launch_conv_bwd_sig(p, s, &used, need_gather);
   if (rc || used) return rc;
   const int EC = 32;
   const int nw = p.C / 32;
@@ -334,6 +335,33 @@ int launch_conv_bwd(const ConvParams& p, cudaStream_t s) {
     MACE_CUDA_TRY(cudaFuncSetAttribute(k_conv_bwd, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   k_conv_bwd<<<(unsigned)(p.N - p.n0), p.C * G, smem, s>>>(p, EC, G);
   MACE_LAUNCH_CHECK("conv_bwd");
+  return MACE_OK;
+}
+
+namespace {
+// d up[n] = sum over n's incoming edges e of the sender-side term of the
+// reverse edge rev(e) (whose sender is n), in edge order: deterministic
+__global__ void k_dup_gather(ConvParams p) {
+  const int64_t n = p.n0 + blockIdx.x;
+  const int64_t e0 = p.row_ptr[n], e1 = p.row_ptr[n + 1];
+  for (int q = threadIdx.x; q < p.in_dim; q += blockDim.x) {
+    float a0 = 0.f, a1 = 0.f;
+    int64_t e = e0;
+    for (; e + 1 < e1; e += 2) {
+      a0 += __ldg(p.tq + (int64_t)p.rev[e] * p.in_dim + q);
+      a1 += __ldg(p.tq + (int64_t)p.rev[e + 1] * p.in_dim + q);
+    }
+    if (e < e1) a0 += __ldg(p.tq + (int64_t)p.rev[e] * p.in_dim + q);
+    p.dup[n * p.in_dim + q] = a0 + a1;
+  }
+}
+}  // namespace
+
+int launch_dup_gather(const ConvParams& p, cudaStream_t s) {
+  if (p.N <= p.n0) return MACE_OK;
+  const int threads = p.in_dim < 512 ? p.in_dim : 512;
+  k_dup_gather<<<(unsigned)(p.N - p.n0), threads, 0, s>>>(p);
+  MACE_LAUNCH_CHECK("dup_gather");
   return MACE_OK;
 }
 

@@ -82,13 +82,14 @@ __device__ __forceinline__ void each_path(F&& f) {
   for_paths<S>(std::make_integer_sequence<int, S::n>{}, f);
 }
 
-// Stage the senders, SH rows and padded M rows of `ne` edges starting at cb.
-template <class S, int EC, int NT>
+// Stage the senders, SH rows and (WITH_M) padded M rows of `ne` edges starting at cb.
+template <class S, int EC, int NT, bool WITH_M = true>
 __device__ __forceinline__ void stage(const ConvParams& p, int64_t cb, int ne, int* sSnd, float* sY, float* sM) {
   const int tid = threadIdx.x;
   for (int j = tid; j < ne; j += NT) sSnd[j] = p.snd[cb + j];
   for (int q = tid; q < ne * 16; q += NT) sY[q] = p.Y[cb * 16 + q];
   __syncthreads();
+  if (!WITH_M) return;
   constexpr int MT = S::mtot();
   each_path<S>([&](auto kc) {
     constexpr int K = decltype(kc)::value;
@@ -219,7 +220,10 @@ __device__ __forceinline__ float warp_sum16(float s[16]) {
   return s[0] + __shfl_xor_sync(FULLMASK, s[0], 1);
 }
 
-template <int C, int G, class S>
+// MODE 0: no input gradient (first layer); 1: sender-side term gathered from
+// the neighbours' dA (as conv.cu); 2: per-edge sender-side terms from this
+// receiver's H tables, written to p.tq and summed by launch_dup_gather
+template <int C, int G, class S, int MODE>
 struct BwdLayout {
   static constexpr int EC = 32;
   static constexpr int NW = C / 32;  // warps per group
@@ -227,21 +231,26 @@ struct BwdLayout {
   static constexpr int SND = 0;
   static constexpr int Y = SND + EC;
   static constexpr int M = Y + EC * 16;
-  static constexpr int RED = M + EC * S::mtot();
+  static constexpr int RED = M + (MODE == 1 ? EC * S::mtot() : 0);
   static constexpr int H = RED + NW * EC * 16;
   static constexpr int DUP = H + C * HP;
-  static constexpr int TOTAL = DUP + G * S::in_ch() * C;  // floats
+  static constexpr int TOTAL = DUP + (MODE == 1 ? G * S::in_ch() * C : 0);  // floats
 };
 
 // Per receiver n, path k and channel u the receiver's gradient enters every
 // edge only through H_k[i][j] = sum_m pw CG_k[i, j, m] dA[n][k][m][u], built
 // once per CTA; then per edge
 //   dw_e[k, u] = sum_{i,j} x1[i] H[i][j] Y_e[j],   dY_e[j] += w sum_i x1[i] H[i][j],
-//   d up[n][l1 slot][i][u] += (-1)^l2 w sum_m M_k,e[i][m] dA[s_e][k][m][u]   (reverse edge).
+// and the gradient of the sender's features, either (MODE 1) gathered at the
+// sender's own CTA through the reverse edge,
+//   d up[n][l1 slot][i][u] += (-1)^l2 w sum_m M_k,e[i][m] dA[s_e][k][m][u],
+// or (MODE 2) formed here from the same H block and written per edge,
+//   T_e[l1 slot][i][u] = sum_k w_e[k, u] sum_j H_k[i][j] Y_e[j],
+// for launch_dup_gather to sum over each node's outgoing edges.
 // G groups of C threads share one receiver: group g takes edges g, g+G, ...
-template <int C, int G, class S>
+template <int C, int G, class S, int MODE>
 __global__ void __launch_bounds__(C * G, 2) k_conv_bwd_sig(ConvParams p) {
-  using Lay = BwdLayout<C, G, S>;
+  using Lay = BwdLayout<C, G, S, MODE>;
   constexpr int EC = Lay::EC, NW = Lay::NW, HP = Lay::HP, MT = S::mtot(), IC = S::in_ch();
   constexpr int NT = C * G;
   extern __shared__ __align__(16) float sm[];
@@ -282,18 +291,21 @@ __global__ void __launch_bounds__(C * G, 2) k_conv_bwd_sig(ConvParams p) {
     });
   }
   __syncthreads();
-  float dup[IC];
+  float dup[MODE == 1 ? IC : 1];
 #pragma unroll
-  for (int q = 0; q < IC; ++q) dup[q] = 0.f;
+  for (int q = 0; q < (MODE == 1 ? IC : 1); ++q) dup[q] = 0.f;
   const int nch = p.wnch;
   constexpr int64_t KSTRIDE = (int64_t)(C / 32) * WT_CHUNK;
   const float4* hrow = reinterpret_cast<const float4*>(sH + u * HP);
   for (int64_t cb = e_beg; cb < e_end; cb += EC) {
     const int ne = (int)imin64(EC, e_end - cb);
-    stage<S, EC, NT>(p, cb, ne, sSnd, sY, sM);
+    stage<S, EC, NT, MODE == 1>(p, cb, ne, sSnd, sY, sM);
     for (int j = grp; j < ne; j += G) {
       const int64_t e = cb + j;
       const int64_t s = sSnd[j];
+      float tq[MODE == 2 ? IC : 1];
+#pragma unroll
+      for (int q = 0; q < (MODE == 2 ? IC : 1); ++q) tq[q] = 0.f;
       float Ye[16];
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
@@ -322,22 +334,27 @@ __global__ void __launch_bounds__(C * G, 2) k_conv_bwd_sig(ConvParams p) {
         constexpr int XO = L1 * L1, YO = L2 * L2;
         constexpr float PAR = (L2 & 1) ? -1.f : 1.f;
         const float w = __ldg(wp + K * KSTRIDE);
-        const int off = p.slot[K].off;
-        float gr[D3];
-#pragma unroll
-        for (int m = 0; m < D3; ++m) gr[m] = __ldg(dAs + off + m * C);
-        // xh[j] = sum_i x1[i] H[i][j]   (flattened H block: f = i * D2 + j)
-        float xh[D2];
+        // xh[j] = sum_i x1[i] H[i][j]; th[i] = sum_j H[i][j] Y[j]   (flattened H block: f = i * D2 + j)
+        float xh[D2], th[D1];
 #pragma unroll
         for (int jj = 0; jj < D2; ++jj) xh[jj] = 0.f;
+#pragma unroll
+        for (int i = 0; i < D1; ++i) th[i] = 0.f;
 #pragma unroll
         for (int q = 0; q < HQ; ++q) {
           const float4 h4 = hrow[S::hoff(K) / 4 + q];
           const float h[4] = {h4.x, h4.y, h4.z, h4.w};
 #pragma unroll
           for (int c = 0; c < 4; ++c)
-            if (4 * q + c < D1 * D2)
-              xh[(4 * q + c) % D2] = fmaf(x[XO + (4 * q + c) / D2], h[c], xh[(4 * q + c) % D2]);
+            if (4 * q + c < D1 * D2) {
+              const int i = (4 * q + c) / D2, jj = (4 * q + c) % D2;
+              xh[jj] = fmaf(x[XO + i], h[c], xh[jj]);
+              if (MODE == 2) th[i] = fmaf(h[c], Ye[YO + jj], th[i]);
+            }
+        }
+        if constexpr (MODE == 2) {
+#pragma unroll
+          for (int i = 0; i < D1; ++i) tq[XO + i] = fmaf(w, th[i], tq[XO + i]);
         }
         float dw = 0.f;
 #pragma unroll
@@ -346,21 +363,32 @@ __global__ void __launch_bounds__(C * G, 2) k_conv_bwd_sig(ConvParams p) {
           sdy[YO + jj] = fmaf(w, xh[jj], sdy[YO + jj]);
         }
         dwp[K * KSTRIDE] = dw;
-        // sender side through the reverse edge: r[i] = sum_m M[i][m] gr[m]   (f = i * D3 + m)
-        float r[D1];
+        if constexpr (MODE == 1) {
+          // sender side through the reverse edge: r[i] = sum_m M[i][m] gr[m]   (f = i * D3 + m)
+          const int off = p.slot[K].off;
+          float gr[D3];
 #pragma unroll
-        for (int i = 0; i < D1; ++i) r[i] = 0.f;
+          for (int m = 0; m < D3; ++m) gr[m] = __ldg(dAs + off + m * C);
+          float r[D1];
 #pragma unroll
-        for (int q = 0; q < MQ; ++q) {
-          const float4 m4 = mrow[S::moff(K) / 4 + q];
-          const float mv[4] = {m4.x, m4.y, m4.z, m4.w};
+          for (int i = 0; i < D1; ++i) r[i] = 0.f;
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
-            if (4 * q + c < D1 * D3) r[(4 * q + c) / D3] = fmaf(mv[c], gr[(4 * q + c) % D3], r[(4 * q + c) / D3]);
+          for (int q = 0; q < MQ; ++q) {
+            const float4 m4 = mrow[S::moff(K) / 4 + q];
+            const float mv[4] = {m4.x, m4.y, m4.z, m4.w};
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+              if (4 * q + c < D1 * D3) r[(4 * q + c) / D3] = fmaf(mv[c], gr[(4 * q + c) % D3], r[(4 * q + c) / D3]);
+          }
+#pragma unroll
+          for (int i = 0; i < D1; ++i) dup[XO + i] = fmaf(PAR * w, r[i], dup[XO + i]);
         }
-#pragma unroll
-        for (int i = 0; i < D1; ++i) dup[XO + i] = fmaf(PAR * w, r[i], dup[XO + i]);
       });
+      if constexpr (MODE == 2) {
+        float* tp = p.tq + e * (int64_t)(IC * C) + u;
+#pragma unroll
+        for (int q = 0; q < IC; ++q) tp[q * C] = tq[q];
+      }
       const float tot = warp_sum16(sdy);
       if ((lane & 1) == 0) sRed[(warp * EC + j) * 16 + (lane >> 1)] = tot;
     }
@@ -374,14 +402,16 @@ __global__ void __launch_bounds__(C * G, 2) k_conv_bwd_sig(ConvParams p) {
     }
     __syncthreads();
   }
+  if constexpr (MODE == 1) {
 #pragma unroll
-  for (int q = 0; q < IC; ++q) sDup[(grp * IC + q) * C + u] = dup[q];
-  __syncthreads();
-  for (int q = tid; q < IC * C; q += NT) {
-    float v = 0.f;
+    for (int q = 0; q < IC; ++q) sDup[(grp * IC + q) * C + u] = dup[q];
+    __syncthreads();
+    for (int q = tid; q < IC * C; q += NT) {
+      float v = 0.f;
 #pragma unroll
-    for (int g = 0; g < G; ++g) v += sDup[g * IC * C + q];  // fixed order: deterministic
-    p.dup[n * p.in_dim + q] = v;
+      for (int g = 0; g < G; ++g) v += sDup[g * IC * C + q];  // fixed order: deterministic
+      p.dup[n * p.in_dim + q] = v;
+    }
   }
 }
 
@@ -409,14 +439,26 @@ int run_fwd(const ConvParams& p, cudaStream_t s) {
   return MACE_OK;
 }
 
-template <int C, int G, class S>
-int run_bwd(const ConvParams& p, cudaStream_t s) {
-  const size_t smem = (size_t)BwdLayout<C, G, S>::TOTAL * sizeof(float);
+template <int C, int G, class S, int MODE>
+int run_bwd_mode(const ConvParams& p, cudaStream_t s) {
+  const size_t smem = (size_t)BwdLayout<C, G, S, MODE>::TOTAL * sizeof(float);
   if (smem > 227 * 1024) return fail(MACE_ERR_UNSUPPORTED, "conv backward tile exceeds shared memory");
-  MACE_CUDA_TRY(cudaFuncSetAttribute(k_conv_bwd_sig<C, G, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  k_conv_bwd_sig<C, G, S><<<(unsigned)(p.N - p.n0), C * G, smem, s>>>(p);
+  MACE_CUDA_TRY(
+      cudaFuncSetAttribute(k_conv_bwd_sig<C, G, S, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  k_conv_bwd_sig<C, G, S, MODE><<<(unsigned)(p.N - p.n0), C * G, smem, s>>>(p);
   MACE_LAUNCH_CHECK("conv_bwd_sig");
   return MACE_OK;
+}
+
+template <int C, int G, class S>
+int run_bwd(const ConvParams& p, cudaStream_t s, bool* need_gather) {
+  *need_gather = false;
+  if (!p.need_dup) return run_bwd_mode<C, G, S, 0>(p, s);
+  if (p.tq && p.in_dim == S::in_ch() * C) {
+    *need_gather = true;
+    return run_bwd_mode<C, G, S, 2>(p, s);
+  }
+  return run_bwd_mode<C, G, S, 1>(p, s);
 }
 
 // layer signatures of the MACE families in use: input 0e only (first layer,
@@ -438,11 +480,11 @@ int try_fwd(const ConvParams& p, cudaStream_t s, bool* used) {
 }
 
 template <int C>
-int try_bwd(const ConvParams& p, cudaStream_t s, bool* used) {
+int try_bwd(const ConvParams& p, cudaStream_t s, bool* used, bool* need_gather) {
   *used = true;
-  if (sig_matches<SigL0>(p)) return run_bwd<C, 2, SigL0>(p, s);
-  if (sig_matches<SigL1>(p)) return run_bwd<C, 2, SigL1>(p, s);
-  if (sig_matches<SigL2>(p)) return run_bwd<C, 2, SigL2>(p, s);
+  if (sig_matches<SigL0>(p)) return run_bwd<C, 2, SigL0>(p, s, need_gather);
+  if (sig_matches<SigL1>(p)) return run_bwd<C, 2, SigL1>(p, s, need_gather);
+  if (sig_matches<SigL2>(p)) return run_bwd<C, 2, SigL2>(p, s, need_gather);
   *used = false;
   return MACE_OK;
 }
@@ -456,10 +498,11 @@ int launch_conv_fwd_sig(const ConvParams& p, cudaStream_t s, bool* used) {
   return MACE_OK;
 }
 
-int launch_conv_bwd_sig(const ConvParams& p, cudaStream_t s, bool* used) {
+int launch_conv_bwd_sig(const ConvParams& p, cudaStream_t s, bool* used, bool* need_gather) {
   *used = false;
-  if (p.C == 128) return try_bwd<128>(p, s, used);
-  if (p.C == 96) return try_bwd<96>(p, s, used);
+  *need_gather = false;
+  if (p.C == 128) return try_bwd<128>(p, s, used, need_gather);
+  if (p.C == 96) return try_bwd<96>(p, s, used, need_gather);
   return MACE_OK;
 }
 

@@ -122,6 +122,8 @@ struct mace_ctx {
   // per-layer dW buffers (when the whole list fits one chunk), so that one
   // layer's MLP backward can overlap the next layer's conv backward
   float* dw_layer[MACE_MAX_LAYERS] = {};
+  // per-edge sender-side terms of the conv backward (one chunk only), or null
+  float* tq = nullptr;
   cudaGraphExec_t gexec = nullptr;
   mace_system g_sys{};
   mace_outputs g_out{};
@@ -232,7 +234,11 @@ int reserve(mace_ctx* c, int64_t N, int64_t E, int64_t EC) {
       cudaDeviceSynchronize() != cudaSuccess)
     return fail(MACE_ERR_CUDA, "workspace memset");
   for (int t = 0; t < T; ++t) c->dw_layer[t] = nullptr;
+  c->tq = nullptr;
   if (EC >= E && T > 1) {
+    int in_max = 0;
+    for (int t = 1; t < T; ++t) in_max = d.layers[t].in.dim > in_max ? d.layers[t].in.dim : in_max;
+    TRY(alloc(c, &c->tq, E * in_max));
     for (int t = 0; t < T; ++t) {
       const int64_t n = wt_floats(EC, d.layers[t].wnumel);
       TRY(alloc(c, &c->dw_layer[t], n));
@@ -364,6 +370,9 @@ ConvParams conv_params(mace_ctx* c, int t, int64_t N, const mace_system* sys) {
   p.dw = c->dw_layer[t] ? c->dw_layer[t] : c->dw;
   p.dY = c->dY;
   p.dup = c->lb[t].dup;
+  p.need_dup = t > 0;
+  p.rev = sys->rev;
+  p.tq = c->tq;
   return p;
 }
 
@@ -667,7 +676,9 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
       ConvParams cp = conv_params(c, t, ch.n1, sys);
       cp.n0 = ch.n0;
       cp.e0 = ch.e0;
-      LAUNCH("conv_bwd", t, launch_conv_bwd(cp, s));
+      bool gather = false;
+      LAUNCH("conv_bwd", t, launch_conv_bwd(cp, s, &gather));
+      if (gather) LAUNCH("dup_gather", t, launch_dup_gather(cp, s));
       if (fork) {
         MACE_CUDA_TRY(cudaEventRecord(ev[1 + T + t], s));
         MACE_CUDA_TRY(cudaStreamWaitEvent(sa, ev[1 + T + t], 0));
