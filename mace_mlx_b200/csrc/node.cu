@@ -19,7 +19,8 @@ namespace {
 
 // ---------------------------------------------------------------------------
 // o3.Linear: out[(n,m), c] (+)= alpha * sum_{ks,u} in[n, k_off[ks] + m*C + u] * W[ks*C+u][c]
-// 64 x 128 output tile per 256-thread CTA, 8 x 4 outputs per thread; K in
+// 64 x 128 output tile per 256-thread CTA, 8 x 4 outputs per thread (32 x 64,
+// 2 x 4 per thread, for small node counts); K in
 // chunks of 32 through shared memory, the next chunk's loads in flight in
 // registers while the current one is multiplied.  Inner step per thread: two
 // broadcast 128-bit loads of A, one 128-bit load of B, 32 FMAs.
@@ -28,24 +29,32 @@ namespace {
 // each with the other rows' A masked to zero: a single pass when the tile's
 // nodes share one element.
 // ---------------------------------------------------------------------------
-constexpr int LR = 64;        // rows per tile
-constexpr int RPT = LR / 8;   // rows per thread
-constexpr int LK = 32;        // k chunk
-constexpr int LAP = LR + 4;   // pitch of the transposed A tile (16-byte rows, no bank conflicts on the stores)
+constexpr int LK = 32;  // k chunk
 
+// LR x LC output tile per 256-thread CTA (64 x 128, or 32 x 64 with the columns
+// split over blockIdx.z when the rows alone would not fill the GPU)
+template <int LR, int LC>
 __global__ void __launch_bounds__(256) k_linear(LinParams p) {
+  constexpr int CT = LC / 4;     // threads across the columns (4 columns each)
+  constexpr int RG = 256 / CT;   // row groups
+  constexpr int RPT = LR / RG;   // rows per thread
+  constexpr int NA = LR / 32;    // float4 of A per thread per chunk
+  constexpr int NBQ = LC / 32;   // float4 of B per thread per chunk
+  constexpr int LAP = LR + 4;    // pitch of the transposed A tile (16-byte rows, no bank conflicts on the stores)
+  static_assert(RPT == 2 || RPT % 4 == 0, "rows per thread");
   __shared__ __align__(16) float sA[LK][LAP];
-  __shared__ __align__(16) float sB[LK][128];
+  __shared__ __align__(16) float sB[LK][LC];
   __shared__ int sZ[LR + 1];  // distinct species of the tile's rows, count in sZ[LR]
   const LinJob& jb = p.job[blockIdx.y];
   const int C = p.C;
   const int rows = (int)(p.N * jb.d);
   const int r0 = blockIdx.x * LR;
-  if (r0 >= rows) return;
+  const int col0 = blockIdx.z * LC;
+  if (r0 >= rows || col0 >= C) return;
   const int tid = threadIdx.x;
-  const int ty = tid >> 5, tx = tid & 31;
+  const int ty = tid / CT, tx = tid % CT;
   // this thread's A row for the loads (fixed across K)
-  const int lr = tid & (LR - 1), lq = tid >> 6;  // row, first 4-wide k group (and lq + 4)
+  const int lr = tid % LR, lq = tid / LR;  // row, first 4-wide k group (then + 256 / LR)
   const int arow = r0 + lr;
   const bool arow_in = arow < rows;
   const float* abase = p.in;
@@ -80,12 +89,13 @@ __global__ void __launch_bounds__(256) k_linear(LinParams p) {
     const int ks = t / nck, kc = (t - ks * nck) * LK;
     const float* ap = abase + jb.k_off[ks] + kc;
 #pragma unroll
-    for (int h = 0; h < 2; ++h)
-      ra[h] = arow_ok ? __ldg(reinterpret_cast<const float4*>(ap + 4 * (lq + 4 * h))) : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int h = 0; h < NA; ++h)
+      ra[h] = arow_ok ? __ldg(reinterpret_cast<const float4*>(ap + 4 * (lq + (256 / LR) * h)))
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
+    for (int q = 0; q < NBQ; ++q) {
       const int idx = tid + 256 * q;
-      const int kk = idx >> 5, c4 = (idx & 31) * 4;
+      const int kk = idx / CT, c4 = col0 + (idx % CT) * 4;
       rb[q] = (c4 < C) ? __ldg(reinterpret_cast<const float4*>(wbase + (int64_t)(ks * C + kc + kk) * jb.ldb + c4))
                        : make_float4(0.f, 0.f, 0.f, 0.f);
     }
@@ -95,54 +105,67 @@ __global__ void __launch_bounds__(256) k_linear(LinParams p) {
   for (int a = 0; a < RPT; ++a)
 #pragma unroll
     for (int b = 0; b < 4; ++b) acc[a][b] = 0.f;
-  float4 ra[2], rb[4];
+  float4 ra[NA], rb[NBQ];
   for (int pass = 0; pass < n_pass; ++pass) {
-  if (jb.species) {
-    const int z = sZ[pass];
-    arow_ok = arow_in && arow_z == z;
-    wbase = jb.w + (int64_t)z * jb.zstride;
-  }
-  load(0, ra, rb);
-  for (int t = 0; t < nchunks; ++t) {
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int k0 = 4 * (lq + 4 * h);
-      sA[k0 + 0][lr] = ra[h].x;
-      sA[k0 + 1][lr] = ra[h].y;
-      sA[k0 + 2][lr] = ra[h].z;
-      sA[k0 + 3][lr] = ra[h].w;
+    if (jb.species) {
+      const int z = sZ[pass];
+      arow_ok = arow_in && arow_z == z;
+      wbase = jb.w + (int64_t)z * jb.zstride;
     }
+    load(0, ra, rb);
+    for (int t = 0; t < nchunks; ++t) {
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int idx = tid + 256 * q;
-      *reinterpret_cast<float4*>(&sB[idx >> 5][(idx & 31) * 4]) = rb[q];
-    }
-    __syncthreads();
-    if (t + 1 < nchunks) load(t + 1, ra, rb);
-#pragma unroll 8
-    for (int kk = 0; kk < LK; ++kk) {
-      const float4 b4 = *reinterpret_cast<const float4*>(&sB[kk][tx * 4]);
-      const float4 a0 = *reinterpret_cast<const float4*>(&sA[kk][ty * RPT]);
-      const float4 a1 = *reinterpret_cast<const float4*>(&sA[kk][ty * RPT + 4]);
-      const float av[RPT] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-#pragma unroll
-      for (int a = 0; a < RPT; ++a) {
-        acc[a][0] = fmaf(av[a], b4.x, acc[a][0]);
-        acc[a][1] = fmaf(av[a], b4.y, acc[a][1]);
-        acc[a][2] = fmaf(av[a], b4.z, acc[a][2]);
-        acc[a][3] = fmaf(av[a], b4.w, acc[a][3]);
+      for (int h = 0; h < NA; ++h) {
+        const int k0 = 4 * (lq + (256 / LR) * h);
+        sA[k0 + 0][lr] = ra[h].x;
+        sA[k0 + 1][lr] = ra[h].y;
+        sA[k0 + 2][lr] = ra[h].z;
+        sA[k0 + 3][lr] = ra[h].w;
       }
+#pragma unroll
+      for (int q = 0; q < NBQ; ++q) {
+        const int idx = tid + 256 * q;
+        *reinterpret_cast<float4*>(&sB[idx / CT][(idx % CT) * 4]) = rb[q];
+      }
+      __syncthreads();
+      if (t + 1 < nchunks) load(t + 1, ra, rb);
+#pragma unroll 8
+      for (int kk = 0; kk < LK; ++kk) {
+        const float4 b4 = *reinterpret_cast<const float4*>(&sB[kk][tx * 4]);
+        float av[RPT];
+        if constexpr (RPT == 2) {
+          const float2 a2 = *reinterpret_cast<const float2*>(&sA[kk][ty * RPT]);
+          av[0] = a2.x;
+          av[1] = a2.y;
+        } else {
+#pragma unroll
+          for (int v = 0; v < RPT / 4; ++v) {
+            const float4 a4 = *reinterpret_cast<const float4*>(&sA[kk][ty * RPT + 4 * v]);
+            av[4 * v + 0] = a4.x;
+            av[4 * v + 1] = a4.y;
+            av[4 * v + 2] = a4.z;
+            av[4 * v + 3] = a4.w;
+          }
+        }
+#pragma unroll
+        for (int a = 0; a < RPT; ++a) {
+          acc[a][0] = fmaf(av[a], b4.x, acc[a][0]);
+          acc[a][1] = fmaf(av[a], b4.y, acc[a][1]);
+          acc[a][2] = fmaf(av[a], b4.z, acc[a][2]);
+          acc[a][3] = fmaf(av[a], b4.w, acc[a][3]);
+        }
+      }
+      __syncthreads();
     }
-    __syncthreads();
-  }
   }  // species passes
-  if (tx * 4 >= C) return;
+  const int c = col0 + tx * 4;
+  if (c >= C) return;
 #pragma unroll
   for (int a = 0; a < RPT; ++a) {
     const int row = r0 + ty * RPT + a;
     if (row >= rows) continue;
     const int node = row / jb.d, m = row - node * jb.d;
-    float4* o = reinterpret_cast<float4*>(p.out + (int64_t)node * p.out_row + jb.out_off + m * C + tx * 4);
+    float4* o = reinterpret_cast<float4*>(p.out + (int64_t)node * p.out_row + jb.out_off + m * C + c);
     float4 v = make_float4(jb.alpha * acc[a][0], jb.alpha * acc[a][1], jb.alpha * acc[a][2], jb.alpha * acc[a][3]);
     if (jb.accumulate) {
       const float4 w = *o;
@@ -359,9 +382,18 @@ int launch_linear(const LinParams& p, cudaStream_t s) {
   if (p.C > 128 || p.C % 32 != 0) return fail(MACE_ERR_UNSUPPORTED, "linear: C must be a multiple of 32, <= 128");
   if (p.N * 7 >= (int64_t)1 << 31) return fail(MACE_ERR_UNSUPPORTED, "linear: too many rows");
   int dmax = 1;
-  for (int j = 0; j < p.n_jobs; ++j) dmax = p.job[j].d > dmax ? p.job[j].d : dmax;
-  dim3 grid((unsigned)((p.N * dmax + LR - 1) / LR), (unsigned)p.n_jobs);
-  k_linear<<<grid, 256, 0, s>>>(p);
+  int64_t rows_all = 0;
+  for (int j = 0; j < p.n_jobs; ++j) {
+    dmax = p.job[j].d > dmax ? p.job[j].d : dmax;
+    rows_all += p.N * p.job[j].d;
+  }
+  if ((rows_all + 63) / 64 >= 148) {  // at least a wave of 64 x 128 tiles
+    dim3 grid((unsigned)((p.N * dmax + 63) / 64), (unsigned)p.n_jobs, 1);
+    k_linear<64, 128><<<grid, 256, 0, s>>>(p);
+  } else {  // small node counts: 32 x 64 tiles, columns split over grid.z
+    dim3 grid((unsigned)((p.N * dmax + 31) / 32), (unsigned)p.n_jobs, (unsigned)((p.C + 63) / 64));
+    k_linear<32, 64><<<grid, 256, 0, s>>>(p);
+  }
   MACE_LAUNCH_CHECK("linear");
   return MACE_OK;
 }
