@@ -2,29 +2,31 @@
 // with a 3-term hi/lo split for fp32-level accuracy; see tc.cuh).
 //
 // One CTA owns a tile of 128 edges (TMEM lane t = edge t of the tile) and runs
-// five warps: warps 0-3 are the epilogue warps (thread t owns edge t), warp 4
-// is the control warp, whose lane 0 issues every bulk copy and every
-// tcgen05.mma.  The warps hand work to one another through mbarriers only, so
-// no warp waits for the slowest one at a block-wide barrier.  About 113 KB of
-// shared memory (forward) and 97 KB (backward): two CTAs per SM.
+// nine warps: eight epilogue warps (quadrant q = warp & 3 owns TMEM lanes /
+// edges 32q..32q+31, group g = warp >> 2 owns half of the columns) and a
+// control warp whose lane 0 issues every bulk copy and every tcgen05.mma.  The
+// warps hand work to one another through mbarriers only.  The activation-side
+// operand A of every MMA lives in TMEM (written with tcgen05.st, read by the
+// MMA), so shared memory only holds weight images, copy stages and output
+// staging; two CTAs per SM (256 of the SM's 512 TMEM columns each, 96
+// registers per thread).
 //
 // Forward:
 //   layer 0 (radial features -> 64) on the CUDA cores; every 64 x 64 hidden
-//   layer as 8 K-blocks x 3 MMAs (M = 128, N = 64, K = 8) from the swizzled
-//   hi/lo activation tile (A) and a pre-split, pre-swizzled weight image (B);
-//   the last layer in 32-column chunks with two B stages and four TMEM
-//   buffers, so the control warp runs up to three chunks ahead of the
-//   epilogue.  Each epilogue warp moves its 32 rows of a finished chunk from
-//   TMEM through a 4 KB staging slice to HBM with one bulk store: the output
-//   is in the 128-edge tile layout (common.cuh), whose chunk rows are exactly
-//   the staging slice.
+//   layer as 8 K-blocks x 3 MMAs (M = 128, N = 64, K = 8) with a pre-split,
+//   pre-swizzled weight image (B); the last layer in 32-column chunks with two
+//   B stages and four TMEM accumulators, the two epilogue groups taking
+//   alternate chunks, each warp moving its 32 rows of a chunk from TMEM
+//   through a double-buffered 4 KB staging slice to HBM with one bulk store:
+//   the output is in the 128-edge tile layout (common.cuh), whose chunk rows
+//   are exactly a staging slice.
 // Backward:
-//   dH = dW (128 x W) . W_last^T in 32-wide K chunks: the control warp copies
-//   a 16 KB dW chunk (already in operand layout) and the matching 16 KB weight
-//   image per stage, the epilogue warps split it into hi/lo in place, and the
-//   control warp accumulates 4 K-blocks x 3 MMAs into TMEM; then every hidden
-//   layer dH <- (dH * SiLU'(a)) . W_j^T on the tensor cores, and the last step
-//   to dL/db on the CUDA cores.
+//   dH = dW (128 x W) . W_last^T in 32-wide K chunks through three copy
+//   stages: the control warp bulk-copies a 16 KB dW chunk (already in operand
+//   layout) and the matching 16 KB weight image, the epilogue warps split the
+//   chunk into tf32 hi/lo straight into TMEM, and the control warp
+//   accumulates 4 K-blocks x 3 MMAs; then every hidden layer dH <- (dH *
+//   SiLU'(a)) . W_j^T on the tensor cores, and dL/db on the CUDA cores.
 //
 // Every mbarrier wait is bounded (about 2 s).  A wait that gives up raises a
 // CTA-wide abort flag that ends every other wait, the kernel records
@@ -40,8 +42,6 @@ constexpr int TM = 128;           // edges per tile (MMA M)
 constexpr int H = 64;             // hidden width
 constexpr int TC32 = 32;          // output columns per forward chunk (MMA N)
 constexpr int KC = 32;            // backward K chunk (one 128-byte panel)
-constexpr int NEPI = 4;           // epilogue warps
-constexpr int NTHR = 32 * (NEPI + 1);
 constexpr int NBUF = 4;           // forward TMEM chunk buffers of 32 columns
 constexpr int MLP_TC_TIMEOUT = 2;
 constexpr int MLP_TC_ALIGN = 8;   // dynamic shared memory not 1024-byte aligned
@@ -49,41 +49,6 @@ constexpr int IMG = 2 * H * H;    // floats of one 64 x 64 hi/lo image
 constexpr int CIMG = 2 * TC32 * H;  // floats of one forward chunk image (32 x 64, hi/lo)
 constexpr int BIMG = 2 * H * KC;    // floats of one backward chunk image (64 x 32, hi/lo)
 static_assert(WT_CHUNK * 4 == TM * 128, "a radial-weight chunk is one 128 x 128-byte operand panel");
-
-__device__ __forceinline__ void put_hilo(unsigned char* a_hi, unsigned char* a_lo, int row, int k0, float4 v) {
-  float4 hi, lo;
-  hi.x = tc::tf32_hi(v.x);
-  hi.y = tc::tf32_hi(v.y);
-  hi.z = tc::tf32_hi(v.z);
-  hi.w = tc::tf32_hi(v.w);
-  lo.x = v.x - hi.x;
-  lo.y = v.y - hi.y;
-  lo.z = v.z - hi.z;
-  lo.w = v.w - hi.w;
-  const uint32_t off = tc::sw128_offset(row, k0, TM);
-  *reinterpret_cast<float4*>(a_hi + off) = hi;
-  *reinterpret_cast<float4*>(a_lo + off) = lo;
-}
-
-// D (128 x N) = A (128 x 64, hi/lo) . B (N x 64, hi/lo)^T, issued by one thread
-template <int N>
-__device__ __forceinline__ void mma_k64(uint32_t tmem, uint32_t a_hi, uint32_t a_lo, uint32_t b_hi, uint32_t b_lo) {
-  constexpr uint32_t IDESC = tc::idesc_tf32(TM, N);
-#pragma unroll
-  for (int kb = 0; kb < H / 8; ++kb) {
-    const uint32_t oa = (kb >> 2) * (TM * 128) + (kb & 3) * 32;
-    const uint32_t ob = (kb >> 2) * (N * 128) + (kb & 3) * 32;
-    tc::mma_tf32(tmem, tc::sw128_desc(a_hi + oa), tc::sw128_desc(b_hi + ob), IDESC, kb > 0);
-    tc::mma_tf32(tmem, tc::sw128_desc(a_hi + oa), tc::sw128_desc(b_lo + ob), IDESC, 1);
-    tc::mma_tf32(tmem, tc::sw128_desc(a_lo + oa), tc::sw128_desc(b_hi + ob), IDESC, 1);
-  }
-}
-
-__device__ __forceinline__ void tmem_row64(uint32_t tmem, int warp, int col0, float* v) {
-  tc::tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + col0, v);
-  tc::tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + col0 + 32, v + 32);
-  tc::tmem_wait_ld();
-}
 
 // the (NB, 64) layer-0 weights into shared memory by the 128 epilogue threads
 template <int NB>
@@ -349,19 +314,36 @@ __global__ void __maxnreg__(96) k_mlp_fwd_tc(MlpParams p) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// backward
+// ---------------------------------------------------------------------------
+constexpr int B_NST = 3;  // copy stages of (dW chunk, weight chunk image)
+// TMEM: [0, 64) the dH accumulator; stage s's dW chunk as A at 64 + 64 s (hi) and
+// 64 + 64 s + 32 (lo); the hidden layers' A (128 x 64) at [64, 128) hi, [128, 192) lo
+constexpr uint32_t B_ASTAGE = 64, B_TAHI = 64, B_TALO = 128;
+
 struct BwdSmem {
-  // stage s at s * STAGE: dW chunk hi (16 KB, written by the bulk copy and
-  // rounded in place), dW chunk lo (16 KB), weight chunk image (16 KB).
-  // After the K loop: trunk A hi [0, 32K), A lo [32K, 64K), B [64K, 96K).
-  static constexpr int STAGE = 49152;
-  static constexpr int W0 = 2 * STAGE;  // layer-0 weights (NB, 64), <= 4 KB
+  // stage s at s * STAGE: the dW chunk (16 KB, bulk-copied in the 128-edge tile
+  // layout, which is the operand layout) and the weight chunk image (16 KB);
+  // after the K loop the hidden layers' weight image uses [0, 32K)
+  static constexpr int STAGE = 32768;
+  static constexpr int W0 = B_NST * STAGE;       // layer-0 weights (NB, 64), <= 4 KB
+  static constexpr int DB = STAGE;               // at the end: 128 rows x 2 groups x 16 partial dL/db (stage 1)
   static constexpr int BARS = W0 + 4096;
   static constexpr int TOTAL = BARS + 256;
-  static constexpr int LD = 0, SPLIT = 2, MMA = 4, TL = 6, A = 7, ACC = 8, NBARS = 9;
+  static constexpr int REQUEST = 112 * 1024;     // two CTAs per SM (256 TMEM columns each)
+  static constexpr int LD = 0, SPLIT = 3, MMA = 6, TL = 9, A = 10, ACC = 11, NBARS = 12;
 };
+static_assert(BwdSmem::TOTAL <= BwdSmem::REQUEST, "backward shared memory");
 
+// dH = dW . W_last^T in 32-wide K chunks: the control warp bulk-copies each
+// dW chunk and its weight image into one of three stages; the epilogue warps
+// (quadrant q = rows, group g = 16 of the chunk's 32 columns) split the chunk
+// into tf32 hi/lo straight into TMEM (tcgen05.st) for the MMAs, which read A
+// from TMEM; the hidden layers follow as in the forward, and dL/db on the
+// CUDA cores with the two column halves summed through shared memory.
 template <int NB>
-__global__ void __launch_bounds__(NTHR, 2) k_mlp_bwd_tc(MlpParams p) {
+__global__ void __maxnreg__(96) k_mlp_bwd_tc(MlpParams p) {
   extern __shared__ __align__(1024) unsigned char sm[];
   using S = BwdSmem;
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
@@ -379,14 +361,14 @@ __global__ void __launch_bounds__(NTHR, 2) k_mlp_bwd_tc(MlpParams p) {
   const int last = nch - 1;
   const uint32_t base = tc::smem_u32(sm);
 
-  if (warp == NEPI) {
-    tc::tmem_alloc(tc::smem_u32(tslot), H);
+  if (warp == F_NEPI) {
+    tc::tmem_alloc(tc::smem_u32(tslot), F_TMEM);
     tc::tmem_relinquish();
   }
   if (t == 0) {
     for (int i = 0; i < S::NBARS; ++i) {
-      const bool by_warps = (i == S::SPLIT) || (i == S::SPLIT + 1) || (i == S::A);
-      tc::mbar_init(BAR(i), by_warps ? NEPI : 1);
+      const bool by_warps = (i >= S::SPLIT && i < S::SPLIT + B_NST) || i == S::A;
+      tc::mbar_init(BAR(i), by_warps ? F_NEPI : 1);
     }
     *abort_flag = 0;
     tc::fence_barrier_init();
@@ -397,7 +379,7 @@ __global__ void __launch_bounds__(NTHR, 2) k_mlp_bwd_tc(MlpParams p) {
   const uint32_t tmem = *tslot;
   bool ok = true;
 
-  if (warp == NEPI) {
+  if (warp == F_NEPI) {
     if (lane == 0) {
       auto wait = [&](int i, uint32_t par) {
         ok = ok && tc::mbar_wait_or_abort(BAR(i), par, abort_flag);
@@ -405,151 +387,172 @@ __global__ void __launch_bounds__(NTHR, 2) k_mlp_bwd_tc(MlpParams p) {
       };
       const float* dw_tile = p.dout + (int64_t)blockIdx.x * nch * WT_CHUNK;
       auto copy_chunk = [&](int k) {
-        const int s = k & 1;
+        const int s = k % B_NST;
         const uint32_t st = base + s * S::STAGE;
         tc::mbar_expect_tx(BAR(S::LD + s), (WT_CHUNK + BIMG) * 4);
         tc::bulk_g2s(st, dw_tile + (int64_t)k * WT_CHUNK, WT_CHUNK * 4, BAR(S::LD + s));
-        tc::bulk_g2s(st + 32768, p.tc_img_bwd + (int64_t)k * BIMG, BIMG * 4, BAR(S::LD + s));
+        tc::bulk_g2s(st + 16384, p.tc_img_bwd + (int64_t)k * BIMG, BIMG * 4, BAR(S::LD + s));
       };
       constexpr uint32_t IDESC = tc::idesc_tf32(TM, H);
-      copy_chunk(0);
-      if (nch > 1) copy_chunk(1);
+      for (int k = 0; k < B_NST && k < nch; ++k) copy_chunk(k);
       for (int kc = 0; kc < nch; ++kc) {
-        const int s = kc & 1;
-        if (!wait(S::SPLIT + s, (kc >> 1) & 1)) break;
+        const int s = kc % B_NST;
+        if (!wait(S::SPLIT + s, (kc / B_NST) & 1)) break;
         tc::fence_after_sync();
-        const uint32_t ah = base + s * S::STAGE, al = ah + 16384, bh = ah + 32768, bl = bh + 8192;
+        const uint32_t ah = tmem + B_ASTAGE + 64 * s, al = ah + 32;
+        const uint32_t bh = base + s * S::STAGE + 16384, bl = bh + 8192;
 #pragma unroll
         for (int kb = 0; kb < KC / 8; ++kb) {
           const uint32_t off = kb * 32;
-          tc::mma_tf32(tmem, tc::sw128_desc(ah + off), tc::sw128_desc(bh + off), IDESC, (kc > 0 || kb > 0));
-          tc::mma_tf32(tmem, tc::sw128_desc(ah + off), tc::sw128_desc(bl + off), IDESC, 1);
-          tc::mma_tf32(tmem, tc::sw128_desc(al + off), tc::sw128_desc(bh + off), IDESC, 1);
+          tc::mma_tf32_ta(tmem, ah + kb * 8, tc::sw128_desc(bh + off), IDESC, (kc > 0 || kb > 0));
+          tc::mma_tf32_ta(tmem, ah + kb * 8, tc::sw128_desc(bl + off), IDESC, 1);
+          tc::mma_tf32_ta(tmem, al + kb * 8, tc::sw128_desc(bh + off), IDESC, 1);
         }
         tc::mma_commit(BAR(S::MMA + s));
-        if (kc + 2 < nch) {  // stage s is free once MMA(kc) is done
-          if (!wait(S::MMA + s, (kc >> 1) & 1)) break;
-          copy_chunk(kc + 2);
+        if (kc + B_NST < nch) {  // stage s (smem and TMEM) is free once MMA(kc) is done
+          if (!wait(S::MMA + s, (kc / B_NST) & 1)) break;
+          copy_chunk(kc + B_NST);
         }
       }
-      // every K-chunk MMA done before the trunk reuses the stages
-      wait(S::MMA + (last & 1), (last >> 1) & 1);
+      // every K-chunk MMA done before the hidden layers reuse stage memory and TMEM
+      wait(S::MMA + (last % B_NST), (last / B_NST) & 1);
       uint32_t pa = 0, pacc = 0, ptl = 0;
-      const uint32_t a_hi = base, a_lo = base + 32768, b_hi = base + 65536, b_lo = b_hi + 16384;
       for (int j = nh - 1; j >= 1 && ok; --j) {
         tc::mbar_expect_tx(BAR(S::TL), IMG * 4);
-        tc::bulk_g2s(b_hi, p.tc_trunk_bwd + (int64_t)(j - 1) * IMG, IMG * 4, BAR(S::TL));
+        tc::bulk_g2s(base, p.tc_trunk_bwd + (int64_t)(j - 1) * IMG, IMG * 4, BAR(S::TL));
         if (!wait(S::A, pa) || !wait(S::TL, ptl)) break;
         pa ^= 1;
         ptl ^= 1;
         tc::fence_after_sync();
-        mma_k64<H>(tmem, a_hi, a_lo, b_hi, b_lo);
+        mma_k64_ta<H>(tmem, tmem + B_TAHI, tmem + B_TALO, base, base + IMG * 2);
         tc::mma_commit(BAR(S::ACC));
-        if (!wait(S::ACC, pacc)) break;  // B is free again
+        if (!wait(S::ACC, pacc)) break;  // the weight image is free again
         pacc ^= 1;
       }
     }
     __syncwarp();
   } else {
-    const int64_t e = (int64_t)blockIdx.x * TM + t;
+    const int q = warp & 3, g = warp >> 2;
+    const int row = q * 32 + lane;
+    const int64_t e = (int64_t)blockIdx.x * TM + row;
     const bool valid = e < p.E;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     auto wwait = [&](int i, uint32_t par) {
       const bool r = ok && tc::mbar_wait_or_abort(BAR(i), par, abort_flag);
       ok = __all_sync(0xffffffffu, r);
       return ok;
     };
     float* sW0 = reinterpret_cast<float*>(sm + S::W0);
-    load_w0<NB>(p, sW0, t);
-    // split each dW chunk into tf32 hi (in place) and lo
+    for (int i = t; i < NB * H / 4; i += 32 * F_NEPI)
+      reinterpret_cast<float4*>(sW0)[i] = __ldg(reinterpret_cast<const float4*>(p.w[0]) + i);
+    tc::named_sync(1, 32 * F_NEPI);
+    // split each dW chunk into tf32 hi / lo, into TMEM
     for (int kc = 0; kc < nch; ++kc) {
-      const int s = kc & 1;
-      if (!wwait(S::LD + s, (kc >> 1) & 1)) break;
-      unsigned char* ah = sm + s * S::STAGE;
-      unsigned char* al = ah + 16384;
+      const int s = kc % B_NST;
+      if (!wwait(S::LD + s, (kc / B_NST) & 1)) break;
+      const unsigned char* src = sm + s * S::STAGE + row * 128;
+      float v[16];
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const uint32_t off = t * 128 + ((q ^ (t & 7)) << 4);
-        const float4 v = *reinterpret_cast<const float4*>(ah + off);
-        float4 hi, lo;
-        hi.x = tc::tf32_hi(v.x);
-        hi.y = tc::tf32_hi(v.y);
-        hi.z = tc::tf32_hi(v.z);
-        hi.w = tc::tf32_hi(v.w);
-        lo.x = v.x - hi.x;
-        lo.y = v.y - hi.y;
-        lo.z = v.z - hi.z;
-        lo.w = v.w - hi.w;
-        *reinterpret_cast<float4*>(ah + off) = hi;
-        *reinterpret_cast<float4*>(al + off) = lo;
+      for (int u = 0; u < 4; ++u) {
+        const float4 x = *reinterpret_cast<const float4*>(src + (((4 * g + u) ^ (row & 7)) << 4));
+        v[4 * u] = x.x;
+        v[4 * u + 1] = x.y;
+        v[4 * u + 2] = x.z;
+        v[4 * u + 3] = x.w;
       }
-      tc::fence_proxy_async();
+      float part[16];
+#pragma unroll
+      for (int o = 0; o < 16; ++o) part[o] = tc::tf32_hi(v[o]);
+      tc::tmem_st16(tmem + lane_base + B_ASTAGE + 64 * s + 16 * g, part);
+#pragma unroll
+      for (int o = 0; o < 16; ++o) part[o] = v[o] - tc::tf32_hi(v[o]);
+      tc::tmem_st16(tmem + lane_base + B_ASTAGE + 64 * s + 32 + 16 * g, part);
+      tc::tmem_wait_st();
+      tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(BAR(S::SPLIT + s));
     }
-    float dh[H];
-    if (wwait(S::MMA + (last & 1), (last >> 1) & 1)) {
+    float dh[32];
+    if (wwait(S::MMA + (last % B_NST), (last / B_NST) & 1)) {
       tc::fence_after_sync();
-      tmem_row64(tmem, warp, 0, dh);
+      tc::tmem_ld32(tmem + lane_base + 32 * g, dh);
+      tc::tmem_wait_ld();
     }
-    // hidden layers nh-1 .. 1 on the tensor cores
-    unsigned char* a_hi_p = sm;
-    unsigned char* a_lo_p = sm + 32768;
+    // hidden layers nh-1 .. 1 on the tensor cores, this group's 32 columns
     uint32_t pacc = 0;
     for (int j = nh - 1; j >= 1 && ok; --j) {
-      const float4* a4 = reinterpret_cast<const float4*>(p.act + e * (int64_t)(nh * H) + j * H);
+      const float4* a4 = reinterpret_cast<const float4*>(p.act + e * (int64_t)(nh * H) + j * H + 32 * g);
 #pragma unroll
-      for (int q = 0; q < H / 4; ++q) {
-        float4 d = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (valid) {
-          const float4 a = a4[q];
-          d = make_float4(dh[4 * q] * silu_grad_f(a.x), dh[4 * q + 1] * silu_grad_f(a.y),
-                          dh[4 * q + 2] * silu_grad_f(a.z), dh[4 * q + 3] * silu_grad_f(a.w));
-        }
-        put_hilo(a_hi_p, a_lo_p, t, 4 * q, d);
+      for (int k = 0; k < 8; ++k) {
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (valid) a = a4[k];
+        dh[4 * k + 0] = valid ? dh[4 * k + 0] * silu_grad_f(a.x) : 0.f;
+        dh[4 * k + 1] = valid ? dh[4 * k + 1] * silu_grad_f(a.y) : 0.f;
+        dh[4 * k + 2] = valid ? dh[4 * k + 2] * silu_grad_f(a.z) : 0.f;
+        dh[4 * k + 3] = valid ? dh[4 * k + 3] * silu_grad_f(a.w) : 0.f;
       }
-      tc::fence_proxy_async();
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        float part[16];
+#pragma unroll
+        for (int o = 0; o < 16; ++o) part[o] = tc::tf32_hi(dh[16 * hf + o]);
+        tc::tmem_st16(tmem + lane_base + B_TAHI + 32 * g + 16 * hf, part);
+#pragma unroll
+        for (int o = 0; o < 16; ++o) part[o] = dh[16 * hf + o] - tc::tf32_hi(dh[16 * hf + o]);
+        tc::tmem_st16(tmem + lane_base + B_TALO + 32 * g + 16 * hf, part);
+      }
+      tc::tmem_wait_st();
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(BAR(S::A));
       if (!wwait(S::ACC, pacc)) break;
       pacc ^= 1;
       tc::fence_after_sync();
-      tmem_row64(tmem, warp, 0, dh);
+      tc::tmem_ld32(tmem + lane_base + 32 * g, dh);
+      tc::tmem_wait_ld();
     }
-    // layer 0 on the CUDA cores: dL/db[i] = sum_o dh[o] SiLU'(a0[o]) W0[i][o]
-    if (ok && valid) {
-      float da[H];
-      const float4* a4 = reinterpret_cast<const float4*>(p.act + e * (int64_t)(nh * H));
+    // layer 0 on the CUDA cores: dL/db[i] = sum_o dh[o] SiLU'(a0[o]) W0[i][o], the
+    // two column halves added through shared memory
+    float* sDb = reinterpret_cast<float*>(sm + S::DB);
+    if (ok) {
+      float da[32];
+      const float4* a4 = reinterpret_cast<const float4*>(p.act + e * (int64_t)(nh * H) + 32 * g);
 #pragma unroll
-      for (int q = 0; q < H / 4; ++q) {
-        const float4 a = a4[q];
-        da[4 * q + 0] = dh[4 * q + 0] * silu_grad_f(a.x);
-        da[4 * q + 1] = dh[4 * q + 1] * silu_grad_f(a.y);
-        da[4 * q + 2] = dh[4 * q + 2] * silu_grad_f(a.z);
-        da[4 * q + 3] = dh[4 * q + 3] * silu_grad_f(a.w);
+      for (int k = 0; k < 8; ++k) {
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (valid) a = a4[k];
+        da[4 * k + 0] = dh[4 * k + 0] * silu_grad_f(a.x);
+        da[4 * k + 1] = dh[4 * k + 1] * silu_grad_f(a.y);
+        da[4 * k + 2] = dh[4 * k + 2] * silu_grad_f(a.z);
+        da[4 * k + 3] = dh[4 * k + 3] * silu_grad_f(a.w);
       }
 #pragma unroll
       for (int i = 0; i < NB; ++i) {
-        const float4* w4 = reinterpret_cast<const float4*>(sW0 + i * H);
+        const float4* w4 = reinterpret_cast<const float4*>(sW0 + i * H + 32 * g);
         float acc = 0.f;
 #pragma unroll
-        for (int q = 0; q < H / 4; ++q) {
-          const float4 w = w4[q];
-          acc = fmaf(da[4 * q + 0], w.x, acc);
-          acc = fmaf(da[4 * q + 1], w.y, acc);
-          acc = fmaf(da[4 * q + 2], w.z, acc);
-          acc = fmaf(da[4 * q + 3], w.w, acc);
+        for (int k = 0; k < 8; ++k) {
+          const float4 w = w4[k];
+          acc = fmaf(da[4 * k + 0], w.x, acc);
+          acc = fmaf(da[4 * k + 1], w.y, acc);
+          acc = fmaf(da[4 * k + 2], w.z, acc);
+          acc = fmaf(da[4 * k + 3], w.w, acc);
         }
-        p.db[e * NB + i] += acc;
+        sDb[(row * 2 + g) * 16 + i] = acc;
       }
+    }
+    tc::named_sync(1, 32 * F_NEPI);
+    if (ok && g == 0 && valid) {
+#pragma unroll
+      for (int i = 0; i < NB; ++i) p.db[e * NB + i] += sDb[(row * 2) * 16 + i] + sDb[(row * 2 + 1) * 16 + i];
     }
   }
   tc::fence_before_sync();
   __syncthreads();
   if (!ok) atomicExch(p.err_flag, MLP_TC_TIMEOUT);
-  if (warp == NEPI) {
+  if (warp == F_NEPI) {
     tc::fence_after_sync();
-    tc::tmem_dealloc(tmem, H);
+    tc::tmem_dealloc(tmem, F_TMEM);
   }
 }
 
@@ -567,11 +570,11 @@ int launch_fwd_nb(const MlpParams& p, cudaStream_t s) {
 
 template <int NB>
 int launch_bwd_nb(const MlpParams& p, cudaStream_t s) {
-  const size_t smem = BwdSmem::TOTAL;
+  const size_t smem = BwdSmem::REQUEST;
   MACE_CUDA_TRY(cudaFuncSetAttribute(k_mlp_bwd_tc<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   MACE_CUDA_TRY(cudaFuncSetAttribute(k_mlp_bwd_tc<NB>, cudaFuncAttributePreferredSharedMemoryCarveout,
                                      (int)cudaSharedmemCarveoutMaxShared));
-  k_mlp_bwd_tc<NB><<<(unsigned)((p.E + TM - 1) / TM), NTHR, smem, s>>>(p);
+  k_mlp_bwd_tc<NB><<<(unsigned)((p.E + TM - 1) / TM), F_NTHR, smem, s>>>(p);
   MACE_LAUNCH_CHECK("mlp_bwd_tc");
   return MACE_OK;
 }
