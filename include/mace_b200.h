@@ -328,6 +328,11 @@ int mace_last_launch_count(const mace_ctx* ctx, int32_t* count);
 int mace_profile_enable(mace_ctx* ctx, int32_t enable);
 int mace_profile_read(mace_ctx* ctx, int32_t max_entries, char* names, int32_t* layers,
                       int32_t* counts, double* total_ms, int32_t* n_entries);
+/* The last profiled step's launches in issue order: name, layer, stream (0 =
+ * the caller's, 1 = the runtime's second stream), start and end in
+ * milliseconds from the step's first launch. */
+int mace_profile_timeline(mace_ctx* ctx, int32_t max_entries, char* names, int32_t* layers,
+                          int32_t* streams, float* start_ms, float* end_ms, int32_t* n_entries);
 
 /* Synchronise the device, return and clear the context's device error flag
  * (1 = an edge's reverse index did not point back to it). */

@@ -195,6 +195,11 @@ struct LinJob {
   // species-indexed weights (skip_tp): row (n, m) uses w + species[n] * zstride
   const int32_t* species;
   int64_t zstride;
+  // this job's output rows, or null for LinParams::out / out_row
+  float* out;
+  int out_row;
+  // tensor-core operand image of w (launch_tc_image), or null (CUDA cores)
+  const float* tc;
 };
 struct LinParams {
   int64_t N;
@@ -205,8 +210,19 @@ struct LinParams {
   int out_row;
   int n_jobs;
   LinJob job[MACE_MAX_MID];
+  int* err_flag;  // device error flag (tensor-core wait timeouts), may be null
 };
+// device error flag values of the tensor-core kernels
+constexpr int TC_ERR_TIMEOUT = 2;  // an mbarrier wait gave up
+constexpr int TC_ERR_ALIGN = 8;    // dynamic shared memory not 1024-byte aligned
+// the tensor-core kernel when every job has an image (linear_tc.cu), else CUDA cores
 int launch_linear(const LinParams& p, cudaStream_t s);
+bool linear_tc_supported(const LinParams& p);
+int launch_linear_tc(const LinParams& p, cudaStream_t s);
+// operand image of the first N columns of the (K x ldb) row-major weight w
+// (Z species blocks zstride apart): tc_image_floats(K, N, Z) floats at img
+int64_t tc_image_floats(int K, int N, int Z);
+int launch_tc_image(const float* w, int K, int ldb, int N, int Z, int64_t zstride, float* img, cudaStream_t s);
 
 struct SkipParams {
   int64_t N;
@@ -221,9 +237,13 @@ struct SkipParams {
   int in_off[MACE_MAX_IN];
   int out_off[MACE_MAX_IN];
   const float* w[MACE_MAX_IN];  // (num_elements, C, C)
+  const float* tc[MACE_MAX_IN];  // their tensor-core images, or null
   int accumulate;
+  int* err_flag;
 };
 int launch_skip(const SkipParams& p, cudaStream_t s);
+// the skip_tp jobs of p as species-indexed linear jobs writing p.out (returns the count)
+int skip_jobs(const SkipParams& p, LinJob* jobs);
 
 struct ScParams {
   int64_t N;

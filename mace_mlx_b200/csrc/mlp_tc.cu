@@ -43,8 +43,8 @@ constexpr int H = 64;             // hidden width
 constexpr int TC32 = 32;          // output columns per forward chunk (MMA N)
 constexpr int KC = 32;            // backward K chunk (one 128-byte panel)
 constexpr int NBUF = 4;           // forward TMEM chunk buffers of 32 columns
-constexpr int MLP_TC_TIMEOUT = 2;
-constexpr int MLP_TC_ALIGN = 8;   // dynamic shared memory not 1024-byte aligned
+constexpr int MLP_TC_TIMEOUT = TC_ERR_TIMEOUT;
+constexpr int MLP_TC_ALIGN = TC_ERR_ALIGN;
 constexpr int IMG = 2 * H * H;    // floats of one 64 x 64 hi/lo image
 constexpr int CIMG = 2 * TC32 * H;  // floats of one forward chunk image (32 x 64, hi/lo)
 constexpr int BIMG = 2 * H * KC;    // floats of one backward chunk image (64 x 32, hi/lo)

@@ -165,7 +165,9 @@ __global__ void __launch_bounds__(256) k_linear(LinParams p) {
     const int row = r0 + ty * RPT + a;
     if (row >= rows) continue;
     const int node = row / jb.d, m = row - node * jb.d;
-    float4* o = reinterpret_cast<float4*>(p.out + (int64_t)node * p.out_row + jb.out_off + m * C + c);
+    float* const outp = jb.out ? jb.out : p.out;
+    const int orow = jb.out ? jb.out_row : p.out_row;
+    float4* o = reinterpret_cast<float4*>(outp + (int64_t)node * orow + jb.out_off + m * C + c);
     float4 v = make_float4(jb.alpha * acc[a][0], jb.alpha * acc[a][1], jb.alpha * acc[a][2], jb.alpha * acc[a][3]);
     if (jb.accumulate) {
       const float4 w = *o;
@@ -381,6 +383,7 @@ int launch_linear(const LinParams& p, cudaStream_t s) {
   if (p.N == 0 || p.n_jobs == 0) return MACE_OK;
   if (p.C > 128 || p.C % 32 != 0) return fail(MACE_ERR_UNSUPPORTED, "linear: C must be a multiple of 32, <= 128");
   if (p.N * 7 >= (int64_t)1 << 31) return fail(MACE_ERR_UNSUPPORTED, "linear: too many rows");
+  if (linear_tc_supported(p)) return launch_linear_tc(p, s);
   int dmax = 1;
   int64_t rows_all = 0;
   for (int j = 0; j < p.n_jobs; ++j) {
@@ -400,18 +403,10 @@ int launch_linear(const LinParams& p, cudaStream_t s) {
 
 // skip_tp with a one-hot species input = per-species (C, C) weights: run as
 // species-indexed linear jobs
-int launch_skip(const SkipParams& p, cudaStream_t s) {
-  if (p.N == 0 || p.n_jobs == 0) return MACE_OK;
-  LinParams lp{};
-  lp.N = p.N;
-  lp.C = p.C;
-  lp.in = p.in;
-  lp.in_row = p.in_row;
-  lp.out = p.out;
-  lp.out_row = p.out_row;
-  lp.n_jobs = p.n_jobs;
+int skip_jobs(const SkipParams& p, LinJob* jobs) {
   for (int q = 0; q < p.n_jobs; ++q) {
-    LinJob& j = lp.job[q];
+    LinJob& j = jobs[q];
+    j = LinJob{};
     j.d = p.d[q];
     j.n_k = 1;
     j.k_off[0] = p.in_off[q];
@@ -422,7 +417,24 @@ int launch_skip(const SkipParams& p, cudaStream_t s) {
     j.accumulate = p.accumulate;
     j.species = p.species;
     j.zstride = (int64_t)p.C * p.C;
+    j.out = p.out;
+    j.out_row = p.out_row;
+    j.tc = p.tc[q];
   }
+  return p.n_jobs;
+}
+
+int launch_skip(const SkipParams& p, cudaStream_t s) {
+  if (p.N == 0 || p.n_jobs == 0) return MACE_OK;
+  LinParams lp{};
+  lp.N = p.N;
+  lp.C = p.C;
+  lp.in = p.in;
+  lp.in_row = p.in_row;
+  lp.out = p.out;
+  lp.out_row = p.out_row;
+  lp.n_jobs = skip_jobs(p, lp.job);
+  lp.err_flag = p.err_flag;
   return launch_linear(lp, s);
 }
 

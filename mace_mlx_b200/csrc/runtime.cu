@@ -96,6 +96,14 @@ struct mace_ctx {
   int* d_err = nullptr;
   // MACE_B200_MLP_CUDA_CORES=1 at context creation selects the CUDA-core MLP kernels
   bool mlp_cuda_cores = false;
+  // MACE_B200_SINGLE_STREAM=1 at context creation keeps every kernel on the
+  // caller's stream (no radial-MLP fork)
+  bool single_stream = false;
+  // tensor-core operand images of the node-linear weights, by weight pointer
+  // (MACE_B200_LINEAR_CUDA_CORES=1 at context creation leaves them out, which
+  // keeps the node linears on the CUDA cores)
+  float* tc_images = nullptr;
+  std::vector<std::pair<const float*, const float*>> tc_index;
   // bookkeeping
   int launches = 0;
   int64_t last_N = 0, last_E = 0;
@@ -106,6 +114,15 @@ struct mace_ctx {
   cudaEvent_t ev[2 * PROF_MAX] = {};
   const char* prof_name[PROF_MAX] = {};
   int prof_layer[PROF_MAX] = {};
+  int prof_stream[PROF_MAX] = {};
+  // the last folded step's launches: start and end relative to its first launch
+  struct ProfSpan {
+    std::string name;
+    int layer;
+    int stream;
+    float t0, t1;
+  };
+  std::vector<ProfSpan> prof_last;
   struct ProfAcc {
     std::string name;
     int layer;
@@ -117,7 +134,7 @@ struct mace_ctx {
   cudaStream_t cap_stream = nullptr;
   // second stream for the radial-MLP chain (forked from and joined into the step's stream)
   cudaStream_t aux = nullptr;
-  static constexpr int NEV = 2 * MACE_MAX_LAYERS + 4;
+  static constexpr int NEV = 4 * MACE_MAX_LAYERS + 4;
   cudaEvent_t fork_ev[NEV] = {};
   // per-layer dW buffers (when the whole list fits one chunk), so that one
   // layer's MLP backward can overlap the next layer's conv backward
@@ -130,6 +147,9 @@ struct mace_ctx {
   int g_flags = -1;
   std::vector<int64_t> g_chunks;  // chunk boundaries of the captured call (host arrays)
   int g_launches = 0;
+  // profiling inside the graph: its event-record nodes fill the first g_prof_n slots
+  bool g_prof = false;
+  int g_prof_n = 0;
 };
 
 namespace {
@@ -180,9 +200,14 @@ int alloc(mace_ctx* c, T** p, int64_t count) {
 int prof_fold(mace_ctx* c) {
   if (c->prof_n == 0) return MACE_OK;
   MACE_CUDA_TRY(cudaEventSynchronize(c->ev[2 * c->prof_n - 1]));
+  for (int i = 0; i < c->prof_n; ++i) MACE_CUDA_TRY(cudaEventSynchronize(c->ev[2 * i + 1]));
+  c->prof_last.clear();
   for (int i = 0; i < c->prof_n; ++i) {
-    float ms = 0.f;
+    float ms = 0.f, t0 = 0.f, t1 = 0.f;
     MACE_CUDA_TRY(cudaEventElapsedTime(&ms, c->ev[2 * i], c->ev[2 * i + 1]));
+    MACE_CUDA_TRY(cudaEventElapsedTime(&t0, c->ev[0], c->ev[2 * i]));
+    MACE_CUDA_TRY(cudaEventElapsedTime(&t1, c->ev[0], c->ev[2 * i + 1]));
+    c->prof_last.push_back({c->prof_name[i], c->prof_layer[i], c->prof_stream[i], t0, t1});
     bool found = false;
     for (auto& a : c->prof_acc)
       if (a.layer == c->prof_layer[i] && a.name == c->prof_name[i]) {
@@ -206,10 +231,12 @@ int launch(mace_ctx* c, const char* name, int layer, cudaStream_t s, Fn&& fn) {
     slot = c->prof_n++;
     c->prof_name[slot] = name;
     c->prof_layer[slot] = layer;
-    MACE_CUDA_TRY(cudaEventRecord(c->ev[2 * slot], s));
+    c->prof_stream[slot] = (s == c->aux && c->aux) ? 1 : 0;
+    // external: inside a stream capture the records become event-record nodes of the graph
+    MACE_CUDA_TRY(cudaEventRecordWithFlags(c->ev[2 * slot], s, cudaEventRecordExternal));
   }
   int rc = fn();
-  if (slot >= 0) MACE_CUDA_TRY(cudaEventRecord(c->ev[2 * slot + 1], s));
+  if (slot >= 0) MACE_CUDA_TRY(cudaEventRecordWithFlags(c->ev[2 * slot + 1], s, cudaEventRecordExternal));
   return rc;
 }
 
@@ -299,9 +326,16 @@ int reserve(mace_ctx* c, int64_t N, int64_t E, int64_t EC) {
 // ---------------------------------------------------------------------------
 // job builders for the node linears
 // ---------------------------------------------------------------------------
-LinJob make_job(int d, int n_k, const int* k_off, int out_off, const float* w, int ldb, float alpha,
-                int accumulate) {
+const float* tc_find(const mace_ctx* c, const float* w) {
+  for (const auto& e : c->tc_index)
+    if (e.first == w) return e.second;
+  return nullptr;
+}
+
+LinJob make_job(const mace_ctx* c, int d, int n_k, const int* k_off, int out_off, const float* w, int ldb,
+                float alpha, int accumulate) {
   LinJob j{};
+  j.tc = tc_find(c, w);
   j.d = d;
   j.n_k = n_k;
   for (int q = 0; q < n_k; ++q) j.k_off[q] = k_off[q];
@@ -325,9 +359,10 @@ int run_linear_slots(mace_ctx* c, const char* name, int layer, int64_t N, const 
   p.out = out;
   p.out_row = out_slots.dim;
   p.n_jobs = in_slots.n;
+  p.err_flag = c->d_err;
   for (int q = 0; q < in_slots.n; ++q) {
     int ko = in_slots.off[q];
-    p.job[q] = make_job(2 * in_slots.l[q] + 1, 1, &ko, out_slots.off[q], F(c, f_w[q]), p.C, 1.f, accumulate);
+    p.job[q] = make_job(c, 2 * in_slots.l[q] + 1, 1, &ko, out_slots.off[q], F(c, f_w[q]), p.C, 1.f, accumulate);
   }
   return launch(c, name, layer, s, [&]() { return launch_linear(p, s); });
 }
@@ -446,6 +481,7 @@ SkipParams skip_params(mace_ctx* c, int t, int64_t N, const int32_t* species, bo
   p.in = in;
   p.out = out;
   p.accumulate = accumulate;
+  p.err_flag = c->d_err;
   p.in_row = transpose ? out_s.dim : in_s.dim;
   p.out_row = transpose ? in_s.dim : out_s.dim;
   for (int q = 0; q < L.n_skip; ++q) {
@@ -460,6 +496,7 @@ SkipParams skip_params(mace_ctx* c, int t, int64_t N, const int32_t* species, bo
       p.out_off[q] = in_s.off[si];
       p.w[q] = F(c, L.f_skip_t[q]);
     }
+    p.tc[q] = tc_find(c, p.w[q]);
   }
   return p;
 }
@@ -497,14 +534,16 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
   // stream forked from and joined back into `s` with events, so the
   // latency-bound node kernels overlap it (inside a captured graph the fork
   // and join become graph edges).
-  const bool fork = !recompute && E > 0 && !sys->halo && c->dw_layer[0] != nullptr;
+  const bool fork = !recompute && E > 0 && !sys->halo && c->dw_layer[0] != nullptr && !c->single_stream;
   if (fork) {
     if (!c->aux) MACE_CUDA_TRY(cudaStreamCreateWithFlags(&c->aux, cudaStreamNonBlocking));
     for (cudaEvent_t& e : c->fork_ev)
       if (!e) MACE_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
   }
   cudaStream_t sa = fork ? c->aux : s;
-  cudaEvent_t* ev = c->fork_ev;  // 0: edges ready; 1+t: mlp_fwd(t); 1+T+t: conv_bwd(t); 1+2T: last mlp_bwd
+  // events: 0 edges ready; 1+t mlp_fwd(t); 1+T+t conv_bwd(t); 1+2T last mlp_bwd;
+  // 2+2T+t dh[t+1] final; 2+3T+t skip_bwd(t) done
+  cudaEvent_t* ev = c->fork_ev;
   const int T = d.num_layers;
   const int C = d.C;
   c->launches = 0;
@@ -553,11 +592,26 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
     LayerBufs& B = c->lb[t];
     // skip connection written first; the product linear accumulates onto it
     MACE_CUDA_TRY(cudaMemsetAsync(c->h[t + 1], 0, sizeof(float) * N * L.hid.dim, s));
-    if (L.residual) {
-      SkipParams sp = skip_params(c, t, N, sys->species, false, L.in, L.hid, c->h[t], c->h[t + 1], 0);
-      LAUNCH("skip_fwd", t, launch_skip(sp, s));
+    {
+      // linear_up (h[t] -> up) and, in residual layers, the skip (h[t] -> h[t+1]) in one launch
+      LinParams lp{};
+      lp.err_flag = c->d_err;
+      lp.N = N;
+      lp.C = C;
+      lp.in = c->h[t];
+      lp.in_row = L.in.dim;
+      lp.out = B.up;
+      lp.out_row = L.in.dim;
+      for (int q = 0; q < L.in.n; ++q) {
+        int ko = L.in.off[q];
+        lp.job[lp.n_jobs++] = make_job(c, 2 * L.in.l[q] + 1, 1, &ko, L.in.off[q], F(c, L.f_up[q]), C, 1.f, 0);
+      }
+      if (L.residual) {
+        SkipParams sp = skip_params(c, t, N, sys->species, false, L.in, L.hid, c->h[t], c->h[t + 1], 0);
+        lp.n_jobs += skip_jobs(sp, lp.job + lp.n_jobs);
+      }
+      LAUNCH("linear_up+skip", t, launch_linear(lp, s));
     }
-    TRY(run_linear_slots(c, "linear_up", t, N, L.in, L.in, L.f_up, c->h[t], B.up, 0, s));
     if (fork) MACE_CUDA_TRY(cudaStreamWaitEvent(s, ev[1 + t], 0));
     for (const Chunk& ch : chunks) {
       MlpParams mp = mlp_params(c, t, ch.e0, ch.e1 - ch.e0);
@@ -569,6 +623,7 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
     }
     {
       LinParams lp{};
+      lp.err_flag = c->d_err;
       lp.N = N;
       lp.C = C;
       lp.in = B.A;
@@ -580,7 +635,7 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
         const mace_lin_group& g = L.lin[l];
         int ko[MACE_MAX_SRC];
         for (int q = 0; q < g.n_src; ++q) ko[q] = L.conv[g.src[q]].off;
-        lp.job[l] = make_job(2 * l + 1, g.n_src, ko, L.inter.off[l], F(c, g.f_w), C, d.inv_avg_num_neighbors, 0);
+        lp.job[l] = make_job(c, 2 * l + 1, g.n_src, ko, L.inter.off[l], F(c, g.f_w), C, d.inv_avg_num_neighbors, 0);
       }
       LAUNCH("linear_msg", t, launch_linear(lp, s));
     }
@@ -639,6 +694,20 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
   for (int t = T - 1; t >= 0; --t) {
     const mace_layer_desc& L = d.layers[t];
     LayerBufs& B = c->lb[t];
+    // the residual skip's gradient (dh[t+1] -> dh[t]) only needs dh[t+1]: it
+    // accumulates into dh[t] first (same order with and without the fork), on
+    // the second stream overlapping this layer's backward and joined before
+    // linear_up_bwd accumulates into dh[t]
+    const bool early_skip = t > 0 && L.residual;
+    if (early_skip) {
+      if (fork) {
+        MACE_CUDA_TRY(cudaEventRecord(ev[2 + 2 * T + t], s));
+        MACE_CUDA_TRY(cudaStreamWaitEvent(sa, ev[2 + 2 * T + t], 0));
+      }
+      SkipParams sp = skip_params(c, t, N, sys->species, true, L.in, L.hid, c->dh[t + 1], c->dh[t], 1);
+      LAUNCH_ON(sa, "skip_bwd", t, launch_skip(sp, sa));
+      if (fork) MACE_CUDA_TRY(cudaEventRecord(ev[2 + 3 * T + t], sa));
+    }
     TRY(run_linear_slots(c, "linear_prod_bwd", t, N, L.hid, L.hid, L.f_prod_t, c->dh[t + 1], B.dB, 0, s));
     float* dsc_in = B.dmsg;
     ScParams scp = sc_params(c, t, N, sys->species, L.residual ? B.msg : B.msg2, nullptr, B.dB,
@@ -652,6 +721,7 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
     {
       // dA[mid slot k] = inv_avg * dmsg[inter slot l_k] @ W_l^T (block q of the concat-K)
       LinParams lp{};
+      lp.err_flag = c->d_err;
       lp.N = N;
       lp.C = C;
       lp.in = dsc_in;
@@ -663,7 +733,7 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
         const mace_lin_group& g = L.lin[l];
         for (int q = 0; q < g.n_src; ++q) {
           int ko = L.inter.off[l];
-          lp.job[lp.n_jobs++] = make_job(2 * l + 1, 1, &ko, L.conv[g.src[q]].off, F(c, g.f_wt) + q * C,
+          lp.job[lp.n_jobs++] = make_job(c, 2 * l + 1, 1, &ko, L.conv[g.src[q]].off, F(c, g.f_wt) + q * C,
                                          g.n_src * C, d.inv_avg_num_neighbors, 0);
         }
       }
@@ -689,11 +759,8 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
     }
     if (t > 0) {
       // dh[t] holds the readout seed of layer t-1
+      if (early_skip && fork) MACE_CUDA_TRY(cudaStreamWaitEvent(s, ev[2 + 3 * T + t], 0));
       TRY(run_linear_slots(c, "linear_up_bwd", t, N, L.in, L.in, L.f_up_t, B.dup, c->dh[t], 1, s));
-      if (L.residual) {
-        SkipParams sp = skip_params(c, t, N, sys->species, true, L.in, L.hid, c->dh[t + 1], c->dh[t], 1);
-        LAUNCH("skip_bwd", t, launch_skip(sp, s));
-      }
       // dh[t]: gradient w.r.t. the features layer t - 1 produced
       if (sys->halo && sys->halo(sys->halo_user, MACE_HALO_GRADIENTS, t - 1, c->dh[t], L.in.dim, s) != 0)
         return fail(MACE_ERR_NCCL, "halo reduction of feature gradients failed");
@@ -889,6 +956,53 @@ int mace_last_error(char* buf, size_t len) {
   return MACE_OK;
 }
 
+// tensor-core images of every node-linear weight the step uses (one
+// allocation, made once: the weights never change)
+int tc_prepare(mace_ctx* c) {
+  const mace_model_desc& d = c->desc;
+  const int C = d.C;
+  struct Want {
+    const float* w;
+    int K, ldb, Z;
+    int64_t zstride;
+  };
+  std::vector<Want> want;
+  for (int t = 0; t < d.num_layers; ++t) {
+    const mace_layer_desc& L = d.layers[t];
+    for (int q = 0; q < L.in.n; ++q) {
+      want.push_back({F(c, L.f_up[q]), C, C, 1, 0});
+      want.push_back({F(c, L.f_up_t[q]), C, C, 1, 0});
+    }
+    for (int q = 0; q < L.hid.n; ++q) {
+      want.push_back({F(c, L.f_prod[q]), C, C, 1, 0});
+      want.push_back({F(c, L.f_prod_t[q]), C, C, 1, 0});
+    }
+    for (int l = 0; l < L.inter.n; ++l) {
+      const mace_lin_group& g = L.lin[l];
+      want.push_back({F(c, g.f_w), g.n_src * C, C, 1, 0});
+      for (int q = 0; q < g.n_src; ++q) want.push_back({F(c, g.f_wt) + q * C, C, g.n_src * C, 1, 0});
+    }
+    for (int q = 0; q < L.n_skip; ++q) {
+      want.push_back({F(c, L.f_skip[q]), C, C, d.num_elements, (int64_t)C * C});
+      want.push_back({F(c, L.f_skip_t[q]), C, C, d.num_elements, (int64_t)C * C});
+    }
+  }
+  int64_t total = 0;
+  for (const Want& x : want) total += tc_image_floats(x.K, C, x.Z);
+  if (total == 0) return MACE_OK;
+  MACE_CUDA_TRY(cudaMalloc(&c->tc_images, sizeof(float) * total));
+  int64_t off = 0;
+  for (const Want& x : want) {
+    if (tc_find(c, x.w)) continue;
+    float* img = c->tc_images + off;
+    TRY(launch_tc_image(x.w, x.K, x.ldb, C, x.Z, x.zstride, img, 0));
+    c->tc_index.push_back({x.w, img});
+    off += tc_image_floats(x.K, C, x.Z);
+  }
+  MACE_CUDA_TRY(cudaStreamSynchronize(0));
+  return MACE_OK;
+}
+
 int mace_ctx_create(const mace_model_desc* desc, int device, mace_ctx** out) {
   if (!desc || !out) return fail(MACE_ERR_BAD_ARG, "null argument");
   if (desc->abi_version != MACE_ABI_VERSION) return fail(MACE_ERR_BAD_ARG, "model description ABI version mismatch");
@@ -923,6 +1037,19 @@ int mace_ctx_create(const mace_model_desc* desc, int device, mace_ctx** out) {
   c->desc.ints = nullptr;
   const char* env = std::getenv("MACE_B200_MLP_CUDA_CORES");
   c->mlp_cuda_cores = env && env[0] == '1';
+  const char* senv = std::getenv("MACE_B200_SINGLE_STREAM");
+  c->single_stream = senv && senv[0] == '1';
+  const char* lenv = std::getenv("MACE_B200_LINEAR_CUDA_CORES");
+  if (!(lenv && lenv[0] == '1')) {
+    const int rc = tc_prepare(c);
+    if (rc) {
+      cudaFree(c->tc_images);
+      cudaFree(c->d_floats);
+      cudaFree(c->d_ints);
+      delete c;
+      return rc;
+    }
+  }
   *out = c;
   return MACE_OK;
 }
@@ -938,6 +1065,7 @@ int mace_ctx_destroy(mace_ctx* c) {
   if (c->aux) cudaStreamDestroy(c->aux);
   for (cudaEvent_t e : c->fork_ev)
     if (e) cudaEventDestroy(e);
+  cudaFree(c->tc_images);
   cudaFree(c->d_floats);
   cudaFree(c->d_ints);
   delete c;
@@ -993,7 +1121,7 @@ int mace_forward_backward(mace_ctx* c, const mace_system* sys, const mace_output
   DeviceGuard g(c->device);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int base_flags = flags & ~MACE_USE_GRAPH;
-  if (!(flags & MACE_USE_GRAPH) || c->prof_on || sys->halo) return forward_backward(c, sys, out, base_flags, s);
+  if (!(flags & MACE_USE_GRAPH) || sys->halo) return forward_backward(c, sys, out, base_flags, s);
   mace_outputs o{};
   if (out) o = *out;
   std::vector<int64_t> chunk_key;
@@ -1001,7 +1129,9 @@ int mace_forward_backward(mace_ctx* c, const mace_system* sys, const mace_output
     chunk_key.assign(sys->chunk_nodes, sys->chunk_nodes + sys->n_chunks + 1);
     chunk_key.insert(chunk_key.end(), sys->chunk_edges, sys->chunk_edges + sys->n_chunks + 1);
   }
-  const bool same = c->gexec && c->g_flags == base_flags && std::memcmp(&c->g_sys, sys, sizeof(mace_system)) == 0 &&
+  if (c->prof_on) TRY(prof_fold(c));  // the previous replay's events
+  const bool same = c->gexec && c->g_flags == base_flags && c->g_prof == c->prof_on &&
+                    std::memcmp(&c->g_sys, sys, sizeof(mace_system)) == 0 &&
                     std::memcmp(&c->g_out, &o, sizeof(mace_outputs)) == 0 && c->g_chunks == chunk_key;
   if (!same) {
     if (c->gexec) {
@@ -1029,11 +1159,14 @@ int mace_forward_backward(mace_ctx* c, const mace_system* sys, const mace_output
     c->g_sys = *sys;
     c->g_out = o;
     c->g_flags = base_flags;
+    c->g_prof = c->prof_on;
+    c->g_prof_n = c->prof_n;
     c->g_chunks = chunk_key;
     c->g_launches = c->launches;
   }
   MACE_CUDA_TRY(cudaGraphLaunch(c->gexec, s));
   c->launches = c->g_launches;
+  if (c->prof_on) c->prof_n = c->g_prof_n;
   c->last_N = sys->n_nodes;
   c->last_E = sys->n_edges;
   return MACE_OK;
@@ -1111,6 +1244,25 @@ int mace_profile_read(mace_ctx* c, int32_t max_entries, char* names, int32_t* la
   }
   *n_entries = n;
   c->prof_acc.clear();
+  return MACE_OK;
+}
+
+int mace_profile_timeline(mace_ctx* c, int32_t max_entries, char* names, int32_t* layers, int32_t* streams,
+                          float* start_ms, float* end_ms, int32_t* n_entries) {
+  if (!c || !n_entries) return fail(MACE_ERR_BAD_ARG, "null argument");
+  DeviceGuard g(c->device);
+  TRY(prof_fold(c));
+  int n = 0;
+  for (const auto& a : c->prof_last) {
+    if (n >= max_entries) break;
+    if (names) std::snprintf(names + 32 * n, 32, "%s", a.name.c_str());
+    if (layers) layers[n] = a.layer;
+    if (streams) streams[n] = a.stream;
+    if (start_ms) start_ms[n] = a.t0;
+    if (end_ms) end_ms[n] = a.t1;
+    ++n;
+  }
+  *n_entries = n;
   return MACE_OK;
 }
 

@@ -289,6 +289,20 @@ class MACEModel:
             out.append({"name": nm, "layer": layers[i], "count": counts[i], "ms": ms[i]})
         return out
 
+    def profile_timeline(self) -> list[dict]:
+        """The last profiled step's launches: name, layer, stream, start/end ms from its first launch."""
+        mx = 256
+        names = C.create_string_buffer(32 * mx)
+        layers = (C.c_int32 * mx)()
+        streams = (C.c_int32 * mx)()
+        t0 = (C.c_float * mx)()
+        t1 = (C.c_float * mx)()
+        n = C.c_int32()
+        nv.check(self.lib.mace_profile_timeline(self.ctx, mx, names, layers, streams, t0, t1, C.byref(n)),
+                 self.lib)
+        return [{"name": names.raw[32 * i: 32 * (i + 1)].split(b"\0", 1)[0].decode(), "layer": layers[i],
+                 "stream": streams[i], "start_ms": t0[i], "end_ms": t1[i]} for i in range(n.value)]
+
     def error_flag(self) -> int:
         c = C.c_int32()
         nv.check(self.lib.mace_ctx_error_flag(self.ctx, C.byref(c)), self.lib)

@@ -122,6 +122,7 @@ EXPORTED = (
     "mace_last_error", "mace_ctx_create", "mace_ctx_destroy", "mace_ctx_reserve", "mace_ctx_reserve_chunked",
     "mace_ctx_workspace_bytes", "mace_nl_build", "mace_forward_backward", "mace_debug_buffer",
     "mace_last_launch_count", "mace_ctx_error_flag", "mace_profile_enable", "mace_profile_read",
+    "mace_profile_timeline",
     "mace_nl_build_noalloc",
 )
 NOALLOC_MAX_ATOMS = 131072
@@ -160,6 +161,8 @@ def load_library(path: str | Path | None = None) -> C.CDLL:
         "mace_profile_enable": ([vp, i32], C.c_int),
         "mace_profile_read": ([vp, i32, C.c_char_p, C.POINTER(i32), C.POINTER(i32), C.POINTER(C.c_double),
                                C.POINTER(i32)], C.c_int),
+        "mace_profile_timeline": ([vp, i32, C.c_char_p, C.POINTER(i32), C.POINTER(i32), C.POINTER(C.c_float),
+                                   C.POINTER(C.c_float), C.POINTER(i32)], C.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)

@@ -180,6 +180,25 @@ def test_tensor_core_mlp_matches_cuda_core_mlp(monkeypatch):
     assert abs(a["energy"][0] - b["energy"][0]) < 1e-5 * max(1.0, abs(b["energy"][0]))
 
 
+def test_tensor_core_linears_match_cuda_core_linears(monkeypatch):
+    """tcgen05 (3-term tf32) node linears and species-indexed skips vs the fp32 CUDA-core kernel.
+
+    A four-element box puts several species in most 128-row tiles (one
+    species pass each); 300 atoms leave ragged last tiles in every job.
+    """
+    st = lipso_box(300, seed=5)
+    config, weights, _ = make_case("medium", st, seed=14)
+    m_tc = MACEModel(config=config, weights=weights, device=0)
+    monkeypatch.setenv("MACE_B200_LINEAR_CUDA_CORES", "1")
+    m_cc = MACEModel(config=config, weights=weights, device=0)
+    a, _, _ = run_gpu(m_tc, st)
+    b, _, _ = run_gpu(m_cc, st)
+    assert rel_err(a["node_energy"], b["node_energy"]) < 2e-5
+    assert rel_err(a["forces"], b["forces"]) < 2e-5
+    assert rel_err(a["stress"], b["stress"]) < 2e-5
+    assert m_tc.error_flag() == 0
+
+
 def _eval(m, st, edges, species, weight=None):
     dev = m.device
     gp = torch.as_tensor(graph_ptr_of(st), device=dev)
