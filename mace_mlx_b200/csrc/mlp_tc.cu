@@ -14,10 +14,11 @@
 // Forward:
 //   layer 0 (radial features -> 64) on the CUDA cores; every 64 x 64 hidden
 //   layer as 8 K-blocks x 3 MMAs (M = 128, N = 64, K = 8) with a pre-split,
-//   pre-swizzled weight image (B); the last layer in 32-column chunks with two
-//   B stages and four TMEM accumulators, the two epilogue groups taking
-//   alternate chunks, each warp moving its 32 rows of a chunk from TMEM
-//   through a double-buffered 4 KB staging slice to HBM with one bulk store:
+//   pre-swizzled weight image (B); the last layer in 32-column chunks with four
+//   B stages (each refilled three chunks ahead, so the image copies stay off
+//   the critical path) and four TMEM accumulators, the two epilogue groups
+//   taking alternate chunks, each warp moving its 32 rows of a chunk from TMEM
+//   through a 4 KB staging slice to HBM with one bulk store:
 //   the output is in the 128-edge tile layout (common.cuh), whose chunk rows
 //   are exactly a staging slice.
 // Backward:
@@ -88,14 +89,17 @@ constexpr int F_NTHR = 32 * (F_NEPI + 1); // + control warp
 constexpr int F_TMEM = 256;               // [0, 128) accumulators, [128, 192) A hi, [192, 256) A lo
 constexpr uint32_t F_AHI = 128, F_ALO = 192;
 
+constexpr int F_NBS = 4;  // forward chunk-image stages
 struct FwdSmem {
-  static constexpr int B = 0;          // 32 KB: one 64 x 64 hidden image, or two 32-row chunk images
-  static constexpr int STG = 32768;    // 8 warps x 2 x 4 KB output staging; holds the layer-0 weights first
-  static constexpr int BARS = STG + F_NEPI * 2 * 4096;
+  // 64 KB: four 32-row chunk images; the 64 x 64 hidden image uses the first 32 KB
+  static constexpr int B = 0;
+  static constexpr int STG = F_NBS * CIMG * 4;  // 8 warps x 4 KB output staging; holds the layer-0 weights first
+  static constexpr int BARS = STG + F_NEPI * 4096;
   static constexpr int TOTAL = BARS + 256;
   // request enough to keep two CTAs per SM (each holds 256 of the SM's 512 TMEM columns)
   static constexpr int REQUEST = 100 * 1024;
-  static constexpr int TL = 0, A = 1, ACC = 2, BST = 3, FULL = 5, FREE = 9, NBARS = 13;
+  static constexpr int TL = 0, A = 1, ACC = 2, BST = 3, FULL = BST + F_NBS, FREE = FULL + NBUF,
+                       NBARS = FREE + NBUF;
 };
 static_assert(FwdSmem::TOTAL <= FwdSmem::REQUEST, "forward shared memory");
 
@@ -115,9 +119,10 @@ __device__ __forceinline__ void mma_k64_ta(uint32_t tmem_d, uint32_t a_hi, uint3
 
 // One CTA per 128-edge tile, 8 epilogue warps + 1 control warp, two CTAs per SM.
 // The activation operand A lives in TMEM (written with tcgen05.st), so shared
-// memory only holds the weight images and the output staging, which each
-// epilogue warp double-buffers: a chunk's bulk store drains while the warp
-// prepares the next one.  The epilogue warp groups take alternate chunks.
+// memory only holds the weight images (four chunk stages, refilled three
+// chunks ahead) and one 4 KB output staging slice per epilogue warp, whose
+// bulk store drains while the warp's group waits for its next chunk.  The
+// epilogue warp groups take alternate chunks.
 template <int NB>
 __global__ void __maxnreg__(96) k_mlp_fwd_tc(MlpParams p) {
   extern __shared__ __align__(1024) unsigned char sm[];
@@ -168,12 +173,14 @@ __global__ void __maxnreg__(96) k_mlp_fwd_tc(MlpParams p) {
         tc::bulk_g2s(b_base, p.tc_trunk + (int64_t)j * IMG, IMG * 4, BAR(S::TL));
       };
       auto copy_chunk = [&](int c) {
-        const int s = c & 1;
+        const int s = c % F_NBS;
         tc::mbar_expect_tx(BAR(S::BST + s), CIMG * 4);
         tc::bulk_g2s(b_base + s * CIMG * 4, p.tc_img + (int64_t)c * CIMG, CIMG * 4, BAR(S::BST + s));
       };
       const uint32_t a_hi = tmem + F_AHI, a_lo = tmem + F_ALO;
       uint32_t pa = 0;
+      // chunk images 2 and 3 do not overlap the hidden-layer image: fetch them now
+      for (int c = 2; c < F_NBS && c < nch; ++c) copy_chunk(c);
       if (nh >= 2) copy_trunk(0);
       for (int j = 1; j < nh; ++j) {  // hidden layer j reads A = SiLU(layer j-1)
         if (!wait(S::TL, (j - 1) & 1) || !wait(S::A, pa)) break;
@@ -190,16 +197,17 @@ __global__ void __maxnreg__(96) k_mlp_fwd_tc(MlpParams p) {
       }
       if (ok && wait(S::A, pa)) {  // A = SiLU(last hidden layer)
         for (int c = 0; c < nch; ++c) {
-          const int s = c & 1, buf = c % NBUF;
-          if (!wait(S::BST + s, (c >> 1) & 1)) break;
+          const int s = c % F_NBS, buf = c % NBUF;
+          if (!wait(S::BST + s, (c / F_NBS) & 1)) break;
           if (c >= NBUF && !wait(S::FREE + buf, ((c / NBUF) - 1) & 1)) break;
           tc::fence_after_sync();
           const uint32_t bs = b_base + s * CIMG * 4;
           mma_k64_ta<TC32>(tmem + buf * TC32, a_hi, a_lo, bs, bs + CIMG * 2);
           tc::mma_commit(BAR(S::FULL + buf));
-          if (c >= 1 && c + 1 < nch) {  // stage (c+1)&1 is free once MMA(c-1) is done
+          // stage (c - 1) % F_NBS is free once MMA(c - 1) is done: chunk c + F_NBS - 1 goes there
+          if (c >= 1 && c + F_NBS - 1 < nch) {
             if (!wait(S::FULL + (c - 1) % NBUF, ((c - 1) / NBUF) & 1)) break;
-            copy_chunk(c + 1);
+            copy_chunk(c + F_NBS - 1);
           }
         }
       }
@@ -275,8 +283,7 @@ __global__ void __maxnreg__(96) k_mlp_fwd_tc(MlpParams p) {
     }
     // output chunks c = g, g + 2, ...: TMEM -> registers -> staging -> bulk store
     float* dst = p.out + (int64_t)blockIdx.x * nch * WT_CHUNK + q * 32 * 32;
-    int k = 0;
-    for (int c = g; c < nch && ok; c += 2, ++k) {
+    for (int c = g; c < nch && ok; c += 2) {
       const int buf = c % NBUF;
       if (!wwait(S::FULL + buf, (c / NBUF) & 1)) break;
       tc::fence_after_sync();
@@ -285,10 +292,10 @@ __global__ void __maxnreg__(96) k_mlp_fwd_tc(MlpParams p) {
       tc::tmem_wait_ld();
       tc::fence_before_sync();
       __syncwarp();
-      unsigned char* stg = sm + S::STG + (warp * 2 + (k & 1)) * 4096;
+      unsigned char* stg = sm + S::STG + warp * 4096;
       if (lane == 0) {
         tc::mbar_arrive(BAR(S::FREE + buf));
-        tc::bulk_wait_read_but_one();  // the store issued from this buffer two chunks ago has read it
+        tc::bulk_wait_read_all();  // this warp's previous store has read its staging buffer
       }
       __syncwarp();
 #pragma unroll
