@@ -139,21 +139,48 @@ __global__ void __launch_bounds__(C) k_conv_fwd_sig(ConvParams p) {
   for (int q = 0; q < S::atot(); ++q) acc[q] = 0.f;
   const int nch = p.wnch;
   constexpr int64_t KSTRIDE = (int64_t)(C / 32) * WT_CHUNK;  // path k+1 is this far from path k
+  // EPI edges per step; the next EPI edges' sender features and radial
+  // weights are loaded while these are computed (small signatures stream more
+  // edges at once: their per-edge arithmetic is short)
+  constexpr int EPI = S::n <= 4 ? 4 : 1;
+  float xn[EPI][S::in_ch()], wn[EPI][S::n];
+  auto fetch = [&](int64_t cb, int j0, int ne) {
+#pragma unroll
+    for (int b = 0; b < EPI; ++b) {
+      if (j0 + b >= ne) break;
+      load_sender<S, C>(p, sSnd[j0 + b], u, xn[b]);
+      const float* wp = p.w + wt_index(cb + j0 + b - p.e0, u, nch);
+#pragma unroll
+      for (int k = 0; k < S::n; ++k) wn[b][k] = __ldg(wp + k * KSTRIDE);
+    }
+  };
   for (int64_t cb = e_beg; cb < e_end; cb += EC) {
     const int ne = (int)imin64(EC, e_end - cb);
     stage<S, EC, C>(p, cb, ne, sSnd, sY, sM);
-    for (int j = 0; j < ne; ++j) {
-      const int64_t e = cb + j;
-      float x[S::in_ch()];
-      load_sender<S, C>(p, sSnd[j], u, x);
-      const float* wp = p.w + wt_index(e - p.e0, u, nch);
+    fetch(cb, 0, ne);
+    for (int j0 = 0; j0 < ne; j0 += EPI) {
+      float xb[EPI][S::in_ch()], wb[EPI][S::n];
+#pragma unroll
+      for (int b = 0; b < EPI; ++b) {
+#pragma unroll
+        for (int q = 0; q < S::in_ch(); ++q) xb[b][q] = xn[b][q];
+#pragma unroll
+        for (int k = 0; k < S::n; ++k) wb[b][k] = wn[b][k];
+      }
+      if (j0 + EPI < ne) fetch(cb, j0 + EPI, ne);
+#pragma unroll
+      for (int b = 0; b < EPI; ++b) {
+      const int j = j0 + b;
+      if (j >= ne) break;
+      const float* x = xb[b];
+      const float* wv = wb[b];
       const float* Mrow = sM + j * MT;
       each_path<S>([&](auto kc) {
         constexpr int K = decltype(kc)::value;
         constexpr int CODE = S::code(K);
         constexpr int L1 = cl1(CODE), D1 = dim(L1), D3 = dim(cl3(CODE)), NQ = up4(D1 * D3) / 4;
         constexpr int XO = L1 * L1, AO = S::aoff(K);
-        const float w = __ldg(wp + K * KSTRIDE);
+        const float w = wv[K];
         const float4* mk = reinterpret_cast<const float4*>(Mrow + S::moff(K));
         float t[D3];
 #pragma unroll
@@ -170,6 +197,7 @@ __global__ void __launch_bounds__(C) k_conv_fwd_sig(ConvParams p) {
 #pragma unroll
         for (int m = 0; m < D3; ++m) acc[AO + m] = fmaf(w, t[m], acc[AO + m]);
       });
+      }
     }
     __syncthreads();
   }
@@ -297,10 +325,39 @@ __global__ void __launch_bounds__(C * G, 2) k_conv_bwd_sig(ConvParams p) {
   const int nch = p.wnch;
   constexpr int64_t KSTRIDE = (int64_t)(C / 32) * WT_CHUNK;
   const float4* hrow = reinterpret_cast<const float4*>(sH + u * HP);
+  // EPI of this group's edges per step; the next EPI edges' sender features
+  // and radial weights are loaded while these are computed
+  constexpr int EPI = S::n <= 4 ? 4 : 1;
+  float xn[EPI][IC], wn[EPI][S::n];
+  auto fetch = [&](int64_t cb, int j0, int ne) {
+#pragma unroll
+    for (int b = 0; b < EPI; ++b) {
+      const int j = j0 + b * G;
+      if (j >= ne) break;
+      load_sender<S, C>(p, sSnd[j], u, xn[b]);
+      const float* wp = p.w + wt_index(cb + j - p.e0, u, nch);
+#pragma unroll
+      for (int k = 0; k < S::n; ++k) wn[b][k] = __ldg(wp + k * KSTRIDE);
+    }
+  };
   for (int64_t cb = e_beg; cb < e_end; cb += EC) {
     const int ne = (int)imin64(EC, e_end - cb);
     stage<S, EC, NT, MODE == 1>(p, cb, ne, sSnd, sY, sM);
-    for (int j = grp; j < ne; j += G) {
+    fetch(cb, grp, ne);
+    for (int j0 = grp; j0 < ne; j0 += EPI * G) {
+      float xb[EPI][IC], wb[EPI][S::n];
+#pragma unroll
+      for (int b = 0; b < EPI; ++b) {
+#pragma unroll
+        for (int q = 0; q < IC; ++q) xb[b][q] = xn[b][q];
+#pragma unroll
+        for (int k = 0; k < S::n; ++k) wb[b][k] = wn[b][k];
+      }
+      if (j0 + EPI * G < ne) fetch(cb, j0 + EPI * G, ne);
+#pragma unroll
+      for (int b = 0; b < EPI; ++b) {
+      const int j = j0 + b * G;
+      if (j >= ne) break;
       const int64_t e = cb + j;
       const int64_t s = sSnd[j];
       float tq[MODE == 2 ? IC : 1];
@@ -315,10 +372,9 @@ __global__ void __launch_bounds__(C * G, 2) k_conv_bwd_sig(ConvParams p) {
         Ye[4 * q + 2] = v.z;
         Ye[4 * q + 3] = v.w;
       }
-      float x[IC];
-      load_sender<S, C>(p, s, u, x);
+      const float* x = xb[b];
+      const float* wv = wb[b];
       const int64_t wi = wt_index(e - p.e0, u, nch);
-      const float* wp = p.w + wi;
       float* dwp = p.dw + wi;
       const float* dAs = p.dA + s * p.mid_dim + u;
       const float4* mrow = reinterpret_cast<const float4*>(sM + j * MT);
@@ -333,7 +389,7 @@ __global__ void __launch_bounds__(C * G, 2) k_conv_bwd_sig(ConvParams p) {
         constexpr int HQ = up4(D1 * D2) / 4, MQ = up4(D1 * D3) / 4;
         constexpr int XO = L1 * L1, YO = L2 * L2;
         constexpr float PAR = (L2 & 1) ? -1.f : 1.f;
-        const float w = __ldg(wp + K * KSTRIDE);
+        const float w = wv[K];
         // xh[j] = sum_i x1[i] H[i][j]; th[i] = sum_j H[i][j] Y[j]   (flattened H block: f = i * D2 + j)
         float xh[D2], th[D1];
 #pragma unroll
@@ -391,6 +447,7 @@ __global__ void __launch_bounds__(C * G, 2) k_conv_bwd_sig(ConvParams p) {
       }
       const float tot = warp_sum16(sdy);
       if ((lane & 1) == 0) sRed[(warp * EC + j) * 16 + (lane >> 1)] = tot;
+      }
     }
     __syncthreads();
     for (int idx = tid; idx < ne * 16; idx += NT) {
