@@ -416,9 +416,11 @@ __global__ void __maxnreg__(96) k_mlp_bwd_tc(MlpParams p) {
           tc::mma_tf32_ta(tmem, al + kb * 8, tc::sw128_desc(bh + off), IDESC, 1);
         }
         tc::mma_commit(BAR(S::MMA + s));
-        if (kc + B_NST < nch) {  // stage s (smem and TMEM) is free once MMA(kc) is done
-          if (!wait(S::MMA + s, (kc / B_NST) & 1)) break;
-          copy_chunk(kc + B_NST);
+        // stage (kc - 1) % B_NST (smem and TMEM) is free once MMA(kc - 1) is done, which
+        // MMA(kc) queued behind it does not wait for: chunk kc - 1 + B_NST goes there
+        if (kc >= 1 && kc - 1 + B_NST < nch) {
+          if (!wait(S::MMA + (kc - 1) % B_NST, ((kc - 1) / B_NST) & 1)) break;
+          copy_chunk(kc - 1 + B_NST);
         }
       }
       // every K-chunk MMA done before the hidden layers reuse stage memory and TMEM
