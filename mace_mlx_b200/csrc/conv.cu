@@ -339,27 +339,52 @@ int launch_conv_bwd(const ConvParams& p, cudaStream_t s, bool* need_gather) {
 }
 
 namespace {
-// d up[n] = sum over n's incoming edges e of the sender-side term of the
-// reverse edge rev(e) (whose sender is n), in edge order: deterministic
+// d up[n] = sum of the sender-side terms of the edges whose sender is n: the
+// conv backward stores the term of edge x in the row of its reverse edge, so
+// these are the contiguous rows of n's incoming edges.  A thread owns four
+// consecutive features (16-byte loads) and keeps eight rows of loads in
+// flight; eight partial sums over the rows in a fixed order (deterministic).
 __global__ void k_dup_gather(ConvParams p) {
   const int64_t n = p.n0 + blockIdx.x;
   const int64_t e0 = p.row_ptr[n], e1 = p.row_ptr[n + 1];
-  for (int q = threadIdx.x; q < p.in_dim; q += blockDim.x) {
-    float a0 = 0.f, a1 = 0.f;
-    int64_t e = e0;
-    for (; e + 1 < e1; e += 2) {
-      a0 += __ldg(p.tq + (int64_t)p.rev[e] * p.in_dim + q);
-      a1 += __ldg(p.tq + (int64_t)p.rev[e + 1] * p.in_dim + q);
-    }
-    if (e < e1) a0 += __ldg(p.tq + (int64_t)p.rev[e] * p.in_dim + q);
-    p.dup[n * p.in_dim + q] = a0 + a1;
+  const int ne = (int)(e1 - e0);
+  const int q4 = threadIdx.x;  // features 4 q4 .. 4 q4 + 3
+  if (4 * q4 >= p.in_dim) return;
+  const int64_t pitch = p.in_dim / 4;
+  const float4* rows = reinterpret_cast<const float4*>(p.tq + e0 * p.in_dim) + q4;
+  float4 acc[8];
+#pragma unroll
+  for (int b = 0; b < 8; ++b) acc[b] = make_float4(0.f, 0.f, 0.f, 0.f);
+  auto add = [](float4& a, const float4& v) {
+    a.x += v.x;
+    a.y += v.y;
+    a.z += v.z;
+    a.w += v.w;
+  };
+  int j = 0;
+  for (; j + 8 <= ne; j += 8) {
+    float4 v[8];
+#pragma unroll
+    for (int b = 0; b < 8; ++b) v[b] = __ldg(rows + (j + b) * pitch);
+#pragma unroll
+    for (int b = 0; b < 8; ++b) add(acc[b], v[b]);
   }
+#pragma unroll
+  for (int b = 0; b < 8; ++b)
+    if (j + b < ne) add(acc[b], __ldg(rows + (j + b) * pitch));
+#pragma unroll
+  for (int b = 1; b < 8; b += 2) add(acc[b - 1], acc[b]);
+  add(acc[0], acc[2]);
+  add(acc[4], acc[6]);
+  add(acc[0], acc[4]);
+  reinterpret_cast<float4*>(p.dup + n * p.in_dim)[q4] = acc[0];
 }
 }  // namespace
 
 int launch_dup_gather(const ConvParams& p, cudaStream_t s) {
   if (p.N <= p.n0) return MACE_OK;
-  const int threads = p.in_dim < 512 ? p.in_dim : 512;
+  if (p.in_dim % 4 != 0 || p.in_dim > 4096) return fail(MACE_ERR_UNSUPPORTED, "dup_gather: input feature count");
+  const int threads = (p.in_dim / 4 + 31) / 32 * 32;  // four features per thread
   k_dup_gather<<<(unsigned)(p.N - p.n0), threads, 0, s>>>(p);
   MACE_LAUNCH_CHECK("dup_gather");
   return MACE_OK;

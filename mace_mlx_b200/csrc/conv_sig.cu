@@ -272,9 +272,10 @@ struct BwdLayout {
 // and the gradient of the sender's features, either (MODE 1) gathered at the
 // sender's own CTA through the reverse edge,
 //   d up[n][l1 slot][i][u] += (-1)^l2 w sum_m M_k,e[i][m] dA[s_e][k][m][u],
-// or (MODE 2) formed here from the same H block and written per edge,
-//   T_e[l1 slot][i][u] = sum_k w_e[k, u] sum_j H_k[i][j] Y_e[j],
-// for launch_dup_gather to sum over each node's outgoing edges.
+// or (MODE 2) formed here from the same H block and written per edge into
+// the row of its reverse edge,
+//   T_e[l1 slot][i][u] = sum_k w_e[k, u] sum_j H_k[i][j] Y_e[j]  -> tq[rev(e)],
+// for launch_dup_gather to sum over each node's (contiguous) incoming rows.
 // G groups of C threads share one receiver: group g takes edges g, g+G, ...
 template <int C, int G, class S, int MODE>
 __global__ void __launch_bounds__(C * G, 2) k_conv_bwd_sig(ConvParams p) {
@@ -441,7 +442,9 @@ __global__ void __launch_bounds__(C * G, 2) k_conv_bwd_sig(ConvParams p) {
         }
       });
       if constexpr (MODE == 2) {
-        float* tp = p.tq + e * (int64_t)(IC * C) + u;
+        // stored at the reverse edge's row: a node's terms are then the
+        // contiguous rows of its own incoming edges
+        float* tp = p.tq + (int64_t)__ldg(p.rev + e) * (IC * C) + u;
 #pragma unroll
         for (int q = 0; q < IC; ++q) tp[q * C] = tq[q];
       }

@@ -328,11 +328,23 @@ __global__ void k_readout(ReadoutParams p) {
   }
   const int H = p.hidden;  // <= 32
   float z = 0.f;
-  // z_j for j = lane (lanes >= H idle)
-  for (int c = 0; c < p.C; ++c) {
-    float hv = h[c];
-    if (lane < H) z = fmaf(hv, __ldg(p.w1 + c * H + lane), z);
+  // z_j for j = lane (lanes >= H idle): the node's scalar row is read once,
+  // coalesced, and broadcast by shuffles; the weight loads of 32 channels are
+  // independent of one another (C is a multiple of 32, at most 128)
+  float hr[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) hr[k] = (32 * k < p.C) ? h[32 * k + lane] : 0.f;
+  const float* w1l = p.w1 + (lane < H ? lane : 0);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    if (32 * k >= p.C) break;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const float hv = __shfl_sync(0xffffffffu, hr[k], i);
+      z = fmaf(hv, __ldg(w1l + (32 * k + i) * H), z);
+    }
   }
+  if (lane >= H) z = 0.f;
   float e = 0.f, dz = 0.f;
   if (lane < H) {
     float w2 = __ldg(p.w2 + lane);

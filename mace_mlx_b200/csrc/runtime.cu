@@ -739,6 +739,7 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
       }
       LAUNCH("linear_msg_bwd", t, launch_linear(lp, s));
     }
+    bool need_gather = false;
     for (const Chunk& ch : chunks) {
       MlpParams mp = mlp_params(c, t, ch.e0, ch.e1 - ch.e0);
       // several chunks share the weight buffers: recompute this chunk's radial weights
@@ -748,7 +749,7 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
       cp.e0 = ch.e0;
       bool gather = false;
       LAUNCH("conv_bwd", t, launch_conv_bwd(cp, s, &gather));
-      if (gather) LAUNCH("dup_gather", t, launch_dup_gather(cp, s));
+      need_gather = need_gather || gather;
       if (fork) {
         MACE_CUDA_TRY(cudaEventRecord(ev[1 + T + t], s));
         MACE_CUDA_TRY(cudaStreamWaitEvent(sa, ev[1 + T + t], 0));
@@ -756,6 +757,11 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
       } else if (ch.e1 > ch.e0) {
         LAUNCH("mlp_bwd", t, launch_mlp_bwd(mp, s));
       }
+    }
+    if (need_gather) {
+      // the sender-side terms of every chunk's edges are in place: sum them per node
+      ConvParams cp = conv_params(c, t, N, sys);
+      LAUNCH("dup_gather", t, launch_dup_gather(cp, s));
     }
     if (t > 0) {
       // dh[t] holds the readout seed of layer t-1
