@@ -536,7 +536,13 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
   // and join become graph edges).
   const bool fork = !recompute && E > 0 && !sys->halo && c->dw_layer[0] != nullptr && !c->single_stream;
   if (fork) {
-    if (!c->aux) MACE_CUDA_TRY(cudaStreamCreateWithFlags(&c->aux, cudaStreamNonBlocking));
+    if (!c->aux) {
+      // lowest priority: when both streams have CTAs waiting, the node/conv
+      // chain (the step's critical path) is scheduled first
+      int least = 0, greatest = 0;
+      MACE_CUDA_TRY(cudaDeviceGetStreamPriorityRange(&least, &greatest));
+      MACE_CUDA_TRY(cudaStreamCreateWithPriority(&c->aux, cudaStreamNonBlocking, least));
+    }
     for (cudaEvent_t& e : c->fork_ev)
       if (!e) MACE_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
   }
@@ -573,6 +579,10 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
   ep.dv = c->dv;
   ep.virial_part = (flags & MACE_WANT_VIRIAL) ? c->vir_part : nullptr;
   if (E > 0) LAUNCH("edge_fwd", -1, launch_edge_fwd(ep, s));
+  // The MLP chain of every layer's forward is issued at once (the MLP kernels
+  // hold their SMs for a whole 128-edge tile, so whatever runs beside them
+  // slows down; issuing mlp_fwd(t) after conv_fwd(t-1), or mlp_bwd(t) beside
+  // conv_bwd(t-1), measured no faster on Si1000).
   if (fork) {
     MACE_CUDA_TRY(cudaEventRecord(ev[0], s));
     MACE_CUDA_TRY(cudaStreamWaitEvent(sa, ev[0], 0));
@@ -1144,7 +1154,12 @@ int mace_forward_backward(mace_ctx* c, const mace_system* sys, const mace_output
       MACE_CUDA_TRY(cudaGraphExecDestroy(c->gexec));
       c->gexec = nullptr;
     }
-    if (!c->cap_stream) MACE_CUDA_TRY(cudaStreamCreateWithFlags(&c->cap_stream, cudaStreamNonBlocking));
+    if (!c->cap_stream) {
+      // highest priority, which the captured kernel nodes keep in the graph
+      int least = 0, greatest = 0;
+      MACE_CUDA_TRY(cudaDeviceGetStreamPriorityRange(&least, &greatest));
+      MACE_CUDA_TRY(cudaStreamCreateWithPriority(&c->cap_stream, cudaStreamNonBlocking, greatest));
+    }
     // order the capture after the caller's prior work (workspace reuse)
     MACE_CUDA_TRY(cudaStreamSynchronize(s));
     MACE_CUDA_TRY(cudaStreamBeginCapture(c->cap_stream, cudaStreamCaptureModeThreadLocal));
