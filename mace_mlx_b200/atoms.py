@@ -28,7 +28,8 @@ class Cell:
 
     @property
     def rank(self) -> int:
-        return int(np.linalg.matrix_rank(self.array)) if np.any(self.array) else 0
+        """Number of non-zero cell vectors (ASE's definition)."""
+        return int(self.array.any(1).sum())
 
     def __array__(self, dtype=None, copy=None):
         return self.array.astype(dtype) if dtype is not None else self.array

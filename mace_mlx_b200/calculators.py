@@ -138,12 +138,14 @@ class MACEMLXCalculator(Calculator):
             return True
         if not np.array_equal(atoms.pbc, self._cache_pbc):
             return True
-        if not np.allclose(np.array(atoms.cell), self._cache_cell, atol=1e-10):
+        # np.allclose(cell, cached, atol=1e-10) written out (it costs tens of us per call)
+        cell = np.asarray(atoms.cell, dtype=np.float64)
+        if not bool(np.all(np.abs(cell - self._cache_cell) <= 1e-10 + 1e-5 * np.abs(self._cache_cell))):
             return True
         if self._skin <= 0:
             return True
-        disp = np.linalg.norm(atoms.positions - self._cache_positions, axis=1)
-        return float(np.max(disp, initial=0.0)) > self._skin / 2
+        d = atoms.positions - self._cache_positions
+        return float(np.einsum("ij,ij->i", d, d).max(initial=0.0)) > (self._skin / 2) ** 2
 
     def _species(self, atoms):
         numbers = atoms.get_atomic_numbers()
