@@ -111,6 +111,7 @@ class MACEMLXCalculator(Calculator):
         self._stress_always = False
         self._out = None
         self._host = None
+        self._blk = self._hblk = None
 
     # ------------------------------------------------------------------
     @classmethod
@@ -156,25 +157,34 @@ class MACEMLXCalculator(Calculator):
             self._graph_ptr_dev = torch.tensor([0, len(numbers)], dtype=torch.int32, device=self._device)
         return self._species_dev
 
+    @staticmethod
+    def _views(n: int, blk_in: torch.Tensor, blk_out: torch.Tensor) -> dict:
+        """Named views of the input block (cell, positions) and the output block
+        (energy, virial, forces, node energies), each starting 64-byte aligned."""
+        f_off = 128
+        ne_off = (f_off + 12 * n + 63) // 64 * 64
+        return {
+            "cell": blk_in[0:9].view(3, 3),
+            "pos": blk_in[16:16 + 3 * n].view(n, 3),
+            "energy": blk_out[0:8].view(torch.float64),
+            "virial": blk_out[8:80].view(torch.float64),
+            "forces": blk_out[f_off:f_off + 12 * n].view(torch.float32).view(n, 3),
+            "node_energy": blk_out[ne_off:ne_off + 4 * n].view(torch.float32),
+        }
+
     def _buffers(self, n: int, stress: bool):
+        # inputs and outputs each in one block, so a step moves one host->device
+        # and one device->host copy
         if self._out is None or self._out["node_energy"].shape[0] != n:
             dev = self._device
-            self._out = {
-                "energy": torch.empty(1, dtype=torch.float64, device=dev),
-                "node_energy": torch.empty(n, dtype=torch.float32, device=dev),
-                "forces": torch.empty(n, 3, dtype=torch.float32, device=dev),
-                "virial": torch.empty(9, dtype=torch.float64, device=dev),
-                "pos": torch.empty(n, 3, dtype=torch.float32, device=dev),
-                "cell": torch.empty(3, 3, dtype=torch.float32, device=dev),
-            }
-            self._host = {
-                "pos": torch.empty(n, 3, dtype=torch.float32, pin_memory=True),
-                "cell": torch.empty(3, 3, dtype=torch.float32, pin_memory=True),
-                "energy": torch.empty(1, dtype=torch.float64, pin_memory=True),
-                "virial": torch.empty(9, dtype=torch.float64, pin_memory=True),
-                "forces": torch.empty(n, 3, dtype=torch.float32, pin_memory=True),
-                "node_energy": torch.empty(n, dtype=torch.float32, pin_memory=True),
-            }
+            n_in = 16 + 3 * n
+            n_out = (128 + 12 * n + 63) // 64 * 64 + 4 * n
+            self._blk = (torch.empty(n_in, dtype=torch.float32, device=dev),
+                         torch.empty(n_out, dtype=torch.uint8, device=dev))
+            self._hblk = (torch.empty(n_in, dtype=torch.float32, pin_memory=True),
+                          torch.empty(n_out, dtype=torch.uint8, pin_memory=True))
+            self._out = self._views(n, *self._blk)
+            self._host = self._views(n, *self._hblk)
         return self._out, self._host
 
     # ------------------------------------------------------------------
@@ -187,15 +197,14 @@ class MACEMLXCalculator(Calculator):
             species = self._species(atoms)
             has_cell = atoms.cell.rank > 0
             out, host = self._buffers(n, False)
-            # host -> device: positions (float32) and cell
+            # host -> device: positions (float32) and cell, one copy
             host["pos"].numpy()[:] = atoms.positions
             pos = out["pos"]
-            pos.copy_(host["pos"], non_blocking=True)
             cell = None
             if has_cell:
-                host["cell"].numpy()[:] = np.array(atoms.cell)
+                host["cell"].numpy()[:] = np.asarray(atoms.cell)
                 cell = out["cell"]
-                cell.copy_(host["cell"], non_blocking=True)
+            self._blk[0].copy_(self._hblk[0], non_blocking=True)
             if self._needs_neighbor_update(atoms):
                 pos64 = torch.as_tensor(atoms.positions, dtype=torch.float64).to(dev)
                 cell64 = torch.as_tensor(np.array(atoms.cell), dtype=torch.float64).to(dev) if has_cell else None
@@ -212,12 +221,8 @@ class MACEMLXCalculator(Calculator):
             # replayed as a CUDA graph: every buffer here keeps its address between steps
             self.model.evaluate(pos, cell, species, self._graph_ptr_dev, self._nl_cache, forces=True,
                                 virial=compute_stress, out=out, graph=self._use_graph)
-            # device -> host
-            host["energy"].copy_(out["energy"], non_blocking=True)
-            host["forces"].copy_(out["forces"], non_blocking=True)
-            host["node_energy"].copy_(out["node_energy"], non_blocking=True)
-            if compute_stress:
-                host["virial"].copy_(out["virial"], non_blocking=True)
+            # device -> host: energy, virial, forces and node energies in one copy
+            self._hblk[1].copy_(self._blk[1], non_blocking=True)
             torch.cuda.current_stream(dev).synchronize()
         energy = float(host["energy"][0])
         self.results["energy"] = energy

@@ -113,24 +113,6 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t phase) {
   }
 }
 
-// As mbar_wait without the suspend hint: for short waits on the critical path
-// (the waiting thread polls instead of sleeping)
-__device__ __forceinline__ bool mbar_wait_poll(uint32_t bar, uint32_t phase) {
-  const uint64_t t0 = globaltimer();
-  for (uint32_t it = 0;; ++it) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(bar), "r"(phase)
-        : "memory");
-    if (ok) return true;
-    if ((it & 255u) == 255u && globaltimer() - t0 > 2000000000ull) return false;
-  }
-}
-
 // As mbar_wait, for kernels whose warps wait on one another: a wait that gives
 // up raises the CTA-wide `abort` flag, and every later wait that sees the flag
 // returns false at once, so the whole CTA leaves its pipeline within one
