@@ -437,17 +437,6 @@ MlpParams mlp_params(mace_ctx* c, int t, int64_t e0, int64_t ne) {
   return p;
 }
 
-// the MLP over tiles [e0 / 128, ...) of the one-chunk buffers (e0 a multiple of 128)
-MlpParams mlp_params_tiles(mace_ctx* c, int t, int64_t e0, int64_t ne) {
-  MlpParams p = mlp_params(c, t, e0, ne);
-  const mace_layer_desc& L = c->desc.layers[t];
-  const int64_t tile_floats = (int64_t)wt_nchunk(L.mlp_w[L.n_mlp]) * WT_CHUNK;
-  p.act += e0 * (int64_t)(L.n_mlp - 1) * L.mlp_w[1];
-  p.out += (e0 / 128) * tile_floats;
-  p.dout += (e0 / 128) * tile_floats;
-  return p;
-}
-
 ScParams sc_params(mace_ctx* c, int t, int64_t N, const int32_t* species, const float* f, float* out,
                    const float* dout, float* df) {
   const mace_layer_desc& L = c->desc.layers[t];
@@ -592,23 +581,15 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
   if (E > 0) LAUNCH("edge_fwd", -1, launch_edge_fwd(ep, s));
   // The MLP chain of every layer's forward is issued at once (the MLP kernels
   // hold their SMs for a whole 128-edge tile, so whatever runs beside them
-  // slows down; issuing mlp_fwd(t) after conv_fwd(t-1), or mlp_bwd(t) beside
-  // conv_bwd(t-1), measured no faster on Si1000).
+  // slows down; issuing mlp_fwd(t) after conv_fwd(t-1), mlp_bwd(t) beside
+  // conv_bwd(t-1), or a later layer's MLP as two launches of half the tiles
+  // measured no faster on Si1000).
   if (fork) {
     MACE_CUDA_TRY(cudaEventRecord(ev[0], s));
     MACE_CUDA_TRY(cudaStreamWaitEvent(sa, ev[0], 0));
     for (int t = 0; t < T; ++t) {
-      if (t == 0 || E < 2 * 128 * 148) {
-        MlpParams mp = mlp_params(c, t, 0, E);
-        LAUNCH_ON(sa, "mlp_fwd", t, launch_mlp_fwd(mp, sa));
-      } else {
-        // later layers overlap the node kernels: two launches of half the tiles
-        // each hold about one CTA per SM and leave room beside them
-        const int64_t half = ((E + 255) / 256) * 128;
-        MlpParams m0 = mlp_params_tiles(c, t, 0, half), m1 = mlp_params_tiles(c, t, half, E - half);
-        LAUNCH_ON(sa, "mlp_fwd", t, launch_mlp_fwd(m0, sa));
-        LAUNCH_ON(sa, "mlp_fwd", t, launch_mlp_fwd(m1, sa));
-      }
+      MlpParams mp = mlp_params(c, t, 0, E);
+      LAUNCH_ON(sa, "mlp_fwd", t, launch_mlp_fwd(mp, sa));
       MACE_CUDA_TRY(cudaEventRecord(ev[1 + t], sa));
     }
   }
@@ -783,14 +764,7 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
       if (fork) {
         MACE_CUDA_TRY(cudaEventRecord(ev[1 + T + t], s));
         MACE_CUDA_TRY(cudaStreamWaitEvent(sa, ev[1 + T + t], 0));
-        if (t == 0 || E < 2 * 128 * 148) {
-          LAUNCH_ON(sa, "mlp_bwd", t, launch_mlp_bwd(mp, sa));
-        } else {  // as the forward: two half launches beside the node kernels
-          const int64_t half = ((E + 255) / 256) * 128;
-          MlpParams m0 = mlp_params_tiles(c, t, 0, half), m1 = mlp_params_tiles(c, t, half, E - half);
-          LAUNCH_ON(sa, "mlp_bwd", t, launch_mlp_bwd(m0, sa));
-          LAUNCH_ON(sa, "mlp_bwd", t, launch_mlp_bwd(m1, sa));
-        }
+        LAUNCH_ON(sa, "mlp_bwd", t, launch_mlp_bwd(mp, sa));
       } else if (ch.e1 > ch.e0) {
         LAUNCH("mlp_bwd", t, launch_mlp_bwd(mp, s));
       }

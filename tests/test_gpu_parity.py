@@ -183,10 +183,12 @@ def test_tensor_core_mlp_matches_cuda_core_mlp(monkeypatch):
 def test_tensor_core_linears_match_cuda_core_linears(monkeypatch):
     """tcgen05 (3-term tf32) node linears and species-indexed skips vs the fp32 CUDA-core kernel.
 
-    A four-element box puts several species in most 128-row tiles (one
-    species pass each); 300 atoms leave ragged last tiles in every job.
+    A four-element box puts several species in every 128-row tile (one
+    species pass each); at 1200 atoms the launch of layer 1's linear_up with
+    its species-indexed skip is large enough for the tensor-core kernel, and
+    1200 rows leave a ragged last tile in every job.
     """
-    st = lipso_box(300, seed=5)
+    st = lipso_box(1200, seed=5)
     config, weights, _ = make_case("medium", st, seed=14)
     m_tc = MACEModel(config=config, weights=weights, device=0)
     monkeypatch.setenv("MACE_B200_LINEAR_CUDA_CORES", "1")
