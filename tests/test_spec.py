@@ -92,3 +92,32 @@ def test_non_residual_first_layer_skip_on_message():
 
 def test_irreps_sh():
     assert str(Irreps.spherical_harmonics(3)) == "1x0e + 1x1o + 1x2e + 1x3o"
+
+
+@pytest.mark.parametrize("n", [1, 7, 1000, 1001])
+def test_calculator_transfer_blocks_are_aligned_and_disjoint(n):
+    """One host->device and one device->host copy per step: the named views of
+    the two blocks start 64-byte aligned, fit their block and do not overlap."""
+    import torch
+
+    from mace_mlx_b200.calculators import MACEMLXCalculator
+
+    n_in = 16 + 3 * n
+    n_out = (128 + 12 * n + 63) // 64 * 64 + 4 * n
+    blk_in = torch.empty(n_in, dtype=torch.float32)
+    blk_out = torch.empty(n_out, dtype=torch.uint8)
+    v = MACEMLXCalculator._views(n, blk_in, blk_out)
+    assert v["pos"].shape == (n, 3) and v["cell"].shape == (3, 3) and v["forces"].shape == (n, 3)
+    assert v["energy"].dtype == torch.float64 and v["energy"].numel() == 1 and v["virial"].numel() == 9
+    assert v["node_energy"].shape == (n,) and v["node_energy"].dtype == torch.float32
+    for blk, names in ((blk_in, ("cell", "pos")), (blk_out, ("energy", "virial", "forces", "node_energy"))):
+        base = blk.data_ptr()
+        spans = []
+        for k in names:
+            t = v[k]
+            off = t.data_ptr() - base
+            assert off % 64 == 0 or k in ("virial",), (k, off)  # virial follows the 8-byte energy
+            spans.append((off, off + t.numel() * t.element_size()))
+        spans.sort()
+        assert spans[-1][1] <= blk.numel() * blk.element_size()
+        assert all(a[1] <= b[0] for a, b in zip(spans, spans[1:]))
