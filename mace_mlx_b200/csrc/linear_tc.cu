@@ -6,13 +6,13 @@
 // One CTA computes a 128-row x C tile of one job in TMEM (128 lanes x C fp32
 // columns per accumulator) over 32-wide K chunks t:
 //   D_small += A_lo B_hi + A_hi B_lo,   D_big[t & 1] += A_hi B_hi
-// (kind::tf32, 4 K-steps of 8), hi = x rounded to tf32, lo = (x - hi)
-// rounded to tf32 (the 3xTF32 split); the epilogue adds the three in fp32.
-// The tensor core truncates when it accumulates, and the error grows with the
-// number of accumulation steps into one accumulator: the small terms in their
-// own accumulator and two alternating big ones keep it near fp32 rounding.
-// with A the 128 x 32 input chunk and B the weight chunk (C rows x 32, the
-// transpose of W's 32 rows).  The weights never change, so their operand
+// (kind::tf32, 4 K-steps of 8) with A the 128 x 32 input chunk and B the
+// weight chunk (C rows x 32, the transpose of W's 32 rows); hi = x rounded to
+// tf32, lo = (x - hi) rounded to tf32 (the 3xTF32 split), and the epilogue
+// adds the three accumulators in fp32.  The tensor core truncates when it
+// accumulates, and the error grows with the number of accumulation steps into
+// one accumulator: the small terms in their own accumulator and two
+// alternating big ones keep it near fp32 rounding.  The weights never change, so their operand
 // images (tf32 hi and lo, 128B-swizzled K-major) are made once per context
 // (k_tc_image); a chunk's image is one contiguous bulk copy.  The input chunk
 // is read with coalesced 16-byte loads (8 threads per 128-byte row segment),
