@@ -142,7 +142,7 @@ __global__ void __launch_bounds__(C) k_conv_fwd_sig(ConvParams p) {
   // EPI edges per step; the next EPI edges' sender features and radial
   // weights are loaded while these are computed (small signatures stream more
   // edges at once: their per-edge arithmetic is short)
-  constexpr int EPI = S::n <= 4 ? 4 : 1;
+  constexpr int EPI = S::n <= 4 ? 4 : (S::n <= 10 ? 2 : 1);
   float xn[EPI][S::in_ch()], wn[EPI][S::n];
   auto fetch = [&](int64_t cb, int j0, int ne) {
 #pragma unroll
