@@ -232,11 +232,18 @@ int launch(mace_ctx* c, const char* name, int layer, cudaStream_t s, Fn&& fn) {
     c->prof_name[slot] = name;
     c->prof_layer[slot] = layer;
     c->prof_stream[slot] = (s == c->aux && c->aux) ? 1 : 0;
-    // external: inside a stream capture the records become event-record nodes of the graph
-    MACE_CUDA_TRY(cudaEventRecordWithFlags(c->ev[2 * slot], s, cudaEventRecordExternal));
+  }
+  // inside a stream capture the records must be external to become
+  // event-record nodes of the graph; outside one that flag is refused
+  unsigned rec_flags = cudaEventRecordDefault;
+  if (slot >= 0) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    MACE_CUDA_TRY(cudaStreamIsCapturing(s, &cs));
+    if (cs == cudaStreamCaptureStatusActive) rec_flags = cudaEventRecordExternal;
+    MACE_CUDA_TRY(cudaEventRecordWithFlags(c->ev[2 * slot], s, rec_flags));
   }
   int rc = fn();
-  if (slot >= 0) MACE_CUDA_TRY(cudaEventRecordWithFlags(c->ev[2 * slot + 1], s, cudaEventRecordExternal));
+  if (slot >= 0) MACE_CUDA_TRY(cudaEventRecordWithFlags(c->ev[2 * slot + 1], s, rec_flags));
   return rc;
 }
 

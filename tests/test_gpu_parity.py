@@ -242,3 +242,28 @@ def test_energy_weights_are_linear():
     scale = np.abs(full["forces"]).max()
     np.testing.assert_allclose(a["forces"] + b["forces"], full["forces"], atol=2e-5 * scale)
     np.testing.assert_allclose(a["virial"] + b["virial"], full["virial"], atol=2e-5 * np.abs(full["virial"]).max())
+
+
+def test_profiler_eager_and_in_graph():
+    """Per-launch event timing works on an eager step and inside the replayed step graph."""
+    config, weights, st = make_case("medium", diamond_si(2, 0.05, 17), seed=17)
+    m = MACEModel(config=config, weights=weights, device=0)
+    _, edges, species = run_gpu(m, st)
+    dev = m.device
+    gp = torch.as_tensor(graph_ptr_of(st), device=dev)
+    pos = torch.tensor(st.positions, dtype=torch.float32, device=dev)
+    cell = torch.tensor(st.cell, dtype=torch.float32, device=dev)
+    sp = torch.as_tensor(species, device=dev)
+    seen = {}
+    for graph in (False, True, True):
+        m.profile_enable(True)
+        m.evaluate(pos, cell, sp, gp, edges, forces=True, graph=graph)
+        torch.cuda.synchronize(dev)
+        rows = m.profile_read()
+        tl = m.profile_timeline()
+        m.profile_enable(False)
+        assert rows and all(r["ms"] > 0 and r["count"] >= 1 for r in rows)
+        assert len(tl) == sum(r["count"] for r in rows)
+        assert all(t["end_ms"] >= t["start_ms"] >= 0 for t in tl)
+        seen[graph] = {(r["name"], r["layer"]) for r in rows}
+    assert seen[False] == seen[True]
