@@ -235,6 +235,77 @@ class MACEMLXCalculator(Calculator):
             s = 0.5 * (g + g.T) / abs(np.linalg.det(np.array(atoms.cell, dtype=np.float64)))
             self.results["stress"] = s[[0, 1, 2, 1, 0, 0], [0, 1, 2, 2, 2, 1]]
 
+    def calculate_batch(self, atoms_list, properties=("energy", "forces")) -> list[dict]:
+        """Energies and forces of several structures in one step on the GPU.
+
+        The structures become the graphs of one system (no edges between
+        them): one neighbour list and one ``mace_forward_backward`` for the
+        whole batch, which keeps the GPU busy where one small structure per
+        step would not (NEB images, adsorption scans, active-learning pools).
+        They must be non-periodic or share one cell and pbc (``batch_layout``).
+        Returns, per structure, the keys ``calculate`` fills except stress
+        (the step accumulates one virial for the whole batch): energy,
+        free_energy, forces, node_energy, energies.  ``self.results`` and the
+        cached neighbour list of ``calculate`` are left untouched.
+        """
+        if "stress" in properties:
+            raise NotImplementedError("calculate_batch gives energies and forces; call calculate() for stress")
+        lay = batch_layout(atoms_list)
+        dev = self._device
+        gp = lay["graph_ptr"]
+        with torch.cuda.device(dev):
+            species = torch.as_tensor(self.model.species_index(lay["numbers"]).astype(np.int32), device=dev)
+            gp_dev = torch.as_tensor(gp, device=dev)
+            pos64 = torch.as_tensor(lay["positions"], dtype=torch.float64).to(dev)
+            cell64 = None if lay["cell"] is None else torch.as_tensor(lay["cell"], dtype=torch.float64).to(dev)
+            edges = self.model.neighbour_list(pos64, cell64, lay["pbc"], gp_dev, self.r_max)
+            out = self.model.evaluate(pos64.float(), None if cell64 is None else cell64.float(), species, gp_dev,
+                                      edges, forces=True, virial=False)
+            energy = out["energy"].cpu().numpy()
+            forces = out["forces"].cpu().numpy()
+            node_energy = out["node_energy"].cpu().numpy()
+        results = []
+        for g in range(len(gp) - 1):
+            a, b = int(gp[g]), int(gp[g + 1])
+            results.append({"energy": float(energy[g]), "free_energy": float(energy[g]),
+                            "forces": forces[a:b].copy(), "node_energy": node_energy[a:b].copy(),
+                            "energies": node_energy[a:b].copy()})
+        return results
+
+
+def batch_layout(atoms_list) -> dict:
+    """Concatenation of several structures into one system of len(atoms_list) graphs.
+
+    The structures must all be non-periodic (a batch of molecules) or share
+    one cell and pbc (NEB images, replicas of one cell): the step's neighbour
+    list and edge vectors use a single cell.  Returns graph_ptr (int32),
+    numbers, positions (float64), cell (3x3 float64 or None) and pbc.
+    """
+    if len(atoms_list) == 0:
+        raise ValueError("calculate_batch needs at least one structure")
+    first = atoms_list[0]
+    pbc = np.array(first.pbc, dtype=bool).reshape(-1)
+    pbc = np.repeat(pbc, 3) if pbc.size == 1 else pbc
+    cell = np.asarray(first.cell, dtype=np.float64)
+    periodic = bool(pbc.any())
+    for k, a in enumerate(atoms_list[1:], start=1):
+        pk = np.array(a.pbc, dtype=bool).reshape(-1)
+        pk = np.repeat(pk, 3) if pk.size == 1 else pk
+        if not np.array_equal(pk, pbc):
+            raise ValueError(f"calculate_batch: structure {k} has pbc {pk.tolist()}, structure 0 {pbc.tolist()}; "
+                             "a batch shares one cell and pbc")
+        if periodic and not np.array_equal(np.asarray(a.cell, dtype=np.float64), cell):
+            raise ValueError(f"calculate_batch: structure {k} has another cell than structure 0; "
+                             "a periodic batch shares one cell")
+    sizes = np.array([len(a) for a in atoms_list], dtype=np.int64)
+    return {
+        "graph_ptr": np.concatenate([[0], np.cumsum(sizes)]).astype(np.int32),
+        "numbers": np.concatenate([np.asarray(a.get_atomic_numbers(), dtype=np.int64) for a in atoms_list]),
+        "positions": np.concatenate([np.asarray(a.positions, dtype=np.float64).reshape(-1, 3) for a in atoms_list]),
+        "cell": cell if periodic else None,
+        "pbc": pbc,
+    }
+
 
 def mace_mp(model: str | None = None, device="cuda", default_dtype: str = "float32", head: str | None = None,
             dispersion: bool = False, return_raw_model: bool = False, **kwargs) -> MACEMLXCalculator:

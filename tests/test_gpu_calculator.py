@@ -109,3 +109,26 @@ def test_api_errors(model_dir, tmp_path, monkeypatch):
     shutil.copytree(model_dir, tmp_path / "small" / "v2")
     calc = mace_mp("small")
     assert calc.model.spec.C == 128
+
+
+def test_calculate_batch_matches_one_structure_at_a_time(model_dir):
+    """One batched step (structures as graphs of one system) equals separate steps."""
+    from mace_mlx_b200.structures import molecule_batch
+
+    calc = MACECalculator(model_path=model_dir, device="cuda", skin=0.0)
+    sts = [diamond_si(2, 0.05, s) for s in (31, 32, 33)]
+    periodic = [Atoms(s.numbers, s.positions, s.cell, True) for s in sts]
+    mols = molecule_batch(3, 7)
+    bounds = np.concatenate([[0], np.cumsum(np.bincount(mols.batch))])
+    molecules = [Atoms(mols.numbers[a:b], mols.positions[a:b]) for a, b in zip(bounds[:-1], bounds[1:])]
+    for batch in (periodic, molecules):
+        got = calc.calculate_batch(batch)
+        assert len(got) == len(batch)
+        for atoms, r in zip(batch, got):
+            calc.calculate(atoms, ["energy", "forces"])
+            ref = calc.results
+            assert abs(r["energy"] - ref["energy"]) <= 1e-6 * max(1.0, abs(ref["energy"])) + 1e-7 * len(atoms)
+            np.testing.assert_allclose(r["forces"], ref["forces"], atol=1e-5 * max(1.0, np.abs(ref["forces"]).max()))
+            np.testing.assert_allclose(r["node_energy"], ref["node_energy"], atol=1e-6)
+    with pytest.raises(NotImplementedError):
+        calc.calculate_batch(periodic, ["energy", "stress"])
