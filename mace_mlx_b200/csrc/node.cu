@@ -334,14 +334,31 @@ __global__ void k_readout(ReadoutParams p) {
   float hr[4];
 #pragma unroll
   for (int k = 0; k < 4; ++k) hr[k] = (32 * k < p.C) ? h[32 * k + lane] : 0.f;
-  const float* w1l = p.w1 + (lane < H ? lane : 0);
+  if (H <= 16) {
+    // the two half-warps take alternate 16-channel halves of each 32-channel
+    // block and add their partial sums: half the dependent chain
+    const int j = lane & 15, half = lane >> 4;
+    const float* w1j = p.w1 + (j < H ? j : 0);
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    if (32 * k >= p.C) break;
+    for (int k = 0; k < 4; ++k) {
+      if (32 * k >= p.C) break;
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const float hv = __shfl_sync(0xffffffffu, hr[k], i);
-      z = fmaf(hv, __ldg(w1l + (32 * k + i) * H), z);
+      for (int i = 0; i < 16; ++i) {
+        const float hv = __shfl_sync(0xffffffffu, hr[k], 16 * half + i);
+        z = fmaf(hv, __ldg(w1j + (32 * k + 16 * half + i) * H), z);
+      }
+    }
+    z += __shfl_xor_sync(0xffffffffu, z, 16);
+  } else {
+    const float* w1l = p.w1 + (lane < H ? lane : 0);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if (32 * k >= p.C) break;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float hv = __shfl_sync(0xffffffffu, hr[k], i);
+        z = fmaf(hv, __ldg(w1l + (32 * k + i) * H), z);
+      }
     }
   }
   if (lane >= H) z = 0.f;
