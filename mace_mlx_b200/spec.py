@@ -14,6 +14,11 @@ reference's module tree so that a ``weights.npz`` written for the reference
 * skip_tp (FullyConnectedTensorProduct, uvw): ``tensor_product.py:1046-1110``
 * symmetric contraction weights: ``symmetric_contraction.py:159-261``
 * readouts: ``blocks.py:540-608``
+* density-normalised blocks (``use_density_normalization``): ``blocks.py:282-490``
+  (``density_fn`` = bias-free Linear(num_bessel -> 1) per layer)
+* Agnesi distance transform (``distance_transform``): ``radial.py:202-262``
+* ZBL pair repulsion (``pair_repulsion``): ``radial.py:127-199``, wired in
+  ``model.py:154-173, 213-231``
 """
 
 from __future__ import annotations
@@ -24,11 +29,14 @@ from dataclasses import dataclass, field
 import numpy as np
 
 from .cg import U_matrix_real, wigner_3j
+from .elements import AGNESI_DEFAULTS, COVALENT_RADII, ZBL_DEFAULTS
 from .irreps import Irrep, Irreps
 
 SUPPORTED_INTERACTIONS = (
     "RealAgnosticResidualInteractionBlock",
     "RealAgnosticInteractionBlock",
+    "RealAgnosticDensityInteractionBlock",
+    "RealAgnosticDensityResidualInteractionBlock",
 )
 
 
@@ -230,6 +238,7 @@ class LayerSpec:
     sc: SCSpec
     prod_linear: LinearSpec
     readout_nonlinear: bool
+    density: bool = False  # message / (sum_e tanh((w_d . b_e)^2) + 1) instead of / avg_num_neighbors
     readout_linear: LinearSpec | None = None  # linear readout (not last)
     readout_1: LinearSpec | None = None  # nonlinear readout
     readout_2: LinearSpec | None = None
@@ -256,20 +265,35 @@ class ModelSpec:
     irreps_sh: Irreps
     interaction_irreps: Irreps
     layers: list[LayerSpec] = field(default_factory=list)
+    density: bool = False
+    agnesi: dict | None = None  # {"q", "p", "a", "covalent_radii" (indexed by Z)}
+    zbl: dict | None = None  # {"p", "a_exp", "a_prefactor", "covalent_radii" (indexed by Z)}
+
+    def species_numbers(self) -> list[int]:
+        """Atomic number of every model element index (z_table)."""
+        if self.z_table is None:
+            raise UnsupportedModel("the distance transform / pair repulsion need the config's z_table")
+        return [int(z) for z in self.z_table]
 
     # ------------------------------------------------------------------
     @staticmethod
     def from_config(config: dict) -> "ModelSpec":
         cfg = dict(config)
         model_type = cfg.get("model_type", "ScaleShiftMACE")
-        for key in ("distance_transform", "pair_repulsion"):
-            if cfg.get(key):
-                raise UnsupportedModel(
-                    f"config key {key!r} (Agnesi transform / ZBL repulsion) is not "
-                    "supported by the B200 step yet"
-                )
-        if cfg.get("use_density_normalization"):
-            raise UnsupportedModel("density-normalised interaction blocks are not supported yet")
+        density = bool(cfg.get("use_density_normalization", False))
+        agnesi = None
+        if cfg.get("distance_transform") is not None:
+            dt = dict(cfg["distance_transform"])
+            agnesi = {k: float(dt.get(k, v)) for k, v in AGNESI_DEFAULTS.items()}
+            # the converter writes the radii table into the config (converter.py:274-282)
+            agnesi["covalent_radii"] = [float(x) for x in (dt.get("covalent_radii") or COVALENT_RADII)]
+        zbl = None
+        if cfg.get("pair_repulsion"):
+            pr = cfg["pair_repulsion"] if isinstance(cfg["pair_repulsion"], dict) else {}
+            zbl = {"p": int(pr.get("p", ZBL_DEFAULTS["p"])), "a_exp": float(pr.get("a_exp", ZBL_DEFAULTS["a_exp"])),
+                   "a_prefactor": float(pr.get("a_prefactor", ZBL_DEFAULTS["a_prefactor"]))}
+            # the reference reads ase.data.covalent_radii at run time (radial.py:150-152)
+            zbl["covalent_radii"] = list(COVALENT_RADII)
         if cfg.get("use_agnostic_product"):
             raise UnsupportedModel("agnostic product blocks are not supported yet")
         if cfg.get("apply_cutoff", True) is False:
@@ -317,7 +341,10 @@ class ModelSpec:
             model_type=model_type, scale=float(cfg.get("scale", 1.0)),
             shift=float(cfg.get("shift", 0.0)), z_table=cfg.get("z_table"),
             atomic_energies=ae, irreps_sh=sh, interaction_irreps=inter_irreps,
+            density=density, agnesi=agnesi, zbl=zbl,
         )
+        if (agnesi or zbl) and spec.z_table is None:
+            raise UnsupportedModel("the distance transform / pair repulsion need the config's z_table")
         if isinstance(spec.scale, list) or isinstance(spec.shift, list):
             raise UnsupportedModel("per-head scale/shift is not supported yet")
 
@@ -343,6 +370,7 @@ class ModelSpec:
                 sc=SCSpec.build(inter_irreps, layer_hidden, corr[t], num_elements),
                 prod_linear=LinearSpec.build(layer_hidden, layer_hidden),
                 readout_nonlinear=(t == T - 1),
+                density=density,
             )
             if t < T - 1:
                 lay.readout_linear = LinearSpec.build(layer_hidden, Irreps("1x0e"))
@@ -368,6 +396,8 @@ class ModelSpec:
             w = lay.mlp_widths
             for j in range(len(w) - 1):
                 s[f"{p}.conv_tp_weights.layers.{2 * j}.weight"] = (w[j + 1], w[j])
+            if lay.density:
+                s[f"{p}.density_fn.weight"] = (1, self.num_bessel)
             for k, sh in enumerate(lay.linear.weight_shapes()):
                 s[f"{p}.linear.weights.{k}"] = sh
             for k, sh in enumerate(lay.skip.weight_shapes()):

@@ -78,12 +78,41 @@ def random_config(
     first_interaction_nonresidual: bool = False,
     atomic_energies: list[float] | None = None,
     model_type: str = "MACE",
+    use_density_normalization: bool = False,
+    distance_transform: dict | None = None,
+    pair_repulsion: dict | None = None,
 ) -> dict:
+    """A converted-model config.  ``use_density_normalization``,
+    ``distance_transform`` (Agnesi; ``{}`` for the defaults) and
+    ``pair_repulsion`` (ZBL; ``{}`` for the defaults) give the mpa-0 family's
+    blocks; the converter's key layout is kept (``converter.py:167-300``)."""
     hidden = hidden_irreps or ARCHS[arch]
     if z_table is None:
         z_table = list(range(1, num_elements + 1))
     num_elements = len(z_table)
-    return {
+    if use_density_normalization:
+        inter_cls = "RealAgnosticDensityInteractionBlock" if first_interaction_nonresidual else \
+            "RealAgnosticDensityResidualInteractionBlock"
+    else:
+        inter_cls = "RealAgnosticInteractionBlock" if first_interaction_nonresidual else \
+            "RealAgnosticResidualInteractionBlock"
+    extra = {}
+    if use_density_normalization:
+        extra["use_density_normalization"] = True
+    if distance_transform is not None:
+        from .elements import AGNESI_DEFAULTS, COVALENT_RADII
+
+        dt = dict(AGNESI_DEFAULTS)
+        dt.update(distance_transform)
+        dt.setdefault("covalent_radii", list(COVALENT_RADII))
+        extra["distance_transform"] = dt
+    if pair_repulsion is not None:
+        from .elements import ZBL_DEFAULTS
+
+        pr = dict(ZBL_DEFAULTS)
+        pr.update(pair_repulsion)
+        extra["pair_repulsion"] = pr
+    return extra | {
         "r_max": float(r_max),
         "num_bessel": int(num_bessel),
         "num_polynomial_cutoff": int(num_polynomial_cutoff),
@@ -97,7 +126,7 @@ def random_config(
         "radial_MLP": list(radial_MLP or [64, 64, 64]),
         "gate": "silu",
         "first_interaction_nonresidual": bool(first_interaction_nonresidual),
-        "interaction_cls": "RealAgnosticResidualInteractionBlock",
+        "interaction_cls": inter_cls,
         "model_type": model_type,
         "scale": 1.0,
         "shift": 0.0,
@@ -122,6 +151,8 @@ def random_weights(spec: ModelSpec, seed: int) -> dict[str, np.ndarray]:
             out[key] = w.astype(np.float32)
         elif ".linear_2.weights." in key:
             out[key] = (rng.standard_normal(shape) * SILU_NORM_FACTOR).astype(np.float32)
+        elif key.endswith(".density_fn.weight"):
+            out[key] = (rng.standard_normal(shape) / np.sqrt(shape[1])).astype(np.float32)
         elif ".symmetric_contractions." in key:
             out[key] = (rng.standard_normal(shape) / shape[1]).astype(np.float32)
         else:

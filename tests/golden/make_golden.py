@@ -3,8 +3,8 @@
 The reference package cannot be imported as a whole here (it needs MLX), but
 its ``mace_mlx/irreps.py`` and ``mace_mlx/clebsch_gordan.py`` depend only on
 numpy/scipy.  This script loads exactly those two files from the reference
-checkout (default ``/root/reference``, or ``$MACE_MLX_REFERENCE``) under a stub
-package and records their outputs:
+checkout (the required ``--reference`` argument, or ``$MACE_MLX_REFERENCE``)
+under a stub package and records their outputs:
 
 * ``cg_golden.npz``: real Wigner 3j symbols for all l <= 4 triples, the
   spherical-harmonics recursion tensors ``so3_clebsch_gordan(l-1, 1, l)``, and
@@ -13,12 +13,14 @@ package and records their outputs:
 * ``irreps_golden.json``: parsing, dims, sort permutations and products of a
   set of irreps strings.
 
-Run once where the reference is available: ``python tests/golden/make_golden.py``.
+Run once where the reference is available:
+``python tests/golden/make_golden.py --reference <path of the mace-mlx checkout>``.
 The tests only read the fixtures.
 """
 
 from __future__ import annotations
 
+import argparse
 import importlib.util
 import json
 import os
@@ -46,8 +48,13 @@ def load_reference(root: str):
 
 
 def main():
-    root = os.environ.get("MACE_MLX_REFERENCE", "/root/reference")
-    rirr, rcg = load_reference(root)
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default=os.environ.get("MACE_MLX_REFERENCE"),
+                    help="path of the mace-mlx checkout (required; or $MACE_MLX_REFERENCE)")
+    args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference <path of the mace-mlx checkout> or set MACE_MLX_REFERENCE")
+    rirr, rcg = load_reference(args.reference)
     out = {}
     for l1 in range(5):
         for l2 in range(5):

@@ -76,11 +76,32 @@ def test_check_weights_reports_mismatch():
 
 def test_unsupported_features_raise():
     cfg = random_config("small")
-    for key, val in [("pair_repulsion", {"p": 5}), ("distance_transform", {"q": 1}),
-                     ("use_density_normalization", True), ("heads", ["a", "b"])]:
+    for key, val in [("heads", ["a", "b"]), ("use_agnostic_product", True), ("apply_cutoff", False),
+                     ("interaction_cls", "RealAgnosticResidualNonLinearInteractionBlock")]:
         c = dict(cfg, **{key: val})
         with pytest.raises(UnsupportedModel):
             ModelSpec.from_config(c)
+
+
+def test_mpa_family_config_and_weight_layout():
+    """Density normalisation, Agnesi and ZBL as the reference's converter
+    writes them (converter.py:205-300): density_fn weights per layer, the
+    Agnesi radii table from the config, ZBL constants, z_table required."""
+    cfg = random_config("medium", z_table=[3, 8], first_interaction_nonresidual=True,
+                        use_density_normalization=True, distance_transform={}, pair_repulsion={"p": 5})
+    assert cfg["interaction_cls"] == "RealAgnosticDensityInteractionBlock"
+    sp = ModelSpec.from_config(cfg)
+    assert all(lay.density for lay in sp.layers)
+    assert sp.agnesi["q"] == pytest.approx(0.9183) and len(sp.agnesi["covalent_radii"]) == 119
+    assert sp.zbl["p"] == 5 and sp.zbl["a_exp"] == pytest.approx(0.3)
+    assert sp.species_numbers() == [3, 8]
+    shapes = sp.weight_shapes()
+    assert shapes["interactions.0.density_fn.weight"] == (1, sp.num_bessel)
+    assert shapes["interactions.1.density_fn.weight"] == (1, sp.num_bessel)
+    c = dict(cfg)
+    c.pop("z_table")
+    with pytest.raises(UnsupportedModel):
+        ModelSpec.from_config(c)
 
 
 def test_non_residual_first_layer_skip_on_message():
