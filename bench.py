@@ -57,24 +57,61 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=20.0, help="budget of the CPU baseline sample")
     ap.add_argument("--device-only", action="store_true",
                     help="only W + K plain device steps, no JSON (the command the ncu captures profile)")
-    ap.add_argument("--config", default="c1", choices=["c1", "c3", "c4"],
-                    help="c1: the headline Si1000 (default); c3: 512 OFF-like molecules sharded by structure; "
+    ap.add_argument("--config", default="c1", choices=["c0", "c1", "c2", "c3", "c4"],
+                    help="c1: the headline Si1000 (default); c0: small-arch Si216 with stress; c2: large-arch "
+                         "LiPSO-8000 with stress; c3: 512 OFF-like molecules sharded by structure; "
                          "c4: 1M-atom Si, spatially domain-decomposed over the ranks")
     return ap.parse_args()
 
 
-def make_structure(rank: int):
-    from mace_mlx_b200.structures import diamond_si
+SINGLE = {
+    # name: (arch, seed, z_table, avg_num_neighbors, stress, workload text)
+    "c0": ("small", 0, list(range(1, 90)), 46.0, True,
+           "config0: small MACE (128x0e, lmax3, corr3, 2 layers, r_max 6.0) random-init seed 0; diamond Si 3x3x3 "
+           "= 216 atoms rattled 0.01 A (seed 0); energy+forces+stress; cached NL r_max+0.5 skin"),
+    "c1": ("medium", 1, list(range(1, 90)), AVG_NUM_NEIGHBORS, False, WORKLOAD),
+    "c2": ("large", 2, [3, 8, 15, 16], 50.0, True,
+           "config2: large MACE (128x0e+128x1o+128x2e, lmax3, corr3, 2 layers, r_max 6.0) random-init seed 2; "
+           "cubic periodic LiPSO box of 8000 atoms (Li:P:S:O 3:1:4:0.5, 0.06 atoms/A^3, 1.8 A rejection, seed 2); "
+           "energy+forces+stress; cached NL r_max+0.5 skin"),
+}
 
+
+def make_structure(rank: int, config: str = "c1"):
+    from mace_mlx_b200.structures import diamond_si, lipso_box
+
+    if config == "c0":
+        return diamond_si(3, 0.01, 0 + 1000 * rank)
+    if config == "c2":
+        return lipso_box(8000, 2 + 1000 * rank)
     return diamond_si(5, 0.05, 1 + 1000 * rank)
 
 
-def make_model_dir(tmp: str) -> str:
+def make_model_dir(tmp: str, config: str = "c1") -> str:
     from mace_mlx_b200.weights import write_random_model
 
-    d = Path(tmp) / "medium_seed1"
-    write_random_model(d, "medium", seed=1, z_table=list(range(1, 90)), avg_num_neighbors=AVG_NUM_NEIGHBORS)
+    arch, seed, z_table, avg, _, _ = SINGLE[config]
+    d = Path(tmp) / f"{arch}_seed{seed}"
+    write_random_model(d, arch, seed=seed, z_table=z_table, avg_num_neighbors=avg)
     return str(d)
+
+
+def cpu_model() -> str:
+    """The host CPU's model name (lscpu), recorded beside every CPU number."""
+    try:
+        out = subprocess.run(["lscpu"], capture_output=True, text=True, timeout=10).stdout
+        for line in out.splitlines():
+            if line.startswith("Model name:"):
+                return line.split(":", 1)[1].strip()
+    except Exception:  # noqa: BLE001
+        pass
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except Exception:  # noqa: BLE001
+        pass
+    return "unknown"
 
 
 # ---------------------------------------------------------------------------
@@ -190,7 +227,7 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # CPU oracle port timing (cpu_baseline and --impl reference)
 # ---------------------------------------------------------------------------
-def time_cpu_port(st, model_dir: str, budget_s: float, max_steps: int, warmup: int = 1):
+def time_cpu_port(st, model_dir: str, budget_s: float, max_steps: int, warmup: int = 1, stress: bool = False):
     import torch
 
     from mace_mlx_b200.weights import load_model_dir
@@ -203,14 +240,15 @@ def time_cpu_port(st, model_dir: str, budget_s: float, max_steps: int, warmup: i
     orc = OracleMACE(config, weights, dtype=torch.float32)
     r_cut = float(config["r_max"]) + 0.5
     i, j, S = neighbour_list(st.positions, st.cell, st.pbc, r_cut)
-    species = st.numbers - 1
+    lut = {int(z): k for k, z in enumerate(config["z_table"])}
+    species = np.array([lut[int(z)] for z in st.numbers])
     for _ in range(max(0, warmup)):
-        orc.compute(st.positions, species, i, j, S, st.cell)
+        orc.compute(st.positions, species, i, j, S, st.cell, stress=stress)
     times = []
     t_start = time.perf_counter()
     while len(times) < max(1, max_steps):
         t0 = time.perf_counter()
-        orc.compute(st.positions, species, i, j, S, st.cell)
+        orc.compute(st.positions, species, i, j, S, st.cell, stress=stress)
         times.append(time.perf_counter() - t0)
         if time.perf_counter() - t_start > budget_s:
             break
@@ -218,40 +256,93 @@ def time_cpu_port(st, model_dir: str, budget_s: float, max_steps: int, warmup: i
     return len(st) / t, threads, len(times), t
 
 
+def cpu_sample_structure(config: str):
+    """A bounded CPU sample of the workload: the full structure for c0/c1, a
+    1000-atom box of the same composition and density for c2."""
+    from mace_mlx_b200.structures import lipso_box
+
+    if config == "c2":
+        return lipso_box(1000, 2), "1000-atom LiPSO box of the same composition and density"
+    return make_structure(0, config), "the full structure"
+
+
 def reference_arm(args, rank: int, world: int):
     if rank != 0:
         return 0
-    st = make_structure(0)
+    cfg = args.config if args.config in SINGLE else "c1"
+    stress = SINGLE[cfg][4]
+    st, what = cpu_sample_structure(cfg)
+    warm = min(args.warmup, 3)
     with tempfile.TemporaryDirectory() as tmp:
-        md = make_model_dir(tmp)
+        md = make_model_dir(tmp, cfg)
         budget = max(30.0, min(150.0, 6.0 * max(1, args.steps)))
-        value, threads, n, t = time_cpu_port(st, md, budget, args.steps, warmup=min(args.warmup, 1))
-    sample = (f"{n} full steps of the 1000-atom Si workload (median {t:.2f} s/step) with the torch-CPU fp32 "
-              f"restatement of the reference algorithm; warm-up {min(args.warmup, 1)}; MLX absent on this host")
+        value, threads, n, t = time_cpu_port(st, md, budget, args.steps, warmup=warm, stress=stress)
+    sample = (f"{n} steps on {what} (median {t:.2f} s/step) with the torch-CPU fp32 restatement of the reference "
+              f"algorithm (pinned to the reference's own execution by tests/golden/ref_*.npz); warm-up {warm}; "
+              f"CPU: {cpu_model()}; MLX absent on this host")
     line = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": n, "warmup": min(args.warmup, 1),
+        "metric": METRIC if cfg == "c1" else f"energy+forces atom-steps/s, {cfg}", "value": value, "unit": UNIT,
+        "n_gpus": args.gpus, "steps": n, "warmup": warm,
         "ms_per_step": t * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic", "impl": "reference",
-        "config": {"workload": WORKLOAD, "parallelism": "single host process"},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+        "config": {"workload": SINGLE[cfg][5], "parallelism": "single host process"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample,
+                         "cpu_model": cpu_model()},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
 
 
+def measure_fp32_peak(dev) -> dict:
+    """FP32 FMA issue rate of this GPU, measured now with the library's probe
+    kernel (8 independent FMA chains per thread, 8 CTAs of 256 threads per SM),
+    CUDA events on the launching stream, best of 5."""
+    import ctypes as C
+
+    import torch
+
+    from mace_mlx_b200 import native as nv
+
+    lib = nv.load_library()
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    blocks, iters = sms * 8, 1000
+    buf = torch.empty(blocks * 256, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    best = 0.0
+    for k in range(6):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        nv.check(lib.mace_fma_probe(C.c_void_p(buf.data_ptr()), blocks, iters, C.c_void_p(stream.cuda_stream)), lib)
+        b.record(stream)
+        b.synchronize()
+        if k:
+            ms = a.elapsed_time(b)
+            best = max(best, blocks * 256 * 8 * 16 * iters * 2 / (ms * 1e-3) / 1e12)
+    return {"tflops": best, "how": f"mace_fma_probe: {blocks} CTAs x 256 threads x 8 FMA chains, best of 5, "
+                                   "CUDA events (measured in this run)"}
+
 
 # ---------------------------------------------------------------------------
 # roofline of the dominant kernel of a profiled step
 # ---------------------------------------------------------------------------
-def roofline_of(work: dict, prof: list[dict], clk, steps: int, traffic_file: bool = True) -> dict:
+def roofline_of(work: dict, prof: list[dict], steps: int, fp32_peak: dict | None,
+                traffic_key: str | None = None) -> dict:
     """Roofline of the kernel with the largest share of `steps` profiled steps.
 
-    ``work`` holds one step's algorithmic FLOPs and bytes per (kernel, layer);
-    the kernel's time per step is its event-timed total over the steps, so a
+    ``work`` holds one step's algorithmic FLOPs, compulsory bytes and
+    materialised bytes per (kernel, layer) (``mace_mlx_b200.workmodel``); the
+    kernel's time per step is its event-timed total over the steps, so a
     kernel launched once per receiver chunk is compared with its whole work.
-    ``traffic`` (ncu DRAM bytes per launch) is filled from
-    profiles/ncu_traffic.json, which was captured on the headline workload.
+
+    Tensor-core kernels (radial MLP, o3 linears) are reported against the
+    measured dense bf16 GEMM peak; CUDA-core kernels against the measured HBM
+    copy bandwidth with their COMPULSORY bytes (node tables and edge list), and
+    -- since these kernels are FP32-issue bound rather than memory bound --
+    against the FP32 FMA peak measured in this run (``fp32``).  ``traffic``
+    is ncu's DRAM bytes per launch of the same kernel from
+    profiles/ncu_traffic.json (captured on the named workload) and
+    ``traffic_over_compulsory`` its ratio to the compulsory bytes.
     """
     peaks = {}
     pp = ROOT / "MEASURED_PEAKS.json"
@@ -259,40 +350,35 @@ def roofline_of(work: dict, prof: list[dict], clk, steps: int, traffic_file: boo
         peaks = json.loads(pp.read_text())
     hbm = float(peaks.get("hbm_gbs", 6650.0))
     bf16 = float(peaks.get("bf16_tflops", 1590.0))
-    peak_src = "measured" if pp.exists() else "fallback"
+    peak_src = "measured (MEASURED_PEAKS.json)" if pp.exists() else "fallback (no MEASURED_PEAKS.json)"
     prof = sorted(prof, key=lambda r: -r["ms"])
     tot_prof = sum(r["ms"] for r in prof)
     top = prof[0]
     avg_ms = top["ms"] / max(1, steps)
-    wk = work.get((top["name"], top["layer"]), {"flops": 0, "bytes": 0})
-    # Tensor-core kernels (radial MLP, o3 linears) are compared with the tensor
-    # pipe when their arithmetic intensity is high; the CUDA-core kernels
-    # (conv, symmetric contraction, edge, forces) with HBM, plus their fp32
-    # issue rate against the FMA peak at the sampled SM clock.
-    tensor_kernel = top["name"].startswith(("mlp", "linear"))
-    intensity = wk["flops"] / max(wk["bytes"], 1)
-    ridge = bf16 * 1e12 / (hbm * 1e9)
-    if tensor_kernel and intensity > ridge * 0.05:
+    wk = work.get((top["name"], top["layer"]), {"flops": 0, "bytes": 0, "bytes_materialised": 0})
+    if top["name"].startswith(("mlp", "linear")):
         ach = wk["flops"] / (avg_ms * 1e-3) / 1e12
         roof = {"bound": "tensor", "achieved": ach, "peak": bf16, "unit": "TFLOP/s", "frac": ach / bf16}
     else:
         ach = wk["bytes"] / (avg_ms * 1e-3) / 1e9
         roof = {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm}
-        clk_mhz = clk.summary().get("sm_mhz") or 1965.0
-        fma_peak = 148 * 128 * 2 * clk_mhz * 1e6 / 1e12
+    if fp32_peak and fp32_peak.get("tflops"):
         fl = wk["flops"] / (avg_ms * 1e-3) / 1e12
-        roof["fp32"] = {"achieved_tflops": fl, "peak_tflops": fma_peak, "frac": fl / fma_peak,
-                        "peak_source": "148 SMs x 128 FMA/clk x sampled SM clock (derived, not measured)"}
+        roof["fp32"] = {"achieved_tflops": fl, "peak_tflops": fp32_peak["tflops"], "frac": fl / fp32_peak["tflops"],
+                        "peak_source": fp32_peak["how"]}
     traffic = None
     tp = ROOT / "profiles" / "ncu_traffic.json"
-    if traffic_file and tp.exists():
+    if traffic_key and tp.exists():
         tr = json.loads(tp.read_text())
-        traffic = tr.get(f"{top['name']}/{top['layer']}")
+        traffic = tr.get(f"{traffic_key}:{top['name']}/{top['layer']}")
     roof.update({
-        "traffic": traffic, "kernel": f"{top['name']} layer {top['layer']}",
+        "traffic": traffic,
+        "traffic_over_compulsory": (traffic / wk["bytes"]) if traffic and wk["bytes"] else None,
+        "kernel": f"{top['name']} layer {top['layer']}",
         "kernel_share": top["ms"] / tot_prof, "avg_launch_ms": top["ms"] / top["count"],
         "kernel_ms_per_step": avg_ms,
-        "algorithmic_flops": wk["flops"], "algorithmic_bytes": wk["bytes"], "peak_source": peak_src,
+        "algorithmic_flops": wk["flops"], "compulsory_bytes": wk["bytes"],
+        "materialised_bytes": wk["bytes_materialised"], "peak_source": peak_src,
         "all_kernels_ms_per_step": {f"{r['name']}/{r['layer']}": r["ms"] / max(1, steps) for r in prof},
     })
     return roof
@@ -310,12 +396,15 @@ def b200_arm(args, rank: int, world: int, local_rank: int):
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    st = make_structure(rank)
+    cfg = args.config
+    stress = SINGLE[cfg][4]
+    props = ["energy", "forces", "stress"] if stress else ["energy", "forces"]
+    st = make_structure(rank, cfg)
     tmp = tempfile.mkdtemp(prefix=f"bench_r{rank}_")
-    md = make_model_dir(tmp)
+    md = make_model_dir(tmp, cfg)
     calc = MACECalculator(model_path=md, device=f"cuda:{local_rank}", skin=0.5)
     atoms = Atoms(st.numbers, st.positions, st.cell, st.pbc)
-    calc.calculate(atoms, ["energy", "forces"])
+    calc.calculate(atoms, props)
     model = calc.model
     edges = calc._nl_cache
     N, E = len(atoms), edges.n_edges
@@ -332,11 +421,11 @@ def b200_arm(args, rank: int, world: int, local_rank: int):
         torch.cuda.synchronize(dev)
 
     def step():
-        model.evaluate(pos, cell, species, gptr, edges, forces=True, virial=False, out=out, graph=True)
+        model.evaluate(pos, cell, species, gptr, edges, forces=True, virial=stress, out=out, graph=True)
 
     if args.device_only:
         for _ in range(args.warmup + args.steps):
-            model.evaluate(pos, cell, species, gptr, edges, forces=True, virial=False, out=out)
+            model.evaluate(pos, cell, species, gptr, edges, forces=True, virial=stress, out=out)
         torch.cuda.synchronize(dev)
         return 0
     for _ in range(max(3, args.warmup)):
@@ -359,12 +448,12 @@ def b200_arm(args, rank: int, world: int, local_rank: int):
     jitter = [st.positions + rng.normal(0, 1e-4, st.positions.shape) for _ in range(args.steps + args.warmup)]
     for k in range(args.warmup):
         atoms.positions = jitter[k]
-        calc.calculate(atoms, ["energy", "forces"])
+        calc.calculate(atoms, props)
     barrier()
     t0 = time.perf_counter()
     for k in range(args.steps):
         atoms.positions = jitter[args.warmup + k]
-        calc.calculate(atoms, ["energy", "forces"])
+        calc.calculate(atoms, props)
     e2e_s = time.perf_counter() - t0
     barrier()
     # per-kernel event timing (separate pass, same inputs)
@@ -373,6 +462,7 @@ def b200_arm(args, rank: int, world: int, local_rank: int):
         step()
     prof = model.profile_read()
     model.profile_enable(False)
+    fp32 = measure_fp32_peak(dev)
     if world > 1:
         tt = torch.tensor([total_ms, e2e_s], dtype=torch.float64, device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
@@ -381,24 +471,30 @@ def b200_arm(args, rank: int, world: int, local_rank: int):
         return 0
     value = world * N * args.steps / (total_ms / 1e3)
     e2e_value = world * N * args.steps / e2e_s
-    roof = roofline_of(kernel_work(model.spec, N, E), prof, clk, args.steps)
+    roof = roofline_of(kernel_work(model.spec, N, E), prof, args.steps, fp32, traffic_key=cfg)
     cpu = None
     if world == 1:
         try:
-            v, threads, n, t = time_cpu_port(st, md, args.cpu_seconds, 3)
-            cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
-                   "sample": f"{n} full 1000-atom Si steps (median {t:.2f} s) of the torch-CPU fp32 oracle port"}
+            cst, what = cpu_sample_structure(cfg)
+            v, threads, n, t = time_cpu_port(cst, md, args.cpu_seconds, 3, stress=stress)
+            cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "cpu_model": cpu_model(),
+                   "sample": f"{n} steps on {what} (median {t:.2f} s) of the torch-CPU fp32 oracle port"}
         except Exception as e:  # noqa: BLE001
             cpu = {"value": None, "unit": UNIT, "cores": os.cpu_count(), "kind": "port", "sample": f"failed: {e}"}
+    # the calculator moves one input block (cell + positions) and one output block
+    # (energy, virial, forces, node energies) per step
+    h2d = calc._blk[0].numel() * calc._blk[0].element_size()
+    d2h = calc._blk[1].numel() * calc._blk[1].element_size()
     line = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "metric": METRIC if cfg == "c1" else f"energy+forces atom-steps/s, {cfg}", "value": value, "unit": UNIT,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "n_atoms_per_gpu": N, "n_edges_per_gpu": E,
+        "config": {"workload": SINGLE[cfg][5], "n_atoms_per_gpu": N, "n_edges_per_gpu": E,
                    "l2": "flushed between timed steps (256 MB write)",
-                   "parallelism": f"structure-sharded x{world} (one independent Si1000 per GPU)"},
-        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": N * 3 * 4 + 9 * 4,
-                "d2h_bytes_per_step": 8 + N * 3 * 4 + N * 4, "ms_per_step": e2e_s * 1e3 / args.steps},
+                   "parallelism": f"structure-sharded x{world} (one independent structure per GPU)"},
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_s * 1e3 / args.steps},
         "gpu_launches": launches * args.steps,
         "clocks": clk.summary(),
         "roofline": roof,
@@ -556,14 +652,14 @@ def partition_arm(args, rank: int, world: int, local_rank: int):
     if rank != 0:
         return 0
     value = n_total * args.steps / (total_ms / 1e3)
-    roof = roofline_of(kernel_work(prof_model.spec, prof_n, prof_e), prof, clk, prof_steps, traffic_file=False)
+    roof = roofline_of(kernel_work(prof_model.spec, prof_n, prof_e), prof, prof_steps, measure_fp32_peak(dev))
     cpu = None
     if world == 1:
         try:
             with tempfile.TemporaryDirectory() as tmp:
                 md = make_model_dir(tmp)
                 v, threads, n, t = time_cpu_port(make_structure(0), md, args.cpu_seconds, 3)
-            cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
+            cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "cpu_model": cpu_model(),
                    "sample": f"{n} full 1000-atom Si steps of the medium model (median {t:.2f} s) of the torch-CPU "
                              f"fp32 oracle port; the per-atom rate stands in for this workload"}
         except Exception as e:  # noqa: BLE001

@@ -51,7 +51,7 @@ extern "C" {
 #define MACE_ERR_UNSUPPORTED 6
 #define MACE_ERR_EDGES 7
 
-#define MACE_ABI_VERSION 6
+#define MACE_ABI_VERSION 7
 
 /* limits of the packed model description */
 #define MACE_MAX_LAYERS 4
@@ -162,6 +162,11 @@ typedef struct {
   int32_t readout_hidden;         /* 16 */
   int64_t f_ro1;                  /* linear: (C); nonlinear: (C, hidden) */
   int64_t f_ro2;                  /* nonlinear: (hidden)                 */
+  /* density normalisation (reference blocks.py:282-490): the message is
+   * divided by (sum over the receiver's edges of tanh((w_d . b_e)^2) + 1)
+   * instead of avg_num_neighbors; f_density = w_d (num_bessel), else -1 */
+  int32_t density;
+  int64_t f_density;
 } mace_layer_desc;
 
 typedef struct {
@@ -181,6 +186,20 @@ typedef struct {
   int64_t f_bessel;               /* (num_bessel) frequencies            */
   int64_t f_sh;                   /* SH recursion tensors T_2, T_3       */
   mace_layer_desc layers[MACE_MAX_LAYERS];
+  /* Agnesi distance transform of the length fed to the Bessel basis
+   * (reference radial.py:202-262): r_t = 1 / (1 + a x^q / (1 + x^(q-p))),
+   * x = max(r / r0, 1e-12), r0 = (R[z_s] + R[z_r]) / 2 with R of f_radius_agnesi */
+  int32_t agnesi;
+  float agnesi_q, agnesi_p, agnesi_a;
+  int64_t f_radius_agnesi;        /* (num_elements) covalent radius per element index */
+  /* ZBL pair repulsion (reference radial.py:127-199), added to the receiver's
+   * interaction energy: 0.5 * 14.3996 Z_s Z_r / r * phi(r / a) * envelope_p(r / (R_s + R_r)),
+   * a = a_prefactor * 0.529 / (Z_s^a_exp + Z_r^a_exp) */
+  int32_t zbl;
+  int32_t zbl_p;
+  float zbl_a_exp, zbl_a_prefactor;
+  int64_t f_radius_zbl;           /* (num_elements) covalent radius per element index */
+  int64_t f_znum;                 /* (num_elements) atomic number per element index (float) */
   const float* floats; int64_t n_floats;    /* host pointers, copied at create */
   const int32_t* ints; int64_t n_ints;
 } mace_model_desc;
@@ -284,13 +303,19 @@ int mace_nl_build(mace_ctx* ctx, const double* pos, const double* cell, const in
  * every GPU loading the library holds until exit, so it works for hosts that
  * own all GPU memory or cannot afford cudaMalloc's implicit synchronisation.
  * Calls nothing that allocates.  Limits: at most MACE_NOALLOC_MAX_ATOMS atoms
- * (larger systems fail with MACE_ERR_BAD_ARG).  The first call on each device
- * looks up the array's device address and should come before any stream
- * capture.  All calls share the array: calls that overlap on the GPU race.
+ * in total and MACE_NOALLOC_MAX_GRAPH_ATOMS per graph (larger systems fail
+ * with MACE_ERR_BAD_ARG).  Cost: always the all-pairs build, O(n_g^2 x periodic
+ * images) per graph of n_g atoms (mace_nl_build switches to cell lists for
+ * large single structures).  With CUDA's default lazy module loading the first
+ * call on a device loads the array (4 MiB): make it before a memory pool takes
+ * all free memory (or set CUDA_MODULE_LOADING=EAGER), and before any stream
+ * capture.  The array's device address is cached per device and CUDA context.
+ * All calls share the array: calls that overlap on the GPU race.
  * Uses the caller's current device.
  */
 #define MACE_NOALLOC_SCRATCH_BYTES (4u << 20)
 #define MACE_NOALLOC_MAX_ATOMS 131072
+#define MACE_NOALLOC_MAX_GRAPH_ATOMS 16384
 int mace_nl_build_noalloc(const double* pos, const double* cell, const int32_t* pbc,
                           const int32_t* graph_ptr, int32_t num_graphs, int64_t n, double r_cut,
                           int32_t* sender, int32_t* receiver, int32_t* shifts, int32_t* row_ptr,
@@ -314,6 +339,16 @@ int mace_forward_backward(mace_ctx* ctx, const mace_system* sys, const mace_outp
  * e % 128, 16-byte group ((c % 32) / 4) XOR (e % 8), position c % 4.
  */
 int mace_debug_buffer(mace_ctx* ctx, int32_t id, const float** ptr, int64_t* len);
+
+/*
+ * Diagnostic (no reference counterpart): FP32 fused multiply-add issue-rate
+ * probe used to measure the CUDA-core peak the benchmark's roofline compares
+ * CUDA-core kernels with.  Launches `blocks` CTAs of 256 threads, each thread
+ * running 8 independent FMA chains of 16 x `iters` steps (FLOPs = blocks x 256
+ * x 8 x 16 x iters x 2) and writing one float per thread to `out`
+ * (blocks x 256 floats, device memory).  Asynchronous on `stream`.
+ */
+int mace_fma_probe(float* out, int32_t blocks, int32_t iters, void* stream);
 
 /* Number of kernel launches the last mace_forward_backward issued. */
 int mace_last_launch_count(const mace_ctx* ctx, int32_t* count);

@@ -67,9 +67,103 @@ struct EdgeParams {
   const float* db;  // (E,nb)
   float* dv;        // (E,3)
   double* virial_part;  // (gridDim, 9)
+  // element-dependent terms (mpa-0 family); species gives the element index per node
+  const int32_t* species;
+  int agnesi;                 // Agnesi transform of the Bessel argument
+  float ag_q, ag_p, ag_a;
+  const float* ag_radius;     // (num_elements)
+  int zbl;                    // ZBL pair repulsion (backward: its gradient)
+  int zbl_p;
+  float zbl_a_exp, zbl_a_pref;
+  const float* zbl_radius;    // (num_elements)
+  const float* znum;          // (num_elements) atomic numbers
+  float zbl_dscale;           // d(node energy) / d(pair energy): ScaleShiftMACE scale, else 1
+  const float* weight;        // (N) energy weight per node, or null (1)
+  // density normalisation gradients, one entry per density layer
+  int n_dens;
+  const float* dens_w[MACE_MAX_LAYERS];  // (nb) density_fn weights
+  const float* dD[MACE_MAX_LAYERS];      // (N) dE / d density of the receiver
 };
 int launch_edge_fwd(const EdgeParams& p, cudaStream_t s);
 int launch_edge_bwd(const EdgeParams& p, int* n_blocks, cudaStream_t s);
+
+// Agnesi transform r_t(r) and dr_t/dr (reference radial.py:235-262)
+__device__ __forceinline__ float agnesi_transform(float r, float r0, float q, float pp, float a, float* drt_dr) {
+  float x = r / r0;
+  const bool clamped = !(x > 1e-12f);
+  x = clamped ? 1e-12f : x;
+  const float xq = powf(x, q), xqp = powf(x, q - pp);
+  const float den = 1.0f + xqp;
+  const float rt = 1.0f / (1.0f + a * xq / den);
+  const float dg_dx = a * (xq / x) * (q + pp * xqp) / (den * den);
+  *drt_dr = clamped ? 0.0f : -rt * rt * dg_dx / r0;
+  return rt;
+}
+
+// polynomial envelope of degree p on u and its derivative (reference radial.py:18-34)
+__device__ __forceinline__ float poly_envelope(float u, int p, float* denv_du) {
+  const float pf = (float)p;
+  float up = 1.f;
+  for (int i = 0; i < p - 1; ++i) up *= u;
+  const float upm1 = p > 0 ? up : 0.f;  // u^(p-1)
+  up = p > 0 ? up * u : 1.f;            // u^p
+  float env = 1.0f - ((pf + 1.0f) * (pf + 2.0f) / 2.0f) * up + pf * (pf + 2.0f) * (up * u) -
+              (pf * (pf + 1.0f) / 2.0f) * (up * u * u);
+  float d = -((pf + 1.0f) * (pf + 2.0f) / 2.0f) * pf * upm1 + pf * (pf + 2.0f) * (pf + 1.0f) * up -
+            (pf * (pf + 1.0f) / 2.0f) * (pf + 2.0f) * (up * u);
+  if (!(u < 1.0f)) {
+    env = 0.f;
+    d = 0.f;
+  }
+  *denv_du = d;
+  return env;
+}
+
+// ZBL pair energy of one directed edge and its derivative in r (reference radial.py:160-197)
+__device__ __forceinline__ float zbl_pair(float r, float zu, float zv, float rmax_pair, float a_exp, float a_pref,
+                                          int p, float* dv_dr) {
+  const float a = a_pref * 0.529f / (powf(zu, a_exp) + powf(zv, a_exp));
+  const float s = r / a;
+  const float e1 = expf(-3.2f * s), e2 = expf(-0.9423f * s), e3 = expf(-0.4028f * s), e4 = expf(-0.2016f * s);
+  const float phi = 0.1818f * e1 + 0.5099f * e2 + 0.2802f * e3 + 0.02817f * e4;
+  const float dphi = -(0.1818f * 3.2f * e1 + 0.5099f * 0.9423f * e2 + 0.2802f * 0.4028f * e3 +
+                       0.02817f * 0.2016f * e4) / a;
+  const float K = 14.3996f * zu * zv;
+  float denv;
+  const float env = poly_envelope(r / rmax_pair, p, &denv);
+  const float v = 0.5f * (K / r) * phi * env;
+  *dv_dr = 0.5f * K * ((dphi / r - phi / (r * r)) * env + (phi / r) * denv / rmax_pair);
+  return v;
+}
+
+// per-node sums over each receiver's edges that need no learned features:
+// density of every density layer and the ZBL pair energy (forward), and the
+// density rescaling of the interaction message and its gradient
+struct NodeSumParams {
+  int64_t N;
+  const int32_t* row_ptr;
+  const int32_t* snd;
+  const int32_t* species;
+  const float* v;   // (E,3) edge vectors
+  const float* b;   // (E,nb) radial basis
+  int nb;
+  int n_dens;
+  const float* dens_w[MACE_MAX_LAYERS];
+  float* D[MACE_MAX_LAYERS];  // (N) density per layer
+  int zbl;
+  int zbl_p;
+  float zbl_a_exp, zbl_a_pref;
+  const float* zbl_radius;
+  const float* znum;
+  float* pair;  // (N) pair energy per receiver
+};
+int launch_node_sums(const NodeSumParams& p, cudaStream_t s);
+// rows[n][:] /= (D[n] + 1)
+int launch_density_scale(float* rows, int64_t row_len, const float* D, int64_t N, cudaStream_t s);
+// dD[n] = -sum_f drows[n][f] rows[n][f] / (D[n] + 1); drows[n][:] *= 1 / (D[n] + 1)
+// (rows are the rescaled forward rows)
+int launch_density_bwd(const float* rows, float* drows, int64_t row_len, const float* D, float* dD, int64_t N,
+                       cudaStream_t s);
 
 struct ForceParams {
   int64_t N;

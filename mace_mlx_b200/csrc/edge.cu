@@ -8,6 +8,13 @@
 //                                          (mace_mlx/spherical_harmonics.py:67-155)
 //   b_n = sqrt(2/r_max) sin(w_n r)/r * envelope(r/r_max)
 //                                          (mace_mlx/radial.py:18-71, 265-321)
+//   with the Agnesi transform, the Bessel argument is r_t(r, element pair)
+//   and the envelope keeps the raw r     (mace_mlx/radial.py:202-262, 294-321)
+// The backward also carries the gradients of two element-dependent terms
+// that depend on the edge length alone: the ZBL pair repulsion
+// (radial.py:127-199) and the density normalisation's per-edge density
+// tanh((w_d . b_e)^2) (blocks.py:389-401), whose per-receiver gradients the
+// node kernels provide.
 // One thread per edge; every edge's result is a pure function of its own
 // inputs, so the reverse edge (j -> i, -S) gets bitwise v_rev = -v and the
 // same r, which the conv backward relies on.
@@ -93,6 +100,17 @@ __device__ __forceinline__ float ipow(float x, int p) {
   return r;
 }
 
+constexpr int MAX_NB = 16;
+
+// Bessel argument of edge e: r, or its Agnesi transform (then *drt = dr_t/dr)
+__device__ __forceinline__ float bessel_arg(const EdgeParams& p, int64_t e, float r, float* drt) {
+  *drt = 1.f;
+  if (!p.agnesi) return r;
+  const int zs = p.species[p.snd[e]], zr = p.species[p.rcv[e]];
+  const float r0 = 0.5f * (__ldg(p.ag_radius + zs) + __ldg(p.ag_radius + zr));
+  return agnesi_transform(r, r0, p.ag_q, p.ag_p, p.ag_a, drt);
+}
+
 __global__ void k_edge_fwd(EdgeParams p) {
   int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (e >= p.E) return;
@@ -111,9 +129,11 @@ __global__ void k_edge_fwd(EdgeParams p) {
   float env = 1.0f - ((pf + 1.0f) * (pf + 2.0f) / 2.0f) * up + pf * (pf + 2.0f) * (up * x) -
               (pf * (pf + 1.0f) / 2.0f) * (up * x * x);
   env = (x < 1.0f) ? env : 0.0f;
+  float drt;
+  const float rb = bessel_arg(p, e, g.r, &drt);
   for (int n = 0; n < p.nb; ++n) {
     float w = __ldg(p.bessel_w + n);
-    float bes = pref * sinf(w * g.r) / g.r;
+    float bes = pref * sinf(w * rb) / rb;
     p.b[(int64_t)p.nb * e + n] = bes * env;
   }
 }
@@ -176,14 +196,36 @@ __global__ void k_edge_bwd(EdgeParams p) {
       env = 0.f;
       denv = 0.f;
     }
-    float dr = 0.f;
+    float drt;
+    const float rb = bessel_arg(p, e, g.r, &drt);
+    float bes[MAX_NB], dbes[MAX_NB], dbn[MAX_NB];
     for (int n = 0; n < p.nb; ++n) {
       float w = __ldg(p.bessel_w + n);
       float sn, cs;
-      sincosf(w * g.r, &sn, &cs);
-      float bes = pref * sn / g.r;
-      float dbes = pref * (w * cs * g.r - sn) / (g.r * g.r);
-      dr += p.db[(int64_t)p.nb * e + n] * (dbes * env + bes * denv);
+      sincosf(w * rb, &sn, &cs);
+      bes[n] = pref * sn / rb;
+      dbes[n] = pref * (w * cs * rb - sn) / (rb * rb) * drt;  // d bes / dr through r_t
+      dbn[n] = p.db[(int64_t)p.nb * e + n];
+    }
+    // density normalisation: d_e = tanh(x^2), x = w_d . b_e, with dE/dD of the receiver
+    for (int t = 0; t < p.n_dens; ++t) {
+      const float* wd = p.dens_w[t];
+      float xd = 0.f;
+      for (int n = 0; n < p.nb; ++n) xd = fmaf(__ldg(wd + n), bes[n] * env, xd);
+      const float th = tanhf(xd * xd);
+      const float gx = p.dD[t][p.rcv[e]] * (1.0f - th * th) * 2.0f * xd;
+      for (int n = 0; n < p.nb; ++n) dbn[n] = fmaf(gx, __ldg(wd + n), dbn[n]);
+    }
+    float dr = 0.f;
+    for (int n = 0; n < p.nb; ++n) dr += dbn[n] * (dbes[n] * env + bes[n] * denv);
+    if (p.zbl) {
+      const int s_n = p.snd[e], r_n = p.rcv[e];
+      const int zs = p.species[s_n], zr = p.species[r_n];
+      float dvdr;
+      zbl_pair(g.r, __ldg(p.znum + zs), __ldg(p.znum + zr), __ldg(p.zbl_radius + zs) + __ldg(p.zbl_radius + zr),
+               p.zbl_a_exp, p.zbl_a_pref, p.zbl_p, &dvdr);
+      const float seed = p.weight ? p.zbl_dscale * p.weight[r_n] : p.zbl_dscale;
+      dr = fmaf(seed, dvdr, dr);
     }
     // u = v / r and r = sqrt(max(|v|^2, eps)): dv = (du - u (u.du)) / r + dr * u
     // (when the clamp is active r is a constant and only du / r remains)
@@ -275,6 +317,7 @@ __global__ void k_virial_reduce(const double* part, int n_part, double* out) {
 
 int launch_edge_fwd(const EdgeParams& p, cudaStream_t s) {
   if (p.E == 0) return MACE_OK;
+  if (p.nb > MAX_NB) return fail(MACE_ERR_UNSUPPORTED, "edge features: at most 16 Bessel functions");
   int64_t blocks = (p.E + 255) / 256;
   k_edge_fwd<<<(unsigned)blocks, 256, 0, s>>>(p);
   MACE_LAUNCH_CHECK("edge_fwd");

@@ -7,18 +7,32 @@
 // hold a mace_ctx, whose workspace is allocated by mace_ctx_reserve.  For them
 // mace_nl_build_noalloc takes only the inputs and caller-owned outputs; its
 // scratch (per-atom counts, graph ids, wrap offsets, the scan's temporary
-// storage, the inverse cell and an error flag) lives in one file-scope
-// __device__ array of MACE_NOALLOC_SCRATCH_BYTES, which every GPU that loads
-// this library holds until the process exits.
+// storage, the inverse cell, the largest graph's size and an error flag) lives
+// in one file-scope __device__ array of MACE_NOALLOC_SCRATCH_BYTES, which every
+// GPU that loads this library holds until the process exits.
 //
 // The host cannot use the array's name as a device address (in host code it
-// names a host-side shadow), so on the first call on each device this file
-// asks the runtime for the device address with cudaGetSymbolAddress, with that
-// device current, and caches it.  That first call should therefore happen
-// before any stream capture.  All calls share the one array and it keeps the
-// previous call's contents: everything that must start at zero is cleared on
-// every call, and calls that overlap on the GPU (different streams, or
-// different host threads on the same device) race on the scratch.
+// names a host-side shadow), so this file asks the runtime for the device
+// address with cudaGetSymbolAddress, with the device current, and caches it
+// per device together with the CUDA context it was looked up in; a call that
+// finds another context current (the primary context was reset and
+// recreated) looks the address up again.  With CUDA's default lazy module
+// loading the module holding the array, and so its 4 MiB, is loaded at the
+// first lookup on a device: a host that sizes its own pool to all free memory
+// should make one call (or set CUDA_MODULE_LOADING=EAGER) before it does so,
+// and the first call on each device should come before any stream capture.
+// All calls share the one array and it keeps the previous call's contents:
+// everything that must start at zero is cleared on every call, and calls that
+// overlap on the GPU (different streams, or different host threads on the
+// same device) race on the scratch.
+//
+// Cost: this entry point always uses the all-pairs kernels (one CTA per
+// receiver scanning every atom of its graph and every periodic image, twice),
+// O(n_g^2 x images) per graph of n_g atoms, because the cell-list build needs
+// a per-edge key buffer that a fixed array cannot hold.  Graphs are therefore
+// limited to MACE_NOALLOC_MAX_GRAPH_ATOMS atoms each (many small graphs up to
+// MACE_NOALLOC_MAX_ATOMS in total are fine); larger single structures belong
+// to mace_nl_build, which switches to cell lists.
 #include <cmath>
 #include <mutex>
 
@@ -32,25 +46,74 @@ constexpr size_t kScratchBytes = MACE_NOALLOC_SCRATCH_BYTES;
 static __device__ __align__(256) unsigned char g_nl_scratch[kScratchBytes];
 
 std::mutex g_addr_mu;
-void* g_addr[64] = {};
+struct ScratchAddr {
+  void* ctx = nullptr;   // CUcontext the address belongs to
+  void* addr = nullptr;  // device address of g_nl_scratch in that context
+};
+ScratchAddr g_addr[64];
 
 size_t align256(size_t b) { return (b + 255) & ~(size_t)255; }
 
-// device address of the scratch array on the current device
+// cuCtxGetCurrent through the runtime's driver entry point (the library does
+// not link libcuda itself)
+using CtxGetCurrentFn = int (*)(void**);
+CtxGetCurrentFn ctx_get_current() {
+  static CtxGetCurrentFn fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      f = nullptr;
+    return reinterpret_cast<CtxGetCurrentFn>(f);
+  }();
+  return fn;
+}
+
+// device address of the scratch array on the current device and context
 int scratch_address(void** out) {
   int dev = -1;
   MACE_CUDA_TRY(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 64) return fail(MACE_ERR_BAD_ARG, "device index out of range for the no-alloc scratch");
+  CtxGetCurrentFn get = ctx_get_current();
+  void* ctx = nullptr;
+  if (get && get(&ctx) != 0) ctx = nullptr;
   std::lock_guard<std::mutex> lk(g_addr_mu);
-  if (!g_addr[dev]) {
+  ScratchAddr& a = g_addr[dev];
+  if (!a.addr || !ctx || a.ctx != ctx || !get) {
     void* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_nl_scratch);
+    if (e == cudaErrorMemoryAllocation)
+      return fail(MACE_ERR_CUDA, "mace_nl_build_noalloc: loading its 4 MiB static scratch failed: the device is "
+                                 "out of memory (make the first call before a memory pool takes all of it)");
     if (e != cudaSuccess || p == nullptr)
       return fail(MACE_ERR_CUDA, std::string("cudaGetSymbolAddress(no-alloc scratch): ") + cudaGetErrorString(e));
-    g_addr[dev] = p;
+    void* now = nullptr;  // the lookup made the device's context current
+    if (get && get(&now) != 0) now = nullptr;
+    a.addr = p;
+    a.ctx = now;
   }
-  *out = g_addr[dev];
+  *out = a.addr;
   return MACE_OK;
+}
+
+// largest graph of graph_ptr (num_graphs + 1 offsets) into *out
+__global__ void k_max_graph(const int32_t* __restrict__ graph_ptr, int32_t num_graphs, int32_t* out) {
+  int32_t m = 0;
+  for (int32_t g = threadIdx.x; g < num_graphs; g += blockDim.x) {
+    const int32_t sz = graph_ptr[g + 1] - graph_ptr[g];
+    m = sz > m ? sz : m;
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    const int32_t v = __shfl_xor_sync(0xffffffffu, m, o);
+    m = v > m ? v : m;
+  }
+  __shared__ int32_t warp_max[32];
+  if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) m = warp_max[w] > m ? warp_max[w] : m;
+    *out = m;
+  }
 }
 
 #define NA_TRY(x)           \
@@ -73,14 +136,16 @@ extern "C" int mace_nl_build_noalloc(const double* pos, const double* cell, cons
   if (n > MACE_NOALLOC_MAX_ATOMS)
     return fail(MACE_ERR_BAD_ARG, "mace_nl_build_noalloc: " + std::to_string(n) + " atoms exceed the limit of " +
                                       std::to_string(MACE_NOALLOC_MAX_ATOMS) + " (use mace_nl_build with a context)");
-  // scratch layout: count (n+1) | node graph (n) | wrap (3n) | inverse cell (9 f64) | error flag | scan temp
+  // scratch layout: count (n+1) | node graph (n) | wrap (3n) | inverse cell (9 f64) | error flag |
+  // largest graph | scan temp
   const size_t scan_bytes = scan_tmp_bytes(n);
   const size_t o_count = 0;
   const size_t o_graph = o_count + align256(sizeof(int32_t) * (n + 1));
   const size_t o_wrap = o_graph + align256(sizeof(int32_t) * n);
   const size_t o_inv = o_wrap + align256(sizeof(int32_t) * 3 * n);
   const size_t o_err = o_inv + align256(sizeof(double) * 9);
-  const size_t o_scan = o_err + align256(sizeof(int));
+  const size_t o_gmax = o_err + align256(sizeof(int));
+  const size_t o_scan = o_gmax + align256(sizeof(int32_t));
   if (o_scan + scan_bytes > kScratchBytes)
     return fail(MACE_ERR_BAD_ARG, "mace_nl_build_noalloc: system does not fit the static scratch array");
   void* base = nullptr;
@@ -91,9 +156,21 @@ extern "C" int mace_nl_build_noalloc(const double* pos, const double* cell, cons
   int32_t* wrap = reinterpret_cast<int32_t*>(sb + o_wrap);
   double* d_inv = reinterpret_cast<double*>(sb + o_inv);
   int* d_err = reinterpret_cast<int*>(sb + o_err);
+  int32_t* d_gmax = reinterpret_cast<int32_t*>(sb + o_gmax);
   void* scan_tmp = sb + o_scan;
 
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  // the all-pairs kernels cost O(n_g^2) per graph: refuse graphs above the per-graph limit
+  k_max_graph<<<1, 256, 0, s>>>(graph_ptr, num_graphs, d_gmax);
+  MACE_CUDA_TRY(cudaGetLastError());
+  int32_t gmax = 0;
+  MACE_CUDA_TRY(cudaMemcpyAsync(&gmax, d_gmax, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+  MACE_CUDA_TRY(cudaStreamSynchronize(s));
+  if (gmax > MACE_NOALLOC_MAX_GRAPH_ATOMS)
+    return fail(MACE_ERR_BAD_ARG, "mace_nl_build_noalloc: a graph of " + std::to_string(gmax) +
+                                      " atoms exceeds the per-graph limit of " +
+                                      std::to_string(MACE_NOALLOC_MAX_GRAPH_ATOMS) +
+                                      " (all-pairs build; use mace_nl_build with a context for cell lists)");
   NlParams p{};
   p.n = n;
   p.pos = pos;

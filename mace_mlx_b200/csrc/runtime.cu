@@ -80,7 +80,9 @@ struct mace_ctx {
   std::vector<float*> h;   // h[t], t = 0..T   (N, row_t)
   std::vector<float*> dh;  // dh[t]
   std::vector<int> h_row;
-  float* e_layers = nullptr;  // (T, N)
+  float* e_layers = nullptr;  // (T, N), then the ZBL pair energies (N) when the model has them
+  float* dens = nullptr;      // (T, N) density of every density-normalised layer
+  float* ddens = nullptr;     // (T, N) its gradient
   LayerBufs lb[MACE_MAX_LAYERS];
   // neighbour-list scratch
   int32_t *nl_count = nullptr, *nl_graph = nullptr, *nl_wrap = nullptr;
@@ -290,7 +292,9 @@ int reserve(mace_ctx* c, int64_t N, int64_t E, int64_t EC) {
     TRY(alloc(c, &c->h[t], N * c->h_row[t]));
     TRY(alloc(c, &c->dh[t], N * c->h_row[t]));
   }
-  TRY(alloc(c, &c->e_layers, (int64_t)T * N));
+  TRY(alloc(c, &c->e_layers, (int64_t)(T + 1) * N));
+  TRY(alloc(c, &c->dens, (int64_t)T * N));
+  TRY(alloc(c, &c->ddens, (int64_t)T * N));
   for (int t = 0; t < T; ++t) {
     const mace_layer_desc& L = d.layers[t];
     LayerBufs& B = c->lb[t];
@@ -585,7 +589,57 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
   ep.db = c->db;
   ep.dv = c->dv;
   ep.virial_part = (flags & MACE_WANT_VIRIAL) ? c->vir_part : nullptr;
+  ep.species = sys->species;
+  ep.agnesi = d.agnesi;
+  if (d.agnesi) {
+    ep.ag_q = d.agnesi_q;
+    ep.ag_p = d.agnesi_p;
+    ep.ag_a = d.agnesi_a;
+    ep.ag_radius = F(c, d.f_radius_agnesi);
+  }
+  ep.zbl = d.zbl;
+  if (d.zbl) {
+    ep.zbl_p = d.zbl_p;
+    ep.zbl_a_exp = d.zbl_a_exp;
+    ep.zbl_a_pref = d.zbl_a_prefactor;
+    ep.zbl_radius = F(c, d.f_radius_zbl);
+    ep.znum = F(c, d.f_znum);
+    ep.zbl_dscale = d.scale_shift ? d.scale : 1.0f;
+    ep.weight = sys->energy_weight;
+  }
+  ep.n_dens = 0;
+  for (int t = 0; t < d.num_layers; ++t) {
+    if (!d.layers[t].density) continue;
+    ep.dens_w[ep.n_dens] = F(c, d.layers[t].f_density);
+    ep.dD[ep.n_dens] = c->ddens + (int64_t)t * N;
+    ++ep.n_dens;
+  }
   if (E > 0) LAUNCH("edge_fwd", -1, launch_edge_fwd(ep, s));
+  if (ep.n_dens > 0 || d.zbl) {
+    // per-receiver densities of the density-normalised layers and ZBL pair energies
+    NodeSumParams np{};
+    np.N = N;
+    np.row_ptr = sys->row_ptr;
+    np.snd = sys->sender;
+    np.species = sys->species;
+    np.v = c->v;
+    np.b = c->b;
+    np.nb = d.num_bessel;
+    for (int t = 0; t < d.num_layers; ++t) {
+      if (!d.layers[t].density) continue;
+      np.dens_w[np.n_dens] = F(c, d.layers[t].f_density);
+      np.D[np.n_dens] = c->dens + (int64_t)t * N;
+      ++np.n_dens;
+    }
+    np.zbl = d.zbl;
+    np.zbl_p = d.zbl_p;
+    np.zbl_a_exp = d.zbl_a_exp;
+    np.zbl_a_pref = d.zbl_a_prefactor;
+    np.zbl_radius = d.zbl ? F(c, d.f_radius_zbl) : nullptr;
+    np.znum = d.zbl ? F(c, d.f_znum) : nullptr;
+    np.pair = c->e_layers + (int64_t)d.num_layers * N;
+    LAUNCH("node_sums", -1, launch_node_sums(np, s));
+  }
   // The MLP chain of every layer's forward is issued at once (the MLP kernels
   // hold their SMs for a whole 128-edge tile, so whatever runs beside them
   // slows down; issuing mlp_fwd(t) after conv_fwd(t-1), mlp_bwd(t) beside
@@ -653,10 +707,13 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
         const mace_lin_group& g = L.lin[l];
         int ko[MACE_MAX_SRC];
         for (int q = 0; q < g.n_src; ++q) ko[q] = L.conv[g.src[q]].off;
-        lp.job[l] = make_job(c, 2 * l + 1, g.n_src, ko, L.inter.off[l], F(c, g.f_w), C, d.inv_avg_num_neighbors, 0);
+        lp.job[l] = make_job(c, 2 * l + 1, g.n_src, ko, L.inter.off[l], F(c, g.f_w), C,
+                             L.density ? 1.0f : d.inv_avg_num_neighbors, 0);
       }
       LAUNCH("linear_msg", t, launch_linear(lp, s));
     }
+    if (L.density)  // message / (density + 1) instead of / avg_num_neighbors
+      LAUNCH("density_scale", t, launch_density_scale(B.msg, L.inter.dim, c->dens + (int64_t)t * N, N, s));
     const float* sc_in = B.msg;
     if (!L.residual) {
       SkipParams sp = skip_params(c, t, N, sys->species, false, L.inter, L.inter, B.msg, B.msg2, 0);
@@ -695,6 +752,7 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
     p.graph_ptr = sys->graph_ptr;
     p.e0 = F(c, d.f_e0);
     p.e_layers = c->e_layers;
+    if (d.zbl) p.T = T + 1;  // the pair energies are one more (scaled) interaction term
     p.scale_shift = d.scale_shift;
     p.scale = d.scale;
     p.shift = d.shift;
@@ -736,6 +794,9 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
       SkipParams sp = skip_params(c, t, N, sys->species, true, L.inter, L.inter, B.dmsg2, B.dmsg, 1);
       LAUNCH("skip_bwd", t, launch_skip(sp, s));
     }
+    if (L.density)  // through message = linear(A) / (D + 1): dD, and dmsg / (D + 1)
+      LAUNCH("density_bwd", t, launch_density_bwd(B.msg, B.dmsg, L.inter.dim, c->dens + (int64_t)t * N,
+                                                  c->ddens + (int64_t)t * N, N, s));
     {
       // dA[mid slot k] = inv_avg * dmsg[inter slot l_k] @ W_l^T (block q of the concat-K)
       LinParams lp{};
@@ -752,7 +813,7 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
         for (int q = 0; q < g.n_src; ++q) {
           int ko = L.inter.off[l];
           lp.job[lp.n_jobs++] = make_job(c, 2 * l + 1, 1, &ko, L.conv[g.src[q]].off, F(c, g.f_wt) + q * C,
-                                         g.n_src * C, d.inv_avg_num_neighbors, 0);
+                                         g.n_src * C, L.density ? 1.0f : d.inv_avg_num_neighbors, 0);
         }
       }
       LAUNCH("linear_msg_bwd", t, launch_linear(lp, s));
@@ -1216,7 +1277,8 @@ int mace_debug_buffer(mace_ctx* c, int32_t id, const float** ptr, int64_t* len) 
       case 4: *ptr = c->db; *len = E * c->desc.num_bessel; break;
       case 5: *ptr = c->dv; *len = E * 3; break;
       case 6: *ptr = c->h[0]; *len = N * c->h_row[0]; break;
-      case 7: *ptr = c->e_layers; *len = N * c->desc.num_layers; break;
+      case 7: *ptr = c->e_layers; *len = N * (c->desc.num_layers + (c->desc.zbl ? 1 : 0)); break;
+      case 8: *ptr = c->dens; *len = N * c->desc.num_layers; break;
       default: return fail(MACE_ERR_BAD_ARG, "unknown debug buffer");
     }
     return MACE_OK;

@@ -19,7 +19,7 @@ MACE_ERR_TIMEOUT = 4
 MACE_ERR_NCCL = 5
 MACE_ERR_UNSUPPORTED = 6
 MACE_ERR_EDGES = 7
-ABI_VERSION = 6
+ABI_VERSION = 7
 
 MAX_LAYERS = 4
 MAX_IN = 4
@@ -36,7 +36,7 @@ STAGES = {
     "up": 0, "w": 1, "A": 2, "msg": 3, "B": 4, "h_out": 5, "dh_out": 6, "dB": 7,
     "dmsg": 8, "dA": 9, "dup": 10, "act": 11, "dh_in": 12, "msg2": 13,
 }
-EDGE_STAGES = {"v": 0, "Y": 1, "b": 2, "dY": 3, "db": 4, "dv": 5, "h0": 6, "e_layers": 7}
+EDGE_STAGES = {"v": 0, "Y": 1, "b": 2, "dY": 3, "db": 4, "dv": 5, "h0": 6, "e_layers": 7, "dens": 8}
 
 i32, i64, f32 = C.c_int32, C.c_int64, C.c_float
 
@@ -75,6 +75,7 @@ class LayerDesc(C.Structure):
         ("f_prod", i64 * MAX_IN), ("f_prod_t", i64 * MAX_IN),
         ("readout_nonlinear", i32), ("readout_hidden", i32),
         ("f_ro1", i64), ("f_ro2", i64),
+        ("density", i32), ("f_density", i64),
     ]
 
 
@@ -85,6 +86,9 @@ class ModelDesc(C.Structure):
         ("r_max", f32), ("inv_avg_num_neighbors", f32), ("scale", f32), ("shift", f32),
         ("f_e0", i64), ("f_emb", i64), ("f_bessel", i64), ("f_sh", i64),
         ("layers", LayerDesc * MAX_LAYERS),
+        ("agnesi", i32), ("agnesi_q", f32), ("agnesi_p", f32), ("agnesi_a", f32), ("f_radius_agnesi", i64),
+        ("zbl", i32), ("zbl_p", i32), ("zbl_a_exp", f32), ("zbl_a_prefactor", f32),
+        ("f_radius_zbl", i64), ("f_znum", i64),
         ("floats", C.POINTER(f32)), ("n_floats", i64),
         ("ints", C.POINTER(i32)), ("n_ints", i64),
     ]
@@ -123,9 +127,10 @@ EXPORTED = (
     "mace_ctx_workspace_bytes", "mace_nl_build", "mace_forward_backward", "mace_debug_buffer",
     "mace_last_launch_count", "mace_ctx_error_flag", "mace_profile_enable", "mace_profile_read",
     "mace_profile_timeline",
-    "mace_nl_build_noalloc",
+    "mace_nl_build_noalloc", "mace_fma_probe",
 )
 NOALLOC_MAX_ATOMS = 131072
+NOALLOC_MAX_GRAPH_ATOMS = 16384
 
 _lib = None
 
@@ -158,6 +163,7 @@ def load_library(path: str | Path | None = None) -> C.CDLL:
         "mace_ctx_error_flag": ([vp, C.POINTER(i32)], C.c_int),
         "mace_nl_build_noalloc": ([vp, vp, C.POINTER(i32), vp, i32, i64, C.c_double, vp, vp, vp, vp, vp,
                                   i64, C.POINTER(i64), vp], C.c_int),
+        "mace_fma_probe": ([vp, i32, i32, vp], C.c_int),
         "mace_profile_enable": ([vp, i32], C.c_int),
         "mace_profile_read": ([vp, i32, C.c_char_p, C.POINTER(i32), C.POINTER(i32), C.POINTER(C.c_double),
                                C.POINTER(i32)], C.c_int),

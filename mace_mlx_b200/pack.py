@@ -365,6 +365,9 @@ def _layer(spec: ModelSpec, lay: LayerSpec, w: dict, tb: _Tables) -> nv.LayerDes
         d.readout_hidden = i1.mul_out
         d.f_ro1 = tb.addf(w[f"readouts.{t}.linear_1.weights.0"].astype(np.float64) * i1.path_weight)
         d.f_ro2 = tb.addf(w[f"readouts.{t}.linear_2.weights.0"][:, 0].astype(np.float64) * i2.path_weight)
+    # density normalisation: density_fn = bias-free Linear(num_bessel -> 1), weight (1, num_bessel)
+    d.density = int(lay.density)
+    d.f_density = tb.addf(w[f"interactions.{t}.density_fn.weight"].reshape(-1)) if lay.density else -1
     return d
 
 
@@ -397,6 +400,21 @@ class PackedModel:
         d.f_sh = tb.addf(np.concatenate([sh_coupling(2).ravel(), sh_coupling(3).ravel()]))
         for t, lay in enumerate(spec.layers):
             d.layers[t] = _layer(spec, lay, weights, tb)
+        d.f_radius_agnesi = d.f_radius_zbl = d.f_znum = -1
+        if spec.agnesi is not None or spec.zbl is not None:
+            znum = spec.species_numbers()
+            d.f_znum = tb.addf(np.asarray(znum, dtype=np.float64))
+        if spec.agnesi is not None:
+            ag = spec.agnesi
+            d.agnesi = 1
+            d.agnesi_q, d.agnesi_p, d.agnesi_a = ag["q"], ag["p"], ag["a"]
+            d.f_radius_agnesi = tb.addf(np.asarray([ag["covalent_radii"][z] for z in znum], dtype=np.float64))
+        if spec.zbl is not None:
+            zb = spec.zbl
+            d.zbl = 1
+            d.zbl_p = zb["p"]
+            d.zbl_a_exp, d.zbl_a_prefactor = zb["a_exp"], zb["a_prefactor"]
+            d.f_radius_zbl = tb.addf(np.asarray([zb["covalent_radii"][z] for z in znum], dtype=np.float64))
         self.floats, self.ints = tb.arrays()
         d.floats = self.floats.ctypes.data_as(nv.C.POINTER(nv.f32))
         d.n_floats = self.floats.size

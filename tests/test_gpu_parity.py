@@ -74,6 +74,31 @@ def test_non_residual_first_layer_and_scale_shift():
     check(cfg, w, st)
 
 
+MPA = dict(use_density_normalization=True, distance_transform={}, pair_repulsion={})
+
+
+@pytest.mark.parametrize("nonres,scale_shift", [(True, True), (False, False)])
+def test_mpa_family_density_agnesi_zbl(nonres, scale_shift):
+    """Density-normalised blocks, the Agnesi transform and ZBL repulsion (the
+    mpa-0 family) on a LiPSO box with pairs inside the ZBL range, with stress."""
+    cfg = random_config("medium", z_table=[3, 8, 15, 16], avg_num_neighbors=50.0, first_interaction_nonresidual=nonres,
+                        atomic_energies=[-1.9, -4.9, -5.4, -4.1],
+                        model_type="ScaleShiftMACE" if scale_shift else "MACE", **MPA)
+    if scale_shift:
+        cfg["scale"], cfg["shift"] = 1.3, -0.2
+    w = random_weights(ModelSpec.from_config(cfg), 6)
+    m, gpu, ref, _ = check(cfg, w, lipso_box(300, 2))
+    pair = m.debug_buffer("e_layers").cpu().numpy().reshape(-1, len(gpu["forces"]))[-1]
+    assert np.abs(pair).max() > 1e-3  # the ZBL term is active in this structure
+
+
+def test_mpa_family_molecules_open_boundaries():
+    st = molecule_batch(6, 5)
+    cfg = random_config("medium", z_table=[1, 6, 7, 8], r_max=5.0, first_interaction_nonresidual=True, **MPA)
+    w = random_weights(ModelSpec.from_config(cfg), 8)
+    check(cfg, w, st, stress=False)
+
+
 @pytest.mark.parametrize("max_ell,corr", [(2, 3), (3, 2), (1, 1)])
 def test_other_lmax_and_correlation(max_ell, corr):
     cfg = random_config("medium", z_table=[14], avg_num_neighbors=40.0, max_ell=max_ell, correlation=corr)

@@ -49,6 +49,9 @@ def test_struct_layout_matches_header(tmp_path):
               ("ModelDesc", "mace_model_desc", "n_ints"), ("LayerDesc", "mace_layer_desc", "conv"),
               ("LayerDesc", "mace_layer_desc", "sc"), ("LayerDesc", "mace_layer_desc", "f_ro2"),
               ("LayerDesc", "mace_layer_desc", "mlp_w"), ("ScOut", "mace_sc_out", "f_G"),
+              ("LayerDesc", "mace_layer_desc", "density"), ("LayerDesc", "mace_layer_desc", "f_density"),
+              ("ModelDesc", "mace_model_desc", "agnesi"), ("ModelDesc", "mace_model_desc", "f_radius_agnesi"),
+              ("ModelDesc", "mace_model_desc", "zbl_a_prefactor"), ("ModelDesc", "mace_model_desc", "f_znum"),
               ("System", "mace_system", "rev")]
     src = ["#include <stdio.h>", "#include <stddef.h>", '#include "mace_b200.h"', "int main(void){"]
     for py, c in structs.items():
