@@ -217,6 +217,9 @@ typedef struct {
  * Return 0, or non-zero to abort the step (reported as MACE_ERR_NCCL).
  * Not used under MACE_USE_GRAPH.
  */
+/* In-library halo exchange over NCCL (see mace_halo_create); opaque. */
+typedef struct mace_halo mace_halo;
+
 #define MACE_HALO_FEATURES 0
 #define MACE_HALO_GRADIENTS 1
 typedef int (*mace_halo_fn)(void* user, int32_t phase, int32_t layer, float* rows, int64_t row_len, void* stream);
@@ -250,6 +253,18 @@ typedef struct {
   /* halo exchange between layers, or NULL (see mace_halo_fn) */
   mace_halo_fn halo;
   void* halo_user;
+  /* Receivers [0, n_active) are evaluated; 0 means all.  Nodes at and beyond
+   * n_active (ghost atoms of a domain decomposition) take part only as
+   * senders: no conv, product, readout or energy work is done for them, their
+   * energy weights must be 0, and the edges they receive (the suffix of the
+   * receiver-sorted list after row_ptr[n_active], which the caller passes as
+   * e_active) get no radial work. */
+  int64_t n_active;
+  int64_t e_active;
+  /* In-library halo exchange between layers (NCCL send/recv on the step's
+   * stream, capturable into the step's CUDA graph), or NULL.  Used instead of
+   * `halo` when set. */
+  mace_halo* halo_exchange;
 } mace_system;
 
 /* Device pointers receiving the results (NULL = not wanted). */
@@ -259,6 +274,31 @@ typedef struct {
   float* forces;                  /* (n_nodes, 3) = -dE/dpos              */
   double* virial;                 /* (9) sum_e v_e (x) dE/dv_e (un-symmetrised) */
 } mace_outputs;
+
+/*
+ * Halo exchange of a spatial domain decomposition inside the library (no
+ * reference counterpart: the reference runs on one device).  One object per
+ * rank; all ranks of the decomposition create theirs together:
+ *   mace_halo_unique_id   on one rank (128 bytes), shared with the others by the caller
+ *   mace_halo_create      on every rank (collective: NCCL communicator init)
+ *   mace_halo_plan        on every rank after each neighbour-list rebuild
+ *                         (allocates; not a hot call); per peer p in rank order:
+ *                         send_rows: the owned local rows p needs (send_counts[p]),
+ *                         recv_rows: the local ghost rows p fills (recv_counts[p]),
+ *                         in the order p sends them; row_cap: the longest row
+ *                         exchanged (floats, a multiple of 4)
+ *   mace_system.halo_exchange = the object, for every step
+ *   mace_halo_destroy
+ * Per step, after each layer but the last, the ghost rows of the node features
+ * are overwritten with their owners' rows; in the backward the ghost rows of
+ * the feature gradients are added onto their owners' rows (in a fixed order)
+ * and zeroed.  NCCL (libnccl.so.2) is loaded on first use.
+ */
+int mace_halo_unique_id(void* id_out, size_t len);
+int mace_halo_create(const void* id, size_t len, int32_t world, int32_t rank, int32_t device, mace_halo** out);
+int mace_halo_plan(mace_halo* h, int64_t n_owned, int64_t n_local, int64_t row_cap, const int64_t* send_counts,
+                   const int32_t* send_rows, const int64_t* recv_counts, const int32_t* recv_rows);
+int mace_halo_destroy(mace_halo* h);
 
 /* Message of the last failed call on this thread (always NUL-terminated). */
 int mace_last_error(char* buf, size_t len);

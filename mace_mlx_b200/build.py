@@ -24,6 +24,19 @@ FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
          "-Xptxas", "-O3", f"-I{INCLUDE}"]
 
 
+def _nccl_include() -> list[str]:
+    """nccl.h of the NCCL that torch ships (the library it dlopens at run time)."""
+    try:
+        import nvidia.nccl  # noqa: F401
+
+        d = Path(list(nvidia.nccl.__path__)[0]) / "include"
+        if (d / "nccl.h").exists():
+            return [f"-I{d}"]
+    except Exception:  # noqa: BLE001
+        pass
+    return []
+
+
 def _nvcc() -> str:
     cand = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
     if not Path(cand).exists():
@@ -44,7 +57,7 @@ def build(verbose: bool = False, extra_flags: list[str] | None = None) -> Path:
     out_dir.mkdir(exist_ok=True)
     sources = sorted(CSRC.glob("*.cu"))
     headers = sorted(CSRC.glob("*.cuh")) + sorted(INCLUDE.glob("*.h"))
-    flags = FLAGS + list(extra_flags or [])
+    flags = FLAGS + _nccl_include() + list(extra_flags or [])
     jobs = []
     for src in sources:
         obj = out_dir / (src.stem + ".o")
@@ -59,7 +72,7 @@ def build(verbose: bool = False, extra_flags: list[str] | None = None) -> Path:
     objs = [str(out_dir / (s.stem + ".o")) for s in sources]
     if jobs or not LIB.exists():
         tmp = LIB.with_suffix(".so.tmp")
-        cmd = [nvcc, *ARCH, "-shared", "-o", str(tmp), *objs, "-lcudart"]
+        cmd = [nvcc, *ARCH, "-shared", "-o", str(tmp), *objs, "-lcudart", "-ldl"]
         res = subprocess.run(cmd, capture_output=True, text=True)
         if res.returncode != 0:
             sys.stderr.write(res.stdout + res.stderr)

@@ -136,6 +136,11 @@ __device__ __forceinline__ float zbl_pair(float r, float zu, float zv, float rma
   return v;
 }
 
+// in-library halo exchange (halo.cu)
+int halo_features(mace_halo* h, float* rows, int64_t row_len, cudaStream_t s);
+int halo_gradients(mace_halo* h, float* rows, int64_t row_len, cudaStream_t s);
+int halo_version(const mace_halo* h);
+
 // per-node sums over each receiver's edges that need no learned features:
 // density of every density layer and the ZBL pair energy (forward), and the
 // density rescaling of the interaction message and its gradient
@@ -264,6 +269,7 @@ struct ConvParams {
   int need_dup;          // 0: the input gradient is not needed (first layer)
   const int32_t* rev;    // (E) reverse edge
   float* tq;             // (E, in_dim) per-edge sender-side terms, or null (then gathered from dA)
+  int64_t n_active;      // receivers >= n_active were not evaluated: their sender terms are skipped (0: all)
 };
 int launch_conv_fwd(const ConvParams& p, cudaStream_t s);
 // *need_gather: the kernel wrote per-edge sender-side terms to p.tq and

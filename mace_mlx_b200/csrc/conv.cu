@@ -344,6 +344,8 @@ namespace {
 // these are the contiguous rows of n's incoming edges.  A thread owns four
 // consecutive features (16-byte loads) and keeps eight rows of loads in
 // flight; eight partial sums over the rows in a fixed order (deterministic).
+// With p.n_active, the rows whose term would come from an inactive receiver
+// (the edge's sender is >= n_active) were never written and count as zero.
 __global__ void k_dup_gather(ConvParams p) {
   const int64_t n = p.n0 + blockIdx.x;
   const int64_t e0 = p.row_ptr[n], e1 = p.row_ptr[n + 1];
@@ -361,17 +363,21 @@ __global__ void k_dup_gather(ConvParams p) {
     a.z += v.z;
     a.w += v.w;
   };
+  const int32_t* snd = p.snd + e0;
+  const int64_t na = p.n_active;
+  auto live = [&](int jj) { return na == 0 || __ldg(snd + jj) < na; };
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
   int j = 0;
   for (; j + 8 <= ne; j += 8) {
     float4 v[8];
 #pragma unroll
-    for (int b = 0; b < 8; ++b) v[b] = __ldg(rows + (j + b) * pitch);
+    for (int b = 0; b < 8; ++b) v[b] = live(j + b) ? __ldg(rows + (j + b) * pitch) : zero;
 #pragma unroll
     for (int b = 0; b < 8; ++b) add(acc[b], v[b]);
   }
 #pragma unroll
   for (int b = 0; b < 8; ++b)
-    if (j + b < ne) add(acc[b], __ldg(rows + (j + b) * pitch));
+    if (j + b < ne && live(j + b)) add(acc[b], __ldg(rows + (j + b) * pitch));
 #pragma unroll
   for (int b = 1; b < 8; b += 2) add(acc[b - 1], acc[b]);
   add(acc[0], acc[2]);

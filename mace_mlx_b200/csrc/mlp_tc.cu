@@ -88,6 +88,7 @@ constexpr int F_NEPI = 8;                 // epilogue warps: quadrant q = warp &
 constexpr int F_NTHR = 32 * (F_NEPI + 1); // + control warp
 constexpr int F_TMEM = 256;               // [0, 128) accumulators, [128, 192) A hi, [192, 256) A lo
 constexpr uint32_t F_AHI = 128, F_ALO = 192;
+constexpr uint32_t F_HSMALL = 64;  // small-term accumulator of the hidden layers (chunk buffers 2, 3 meanwhile free)
 
 constexpr int F_NBS = 4;  // forward chunk-image stages
 struct FwdSmem {
@@ -103,7 +104,35 @@ struct FwdSmem {
 };
 static_assert(FwdSmem::TOTAL <= FwdSmem::REQUEST, "forward shared memory");
 
-// D (128 x N) = A (TMEM, 128 x 64, hi/lo) . B (N x 64, hi/lo)^T, issued by one thread
+// The tensor core does not round to nearest when it adds into an fp32
+// accumulator: every accumulation step can lose up to one unit in the last
+// place of the running sum, always in the same direction.  The two small
+// cross terms of the 3xTF32 product (hi.lo, lo.hi) therefore never go into
+// the running sum of the large hi.hi term: they get their own accumulator
+// (whose magnitude is 2^-11 of the large one, so its steps are harmless), or,
+// where no TMEM is free, they are issued first while the running sum is
+// still small; the two sums are added in fp32 on the CUDA cores.
+
+// D_big (+)= A_hi . B_hi^T and D_small (+)= A_hi . B_lo^T + A_lo . B_hi^T over K = 64
+// (D 128 x N, A in TMEM 128 x 64, B N x 64), issued by one thread
+template <int N>
+__device__ __forceinline__ void mma_k64_split(uint32_t d_big, uint32_t d_small, uint32_t a_hi, uint32_t a_lo,
+                                              uint32_t b_hi, uint32_t b_lo) {
+  constexpr uint32_t IDESC = tc::idesc_tf32(TM, N);
+#pragma unroll
+  for (int kb = 0; kb < H / 8; ++kb) {
+    const uint32_t ob = (kb >> 2) * (N * 128) + (kb & 3) * 32;
+    tc::mma_tf32_ta(d_small, a_hi + kb * 8, tc::sw128_desc(b_lo + ob), IDESC, kb > 0);
+    tc::mma_tf32_ta(d_small, a_lo + kb * 8, tc::sw128_desc(b_hi + ob), IDESC, 1);
+  }
+#pragma unroll
+  for (int kb = 0; kb < H / 8; ++kb) {
+    const uint32_t ob = (kb >> 2) * (N * 128) + (kb & 3) * 32;
+    tc::mma_tf32_ta(d_big, a_hi + kb * 8, tc::sw128_desc(b_hi + ob), IDESC, kb > 0);
+  }
+}
+
+// D (128 x N) = A . B^T in one accumulator, the small cross terms first
 template <int N>
 __device__ __forceinline__ void mma_k64_ta(uint32_t tmem_d, uint32_t a_hi, uint32_t a_lo, uint32_t b_hi,
                                            uint32_t b_lo) {
@@ -111,9 +140,13 @@ __device__ __forceinline__ void mma_k64_ta(uint32_t tmem_d, uint32_t a_hi, uint3
 #pragma unroll
   for (int kb = 0; kb < H / 8; ++kb) {
     const uint32_t ob = (kb >> 2) * (N * 128) + (kb & 3) * 32;
-    tc::mma_tf32_ta(tmem_d, a_hi + kb * 8, tc::sw128_desc(b_hi + ob), IDESC, kb > 0);
-    tc::mma_tf32_ta(tmem_d, a_hi + kb * 8, tc::sw128_desc(b_lo + ob), IDESC, 1);
+    tc::mma_tf32_ta(tmem_d, a_hi + kb * 8, tc::sw128_desc(b_lo + ob), IDESC, kb > 0);
     tc::mma_tf32_ta(tmem_d, a_lo + kb * 8, tc::sw128_desc(b_hi + ob), IDESC, 1);
+  }
+#pragma unroll
+  for (int kb = 0; kb < H / 8; ++kb) {
+    const uint32_t ob = (kb >> 2) * (N * 128) + (kb & 3) * 32;
+    tc::mma_tf32_ta(tmem_d, a_hi + kb * 8, tc::sw128_desc(b_hi + ob), IDESC, 1);
   }
 }
 
@@ -186,7 +219,7 @@ __global__ void __maxnreg__(96) k_mlp_fwd_tc(MlpParams p) {
         if (!wait(S::TL, (j - 1) & 1) || !wait(S::A, pa)) break;
         pa ^= 1;
         tc::fence_after_sync();
-        mma_k64_ta<H>(tmem, a_hi, a_lo, b_base, b_base + IMG * 2);
+        mma_k64_split<H>(tmem, tmem + F_HSMALL, a_hi, a_lo, b_base, b_base + IMG * 2);
         tc::mma_commit(BAR(S::ACC));
         if (!wait(S::ACC, (j - 1) & 1)) break;  // B is free again
         if (j + 1 < nh) copy_trunk(j);
@@ -279,6 +312,8 @@ __global__ void __maxnreg__(96) k_mlp_fwd_tc(MlpParams p) {
         tc::fence_after_sync();
         tc::tmem_ld32(tmem + lane_base + 32 * g, y);
         tc::tmem_wait_ld();
+        tc::tmem_ld16_add(tmem + lane_base + F_HSMALL + 32 * g, y);
+        tc::tmem_ld16_add(tmem + lane_base + F_HSMALL + 32 * g + 16, y + 16);
       }
     }
     // output chunks c = g, g + 2, ...: TMEM -> registers -> staging -> bulk store
@@ -324,10 +359,11 @@ __global__ void __maxnreg__(96) k_mlp_fwd_tc(MlpParams p) {
 // ---------------------------------------------------------------------------
 // backward
 // ---------------------------------------------------------------------------
-constexpr int B_NST = 3;  // copy stages of (dW chunk, weight chunk image)
-// TMEM: [0, 64) the dH accumulator; stage s's dW chunk as A at 64 + 64 s (hi) and
+constexpr int B_NST = 2;  // copy stages of (dW chunk, weight chunk image)
+// TMEM: [0, 64) the dH accumulator of the hi.hi products and [192, 256) that of
+// the small cross terms; stage s's dW chunk as A at 64 + 64 s (hi) and
 // 64 + 64 s + 32 (lo); the hidden layers' A (128 x 64) at [64, 128) hi, [128, 192) lo
-constexpr uint32_t B_ASTAGE = 64, B_TAHI = 64, B_TALO = 128;
+constexpr uint32_t B_ASTAGE = 64, B_TAHI = 64, B_TALO = 128, B_SMALL = 192;
 
 struct BwdSmem {
   // stage s at s * STAGE: the dW chunk (16 KB, bulk-copied in the 128-edge tile
@@ -411,9 +447,9 @@ __global__ void __maxnreg__(96) k_mlp_bwd_tc(MlpParams p) {
 #pragma unroll
         for (int kb = 0; kb < KC / 8; ++kb) {
           const uint32_t off = kb * 32;
+          tc::mma_tf32_ta(tmem + B_SMALL, ah + kb * 8, tc::sw128_desc(bl + off), IDESC, (kc > 0 || kb > 0));
+          tc::mma_tf32_ta(tmem + B_SMALL, al + kb * 8, tc::sw128_desc(bh + off), IDESC, 1);
           tc::mma_tf32_ta(tmem, ah + kb * 8, tc::sw128_desc(bh + off), IDESC, (kc > 0 || kb > 0));
-          tc::mma_tf32_ta(tmem, ah + kb * 8, tc::sw128_desc(bl + off), IDESC, 1);
-          tc::mma_tf32_ta(tmem, al + kb * 8, tc::sw128_desc(bh + off), IDESC, 1);
         }
         tc::mma_commit(BAR(S::MMA + s));
         // stage (kc - 1) % B_NST (smem and TMEM) is free once MMA(kc - 1) is done, which
@@ -433,7 +469,7 @@ __global__ void __maxnreg__(96) k_mlp_bwd_tc(MlpParams p) {
         pa ^= 1;
         ptl ^= 1;
         tc::fence_after_sync();
-        mma_k64_ta<H>(tmem, tmem + B_TAHI, tmem + B_TALO, base, base + IMG * 2);
+        mma_k64_split<H>(tmem, tmem + B_SMALL, tmem + B_TAHI, tmem + B_TALO, base, base + IMG * 2);
         tc::mma_commit(BAR(S::ACC));
         if (!wait(S::ACC, pacc)) break;  // the weight image is free again
         pacc ^= 1;
@@ -486,6 +522,8 @@ __global__ void __maxnreg__(96) k_mlp_bwd_tc(MlpParams p) {
       tc::fence_after_sync();
       tc::tmem_ld32(tmem + lane_base + 32 * g, dh);
       tc::tmem_wait_ld();
+      tc::tmem_ld16_add(tmem + lane_base + B_SMALL + 32 * g, dh);
+      tc::tmem_ld16_add(tmem + lane_base + B_SMALL + 32 * g + 16, dh + 16);
     }
     // hidden layers nh-1 .. 1 on the tensor cores, this group's 32 columns
     uint32_t pacc = 0;
@@ -519,6 +557,8 @@ __global__ void __maxnreg__(96) k_mlp_bwd_tc(MlpParams p) {
       tc::fence_after_sync();
       tc::tmem_ld32(tmem + lane_base + 32 * g, dh);
       tc::tmem_wait_ld();
+      tc::tmem_ld16_add(tmem + lane_base + B_SMALL + 32 * g, dh);
+      tc::tmem_ld16_add(tmem + lane_base + B_SMALL + 32 * g + 16, dh + 16);
     }
     // layer 0 on the CUDA cores: dL/db[i] = sum_o dh[o] SiLU'(a0[o]) W0[i][o], the
     // two column halves added through shared memory

@@ -149,6 +149,7 @@ struct mace_ctx {
   int g_flags = -1;
   std::vector<int64_t> g_chunks;  // chunk boundaries of the captured call (host arrays)
   int g_launches = 0;
+  int g_halo_version = 0;  // plan version of the captured step's halo exchange
   // profiling inside the graph: its event-record nodes fill the first g_prof_n slots
   bool g_prof = false;
   int g_prof_n = 0;
@@ -519,18 +520,22 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
   if (N > c->cap_nodes || E > c->cap_edges)
     return fail(MACE_ERR_BAD_ARG, "system larger than the reserved workspace (call mace_ctx_reserve)");
   if (N <= 0) return fail(MACE_ERR_BAD_ARG, "empty system");
+  // active receivers [0, NA) and their edges [0, EA); nodes beyond are senders only
+  const int64_t NA = (sys->n_active > 0 && sys->n_active < N) ? sys->n_active : N;
+  const int64_t EA = NA < N ? sys->e_active : E;
+  if (EA < 0 || EA > E) return fail(MACE_ERR_BAD_ARG, "e_active outside 0 .. n_edges");
   struct Chunk {
     int64_t n0, n1, e0, e1;
   };
   std::vector<Chunk> chunks;
   if (sys->n_chunks <= 1) {
-    chunks.push_back({0, N, 0, E});
+    chunks.push_back({0, NA, 0, EA});
   } else {
     if (!sys->chunk_nodes || !sys->chunk_edges) return fail(MACE_ERR_BAD_ARG, "chunks without boundary arrays");
     const int64_t* cn = sys->chunk_nodes;
     const int64_t* ce = sys->chunk_edges;
-    if (cn[0] != 0 || ce[0] != 0 || cn[sys->n_chunks] != N || ce[sys->n_chunks] != E)
-      return fail(MACE_ERR_BAD_ARG, "chunk boundaries must run from 0 to n_nodes / n_edges");
+    if (cn[0] != 0 || ce[0] != 0 || cn[sys->n_chunks] != NA || ce[sys->n_chunks] != EA)
+      return fail(MACE_ERR_BAD_ARG, "chunk boundaries must run from 0 to n_active / e_active (n_nodes / n_edges)");
     for (int k = 0; k < sys->n_chunks; ++k) {
       if (cn[k + 1] < cn[k] || ce[k + 1] < ce[k]) return fail(MACE_ERR_BAD_ARG, "chunk boundaries must not decrease");
       chunks.push_back({cn[k], cn[k + 1], ce[k], ce[k + 1]});
@@ -545,7 +550,7 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
   // stream forked from and joined back into `s` with events, so the
   // latency-bound node kernels overlap it (inside a captured graph the fork
   // and join become graph edges).
-  const bool fork = !recompute && E > 0 && !sys->halo && c->dw_layer[0] != nullptr && !c->single_stream;
+  const bool fork = !recompute && EA > 0 && !sys->halo && c->dw_layer[0] != nullptr && !c->single_stream;
   if (fork) {
     if (!c->aux) {
       // lowest priority: when both streams have CTAs waiting, the node/conv
@@ -614,6 +619,11 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
     ep.dD[ep.n_dens] = c->ddens + (int64_t)t * N;
     ++ep.n_dens;
   }
+  if (NA < N) {
+    // inactive rows are never written by the per-receiver kernels: zero what is read for them
+    MACE_CUDA_TRY(cudaMemsetAsync(c->e_layers, 0, sizeof(float) * (size_t)(T + 1) * N, s));
+    MACE_CUDA_TRY(cudaMemsetAsync(c->ddens, 0, sizeof(float) * (size_t)T * N, s));
+  }
   if (E > 0) LAUNCH("edge_fwd", -1, launch_edge_fwd(ep, s));
   if (ep.n_dens > 0 || d.zbl) {
     // per-receiver densities of the density-normalised layers and ZBL pair energies
@@ -649,7 +659,7 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
     MACE_CUDA_TRY(cudaEventRecord(ev[0], s));
     MACE_CUDA_TRY(cudaStreamWaitEvent(sa, ev[0], 0));
     for (int t = 0; t < T; ++t) {
-      MlpParams mp = mlp_params(c, t, 0, E);
+      MlpParams mp = mlp_params(c, t, 0, EA);
       LAUNCH_ON(sa, "mlp_fwd", t, launch_mlp_fwd(mp, sa));
       MACE_CUDA_TRY(cudaEventRecord(ev[1 + t], sa));
     }
@@ -698,6 +708,7 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
       lp.err_flag = c->d_err;
       lp.N = N;
       lp.C = C;
+      lp.N = NA;
       lp.in = B.A;
       lp.in_row = L.mid.dim;
       lp.out = B.msg;
@@ -713,19 +724,21 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
       LAUNCH("linear_msg", t, launch_linear(lp, s));
     }
     if (L.density)  // message / (density + 1) instead of / avg_num_neighbors
-      LAUNCH("density_scale", t, launch_density_scale(B.msg, L.inter.dim, c->dens + (int64_t)t * N, N, s));
+      LAUNCH("density_scale", t, launch_density_scale(B.msg, L.inter.dim, c->dens + (int64_t)t * N, NA, s));
     const float* sc_in = B.msg;
     if (!L.residual) {
-      SkipParams sp = skip_params(c, t, N, sys->species, false, L.inter, L.inter, B.msg, B.msg2, 0);
+      SkipParams sp = skip_params(c, t, NA, sys->species, false, L.inter, L.inter, B.msg, B.msg2, 0);
       MACE_CUDA_TRY(cudaMemsetAsync(B.msg2, 0, sizeof(float) * N * L.inter.dim, s));
       LAUNCH("skip_fwd", t, launch_skip(sp, s));
       sc_in = B.msg2;
     }
-    ScParams scp = sc_params(c, t, N, sys->species, sc_in, B.B, nullptr, nullptr);
+    ScParams scp = sc_params(c, t, NA, sys->species, sc_in, B.B, nullptr, nullptr);
     LAUNCH("sc_fwd", t, launch_sc_fwd(scp, s));
-    TRY(run_linear_slots(c, "linear_prod", t, N, L.hid, L.hid, L.f_prod, B.B, c->h[t + 1], 1, s));
+    TRY(run_linear_slots(c, "linear_prod", t, NA, L.hid, L.hid, L.f_prod, B.B, c->h[t + 1], 1, s));
+    if (NA < N)  // readout seeds exist for active rows only
+      MACE_CUDA_TRY(cudaMemsetAsync(c->dh[t + 1] + NA * L.hid.dim, 0, sizeof(float) * (N - NA) * L.hid.dim, s));
     ReadoutParams rp{};
-    rp.N = N;
+    rp.N = NA;
     rp.C = C;
     rp.h = c->h[t + 1];
     rp.h_row = L.hid.dim;
@@ -738,7 +751,9 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
     rp.dscale = dscale;
     rp.weight = sys->energy_weight;
     LAUNCH("readout", t, launch_readout(rp, s));
-    if (sys->halo && t + 1 < T) {
+    if (sys->halo_exchange && t + 1 < T) {
+      TRY(launch(c, "halo_features", t, s, [&]() { return halo_features(sys->halo_exchange, c->h[t + 1], L.hid.dim, s); }));
+    } else if (sys->halo && t + 1 < T) {
       if (sys->halo(sys->halo_user, MACE_HALO_FEATURES, t, c->h[t + 1], L.hid.dim, s) != 0)
         return fail(MACE_ERR_NCCL, "halo exchange of node features failed");
     }
@@ -780,29 +795,30 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
         MACE_CUDA_TRY(cudaEventRecord(ev[2 + 2 * T + t], s));
         MACE_CUDA_TRY(cudaStreamWaitEvent(sa, ev[2 + 2 * T + t], 0));
       }
-      SkipParams sp = skip_params(c, t, N, sys->species, true, L.in, L.hid, c->dh[t + 1], c->dh[t], 1);
+      SkipParams sp = skip_params(c, t, NA, sys->species, true, L.in, L.hid, c->dh[t + 1], c->dh[t], 1);
       LAUNCH_ON(sa, "skip_bwd", t, launch_skip(sp, sa));
       if (fork) MACE_CUDA_TRY(cudaEventRecord(ev[2 + 3 * T + t], sa));
     }
-    TRY(run_linear_slots(c, "linear_prod_bwd", t, N, L.hid, L.hid, L.f_prod_t, c->dh[t + 1], B.dB, 0, s));
+    TRY(run_linear_slots(c, "linear_prod_bwd", t, NA, L.hid, L.hid, L.f_prod_t, c->dh[t + 1], B.dB, 0, s));
     float* dsc_in = B.dmsg;
-    ScParams scp = sc_params(c, t, N, sys->species, L.residual ? B.msg : B.msg2, nullptr, B.dB,
+    ScParams scp = sc_params(c, t, NA, sys->species, L.residual ? B.msg : B.msg2, nullptr, B.dB,
                              L.residual ? B.dmsg : B.dmsg2);
     LAUNCH("sc_bwd", t, launch_sc_bwd(scp, s));
     if (!L.residual) {
       MACE_CUDA_TRY(cudaMemsetAsync(B.dmsg, 0, sizeof(float) * N * L.inter.dim, s));
-      SkipParams sp = skip_params(c, t, N, sys->species, true, L.inter, L.inter, B.dmsg2, B.dmsg, 1);
+      SkipParams sp = skip_params(c, t, NA, sys->species, true, L.inter, L.inter, B.dmsg2, B.dmsg, 1);
       LAUNCH("skip_bwd", t, launch_skip(sp, s));
     }
     if (L.density)  // through message = linear(A) / (D + 1): dD, and dmsg / (D + 1)
       LAUNCH("density_bwd", t, launch_density_bwd(B.msg, B.dmsg, L.inter.dim, c->dens + (int64_t)t * N,
-                                                  c->ddens + (int64_t)t * N, N, s));
+                                                  c->ddens + (int64_t)t * N, NA, s));
     {
       // dA[mid slot k] = inv_avg * dmsg[inter slot l_k] @ W_l^T (block q of the concat-K)
       LinParams lp{};
       lp.err_flag = c->d_err;
       lp.N = N;
       lp.C = C;
+      lp.N = NA;
       lp.in = dsc_in;
       lp.in_row = L.inter.dim;
       lp.out = B.dA;
@@ -817,6 +833,8 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
         }
       }
       LAUNCH("linear_msg_bwd", t, launch_linear(lp, s));
+      if (NA < N)  // receivers beyond n_active carry no gradient
+        MACE_CUDA_TRY(cudaMemsetAsync(B.dA + NA * L.mid.dim, 0, sizeof(float) * (N - NA) * L.mid.dim, s));
     }
     bool need_gather = false;
     for (const Chunk& ch : chunks) {
@@ -827,7 +845,11 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
       cp.n0 = ch.n0;
       cp.e0 = ch.e0;
       bool gather = false;
+      cp.n_active = NA < N ? NA : 0;
       LAUNCH("conv_bwd", t, launch_conv_bwd(cp, s, &gather));
+      if (NA < N && t > 0 && !gather)
+        return fail(MACE_ERR_UNSUPPORTED, "n_active needs the per-edge sender terms of the conv backward (one radial "
+                                          "chunk and a layer signature of conv_sig.cu)");
       need_gather = need_gather || gather;
       if (fork) {
         MACE_CUDA_TRY(cudaEventRecord(ev[1 + T + t], s));
@@ -840,6 +862,7 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
     if (need_gather) {
       // the sender-side terms of every chunk's edges are in place: sum them per node
       ConvParams cp = conv_params(c, t, N, sys);
+      cp.n_active = NA < N ? NA : 0;
       LAUNCH("dup_gather", t, launch_dup_gather(cp, s));
     }
     if (t > 0) {
@@ -847,8 +870,12 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
       if (early_skip && fork) MACE_CUDA_TRY(cudaStreamWaitEvent(s, ev[2 + 3 * T + t], 0));
       TRY(run_linear_slots(c, "linear_up_bwd", t, N, L.in, L.in, L.f_up_t, B.dup, c->dh[t], 1, s));
       // dh[t]: gradient w.r.t. the features layer t - 1 produced
-      if (sys->halo && sys->halo(sys->halo_user, MACE_HALO_GRADIENTS, t - 1, c->dh[t], L.in.dim, s) != 0)
+      if (sys->halo_exchange) {
+        TRY(launch(c, "halo_gradients", t - 1, s,
+                   [&]() { return halo_gradients(sys->halo_exchange, c->dh[t], L.in.dim, s); }));
+      } else if (sys->halo && sys->halo(sys->halo_user, MACE_HALO_GRADIENTS, t - 1, c->dh[t], L.in.dim, s) != 0) {
         return fail(MACE_ERR_NCCL, "halo reduction of feature gradients failed");
+      }
     }
   }
   if (fork) {  // join: every MLP backward has accumulated into db
@@ -1217,7 +1244,8 @@ int mace_forward_backward(mace_ctx* c, const mace_system* sys, const mace_output
   if (c->prof_on) TRY(prof_fold(c));  // the previous replay's events
   const bool same = c->gexec && c->g_flags == base_flags && c->g_prof == c->prof_on &&
                     std::memcmp(&c->g_sys, sys, sizeof(mace_system)) == 0 &&
-                    std::memcmp(&c->g_out, &o, sizeof(mace_outputs)) == 0 && c->g_chunks == chunk_key;
+                    std::memcmp(&c->g_out, &o, sizeof(mace_outputs)) == 0 && c->g_chunks == chunk_key &&
+                    c->g_halo_version == halo_version(sys->halo_exchange);
   if (!same) {
     if (c->gexec) {
       MACE_CUDA_TRY(cudaGraphExecDestroy(c->gexec));
@@ -1253,6 +1281,7 @@ int mace_forward_backward(mace_ctx* c, const mace_system* sys, const mace_output
     c->g_prof_n = c->prof_n;
     c->g_chunks = chunk_key;
     c->g_launches = c->launches;
+    c->g_halo_version = halo_version(sys->halo_exchange);
   }
   MACE_CUDA_TRY(cudaGraphLaunch(c->gexec, s));
   c->launches = c->g_launches;

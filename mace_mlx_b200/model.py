@@ -201,7 +201,7 @@ class MACEModel:
     def evaluate(self, pos: torch.Tensor, cell: torch.Tensor | None, species: torch.Tensor,
                  graph_ptr: torch.Tensor, edges: EdgeSet, *, forces: bool = True, virial: bool = False,
                  out: dict | None = None, graph: bool = False, energy_weight: torch.Tensor | None = None,
-                 halo=None) -> dict:
+                 halo=None, halo_exchange=None, active: tuple[int, int] | None = None) -> dict:
         """Energy per graph (float64), node energies, forces and the raw virial.
 
         All inputs are device tensors: pos (N,3) float32, cell (3,3) float32 or
@@ -215,6 +215,10 @@ class MACEModel:
         ``halo(phase, layer, rows)`` is called between layers with the (N, row)
         node-feature (phase 0) or feature-gradient (phase 1) rows, on the step's
         stream (domain decomposition; see mace_halo_fn in include/mace_b200.h).
+        ``halo_exchange`` (a ``distributed.NativeHaloExchange``) does the same
+        inside the library, graph replay included.  ``active = (n, e)`` makes
+        nodes [0, n) the only receivers (their edges are [0, e)); later nodes
+        are senders only (ghost atoms, energy weight 0).
         """
         N = pos.shape[0]
         E = edges.n_edges
@@ -232,6 +236,12 @@ class MACEModel:
             species=species.data_ptr(), graph_ptr=graph_ptr.data_ptr(), sender=edges.sender.data_ptr(),
             receiver=edges.receiver.data_ptr(), shifts=edges.shifts.data_ptr(), row_ptr=edges.row_ptr.data_ptr(),
             rev=edges.rev.data_ptr(), energy_weight=_ptr(energy_weight))
+        if active is not None and E <= self.max_chunk_edges:
+            # (a list split into radial chunks keeps every receiver: the per-edge
+            # sender terms that inactive receivers rely on need a one-chunk list)
+            sysd.n_active, sysd.e_active = int(active[0]), int(active[1])
+        if halo_exchange is not None:
+            sysd.halo_exchange = halo_exchange.handle
         if halo is not None:
             dev = self.device
 

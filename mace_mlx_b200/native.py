@@ -108,6 +108,7 @@ class System(C.Structure):
         ("shifts", C.c_void_p), ("row_ptr", C.c_void_p), ("rev", C.c_void_p),
         ("energy_weight", C.c_void_p), ("n_chunks", i32), ("chunk_nodes", C.c_void_p),
         ("chunk_edges", C.c_void_p), ("halo", C.c_void_p), ("halo_user", C.c_void_p),
+        ("n_active", i64), ("e_active", i64), ("halo_exchange", C.c_void_p),
     ]
 
 
@@ -128,6 +129,7 @@ EXPORTED = (
     "mace_last_launch_count", "mace_ctx_error_flag", "mace_profile_enable", "mace_profile_read",
     "mace_profile_timeline",
     "mace_nl_build_noalloc", "mace_fma_probe",
+    "mace_halo_unique_id", "mace_halo_create", "mace_halo_plan", "mace_halo_destroy",
 )
 NOALLOC_MAX_ATOMS = 131072
 NOALLOC_MAX_GRAPH_ATOMS = 16384
@@ -164,6 +166,10 @@ def load_library(path: str | Path | None = None) -> C.CDLL:
         "mace_nl_build_noalloc": ([vp, vp, C.POINTER(i32), vp, i32, i64, C.c_double, vp, vp, vp, vp, vp,
                                   i64, C.POINTER(i64), vp], C.c_int),
         "mace_fma_probe": ([vp, i32, i32, vp], C.c_int),
+        "mace_halo_unique_id": ([vp, C.c_size_t], C.c_int),
+        "mace_halo_create": ([vp, C.c_size_t, i32, i32, i32, C.POINTER(vp)], C.c_int),
+        "mace_halo_plan": ([vp, i64, i64, i64, vp, vp, vp, vp], C.c_int),
+        "mace_halo_destroy": ([vp], C.c_int),
         "mace_profile_enable": ([vp, i32], C.c_int),
         "mace_profile_read": ([vp, i32, C.c_char_p, C.POINTER(i32), C.POINTER(i32), C.POINTER(C.c_double),
                                C.POINTER(i32)], C.c_int),

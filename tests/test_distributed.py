@@ -156,7 +156,7 @@ def _halo_rank(rank, world, port, path, pos, cell):
 
         grid = grid_for(world)
         plan = plan_domain(pos, cell, grid, rank, 3.5)
-        hx = HaloExchange(plan, domain_of(pos, cell, grid), world, "cpu")
+        hx = HaloExchange.from_plan(plan, domain_of(pos, cell, grid), world, "cpu")
         gid = torch.as_tensor(plan.local_index, dtype=torch.float64)
         rows = torch.stack([gid, 2 * gid + 1, -gid], dim=1)
         rows[plan.n_owned:] = -7.0

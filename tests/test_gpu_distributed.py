@@ -1,7 +1,11 @@
-"""Spatial domain decomposition on two GPUs (NCCL) against one GPU on the whole cell.
+"""Spatial domain decomposition on two GPUs against one GPU on the whole cell.
 
 Runs only where two GPUs are visible; the CPU suite covers the same host logic
-with gloo ranks and the float64 oracle (test_distributed.py).
+with gloo ranks and the float64 oracle (test_distributed.py).  Three modes:
+the library's own halo exchange (NCCL send/recv inside the step, owned atoms
+the only receivers, the step replayed as a CUDA graph, positions and forces
+moved halo-sized per step), the host-callback halo with torch collectives,
+and the 2 r_max ghost shell without exchange between layers.
 """
 
 import os
@@ -27,16 +31,7 @@ def _case():
     return st, config, weights
 
 
-def _run(model, st, world, rank, halo=True):
-    runner = SpatialRunner(model, st.numbers, st.cell, world, rank, skin=0.5, halo=halo)
-    pos = torch.tensor(st.positions, dtype=torch.float64, device=model.device)
-    out = runner.evaluate(pos, virial=True)
-    res = runner.reduce(out, len(st), virial=True)
-    torch.cuda.synchronize(model.device)
-    return {k: v.cpu().numpy().astype(np.float64) for k, v in res.items()}, runner.plan
-
-
-def _rank_main(rank, world, port, path, halo):
+def _rank_main(rank, world, port, path, mode):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     torch.cuda.set_device(rank)
@@ -44,29 +39,51 @@ def _rank_main(rank, world, port, path, halo):
     try:
         st, config, weights = _case()
         model = MACEModel(config=config, weights=weights, device=rank)
-        res, plan = _run(model, st, world, rank, halo)
+        runner = SpatialRunner(model, st.numbers, st.cell, world, rank, skin=0.5, halo=mode != "shell",
+                               native=mode == "native")
+        runner.graph = mode == "native"
+        pos = torch.tensor(st.positions, dtype=torch.float64, device=model.device)
+        out = runner.evaluate(pos, virial=True)
+        res = runner.reduce(out, len(st), virial=True)
+        res = {k: v.cpu().numpy().astype(np.float64) for k, v in res.items()}
+        # the halo-sized step path, twice (the second replays the captured graph)
+        own = pos[torch.as_tensor(runner.owned_index, device=pos.device)]
+        for _ in range(2):
+            step = runner.step(own, virial=True)
+        f_all = [None] * world
+        torch.distributed.all_gather_object(f_all, (runner.owned_index, step["forces"].cpu().numpy()))
+        forces = np.zeros((len(st), 3))
+        for idx, f in f_all:
+            forces[idx] = f
         if rank == 0:
-            np.savez(path, n_local=plan.n_local, n_owned=plan.n_owned, **res)
+            np.savez(path, n_local=runner.plan.n_local, n_owned=runner.plan.n_owned, step_forces=forces,
+                     step_energy=step["energy"].cpu().numpy(), step_virial=step["virial"].cpu().numpy(), **res)
         torch.distributed.barrier()
+        runner.close()
     finally:
         torch.distributed.destroy_process_group()
 
 
-@pytest.mark.parametrize("halo", [True, False])
-def test_two_gpu_domains_match_one_gpu(halo):
-    """halo: r_max ghost shell with layer features exchanged over NCCL; else a 2 r_max shell."""
+@pytest.mark.parametrize("mode", ["native", "callback", "shell"])
+def test_two_gpu_domains_match_one_gpu(mode):
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
     with tempfile.TemporaryDirectory() as tmp:
         path = os.path.join(tmp, "rank0.npz")
-        torch.multiprocessing.spawn(_rank_main, args=(2, port, path, halo), nprocs=2, join=True)
+        torch.multiprocessing.spawn(_rank_main, args=(2, port, path, mode), nprocs=2, join=True)
         got = dict(np.load(path))
     st, config, weights = _case()
-    ref, _ = _run(MACEModel(config=config, weights=weights, device=0), st, 1, 0)
+    model = MACEModel(config=config, weights=weights, device=0)
+    runner = SpatialRunner(model, st.numbers, st.cell, 1, 0)
+    ref = runner.reduce(runner.evaluate(torch.tensor(st.positions, dtype=torch.float64, device=model.device),
+                                        virial=True), len(st), virial=True)
+    ref = {k: v.cpu().numpy().astype(np.float64) for k, v in ref.items()}
     assert got["n_owned"] < got["n_local"]
     n = len(st)
-    assert abs(got["energy"][0] - ref["energy"][0]) / n < 1e-6
     scale = np.abs(ref["forces"]).max()
-    np.testing.assert_allclose(got["forces"], ref["forces"], atol=1e-4 * max(scale, 1e-3))
-    np.testing.assert_allclose(got["virial"], ref["virial"], atol=1e-5 * np.abs(ref["virial"]).max())
+    for e, f, v in ((got["energy"], got["forces"], got["virial"]),
+                    (got["step_energy"], got["step_forces"], got["step_virial"])):
+        assert abs(e[0] - ref["energy"][0]) / n < 1e-6
+        np.testing.assert_allclose(f, ref["forces"], atol=1e-4 * max(scale, 1e-3))
+        np.testing.assert_allclose(v, ref["virial"], atol=1e-5 * np.abs(ref["virial"]).max())
