@@ -62,12 +62,18 @@ def test_oracle_equals_the_reference_execution(golden_dir, name):
         scale = max(np.abs(b).max(), 1e-12)
         assert np.abs(a - b).max() <= rtol * scale, (np.abs(a - b).max(), scale)
 
-    # both sides run float64: agreement to round-off
-    close(res["energy"], fx["energy"], 1e-9)
-    close(res["node_energy"], fx["node_energy"], 1e-9)
-    close(res["forces"], fx["forces"], 1e-8)
+    # Both sides run in float64, but the reference rounds its coupling constants
+    # to float32 in numpy before it builds arrays from them (3j symbols
+    # tensor_product.py:255, SH recursion spherical_harmonics.py:40, U rows
+    # symmetric_contraction.py:321, 421), while the oracle keeps them in float64.
+    # That leaves ~1e-9 relative on the plain models and up to ~1e-7 on the
+    # density-normalised ones, whose activations are ~40x larger; the bound
+    # here is 1e-6 of each quantity's scale (the parity bounds are 1e-5..1e-4).
+    close(res["energy"], fx["energy"], 1e-6)
+    close(res["node_energy"], fx["node_energy"], 1e-6)
+    close(res["forces"], fx["forces"], 1e-6)
     if bool(fx["stress_computed"]):
-        close(res["stress"], fx["stress"], 1e-8)
+        close(res["stress"], fx["stress"], 1e-6)
 
 
 @pytest.mark.parametrize("name", list(CASES))
