@@ -16,8 +16,14 @@ through the public calculator API (host positions in, host forces out);
 ``roofline`` is the dominant kernel's algorithmic work over its event-timed
 launch duration; ``cpu_baseline`` times the CPU oracle port on this host.
 
-With N > 1 (torchrun), every rank evaluates its own independent Si1000
-structure (structure sharding, no data-path collective): weak scaling.
+With N > 1 (torchrun), the ranks evaluate ONE periodic diamond-Si structure
+of N Si1000 blocks (5x5x5 conventional cells per rank), spatially decomposed
+on the domain grid 1x1x2 / 1x2x2 / 2x2x2: each rank owns one block, holds
+r_max + skin ghost shells, computes its owned atoms' edges only, and the
+layer-1 input features of the ghosts and their gradients cross the ranks
+inside the step (the library's NCCL halo exchange), with ghost positions
+and forces moved per step: weak scaling with the halo exchange on the data
+path.
 
 ``--impl reference`` times the reference algorithm's CPU restatement (the
 reference itself runs on MLX/Metal, absent here) on the host cores, rank 0 only.
@@ -504,6 +510,120 @@ def b200_arm(args, rank: int, world: int, local_rank: int):
     return 0
 
 
+def spatial_weak_arm(args, rank: int, world: int, local_rank: int):
+    """N Si1000 blocks as one periodic structure, one block per rank (see the module docstring)."""
+    import torch
+    import torch.distributed as dist
+
+    from mace_mlx_b200.distributed import SpatialRunner, grid_for
+    from mace_mlx_b200.model import MACEModel
+    from mace_mlx_b200.spec import ModelSpec
+    from mace_mlx_b200.structures import diamond_si
+    from mace_mlx_b200.weights import random_config, random_weights
+    from mace_mlx_b200.workmodel import kernel_work
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    grid = grid_for(world)
+    st = diamond_si(tuple(5 * g for g in grid), 0.05, 1)
+    config = random_config("medium", z_table=list(range(1, 90)), avg_num_neighbors=AVG_NUM_NEIGHBORS)
+    model = MACEModel(config=config, weights=random_weights(ModelSpec.from_config(config), seed=1), device=dev)
+    runner = SpatialRunner(model, st.numbers, st.cell, world, rank, skin=0.5)
+    runner.graph = True
+    pos_global = torch.tensor(st.positions, dtype=torch.float64, device=dev)
+    runner.evaluate(pos_global)
+    own_idx = torch.as_tensor(runner.owned_index, device=dev)
+    own_pos = pos_global[own_idx].clone()
+    n_total = len(st)
+    pl = runner.plan
+
+    def barrier():
+        dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    def step():
+        return runner.step(own_pos, check_skin=False)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    barrier()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with ClockSampler(local_rank) as clk:
+        barrier()
+        for k in range(args.steps):
+            ev[k][0].record()
+            step()
+            ev[k][1].record()
+        barrier()
+    total_ms = float(sum(a.elapsed_time(b) for a, b in ev))
+    launches = model.last_launch_count()
+    # e2e: host owned positions in (pinned), the skin check, forces and energy back to the host
+    host_pos = torch.empty(own_pos.shape, dtype=torch.float64, pin_memory=True)
+    host_pos.copy_(own_pos)
+    host_f = torch.empty(own_pos.shape, dtype=torch.float32, pin_memory=True)
+    host_e = torch.empty(1, dtype=torch.float64, pin_memory=True)
+
+    def step_e2e():
+        own_pos.copy_(host_pos, non_blocking=True)
+        res = runner.step(own_pos)
+        host_f.copy_(res["forces"], non_blocking=True)
+        host_e.copy_(res["energy"], non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()
+        return float(host_e[0])
+
+    for _ in range(max(1, args.warmup // 2)):
+        step_e2e()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step_e2e()
+    barrier()
+    e2e_s = time.perf_counter() - t0
+    model.profile_enable(True)
+    prof_steps = min(args.steps, 5)
+    for _ in range(prof_steps):
+        step()
+    torch.cuda.synchronize(dev)
+    prof = model.profile_read()
+    model.profile_enable(False)
+    fp32 = measure_fp32_peak(dev)
+    tt = torch.tensor([total_ms, e2e_s], dtype=torch.float64, device=dev)
+    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    total_ms, e2e_s = float(tt[0]), float(tt[1])
+    counts = torch.tensor([pl.n_owned, pl.n_local], dtype=torch.int64, device=dev)
+    all_counts = [torch.empty_like(counts) for _ in range(world)]
+    dist.all_gather(all_counts, counts)
+    runner.close()
+    if rank != 0:
+        return 0
+    e_act = runner.active[1] if runner.active else runner.edges.n_edges
+    roof = roofline_of(kernel_work(model.spec, pl.n_owned, e_act), prof, prof_steps, fp32)
+    line = {
+        "metric": METRIC, "value": n_total * args.steps / (total_ms / 1e3), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": (f"medium MACE as config 1 (seed 1); one periodic diamond Si structure of "
+                                f"{world} Si1000 blocks ({5 * grid[0]}x{5 * grid[1]}x{5 * grid[2]} cells, "
+                                f"{n_total} atoms, rattled 0.05 A, seed 1); energy+forces"),
+                   "n_atoms_total": n_total,
+                   "owned_local_atoms_per_rank": [[int(c[0]), int(c[1])] for c in all_counts],
+                   "parallelism": (f"spatial domains {grid[0]}x{grid[1]}x{grid[2]}, r_max+skin ghost shells, owned "
+                                   "atoms the only receivers, layer-1 features and their gradients halo-exchanged "
+                                   "in the step (NCCL send/recv issued by the library, step replayed as a CUDA "
+                                   "graph), ghost positions/forces exchanged per step, energy all-reduced"),
+                   "l2": "inputs per rank below L2; no flush (a flush would serialise the ranks' NCCL traffic)"},
+        "e2e": {"value": n_total * args.steps / e2e_s, "unit": UNIT,
+                "h2d_bytes_per_step": int(own_pos.numel() * 8), "d2h_bytes_per_step": int(own_pos.numel() * 4 + 8),
+                "ms_per_step": e2e_s * 1e3 / args.steps},
+        "gpu_launches": launches * args.steps,
+        "clocks": clk.summary(),
+        "roofline": roof,
+        "cpu_baseline": None,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 # ---------------------------------------------------------------------------
 # partitioned configurations: c3 (structure sharding), c4 (spatial domains)
 # ---------------------------------------------------------------------------
@@ -512,16 +632,17 @@ C3_WORKLOAD = ("config3: MACE-OFF-medium-like (96x0e+96x1o, lmax3, corr3, 2 laye
                "sharded over the ranks by atom count")
 C4_WORKLOAD = ("config4: medium MACE as config 1 (seed 1); diamond Si 50x50x50 = 1,000,000 atoms rattled 0.05 A "
                "(seed 4); energy+forces+stress; spatial domains (grid 1x1x2, 1x2x2, 2x2x2) periodic along unsplit "
-               "axes, r_max + skin = 6.5 A ghost shells across split axes; layer-1 node features halo-exchanged and "
-               "their gradients halo-reduced (NCCL all-to-all); positions all-gathered, forces/energy/virial "
-               "all-reduced")
+               "axes, r_max + skin = 6.5 A ghost shells across split axes, owned atoms the only receivers; layer-1 "
+               "node features and their gradients halo-exchanged inside the step (library NCCL send/recv, step "
+               "replayed as a CUDA graph); ghost positions and forces exchanged per step (halo-sized), "
+               "energy/virial all-reduced")
 
 
 def partition_arm(args, rank: int, world: int, local_rank: int):
     import torch
     import torch.distributed as dist
 
-    from mace_mlx_b200.distributed import PositionExchange, SpatialRunner, plan_domain, shard_structures
+    from mace_mlx_b200.distributed import SpatialRunner, shard_structures
     from mace_mlx_b200.model import MACEModel
     from mace_mlx_b200.spec import ModelSpec
     from mace_mlx_b200.structures import diamond_si, molecule_batch
@@ -541,37 +662,33 @@ def partition_arm(args, rank: int, world: int, local_rank: int):
         config = random_config("medium", z_table=list(range(1, 90)), avg_num_neighbors=AVG_NUM_NEIGHBORS)
         model = MACEModel(config=config, weights=random_weights(ModelSpec.from_config(config), seed=1), device=dev)
         runner = SpatialRunner(model, st.numbers, st.cell, world, rank, skin=0.5)
+        runner.graph = True
         pos_global = torch.tensor(st.positions, dtype=torch.float64, device=dev)
         n_total = len(st)
         virial = True
         runner.evaluate(pos_global, virial=True)
-        owned = [plan_domain(st.positions, st.cell, runner.grid, r, runner.ghost_width).owned_index
-                 for r in range(world)] if world > 1 else [np.arange(n_total)]
-        exch = PositionExchange(owned, dev) if world > 1 else None
-        own_idx = torch.as_tensor(owned[rank], device=dev)
+        own_idx = torch.as_tensor(runner.owned_index, device=dev)
         own_pos = pos_global[own_idx].clone()
+        owned = {rank: runner.owned_index}
+        del pos_global
 
         def step():
-            if exch is not None:
-                exch(own_pos, pos_global)
-            out = runner.evaluate(pos_global, virial=True)
-            return runner.reduce(out, n_total, virial=True)
+            return runner.step(own_pos, virial=True, check_skin=False)
 
-        host_pos = torch.empty(len(owned[rank]), 3, dtype=torch.float64, pin_memory=True)
+        host_pos = torch.empty(own_pos.shape, dtype=torch.float64, pin_memory=True)
         host_pos.copy_(own_pos)
-        host_f = torch.empty(len(owned[rank]), 3, dtype=torch.float32, pin_memory=True)
+        host_f = torch.empty(own_pos.shape, dtype=torch.float32, pin_memory=True)
 
         def step_e2e():
             own_pos.copy_(host_pos, non_blocking=True)
-            if exch is None:
-                pos_global.copy_(own_pos)
-            res = step()
-            host_f.copy_(res["forces"][own_idx], non_blocking=True)
+            res = runner.step(own_pos, virial=True)
+            host_f.copy_(res["forces"], non_blocking=True)
             e = res["energy"].item()  # synchronises
             return e
 
         h2d, d2h = len(owned[rank]) * 24, len(owned[rank]) * 12 + 8
-        n_local, e_local = runner.plan.n_local, runner.edges.n_edges
+        n_local = runner.plan.n_owned if runner.active else runner.plan.n_local
+        e_local = runner.active[1] if runner.active else runner.edges.n_edges
         workload, scaling = C4_WORKLOAD, "strong"
         parallel = f"spatial domains {runner.grid[0]}x{runner.grid[1]}x{runner.grid[2]}"
         prof_model, prof_n, prof_e = model, n_local, e_local
@@ -701,6 +818,8 @@ def main():
     try:
         if args.config in ("c3", "c4"):
             return partition_arm(args, rank, world, local_rank)
+        if world > 1 and args.config == "c1":
+            return spatial_weak_arm(args, rank, world, local_rank)
         return b200_arm(args, rank, world, local_rank)
     finally:
         if world > 1:

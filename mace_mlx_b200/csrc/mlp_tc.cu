@@ -360,10 +360,13 @@ __global__ void __maxnreg__(96) k_mlp_fwd_tc(MlpParams p) {
 // backward
 // ---------------------------------------------------------------------------
 constexpr int B_NST = 2;  // copy stages of (dW chunk, weight chunk image)
-// TMEM: [0, 64) the dH accumulator of the hi.hi products and [192, 256) that of
-// the small cross terms; stage s's dW chunk as A at 64 + 64 s (hi) and
-// 64 + 64 s + 32 (lo); the hidden layers' A (128 x 64) at [64, 128) hi, [128, 192) lo
+constexpr int B_GROUP = 2;  // K chunks per dH partial sum (drained to fp32 registers, see below)
+// TMEM: the dH partial sums of even / odd chunk groups at [0, 64) / [192, 256);
+// stage s's dW chunk as A at 64 + 64 s (hi) and 64 + 64 s + 32 (lo); after the
+// K loop the hidden layers' A (128 x 64) at [64, 128) hi, [128, 192) lo, their
+// hi.hi accumulator at [0, 64) and small-term accumulator at [192, 256)
 constexpr uint32_t B_ASTAGE = 64, B_TAHI = 64, B_TALO = 128, B_SMALL = 192;
+__device__ __forceinline__ uint32_t b_part(int group) { return (group & 1) ? B_SMALL : 0u; }
 
 struct BwdSmem {
   // stage s at s * STAGE: the dW chunk (16 KB, bulk-copied in the 128-edge tile
@@ -375,7 +378,7 @@ struct BwdSmem {
   static constexpr int BARS = W0 + 4096;
   static constexpr int TOTAL = BARS + 256;
   static constexpr int REQUEST = 112 * 1024;     // two CTAs per SM (256 TMEM columns each)
-  static constexpr int LD = 0, SPLIT = 3, MMA = 6, TL = 9, A = 10, ACC = 11, NBARS = 12;
+  static constexpr int LD = 0, SPLIT = 3, MMA = 6, TL = 9, A = 10, ACC = 11, DRAIN = 12, NBARS = 14;
 };
 static_assert(BwdSmem::TOTAL <= BwdSmem::REQUEST, "backward shared memory");
 
@@ -410,7 +413,7 @@ __global__ void __maxnreg__(96) k_mlp_bwd_tc(MlpParams p) {
   }
   if (t == 0) {
     for (int i = 0; i < S::NBARS; ++i) {
-      const bool by_warps = (i >= S::SPLIT && i < S::SPLIT + B_NST) || i == S::A;
+      const bool by_warps = (i >= S::SPLIT && i < S::SPLIT + B_NST) || i == S::A || i >= S::DRAIN;
       tc::mbar_init(BAR(i), by_warps ? F_NEPI : 1);
     }
     *abort_flag = 0;
@@ -440,16 +443,26 @@ __global__ void __maxnreg__(96) k_mlp_bwd_tc(MlpParams p) {
       for (int k = 0; k < B_NST && k < nch; ++k) copy_chunk(k);
       for (int kc = 0; kc < nch; ++kc) {
         const int s = kc % B_NST;
+        const int grp = kc / B_GROUP;
         if (!wait(S::SPLIT + s, (kc / B_NST) & 1)) break;
+        // the partial-sum buffer of this group was drained two groups ago
+        if (kc % B_GROUP == 0 && grp >= 2 && !wait(S::DRAIN + (grp & 1), ((grp - 2) >> 1) & 1)) break;
         tc::fence_after_sync();
         const uint32_t ah = tmem + B_ASTAGE + 64 * s, al = ah + 32;
         const uint32_t bh = base + s * S::STAGE + 16384, bl = bh + 8192;
+        const uint32_t d = tmem + b_part(grp);
+        const bool fresh = kc % B_GROUP == 0;
+        // small cross terms first, while the group's partial sum is still small
 #pragma unroll
         for (int kb = 0; kb < KC / 8; ++kb) {
           const uint32_t off = kb * 32;
-          tc::mma_tf32_ta(tmem + B_SMALL, ah + kb * 8, tc::sw128_desc(bl + off), IDESC, (kc > 0 || kb > 0));
-          tc::mma_tf32_ta(tmem + B_SMALL, al + kb * 8, tc::sw128_desc(bh + off), IDESC, 1);
-          tc::mma_tf32_ta(tmem, ah + kb * 8, tc::sw128_desc(bh + off), IDESC, (kc > 0 || kb > 0));
+          tc::mma_tf32_ta(d, ah + kb * 8, tc::sw128_desc(bl + off), IDESC, !(fresh && kb == 0));
+          tc::mma_tf32_ta(d, al + kb * 8, tc::sw128_desc(bh + off), IDESC, 1);
+        }
+#pragma unroll
+        for (int kb = 0; kb < KC / 8; ++kb) {
+          const uint32_t off = kb * 32;
+          tc::mma_tf32_ta(d, ah + kb * 8, tc::sw128_desc(bh + off), IDESC, 1);
         }
         tc::mma_commit(BAR(S::MMA + s));
         // stage (kc - 1) % B_NST (smem and TMEM) is free once MMA(kc - 1) is done, which
@@ -491,7 +504,13 @@ __global__ void __maxnreg__(96) k_mlp_bwd_tc(MlpParams p) {
     for (int i = t; i < NB * H / 4; i += 32 * F_NEPI)
       reinterpret_cast<float4*>(sW0)[i] = __ldg(reinterpret_cast<const float4*>(p.w[0]) + i);
     tc::named_sync(1, 32 * F_NEPI);
-    // split each dW chunk into tf32 hi / lo, into TMEM
+    // split each dW chunk into tf32 hi / lo, into TMEM; after the last chunk of
+    // every group of B_GROUP chunks add the group's dH partial sum (this warp
+    // group's 32 columns) into fp32 registers, so that no tensor-core
+    // accumulator sums more than B_GROUP chunks
+    float dh[32];
+#pragma unroll
+    for (int o = 0; o < 32; ++o) dh[o] = 0.f;
     for (int kc = 0; kc < nch; ++kc) {
       const int s = kc % B_NST;
       if (!wwait(S::LD + s, (kc / B_NST) & 1)) break;
@@ -516,14 +535,17 @@ __global__ void __maxnreg__(96) k_mlp_bwd_tc(MlpParams p) {
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(BAR(S::SPLIT + s));
-    }
-    float dh[32];
-    if (wwait(S::MMA + (last % B_NST), (last / B_NST) & 1)) {
-      tc::fence_after_sync();
-      tc::tmem_ld32(tmem + lane_base + 32 * g, dh);
-      tc::tmem_wait_ld();
-      tc::tmem_ld16_add(tmem + lane_base + B_SMALL + 32 * g, dh);
-      tc::tmem_ld16_add(tmem + lane_base + B_SMALL + 32 * g + 16, dh + 16);
+      if (kc % B_GROUP == B_GROUP - 1 || kc == last) {
+        const int grp = kc / B_GROUP;
+        if (!wwait(S::MMA + s, (kc / B_NST) & 1)) break;
+        tc::fence_after_sync();
+        const uint32_t part_col = tmem + lane_base + b_part(grp) + 32 * g;
+        tc::tmem_ld16_add(part_col, dh);
+        tc::tmem_ld16_add(part_col + 16, dh + 16);
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(BAR(S::DRAIN + (grp & 1)));
+      }
     }
     // hidden layers nh-1 .. 1 on the tensor cores, this group's 32 columns
     uint32_t pacc = 0;

@@ -41,14 +41,15 @@ class Structure:
         return 1 if self.batch is None else int(self.batch.max()) + 1
 
 
-def diamond_si(reps: int, sigma: float, seed: int) -> Structure:
-    r = np.arange(reps)
-    grid = np.stack(np.meshgrid(r, r, r, indexing="ij"), -1).reshape(-1, 3)
+def diamond_si(reps, sigma: float, seed: int) -> Structure:
+    """``reps`` conventional cells per axis (an int, or three ints)."""
+    nx, ny, nz = (reps, reps, reps) if np.ndim(reps) == 0 else tuple(int(x) for x in reps)
+    grid = np.stack(np.meshgrid(np.arange(nx), np.arange(ny), np.arange(nz), indexing="ij"), -1).reshape(-1, 3)
     frac = (grid[:, None, :] + _DIAMOND_FRAC[None]).reshape(-1, 3)
     pos = frac * SI_A
     rng = np.random.default_rng(seed)
     pos = pos + rng.normal(0.0, sigma, size=pos.shape)
-    cell = np.eye(3) * SI_A * reps
+    cell = np.diag([nx, ny, nz]).astype(np.float64) * SI_A
     return Structure(pos, np.full(len(pos), 14), cell, np.ones(3, dtype=bool))
 
 
