@@ -359,13 +359,16 @@ __global__ void __maxnreg__(96) k_mlp_fwd_tc(MlpParams p) {
 // ---------------------------------------------------------------------------
 // backward
 // ---------------------------------------------------------------------------
-constexpr int B_NST = 2;  // copy stages of (dW chunk, weight chunk image)
+constexpr int B_NST = 3;  // copy stages of (dW chunk, weight chunk image)
 constexpr int B_GROUP = 2;  // K chunks per dH partial sum (drained to fp32 registers, see below)
-// TMEM: the dH partial sums of even / odd chunk groups at [0, 64) / [192, 256);
-// stage s's dW chunk as A at 64 + 64 s (hi) and 64 + 64 s + 32 (lo); after the
-// K loop the hidden layers' A (128 x 64) at [64, 128) hi, [128, 192) lo, their
-// hi.hi accumulator at [0, 64) and small-term accumulator at [192, 256)
-constexpr uint32_t B_ASTAGE = 64, B_TAHI = 64, B_TALO = 128, B_SMALL = 192;
+// The dW chunk's tf32 hi part is the MMA's A operand straight from shared
+// memory (the epilogue rounds the bulk-copied chunk in place; it is already in
+// the 128B-swizzled K-major operand layout) and only its lo part goes to TMEM.
+// TMEM: the dH partial sums of even / odd chunk groups at [0, 64) / [64, 128);
+// stage s's lo part at 128 + 32 s; after the K loop the hidden layers' A
+// (128 x 64) at [128, 192) hi, [192, 256) lo, their hi.hi accumulator at
+// [0, 64) and small-term accumulator at [64, 128)
+constexpr uint32_t B_ALO = 128, B_TAHI = 128, B_TALO = 192, B_SMALL = 64;
 __device__ __forceinline__ uint32_t b_part(int group) { return (group & 1) ? B_SMALL : 0u; }
 
 struct BwdSmem {
@@ -448,7 +451,7 @@ __global__ void __maxnreg__(96) k_mlp_bwd_tc(MlpParams p) {
         // the partial-sum buffer of this group was drained two groups ago
         if (kc % B_GROUP == 0 && grp >= 2 && !wait(S::DRAIN + (grp & 1), ((grp - 2) >> 1) & 1)) break;
         tc::fence_after_sync();
-        const uint32_t ah = tmem + B_ASTAGE + 64 * s, al = ah + 32;
+        const uint32_t ah = base + s * S::STAGE, al = tmem + B_ALO + 32 * s;  // A hi in smem, lo in TMEM
         const uint32_t bh = base + s * S::STAGE + 16384, bl = bh + 8192;
         const uint32_t d = tmem + b_part(grp);
         const bool fresh = kc % B_GROUP == 0;
@@ -456,13 +459,13 @@ __global__ void __maxnreg__(96) k_mlp_bwd_tc(MlpParams p) {
 #pragma unroll
         for (int kb = 0; kb < KC / 8; ++kb) {
           const uint32_t off = kb * 32;
-          tc::mma_tf32_ta(d, ah + kb * 8, tc::sw128_desc(bl + off), IDESC, !(fresh && kb == 0));
+          tc::mma_tf32(d, tc::sw128_desc(ah + off), tc::sw128_desc(bl + off), IDESC, !(fresh && kb == 0));
           tc::mma_tf32_ta(d, al + kb * 8, tc::sw128_desc(bh + off), IDESC, 1);
         }
 #pragma unroll
         for (int kb = 0; kb < KC / 8; ++kb) {
           const uint32_t off = kb * 32;
-          tc::mma_tf32_ta(d, ah + kb * 8, tc::sw128_desc(bh + off), IDESC, 1);
+          tc::mma_tf32(d, tc::sw128_desc(ah + off), tc::sw128_desc(bh + off), IDESC, 1);
         }
         tc::mma_commit(BAR(S::MMA + s));
         // stage (kc - 1) % B_NST (smem and TMEM) is free once MMA(kc - 1) is done, which
@@ -511,10 +514,23 @@ __global__ void __maxnreg__(96) k_mlp_bwd_tc(MlpParams p) {
     float dh[32];
 #pragma unroll
     for (int o = 0; o < 32; ++o) dh[o] = 0.f;
+    // drain the group that ended at chunk kc_end (its MMAs have to be complete)
+    auto drain = [&](int kc_end) {
+      const int grp = kc_end / B_GROUP;
+      if (!wwait(S::MMA + kc_end % B_NST, (kc_end / B_NST) & 1)) return false;
+      tc::fence_after_sync();
+      const uint32_t part_col = tmem + lane_base + b_part(grp) + 32 * g;
+      tc::tmem_ld16_add(part_col, dh);
+      tc::tmem_ld16_add(part_col + 16, dh + 16);
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(BAR(S::DRAIN + (grp & 1)));
+      return true;
+    };
     for (int kc = 0; kc < nch; ++kc) {
       const int s = kc % B_NST;
       if (!wwait(S::LD + s, (kc / B_NST) & 1)) break;
-      const unsigned char* src = sm + s * S::STAGE + row * 128;
+      unsigned char* src = sm + s * S::STAGE + row * 128;
       float v[16];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
@@ -524,29 +540,25 @@ __global__ void __maxnreg__(96) k_mlp_bwd_tc(MlpParams p) {
         v[4 * u + 2] = x.z;
         v[4 * u + 3] = x.w;
       }
+      // hi part in place (the MMA's shared-memory A operand), lo part into TMEM
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        *reinterpret_cast<float4*>(src + (((4 * g + u) ^ (row & 7)) << 4)) =
+            make_float4(tc::tf32_hi(v[4 * u]), tc::tf32_hi(v[4 * u + 1]), tc::tf32_hi(v[4 * u + 2]),
+                        tc::tf32_hi(v[4 * u + 3]));
       float part[16];
 #pragma unroll
-      for (int o = 0; o < 16; ++o) part[o] = tc::tf32_hi(v[o]);
-      tc::tmem_st16(tmem + lane_base + B_ASTAGE + 64 * s + 16 * g, part);
-#pragma unroll
       for (int o = 0; o < 16; ++o) part[o] = v[o] - tc::tf32_hi(v[o]);
-      tc::tmem_st16(tmem + lane_base + B_ASTAGE + 64 * s + 32 + 16 * g, part);
+      tc::tmem_st16(tmem + lane_base + B_ALO + 32 * s + 16 * g, part);
+      tc::fence_proxy_async();  // the in-place hi values are read by the tensor core (async proxy)
       tc::tmem_wait_st();
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(BAR(S::SPLIT + s));
-      if (kc % B_GROUP == B_GROUP - 1 || kc == last) {
-        const int grp = kc / B_GROUP;
-        if (!wwait(S::MMA + s, (kc / B_NST) & 1)) break;
-        tc::fence_after_sync();
-        const uint32_t part_col = tmem + lane_base + b_part(grp) + 32 * g;
-        tc::tmem_ld16_add(part_col, dh);
-        tc::tmem_ld16_add(part_col + 16, dh + 16);
-        tc::fence_before_sync();
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive(BAR(S::DRAIN + (grp & 1)));
-      }
+      // the previous group's partial sum, once this chunk is staged (overlaps its MMAs)
+      if (kc >= 1 && (kc - 1) % B_GROUP == B_GROUP - 1 && !drain(kc - 1)) break;
     }
+    if (ok) drain(last);
     // hidden layers nh-1 .. 1 on the tensor cores, this group's 32 columns
     uint32_t pacc = 0;
     for (int j = nh - 1; j >= 1 && ok; --j) {
