@@ -261,6 +261,9 @@ class SpatialRunner:
         self.ref_pos = loc.clone()
         self.loc32 = loc.float()
         self.out = None
+        # the first step after a (re)plan runs eagerly: NCCL sets up its peer
+        # connections on first use, which must not happen inside a graph capture
+        self._eager_next = True
 
     @property
     def owned_index(self) -> np.ndarray:
@@ -278,10 +281,12 @@ class SpatialRunner:
         return bool(flag.item())
 
     def _run(self, virial: bool):
+        graph = self.graph and self.halo is None and not self._eager_next
         self.out = self.model.evaluate(self.loc32, self.cell32, self.species, self.graph_ptr, self.edges,
                                        forces=True, virial=virial, out=self.out, energy_weight=self.weight,
                                        halo=self.halo, halo_exchange=self.nx if self.native else None,
-                                       active=self.active, graph=self.graph and self.halo is None)
+                                       active=self.active, graph=graph)
+        self._eager_next = False
         return self.out
 
     # -- one step ------------------------------------------------------
