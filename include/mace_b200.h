@@ -288,7 +288,9 @@ typedef struct {
  *                         in the order p sends them; row_cap: the longest row
  *                         exchanged (floats, a multiple of 4)
  *   mace_system.halo_exchange = the object, for every step
- *   mace_halo_destroy
+ *   mace_halo_destroy     on every rank; first releases the captured step
+ *                         graphs of the contexts that hold this halo's NCCL
+ *                         operations (NCCL's destroy waits until none does)
  * Per step, after each layer but the last, the ghost rows of the node features
  * are overwritten with their owners' rows; in the backward the ghost rows of
  * the feature gradients are added onto their owners' rows (in a fixed order)

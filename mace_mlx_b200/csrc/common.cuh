@@ -140,6 +140,13 @@ __device__ __forceinline__ float zbl_pair(float r, float zu, float zv, float rma
 int halo_features(mace_halo* h, float* rows, int64_t row_len, cudaStream_t s);
 int halo_gradients(mace_halo* h, float* rows, int64_t row_len, cudaStream_t s);
 int halo_version(const mace_halo* h);
+// A context whose captured step graph holds NCCL operations of halo `h`
+// registers itself; destroying the halo first releases those graphs (NCCL
+// waits, in ncclCommDestroy, until no graph holds operations of the
+// communicator).  ctx_drop_graph releases a context's captured step.
+void halo_attach_graph(mace_halo* h, mace_ctx* c);
+void halo_detach_graph(mace_halo* h, mace_ctx* c);
+void ctx_drop_graph(mace_ctx* c);
 
 // per-node sums over each receiver's edges that need no learned features:
 // density of every density layer and the ZBL pair energy (forward), and the

@@ -164,6 +164,7 @@ struct mace_halo {
   float* d_rbuf = nullptr;
   int version = 0;
   std::vector<void*> allocs;
+  std::vector<mace_ctx*> graph_users;  // contexts whose captured step holds this halo's operations
 };
 
 namespace mace {
@@ -244,6 +245,15 @@ int halo_gradients(mace_halo* h, float* rows, int64_t row_len, cudaStream_t s) {
 }
 
 int halo_version(const mace_halo* h) { return h ? h->version : 0; }
+
+void halo_attach_graph(mace_halo* h, mace_ctx* c) {
+  if (h && std::find(h->graph_users.begin(), h->graph_users.end(), c) == h->graph_users.end())
+    h->graph_users.push_back(c);
+}
+
+void halo_detach_graph(mace_halo* h, mace_ctx* c) {
+  if (h) h->graph_users.erase(std::remove(h->graph_users.begin(), h->graph_users.end(), c), h->graph_users.end());
+}
 
 }  // namespace mace
 
@@ -349,6 +359,12 @@ int mace_halo_destroy(mace_halo* h) {
   if (!h) return MACE_OK;
   cudaSetDevice(h->device);
   cudaDeviceSynchronize();
+  // captured steps that hold this communicator's operations go first: NCCL's
+  // destroy waits until no graph holds any
+  const std::vector<mace_ctx*> users = h->graph_users;
+  for (mace_ctx* c : users) ctx_drop_graph(c);
+  h->graph_users.clear();
+  cudaSetDevice(h->device);
   halo_free_plan(h);
   if (h->comm && h->api) h->api->comm_destroy(h->comm);
   delete h;

@@ -150,6 +150,7 @@ struct mace_ctx {
   std::vector<int64_t> g_chunks;  // chunk boundaries of the captured call (host arrays)
   int g_launches = 0;
   int g_halo_version = 0;  // plan version of the captured step's halo exchange
+  mace_halo* g_halo = nullptr;  // the halo whose NCCL operations the captured step holds
   // profiling inside the graph: its event-record nodes fill the first g_prof_n slots
   bool g_prof = false;
   int g_prof_n = 0;
@@ -166,11 +167,16 @@ int max_wnumel(const mace_model_desc& d) {
   return m;
 }
 
+// release the captured step (and its registration with the halo it holds)
+void drop_graph(mace_ctx* c) {
+  if (c->gexec) cudaGraphExecDestroy(c->gexec);
+  c->gexec = nullptr;
+  if (c->g_halo) halo_detach_graph(c->g_halo, c);
+  c->g_halo = nullptr;
+}
+
 void free_ws(mace_ctx* c) {
-  if (c->gexec) {  // a captured step refers to the workspace being released
-    cudaGraphExecDestroy(c->gexec);
-    c->gexec = nullptr;
-  }
+  drop_graph(c);  // a captured step refers to the workspace being released
   for (void* p : c->allocs) cudaFree(p);
   c->allocs.clear();
   if (c->nl_keys) cudaFree(c->nl_keys);
@@ -1060,6 +1066,13 @@ int nl_build(mace_ctx* c, const double* pos, const double* cell, const int32_t* 
 
 }  // namespace
 
+namespace mace {
+void ctx_drop_graph(mace_ctx* c) {
+  DeviceGuard g(c->device);
+  drop_graph(c);
+}
+}  // namespace mace
+
 extern "C" {
 
 int mace_last_error(char* buf, size_t len) {
@@ -1172,7 +1185,7 @@ int mace_ctx_destroy(mace_ctx* c) {
   free_ws(c);
   if (c->ev[0])
     for (int i = 0; i < 2 * mace_ctx::PROF_MAX; ++i) cudaEventDestroy(c->ev[i]);
-  if (c->gexec) cudaGraphExecDestroy(c->gexec);
+  drop_graph(c);
   if (c->cap_stream) cudaStreamDestroy(c->cap_stream);
   if (c->aux) cudaStreamDestroy(c->aux);
   for (cudaEvent_t e : c->fork_ev)
@@ -1247,10 +1260,7 @@ int mace_forward_backward(mace_ctx* c, const mace_system* sys, const mace_output
                     std::memcmp(&c->g_out, &o, sizeof(mace_outputs)) == 0 && c->g_chunks == chunk_key &&
                     c->g_halo_version == halo_version(sys->halo_exchange);
   if (!same) {
-    if (c->gexec) {
-      MACE_CUDA_TRY(cudaGraphExecDestroy(c->gexec));
-      c->gexec = nullptr;
-    }
+    drop_graph(c);
     if (!c->cap_stream) {
       // highest priority, which the captured kernel nodes keep in the graph
       int least = 0, greatest = 0;
@@ -1282,6 +1292,8 @@ int mace_forward_backward(mace_ctx* c, const mace_system* sys, const mace_output
     c->g_chunks = chunk_key;
     c->g_launches = c->launches;
     c->g_halo_version = halo_version(sys->halo_exchange);
+    c->g_halo = sys->halo_exchange;
+    halo_attach_graph(c->g_halo, c);
   }
   MACE_CUDA_TRY(cudaGraphLaunch(c->gexec, s));
   c->launches = c->g_launches;

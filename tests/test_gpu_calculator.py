@@ -112,9 +112,14 @@ def test_api_errors(model_dir, tmp_path, monkeypatch):
 
 
 def test_calculate_batch_matches_one_structure_at_a_time(model_dir):
-    """One batched step (structures as graphs of one system) equals separate steps."""
+    """One batched step (structures as graphs of one system) equals separate steps,
+    and each structure's energy and forces equal the float64 oracle on it alone:
+    a periodic batch of perturbed replicas of one cell and a molecule batch."""
     from mace_mlx_b200.structures import molecule_batch
+    from mace_mlx_b200.weights import load_model_dir
 
+    config, weights = load_model_dir(model_dir)
+    orc = OracleMACE(config, weights)
     calc = MACECalculator(model_path=model_dir, device="cuda", skin=0.0)
     sts = [diamond_si(2, 0.05, s) for s in (31, 32, 33)]
     periodic = [Atoms(s.numbers, s.positions, s.cell, True) for s in sts]
@@ -130,5 +135,11 @@ def test_calculate_batch_matches_one_structure_at_a_time(model_dir):
             assert abs(r["energy"] - ref["energy"]) <= 1e-6 * max(1.0, abs(ref["energy"])) + 1e-7 * len(atoms)
             np.testing.assert_allclose(r["forces"], ref["forces"], atol=1e-5 * max(1.0, np.abs(ref["forces"]).max()))
             np.testing.assert_allclose(r["node_energy"], ref["node_energy"], atol=1e-6)
+            i, j, S = neighbour_list(atoms.positions, atoms.get_cell(), atoms.pbc, 6.0)
+            want = orc.compute(atoms.positions, atoms.numbers - 1, i, j, S,
+                               atoms.get_cell() if np.any(atoms.pbc) else None)
+            mine = {"energy": np.array([r["energy"]]), "forces": np.asarray(r["forces"], np.float64),
+                    "node_energy": np.asarray(r["node_energy"], np.float64)}
+            assert_parity(mine, want, len(atoms))
     with pytest.raises(NotImplementedError):
         calc.calculate_batch(periodic, ["energy", "stress"])

@@ -8,6 +8,8 @@ moved halo-sized per step), the host-callback halo with torch collectives,
 and the 2 r_max ghost shell without exchange between layers.
 """
 
+import datetime
+import faulthandler
 import os
 import socket
 import tempfile
@@ -32,10 +34,14 @@ def _case():
 
 
 def _rank_main(rank, world, port, path, mode):
+    # a rank that is still running after four minutes prints its stack and exits,
+    # so that a stuck exchange fails the test instead of holding both GPUs
+    faulthandler.dump_traceback_later(240, exit=True)
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     torch.cuda.set_device(rank)
-    torch.distributed.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    torch.distributed.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                                         timeout=datetime.timedelta(seconds=120))
     try:
         st, config, weights = _case()
         model = MACEModel(config=config, weights=weights, device=rank)
@@ -64,7 +70,7 @@ def _rank_main(rank, world, port, path, mode):
         torch.distributed.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode", ["native", "callback", "shell"])
+@pytest.mark.parametrize("mode", ["shell", "callback", "native"])
 def test_two_gpu_domains_match_one_gpu(mode):
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
