@@ -63,6 +63,9 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=20.0, help="budget of the CPU baseline sample")
     ap.add_argument("--device-only", action="store_true",
                     help="only W + K plain device steps, no JSON (the command the ncu captures profile)")
+    ap.add_argument("--timeline", action="store_true",
+                    help="also print (to stderr) the per-launch timeline of one graph-replayed step, from the event "
+                         "records the profiler places in the graph: stream, start and end of every launch")
     ap.add_argument("--config", default="c1", choices=["c0", "c1", "c2", "c3", "c4"],
                     help="c1: the headline Si1000 (default); c0: small-arch Si216 with stress; c2: large-arch "
                          "LiPSO-8000 with stress; c3: 512 OFF-like molecules sharded by structure; "
@@ -392,6 +395,16 @@ def roofline_of(work: dict, prof: list[dict], steps: int, fp32_peak: dict | None
 # ---------------------------------------------------------------------------
 # B200 arm
 # ---------------------------------------------------------------------------
+def print_timeline(tl: list[dict]) -> None:
+    """One profiled step's launches in start order (stream 0: main, 1: radial-MLP stream), to stderr."""
+    end = max((t["end_ms"] for t in tl), default=0.0)
+    print(f"timeline of one profiled step: {len(tl)} launches, span {end * 1e3:.1f} us "
+          "(the event records add about 3 us per launch)", file=sys.stderr)
+    for t in sorted(tl, key=lambda t: t["start_ms"]):
+        print(f"  s{t['stream']} {t['name']:18s} L{t['layer']:2d} {t['start_ms'] * 1e3:8.1f} {t['end_ms'] * 1e3:8.1f}"
+              f" {(t['end_ms'] - t['start_ms']) * 1e3:7.1f} us", file=sys.stderr)
+
+
 def b200_arm(args, rank: int, world: int, local_rank: int):
     import torch
     import torch.distributed as dist
@@ -467,6 +480,8 @@ def b200_arm(args, rank: int, world: int, local_rank: int):
     for _ in range(args.steps):
         step()
     prof = model.profile_read()
+    if args.timeline:
+        print_timeline(model.profile_timeline())
     model.profile_enable(False)
     fp32 = measure_fp32_peak(dev)
     if world > 1:
