@@ -14,13 +14,15 @@
 // Forward:
 //   layer 0 (radial features -> 64) on the CUDA cores; every 64 x 64 hidden
 //   layer as 8 K-blocks x 3 MMAs (M = 128, N = 64, K = 8) with a pre-split,
-//   pre-swizzled weight image (B); the last layer in 32-column chunks with four
-//   B stages (each refilled three chunks ahead, so the image copies stay off
-//   the critical path) and four TMEM accumulators, the two epilogue groups
-//   taking alternate chunks, each warp moving its 32 rows of a chunk from TMEM
-//   through a 4 KB staging slice to HBM with one bulk store:
-//   the output is in the 128-edge tile layout (common.cuh), whose chunk rows
-//   are exactly a staging slice.
+//   pre-swizzled weight image (B); the last layer in 64-column chunks (MMA
+//   N = 64: a tcgen05.mma costs about the same issue time at N = 32 as at
+//   N = 128, so wide chunks halve the instruction count per output column)
+//   with two B stages (the next chunk's image copied while this one
+//   multiplies) and two TMEM accumulators; both epilogue groups drain every
+//   chunk, group g its 32-column half, each warp moving its 32 rows of the
+//   half from TMEM through a 4 KB staging slice to HBM with one bulk store:
+//   the output is in the 128-edge tile layout (common.cuh), whose 32-column
+//   chunk rows are exactly a staging slice.
 // Backward:
 //   dH = dW (128 x W) . W_last^T in 32-wide K chunks through three copy
 //   stages: the control warp bulk-copies a 16 KB dW chunk (already in operand
@@ -41,13 +43,13 @@ namespace {
 
 constexpr int TM = 128;           // edges per tile (MMA M)
 constexpr int H = 64;             // hidden width
-constexpr int TC32 = 32;          // output columns per forward chunk (MMA N)
+constexpr int FC = 64;            // output columns per forward chunk (MMA N)
 constexpr int KC = 32;            // backward K chunk (one 128-byte panel)
-constexpr int NBUF = 4;           // forward TMEM chunk buffers of 32 columns
+constexpr int NBUF = 2;           // forward TMEM chunk buffers of FC columns
 constexpr int MLP_TC_TIMEOUT = TC_ERR_TIMEOUT;
 constexpr int MLP_TC_ALIGN = TC_ERR_ALIGN;
 constexpr int IMG = 2 * H * H;    // floats of one 64 x 64 hi/lo image
-constexpr int CIMG = 2 * TC32 * H;  // floats of one forward chunk image (32 x 64, hi/lo)
+constexpr int CIMG = 2 * FC * H;    // floats of one forward chunk image (64 x 64, hi/lo)
 constexpr int BIMG = 2 * H * KC;    // floats of one backward chunk image (64 x 32, hi/lo)
 static_assert(WT_CHUNK * 4 == TM * 128, "a radial-weight chunk is one 128 x 128-byte operand panel");
 
@@ -88,11 +90,11 @@ constexpr int F_NEPI = 8;                 // epilogue warps: quadrant q = warp &
 constexpr int F_NTHR = 32 * (F_NEPI + 1); // + control warp
 constexpr int F_TMEM = 256;               // [0, 128) accumulators, [128, 192) A hi, [192, 256) A lo
 constexpr uint32_t F_AHI = 128, F_ALO = 192;
-constexpr uint32_t F_HSMALL = 64;  // small-term accumulator of the hidden layers (chunk buffers 2, 3 meanwhile free)
+constexpr uint32_t F_HSMALL = 64;  // small-term accumulator of the hidden layers (chunk buffer 1 meanwhile free)
 
-constexpr int F_NBS = 4;  // forward chunk-image stages
+constexpr int F_NBS = 2;  // forward chunk-image stages
 struct FwdSmem {
-  // 64 KB: four 32-row chunk images; the 64 x 64 hidden image uses the first 32 KB
+  // 64 KB: two 64-row chunk images; the 64 x 64 hidden image uses the first 32 KB
   static constexpr int B = 0;
   static constexpr int STG = F_NBS * CIMG * 4;  // 8 warps x 4 KB output staging; holds the layer-0 weights first
   static constexpr int BARS = STG + F_NEPI * 4096;
@@ -171,7 +173,8 @@ __global__ void __maxnreg__(96) k_mlp_fwd_tc(MlpParams p) {
   auto BAR = [&](int i) { return tc::smem_u32(&bars[i]); };
   const int nh = p.n_layers - 1;
   const int wout = p.widths[p.n_layers];
-  const int nch = wt_nchunk(wout);
+  const int nch = wt_nchunk(wout);  // 32-column chunks of the output layout
+  const int nfc = (nch + 1) / 2;    // 64-column MMA chunks
   const uint32_t b_base = tc::smem_u32(sm + S::B);
 
   if (warp == F_NEPI) {
@@ -182,7 +185,7 @@ __global__ void __maxnreg__(96) k_mlp_fwd_tc(MlpParams p) {
     for (int i = 0; i < S::NBARS; ++i) {
       int count = 1;
       if (i == S::A) count = F_NEPI;
-      if (i >= S::FREE && i < S::FREE + NBUF) count = F_NEPI / 2;  // one group drains a buffer
+      if (i >= S::FREE && i < S::FREE + NBUF) count = F_NEPI;  // both groups drain every buffer
       tc::mbar_init(BAR(i), count);
     }
     *abort_flag = 0;
@@ -212,8 +215,8 @@ __global__ void __maxnreg__(96) k_mlp_fwd_tc(MlpParams p) {
       };
       const uint32_t a_hi = tmem + F_AHI, a_lo = tmem + F_ALO;
       uint32_t pa = 0;
-      // chunk images 2 and 3 do not overlap the hidden-layer image: fetch them now
-      for (int c = 2; c < F_NBS && c < nch; ++c) copy_chunk(c);
+      // chunk image 1 does not overlap the hidden-layer image: fetch it now
+      if (nfc > 1) copy_chunk(1);
       if (nh >= 2) copy_trunk(0);
       for (int j = 1; j < nh; ++j) {  // hidden layer j reads A = SiLU(layer j-1)
         if (!wait(S::TL, (j - 1) & 1) || !wait(S::A, pa)) break;
@@ -224,21 +227,18 @@ __global__ void __maxnreg__(96) k_mlp_fwd_tc(MlpParams p) {
         if (!wait(S::ACC, (j - 1) & 1)) break;  // B is free again
         if (j + 1 < nh) copy_trunk(j);
       }
-      if (ok) {
-        copy_chunk(0);
-        if (nch > 1) copy_chunk(1);
-      }
+      if (ok) copy_chunk(0);  // the hidden-layer image is no longer read
       if (ok && wait(S::A, pa)) {  // A = SiLU(last hidden layer)
-        for (int c = 0; c < nch; ++c) {
+        for (int c = 0; c < nfc; ++c) {
           const int s = c % F_NBS, buf = c % NBUF;
           if (!wait(S::BST + s, (c / F_NBS) & 1)) break;
           if (c >= NBUF && !wait(S::FREE + buf, ((c / NBUF) - 1) & 1)) break;
           tc::fence_after_sync();
           const uint32_t bs = b_base + s * CIMG * 4;
-          mma_k64_ta<TC32>(tmem + buf * TC32, a_hi, a_lo, bs, bs + CIMG * 2);
+          mma_k64_ta<FC>(tmem + buf * FC, a_hi, a_lo, bs, bs + CIMG * 2);
           tc::mma_commit(BAR(S::FULL + buf));
           // stage (c - 1) % F_NBS is free once MMA(c - 1) is done: chunk c + F_NBS - 1 goes there
-          if (c >= 1 && c + F_NBS - 1 < nch) {
+          if (c >= 1 && c + F_NBS - 1 < nfc) {
             if (!wait(S::FULL + (c - 1) % NBUF, ((c - 1) / NBUF) & 1)) break;
             copy_chunk(c + F_NBS - 1);
           }
@@ -316,14 +316,14 @@ __global__ void __maxnreg__(96) k_mlp_fwd_tc(MlpParams p) {
         tc::tmem_ld16_add(tmem + lane_base + F_HSMALL + 32 * g + 16, y + 16);
       }
     }
-    // output chunks c = g, g + 2, ...: TMEM -> registers -> staging -> bulk store
+    // output chunk 2c + g (columns 32g.. of MMA chunk c): TMEM -> registers -> staging -> bulk store
     float* dst = p.out + (int64_t)blockIdx.x * nch * WT_CHUNK + q * 32 * 32;
-    for (int c = g; c < nch && ok; c += 2) {
+    for (int c = 0; c < nfc && ok; ++c) {
       const int buf = c % NBUF;
       if (!wwait(S::FULL + buf, (c / NBUF) & 1)) break;
       tc::fence_after_sync();
       float v[32];
-      tc::tmem_ld32(tmem + lane_base + buf * TC32, v);
+      tc::tmem_ld32(tmem + lane_base + buf * FC + 32 * g, v);
       tc::tmem_wait_ld();
       tc::fence_before_sync();
       __syncwarp();
@@ -339,8 +339,8 @@ __global__ void __maxnreg__(96) k_mlp_fwd_tc(MlpParams p) {
             make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
       tc::fence_proxy_async();
       __syncwarp();
-      if (lane == 0) {
-        tc::bulk_s2g(dst + (int64_t)c * WT_CHUNK, tc::smem_u32(stg), 4096);
+      if (lane == 0 && 2 * c + g < nch) {  // an odd chunk count leaves the last half unwritten
+        tc::bulk_s2g(dst + (int64_t)(2 * c + g) * WT_CHUNK, tc::smem_u32(stg), 4096);
         tc::bulk_commit();
       }
     }

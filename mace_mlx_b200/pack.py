@@ -122,15 +122,16 @@ def mlp_tc_images(w_last_out_in: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
     """Operand images of the last radial-MLP layer for the tcgen05 kernels.
 
     ``w_last_out_in`` is the converted (out, in) weight with in = 64.  Forward:
-    per 32-output chunk the (32 x 64) slice, tf32 hi then lo.  Backward: per
-    32-output chunk the (64 x 32) slice of the transpose, hi then lo.
+    per 64-output chunk the (64 x 64) slice (zero rows past the last output),
+    tf32 hi then lo.  Backward: per 32-output chunk the (64 x 32) slice of the
+    transpose, hi then lo.
     """
     W = np.asarray(w_last_out_in, dtype=np.float32)
     n_out, n_in = W.shape
-    pad_f = -(-n_out // 32) * 32
+    pad_f = -(-n_out // 64) * 64
     Wf = np.zeros((pad_f, n_in), np.float32)
     Wf[:n_out] = W
-    fwd = np.concatenate([_hilo_image(Wf[c:c + 32]) for c in range(0, pad_f, 32)])
+    fwd = np.concatenate([_hilo_image(Wf[c:c + 64]) for c in range(0, pad_f, 64)])
     pad_b = -(-n_out // 32) * 32
     Wb = np.zeros((n_in, pad_b), np.float32)
     Wb[:, :n_out] = W.T

@@ -123,13 +123,17 @@ def test_tf32_split_and_swizzled_images_round_trip():
     assert len(set(off.ravel().tolist())) == a.size
     w = rng.normal(size=(200, 64)).astype(np.float32)  # (out, in) with out not a multiple of 128
     fwd, bwd = mlp_tc_images(w)
-    assert fwd.size == 7 * 2 * 32 * 64 and bwd.size == 7 * 2 * 64 * 32
-    # forward chunk 6 (outputs 192..223), hi part, row 7 (output 199) holds w[199] up to tf32 rounding
-    ch = fwd[6 * 2 * 32 * 64: 6 * 2 * 32 * 64 + 32 * 64]
+    assert fwd.size == 4 * 2 * 64 * 64 and bwd.size == 7 * 2 * 64 * 32
+    # forward chunk 3 (outputs 192..255), hi part, row 7 (output 199) holds w[199] up to tf32 rounding
+    ch = fwd[3 * 2 * 64 * 64: 3 * 2 * 64 * 64 + 64 * 64]
     rr = 7
     kk = np.arange(64)
-    got = ch[(kk // 32) * 32 * 32 + rr * 32 + (((kk % 32) // 4) ^ (rr % 8)) * 4 + (kk % 4)]
+    got = ch[(kk // 32) * 64 * 32 + rr * 32 + (((kk % 32) // 4) ^ (rr % 8)) * 4 + (kk % 4)]
     np.testing.assert_allclose(got, w[199], rtol=2.0 ** -11)
+    # rows past the last output are zero (hi and lo)
+    rr = 40  # output 232
+    got = ch[(kk // 32) * 64 * 32 + rr * 32 + (((kk % 32) // 4) ^ (rr % 8)) * 4 + (kk % 4)]
+    assert not np.any(got)
 
 
 def test_edge_tile_layout_round_trip():
