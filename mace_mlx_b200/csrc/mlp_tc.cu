@@ -26,10 +26,13 @@
 // Backward:
 //   dH = dW (128 x W) . W_last^T in 32-wide K chunks through three copy
 //   stages: the control warp bulk-copies a 16 KB dW chunk (already in operand
-//   layout) and the matching 16 KB weight image, the epilogue warps split the
-//   chunk into tf32 hi/lo straight into TMEM, and the control warp
-//   accumulates 4 K-blocks x 3 MMAs; then every hidden layer dH <- (dH *
-//   SiLU'(a)) . W_j^T on the tensor cores, and dL/db on the CUDA cores.
+//   layout) and the matching 16 KB weight image (hi rows then lo rows), the
+//   epilogue warps split the chunk into tf32 hi (in place) and lo (TMEM), and
+//   the control warp issues per K-block one N = 128 MMA of A_hi against the
+//   stacked hi|lo weight rows (the large term and one small term side by
+//   side) and one N = 64 MMA of A_lo against the hi rows; then every hidden
+//   layer dH <- (dH * SiLU'(a)) . W_j^T on the tensor cores, and dL/db on the
+//   CUDA cores.
 //
 // Every mbarrier wait is bounded (about 2 s).  A wait that gives up raises a
 // CTA-wide abort flag that ends every other wait, the kernel records
@@ -364,12 +367,12 @@ constexpr int B_GROUP = 2;  // K chunks per dH partial sum (drained to fp32 regi
 // The dW chunk's tf32 hi part is the MMA's A operand straight from shared
 // memory (the epilogue rounds the bulk-copied chunk in place; it is already in
 // the 128B-swizzled K-major operand layout) and only its lo part goes to TMEM.
-// TMEM: the dH partial sums of even / odd chunk groups at [0, 64) / [64, 128);
+// TMEM: the dH partial sum of the current chunk group, hi.hi at [0, 64) and
+// the two small terms at [64, 128) (one N = 128 MMA writes both halves);
 // stage s's lo part at 128 + 32 s; after the K loop the hidden layers' A
 // (128 x 64) at [128, 192) hi, [192, 256) lo, their hi.hi accumulator at
 // [0, 64) and small-term accumulator at [64, 128)
 constexpr uint32_t B_ALO = 128, B_TAHI = 128, B_TALO = 192, B_SMALL = 64;
-__device__ __forceinline__ uint32_t b_part(int group) { return (group & 1) ? B_SMALL : 0u; }
 
 struct BwdSmem {
   // stage s at s * STAGE: the dW chunk (16 KB, bulk-copied in the 128-edge tile
@@ -443,29 +446,24 @@ __global__ void __maxnreg__(96) k_mlp_bwd_tc(MlpParams p) {
         tc::bulk_g2s(st + 16384, p.tc_img_bwd + (int64_t)k * BIMG, BIMG * 4, BAR(S::LD + s));
       };
       constexpr uint32_t IDESC = tc::idesc_tf32(TM, H);
+      constexpr uint32_t IDESC2 = tc::idesc_tf32(TM, 2 * H);  // B = the stacked hi|lo weight rows
       for (int k = 0; k < B_NST && k < nch; ++k) copy_chunk(k);
       for (int kc = 0; kc < nch; ++kc) {
         const int s = kc % B_NST;
         const int grp = kc / B_GROUP;
         if (!wait(S::SPLIT + s, (kc / B_NST) & 1)) break;
-        // the partial-sum buffer of this group was drained two groups ago
-        if (kc % B_GROUP == 0 && grp >= 2 && !wait(S::DRAIN + (grp & 1), ((grp - 2) >> 1) & 1)) break;
+        // the previous group's partial sum has been drained into registers
+        if (kc % B_GROUP == 0 && grp >= 1 && !wait(S::DRAIN + ((grp - 1) & 1), ((grp - 1) >> 1) & 1)) break;
         tc::fence_after_sync();
         const uint32_t ah = base + s * S::STAGE, al = tmem + B_ALO + 32 * s;  // A hi in smem, lo in TMEM
-        const uint32_t bh = base + s * S::STAGE + 16384, bl = bh + 8192;
-        const uint32_t d = tmem + b_part(grp);
+        const uint32_t bh = base + s * S::STAGE + 16384;  // hi rows [0, 64), lo rows [64, 128)
         const bool fresh = kc % B_GROUP == 0;
-        // small cross terms first, while the group's partial sum is still small
 #pragma unroll
         for (int kb = 0; kb < KC / 8; ++kb) {
           const uint32_t off = kb * 32;
-          tc::mma_tf32(d, tc::sw128_desc(ah + off), tc::sw128_desc(bl + off), IDESC, !(fresh && kb == 0));
-          tc::mma_tf32_ta(d, al + kb * 8, tc::sw128_desc(bh + off), IDESC, 1);
-        }
-#pragma unroll
-        for (int kb = 0; kb < KC / 8; ++kb) {
-          const uint32_t off = kb * 32;
-          tc::mma_tf32(d, tc::sw128_desc(ah + off), tc::sw128_desc(bh + off), IDESC, 1);
+          // [A_hi B_hi | A_hi B_lo] into [0, 128), then A_lo B_hi into the small half
+          tc::mma_tf32(tmem, tc::sw128_desc(ah + off), tc::sw128_desc(bh + off), IDESC2, !(fresh && kb == 0));
+          tc::mma_tf32_ta(tmem + B_SMALL, al + kb * 8, tc::sw128_desc(bh + off), IDESC, 1);
         }
         tc::mma_commit(BAR(S::MMA + s));
         // stage (kc - 1) % B_NST (smem and TMEM) is free once MMA(kc - 1) is done, which
@@ -519,7 +517,9 @@ __global__ void __maxnreg__(96) k_mlp_bwd_tc(MlpParams p) {
       const int grp = kc_end / B_GROUP;
       if (!wwait(S::MMA + kc_end % B_NST, (kc_end / B_NST) & 1)) return false;
       tc::fence_after_sync();
-      const uint32_t part_col = tmem + lane_base + b_part(grp) + 32 * g;
+      const uint32_t part_col = tmem + lane_base + 32 * g;
+      tc::tmem_ld16_add(part_col + B_SMALL, dh);
+      tc::tmem_ld16_add(part_col + B_SMALL + 16, dh + 16);
       tc::tmem_ld16_add(part_col, dh);
       tc::tmem_ld16_add(part_col + 16, dh + 16);
       tc::fence_before_sync();
