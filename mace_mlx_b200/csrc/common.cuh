@@ -277,7 +277,19 @@ struct ConvParams {
   const int32_t* rev;    // (E) reverse edge
   float* tq;             // (E, in_dim) per-edge sender-side terms, or null (then gathered from dA)
   int64_t n_active;      // receivers >= n_active were not evaluated: their sender terms are skipped (0: all)
+  // A layer's conv in two launches, each beside part of the radial-MLP tiles:
+  // part 1 takes the receivers whose edges lie below e_split (split_first = 0,
+  // the forward: all of their edges; 1, the backward: their first edge), part 2
+  // the other receivers; split_part 0 takes every receiver.
+  int split_part;
+  int split_first;
+  int64_t e_split;
 };
+__device__ __forceinline__ bool conv_receiver_skipped(const ConvParams& p, int64_t n) {
+  if (!p.split_part) return false;
+  const bool below = p.split_first ? p.row_ptr[n] < p.e_split : p.row_ptr[n + 1] <= p.e_split;
+  return below != (p.split_part == 1);
+}
 int launch_conv_fwd(const ConvParams& p, cudaStream_t s);
 // *need_gather: the kernel wrote per-edge sender-side terms to p.tq and
 // launch_dup_gather must sum them into p.dup

@@ -94,6 +94,7 @@ __global__ void k_conv_fwd(ConvParams p, int EC) {
   float* sY = sm + EC;
   float* sM = sY + EC * 16;
   const int64_t n = p.n0 + blockIdx.x;
+  if (conv_receiver_skipped(p, n)) return;  // the other part of a split launch
   const int64_t e_beg = p.row_ptr[n], e_end = p.row_ptr[n + 1];
   if (e_beg == e_end) {
     for (int q = threadIdx.x; q < p.mid_dim; q += blockDim.x) p.A[n * p.mid_dim + q] = 0.f;
@@ -215,6 +216,7 @@ __global__ void __launch_bounds__(512, 2) k_conv_bwd(ConvParams p, int EC, int G
   float* sH = sRed + nw * EC * 16;         // h_tot x C
   float* sDupAll = sH + p.h_tot * C;       // G x in_dim
   const int64_t n = p.n0 + blockIdx.x;
+  if (conv_receiver_skipped(p, n)) return;  // the other part of a split launch
   const int tid = threadIdx.x;
   const int u = tid % C, grp = tid / C;
   float* sDup = sDupAll + grp * p.in_dim;

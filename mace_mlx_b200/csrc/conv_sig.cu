@@ -132,6 +132,7 @@ __global__ void __launch_bounds__(C) k_conv_fwd_sig(ConvParams p) {
   float* sY = sm + EC;
   float* sM = sY + EC * 16;
   const int64_t n = p.n0 + blockIdx.x;
+  if (conv_receiver_skipped(p, n)) return;  // the other part of a split launch
   const int u = threadIdx.x;
   const int64_t e_beg = p.row_ptr[n], e_end = p.row_ptr[n + 1];
   float acc[S::atot()];
@@ -277,8 +278,11 @@ struct BwdLayout {
 //   T_e[l1 slot][i][u] = sum_k w_e[k, u] sum_j H_k[i][j] Y_e[j]  -> tq[rev(e)],
 // for launch_dup_gather to sum over each node's (contiguous) incoming rows.
 // G groups of C threads share one receiver: group g takes edges g, g+G, ...
+// Three CTAs per SM (at most 85 registers a thread at 256 threads) where the
+// signature has at most 10 paths: the medium model's layers then compile
+// without spills and the extra warps hide the sender and weight loads.
 template <int C, int G, class S, int MODE>
-__global__ void __launch_bounds__(C * G, 2) k_conv_bwd_sig(ConvParams p) {
+__global__ void __launch_bounds__(C * G, (S::n <= 10 ? 3 : 2)) k_conv_bwd_sig(ConvParams p) {
   using Lay = BwdLayout<C, G, S, MODE>;
   constexpr int EC = Lay::EC, NW = Lay::NW, HP = Lay::HP, MT = S::mtot(), IC = S::in_ch();
   constexpr int NT = C * G;
@@ -290,6 +294,7 @@ __global__ void __launch_bounds__(C * G, 2) k_conv_bwd_sig(ConvParams p) {
   float* sH = sm + Lay::H;
   float* sDup = sm + Lay::DUP;
   const int64_t n = p.n0 + blockIdx.x;
+  if (conv_receiver_skipped(p, n)) return;  // the other part of a split launch
   const int tid = threadIdx.x;
   const int u = tid % C, grp = tid / C;
   const int warp = u >> 5, lane = tid & 31;

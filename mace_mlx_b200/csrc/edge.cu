@@ -78,7 +78,7 @@ __device__ __forceinline__ void sh_eval(const float* __restrict__ T, int lmax, c
 #pragma unroll
     for (int i = 0; i < 3; ++i)
 #pragma unroll
-      for (int j = 0; j < 3; ++j) a += Y[1 + i] * Y[1 + j] * __ldg(T + (i * 3 + j) * 5 + k);
+      for (int j = 0; j < 3; ++j) a += Y[1 + i] * Y[1 + j] * T[(i * 3 + j) * 5 + k];
     Y[4 + k] = a;
   }
   if (lmax < 3) return;
@@ -89,7 +89,7 @@ __device__ __forceinline__ void sh_eval(const float* __restrict__ T, int lmax, c
 #pragma unroll
     for (int i = 0; i < 5; ++i)
 #pragma unroll
-      for (int j = 0; j < 3; ++j) a += Y[4 + i] * Y[1 + j] * __ldg(T3 + (i * 3 + j) * 7 + k);
+      for (int j = 0; j < 3; ++j) a += Y[4 + i] * Y[1 + j] * T3[(i * 3 + j) * 7 + k];
     Y[9 + k] = a;
   }
 }
@@ -111,7 +111,18 @@ __device__ __forceinline__ float bessel_arg(const EdgeParams& p, int64_t e, floa
   return agnesi_transform(r, r0, p.ag_q, p.ag_p, p.ag_a, drt);
 }
 
+// The recursion tables T2 (45 floats) and T3 (105) in shared memory: every
+// thread reads all of them, from the same addresses (broadcast).
+constexpr int SH_T_FLOATS = 45 + 105;
+__device__ __forceinline__ void stage_sh_tables(const EdgeParams& p, float* sT) {
+  const int n = p.max_ell >= 3 ? SH_T_FLOATS : (p.max_ell == 2 ? 45 : 0);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) sT[i] = __ldg(p.sh_T + i);
+  __syncthreads();
+}
+
 __global__ void k_edge_fwd(EdgeParams p) {
+  __shared__ float sT[SH_T_FLOATS];
+  stage_sh_tables(p, sT);
   int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (e >= p.E) return;
   EdgeGeom g = edge_geom(p, e);
@@ -119,7 +130,7 @@ __global__ void k_edge_fwd(EdgeParams p) {
   p.v[3 * e + 1] = g.v[1];
   p.v[3 * e + 2] = g.v[2];
   float Y[16];
-  sh_eval(p.sh_T, p.max_ell, g.u, Y);
+  sh_eval(sT, p.max_ell, g.u, Y);
 #pragma unroll
   for (int i = 0; i < 16; ++i) p.Y[16 * e + i] = Y[i];
   const float pref = sqrtf(2.0f / p.r_max);
@@ -139,6 +150,8 @@ __global__ void k_edge_fwd(EdgeParams p) {
 }
 
 __global__ void k_edge_bwd(EdgeParams p) {
+  __shared__ float sT[SH_T_FLOATS];
+  stage_sh_tables(p, sT);
   int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   double vir[9];
 #pragma unroll
@@ -146,7 +159,7 @@ __global__ void k_edge_bwd(EdgeParams p) {
   if (e < p.E) {
     EdgeGeom g = edge_geom(p, e);
     float Y[16];
-    sh_eval(p.sh_T, p.max_ell, g.u, Y);
+    sh_eval(sT, p.max_ell, g.u, Y);
     float dYv[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) dYv[i] = p.dY[16 * e + i];
@@ -154,14 +167,14 @@ __global__ void k_edge_bwd(EdgeParams p) {
     float dY1[3] = {dYv[1], dYv[2], dYv[3]};
     float dY2[5] = {dYv[4], dYv[5], dYv[6], dYv[7], dYv[8]};
     if (p.max_ell >= 3) {
-      const float* T3 = p.sh_T + 45;
+      const float* T3 = sT + 45;
 #pragma unroll
       for (int i = 0; i < 5; ++i)
 #pragma unroll
         for (int j = 0; j < 3; ++j) {
           float acc = 0.f;
 #pragma unroll
-          for (int k = 0; k < 7; ++k) acc += __ldg(T3 + (i * 3 + j) * 7 + k) * dYv[9 + k];
+          for (int k = 0; k < 7; ++k) acc += T3[(i * 3 + j) * 7 + k] * dYv[9 + k];
           dY2[i] += acc * Y[1 + j];
           dY1[j] += acc * Y[4 + i];
         }
@@ -173,7 +186,7 @@ __global__ void k_edge_bwd(EdgeParams p) {
         for (int j = 0; j < 3; ++j) {
           float acc = 0.f;
 #pragma unroll
-          for (int k = 0; k < 5; ++k) acc += __ldg(p.sh_T + (i * 3 + j) * 5 + k) * dY2[k];
+          for (int k = 0; k < 5; ++k) acc += sT[(i * 3 + j) * 5 + k] * dY2[k];
           dY1[i] += acc * Y[1 + j];
           dY1[j] += acc * Y[1 + i];
         }

@@ -65,6 +65,7 @@ struct LayerBufs {
 
 struct mace_ctx {
   int device = 0;
+  int sm_count = 0;  // multiprocessors of the device (queried on first use)
   mace_model_desc desc{};
   float* d_floats = nullptr;
   int32_t* d_ints = nullptr;
@@ -136,7 +137,7 @@ struct mace_ctx {
   cudaStream_t cap_stream = nullptr;
   // second stream for the radial-MLP chain (forked from and joined into the step's stream)
   cudaStream_t aux = nullptr;
-  static constexpr int NEV = 4 * MACE_MAX_LAYERS + 4;
+  static constexpr int NEV = 6 * MACE_MAX_LAYERS + 4;  // indices up to 4 + 5 T (forward_backward)
   cudaEvent_t fork_ev[NEV] = {};
   // per-layer dW buffers (when the whole list fits one chunk), so that one
   // layer's MLP backward can overlap the next layer's conv backward
@@ -455,6 +456,21 @@ MlpParams mlp_params(mace_ctx* c, int t, int64_t e0, int64_t ne) {
   return p;
 }
 
+// MLP launch over edges [e0, e0 + ne) of the whole-list buffers (e0 a multiple
+// of the 128-edge tile): its rows of every per-edge array and its tiles of
+// the radial weights and their gradient
+MlpParams mlp_params_tiles(mace_ctx* c, int t, int64_t e0, int64_t ne) {
+  MlpParams p = mlp_params(c, t, e0, ne);
+  const mace_layer_desc& L = c->desc.layers[t];
+  int64_t act_row = 0;
+  for (int j = 1; j < L.n_mlp; ++j) act_row += L.mlp_w[j];
+  const int64_t tile_floats = (int64_t)wt_nchunk(L.mlp_w[L.n_mlp]) * WT_CHUNK;
+  p.act += e0 * act_row;
+  p.out += (e0 / WT_TILE) * tile_floats;
+  p.dout += (e0 / WT_TILE) * tile_floats;
+  return p;
+}
+
 ScParams sc_params(mace_ctx* c, int t, int64_t N, const int32_t* species, const float* f, float* out,
                    const float* dout, float* df) {
   const mace_layer_desc& L = c->desc.layers[t];
@@ -569,8 +585,22 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
       if (!e) MACE_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
   }
   cudaStream_t sa = fork ? c->aux : s;
+  // Layer 0's radial MLP and conv in two parts each when its tiles exceed one
+  // round of MLP CTAs (two per SM): forward, the first round of tiles, then
+  // the conv of the receivers whose edges it covers beside the remaining
+  // tiles, then the other receivers; backward, the conv of the receivers
+  // below the split, then the MLP of those tiles beside the other receivers'
+  // conv, then one round of MLP tiles.  The serial MLP work at the start and
+  // the end of the step shrinks to about one tile each.
+  if (fork && c->sm_count == 0)
+    MACE_CUDA_TRY(cudaDeviceGetAttribute(&c->sm_count, cudaDevAttrMultiProcessorCount, c->device));
+  const int64_t mlp_round = 2 * (int64_t)c->sm_count;  // MLP tiles resident at once
+  const int64_t ntile0 = (EA + WT_TILE - 1) / WT_TILE;
+  const bool split0 = fork && ntile0 > mlp_round;
+  const int64_t e_split_f = split0 ? mlp_round * WT_TILE : 0;             // forward: first round of tiles
+  const int64_t e_split_b = split0 ? (ntile0 - mlp_round) * WT_TILE : 0;  // backward: the last round after
   // events: 0 edges ready; 1+t mlp_fwd(t); 1+T+t conv_bwd(t); 1+2T last mlp_bwd;
-  // 2+2T+t dh[t+1] final; 2+3T+t skip_bwd(t) done
+  // 2+2T+t dh[t+1] final; 2+3T+t skip_bwd(t) done; 2+4T+t conv_fwd(t) done; 2+5T readouts done
   cudaEvent_t* ev = c->fork_ev;
   const int T = d.num_layers;
   const int C = d.C;
@@ -656,19 +686,25 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
     np.pair = c->e_layers + (int64_t)d.num_layers * N;
     LAUNCH("node_sums", -1, launch_node_sums(np, s));
   }
-  // The MLP chain of every layer's forward is issued at once (the MLP kernels
-  // hold their SMs for a whole 128-edge tile, so whatever runs beside them
-  // slows down; issuing mlp_fwd(t) after conv_fwd(t-1), mlp_bwd(t) beside
-  // conv_bwd(t-1), or a later layer's MLP as two launches of half the tiles
-  // measured no faster on Si1000).
+  // Layer 0's radial MLP starts as soon as the edge features exist; a later
+  // layer's starts once the previous layer's conv is done (below).  The MLP
+  // CTAs (two per SM, most of its registers and shared memory) leave no room
+  // for conv CTAs, so beside a conv they only delay it; beside the node ops
+  // of the previous layer (latency-bound, on few SMs) they cost little.
   if (fork) {
     MACE_CUDA_TRY(cudaEventRecord(ev[0], s));
     MACE_CUDA_TRY(cudaStreamWaitEvent(sa, ev[0], 0));
-    for (int t = 0; t < T; ++t) {
-      MlpParams mp = mlp_params(c, t, 0, EA);
-      LAUNCH_ON(sa, "mlp_fwd", t, launch_mlp_fwd(mp, sa));
-      MACE_CUDA_TRY(cudaEventRecord(ev[1 + t], sa));
+    if (split0) {
+      MlpParams ma = mlp_params_tiles(c, 0, 0, e_split_f);
+      LAUNCH_ON(sa, "mlp_fwd", 0, launch_mlp_fwd(ma, sa));
+      MACE_CUDA_TRY(cudaEventRecord(ev[3 + 5 * T], sa));
+      MlpParams mb = mlp_params_tiles(c, 0, e_split_f, EA - e_split_f);
+      LAUNCH_ON(sa, "mlp_fwd", 0, launch_mlp_fwd(mb, sa));
+    } else {
+      MlpParams mp = mlp_params(c, 0, 0, EA);
+      LAUNCH_ON(sa, "mlp_fwd", 0, launch_mlp_fwd(mp, sa));
     }
+    MACE_CUDA_TRY(cudaEventRecord(ev[1], sa));
   }
   {
     EmbedParams p{N, C, sys->species, F(c, d.f_emb), c->h[0]};
@@ -700,14 +736,32 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
       }
       LAUNCH("linear_up+skip", t, launch_linear(lp, s));
     }
-    if (fork) MACE_CUDA_TRY(cudaStreamWaitEvent(s, ev[1 + t], 0));
-    for (const Chunk& ch : chunks) {
-      MlpParams mp = mlp_params(c, t, ch.e0, ch.e1 - ch.e0);
-      if (!fork && ch.e1 > ch.e0) LAUNCH("mlp_fwd", t, launch_mlp_fwd(mp, s));
-      ConvParams cp = conv_params(c, t, ch.n1, sys);
-      cp.n0 = ch.n0;
-      cp.e0 = ch.e0;
-      LAUNCH("conv_fwd", t, launch_conv_fwd(cp, s));
+    if (t == 0 && split0) {
+      ConvParams cp = conv_params(c, 0, NA, sys);
+      cp.e_split = e_split_f;
+      cp.split_part = 1;
+      MACE_CUDA_TRY(cudaStreamWaitEvent(s, ev[3 + 5 * T], 0));
+      LAUNCH("conv_fwd", 0, launch_conv_fwd(cp, s));
+      cp.split_part = 2;
+      MACE_CUDA_TRY(cudaStreamWaitEvent(s, ev[1], 0));
+      LAUNCH("conv_fwd", 0, launch_conv_fwd(cp, s));
+    } else {
+      if (fork) MACE_CUDA_TRY(cudaStreamWaitEvent(s, ev[1 + t], 0));
+      for (const Chunk& ch : chunks) {
+        MlpParams mp = mlp_params(c, t, ch.e0, ch.e1 - ch.e0);
+        if (!fork && ch.e1 > ch.e0) LAUNCH("mlp_fwd", t, launch_mlp_fwd(mp, s));
+        ConvParams cp = conv_params(c, t, ch.n1, sys);
+        cp.n0 = ch.n0;
+        cp.e0 = ch.e0;
+        LAUNCH("conv_fwd", t, launch_conv_fwd(cp, s));
+      }
+    }
+    if (fork && t + 1 < T) {
+      MACE_CUDA_TRY(cudaEventRecord(ev[2 + 4 * T + t], s));
+      MACE_CUDA_TRY(cudaStreamWaitEvent(sa, ev[2 + 4 * T + t], 0));
+      MlpParams mp = mlp_params(c, t + 1, 0, EA);
+      LAUNCH_ON(sa, "mlp_fwd", t + 1, launch_mlp_fwd(mp, sa));
+      MACE_CUDA_TRY(cudaEventRecord(ev[2 + t], sa));
     }
     {
       LinParams lp{};
@@ -780,7 +834,15 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
     p.node_energy = out ? out->node_energy : nullptr;
     p.energy = out ? out->energy : nullptr;
     p.weight = sys->energy_weight;
-    LAUNCH("energy", -1, launch_energy(p, s));
+    if (fork && want_grad) {
+      // nothing in the backward reads the energies: the assembly runs on the
+      // second stream (joined with it at the end of the step)
+      MACE_CUDA_TRY(cudaEventRecord(ev[2 + 5 * T], s));
+      MACE_CUDA_TRY(cudaStreamWaitEvent(sa, ev[2 + 5 * T], 0));
+      LAUNCH_ON(sa, "energy", -1, launch_energy(p, sa));
+    } else {
+      LAUNCH("energy", -1, launch_energy(p, s));
+    }
   }
   if (!want_grad) return MACE_OK;
 
@@ -852,6 +914,27 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
       cp.e0 = ch.e0;
       bool gather = false;
       cp.n_active = NA < N ? NA : 0;
+      if (t == 0 && split0) {
+        // receivers whose first edge is below the split, then those tiles' MLP
+        // backward beside the other receivers' conv, then the last round of tiles
+        cp.e_split = e_split_b;
+        cp.split_first = 1;
+        cp.split_part = 1;
+        LAUNCH("conv_bwd", 0, launch_conv_bwd(cp, s, &gather));
+        MACE_CUDA_TRY(cudaEventRecord(ev[4 + 5 * T], s));
+        MACE_CUDA_TRY(cudaStreamWaitEvent(sa, ev[4 + 5 * T], 0));
+        MlpParams ma = mlp_params_tiles(c, 0, 0, e_split_b);
+        LAUNCH_ON(sa, "mlp_bwd", 0, launch_mlp_bwd(ma, sa));
+        bool gather2 = false;
+        cp.split_part = 2;
+        LAUNCH("conv_bwd", 0, launch_conv_bwd(cp, s, &gather2));
+        need_gather = need_gather || gather || gather2;
+        MACE_CUDA_TRY(cudaEventRecord(ev[1 + T], s));
+        MACE_CUDA_TRY(cudaStreamWaitEvent(sa, ev[1 + T], 0));
+        MlpParams mb = mlp_params_tiles(c, 0, e_split_b, EA - e_split_b);
+        LAUNCH_ON(sa, "mlp_bwd", 0, launch_mlp_bwd(mb, sa));
+        continue;
+      }
       LAUNCH("conv_bwd", t, launch_conv_bwd(cp, s, &gather));
       if (NA < N && t > 0 && !gather)
         return fail(MACE_ERR_UNSUPPORTED, "n_active needs the per-edge sender terms of the conv backward (one radial "
