@@ -292,3 +292,23 @@ def test_profiler_eager_and_in_graph():
         assert all(t["end_ms"] >= t["start_ms"] >= 0 for t in tl)
         seen[graph] = {(r["name"], r["layer"]) for r in rows}
     assert seen[False] == seen[True]
+
+
+def test_two_stream_schedule_matches_single_stream(monkeypatch):
+    """The two-stream step (radial MLP on a second stream; layer 0's MLP and
+    conv in two parts each when the edge tiles exceed one round of MLP CTAs)
+    runs the same per-edge and per-receiver arithmetic in the same
+    accumulation order as the single-stream step: identical results.
+    Si 6x6x6 (1728 atoms, ~80 000 edges) has more than two tiles per SM."""
+    st = diamond_si(6, 0.05, 61)
+    config, weights, _ = make_case("medium", st, seed=61, avg_num_neighbors=44.0)
+    m2 = MACEModel(config=config, weights=weights, device=0)
+    monkeypatch.setenv("MACE_B200_SINGLE_STREAM", "1")
+    m1 = MACEModel(config=config, weights=weights, device=0)
+    a, edges, _ = run_gpu(m2, st)
+    b, _, _ = run_gpu(m1, st)
+    n_tiles = (edges.n_edges + 127) // 128
+    assert n_tiles > 2 * torch.cuda.get_device_properties(0).multi_processor_count
+    for k in ("energy", "node_energy", "forces", "stress"):
+        np.testing.assert_array_equal(a[k], b[k], err_msg=k)
+    assert m2.error_flag() == 0 and m1.error_flag() == 0
