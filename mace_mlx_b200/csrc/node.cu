@@ -499,6 +499,8 @@ int launch_sc_bwd(const ScParams& p, cudaStream_t s) {
 int launch_readout(const ReadoutParams& p, cudaStream_t s) {
   if (p.N == 0) return MACE_OK;
   if (p.nonlinear && p.hidden > 32) return fail(MACE_ERR_UNSUPPORTED, "readout hidden width must be <= 32");
+  // the non-linear readout holds a node's scalar row in four registers a lane
+  if (p.nonlinear && p.C > 128) return fail(MACE_ERR_UNSUPPORTED, "non-linear readout: C must be <= 128");
   int64_t threads = p.N * 32;
   k_readout<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(p);
   MACE_LAUNCH_CHECK("readout");
