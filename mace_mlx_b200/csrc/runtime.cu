@@ -599,8 +599,9 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
   const bool split0 = fork && ntile0 > mlp_round;
   const int64_t e_split_f = split0 ? mlp_round * WT_TILE : 0;             // forward: first round of tiles
   const int64_t e_split_b = split0 ? (ntile0 - mlp_round) * WT_TILE : 0;  // backward: the last round after
-  // events: 0 edges ready; 1+t mlp_fwd(t); 1+T+t conv_bwd(t); 1+2T last mlp_bwd;
-  // 2+2T+t dh[t+1] final; 2+3T+t skip_bwd(t) done; 2+4T+t conv_fwd(t) done; 2+5T readouts done
+  // events: 0 step start (the second stream's edge front end waits on it);
+  // 1+t mlp_fwd(t); 1+T+t conv_bwd(t); 1+2T last mlp_bwd; 2+2T+t dh[t+1] final; 2+3T+t skip_bwd(t) done; 2+4T+t conv_fwd(t) done; 2+5T readouts done;
+  // 3+5T first MLP part done; 4+5T first conv_bwd part done
   cudaEvent_t* ev = c->fork_ev;
   const int T = d.num_layers;
   const int C = d.C;
@@ -660,7 +661,17 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
     MACE_CUDA_TRY(cudaMemsetAsync(c->e_layers, 0, sizeof(float) * (size_t)(T + 1) * N, s));
     MACE_CUDA_TRY(cudaMemsetAsync(c->ddens, 0, sizeof(float) * (size_t)T * N, s));
   }
-  if (E > 0) LAUNCH("edge_fwd", -1, launch_edge_fwd(ep, s));
+  // In the two-stream step the edge front end (and the per-receiver sums built
+  // on it) runs on the second stream ahead of the radial MLP, so that the
+  // embedding and layer 0's linear_up run beside it on the main stream instead
+  // of waiting for SMs the MLP holds.
+  cudaStream_t se = s;
+  if (fork) {
+    MACE_CUDA_TRY(cudaEventRecord(ev[0], s));
+    MACE_CUDA_TRY(cudaStreamWaitEvent(sa, ev[0], 0));
+    se = sa;
+  }
+  if (E > 0) LAUNCH_ON(se, "edge_fwd", -1, launch_edge_fwd(ep, se));
   if (ep.n_dens > 0 || d.zbl) {
     // per-receiver densities of the density-normalised layers and ZBL pair energies
     NodeSumParams np{};
@@ -684,7 +695,7 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
     np.zbl_radius = d.zbl ? F(c, d.f_radius_zbl) : nullptr;
     np.znum = d.zbl ? F(c, d.f_znum) : nullptr;
     np.pair = c->e_layers + (int64_t)d.num_layers * N;
-    LAUNCH("node_sums", -1, launch_node_sums(np, s));
+    LAUNCH_ON(se, "node_sums", -1, launch_node_sums(np, se));
   }
   // Layer 0's radial MLP starts as soon as the edge features exist; a later
   // layer's starts once the previous layer's conv is done (below).  The MLP
@@ -692,8 +703,6 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
   // for conv CTAs, so beside a conv they only delay it; beside the node ops
   // of the previous layer (latency-bound, on few SMs) they cost little.
   if (fork) {
-    MACE_CUDA_TRY(cudaEventRecord(ev[0], s));
-    MACE_CUDA_TRY(cudaStreamWaitEvent(sa, ev[0], 0));
     if (split0) {
       MlpParams ma = mlp_params_tiles(c, 0, 0, e_split_f);
       LAUNCH_ON(sa, "mlp_fwd", 0, launch_mlp_fwd(ma, sa));
