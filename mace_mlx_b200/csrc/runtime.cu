@@ -600,7 +600,8 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
   const int64_t e_split_f = split0 ? mlp_round * WT_TILE : 0;             // forward: first round of tiles
   const int64_t e_split_b = split0 ? (ntile0 - mlp_round) * WT_TILE : 0;  // backward: the last round after
   // events: 0 step start (the second stream's edge front end waits on it);
-  // 1+t mlp_fwd(t); 1+T+t conv_bwd(t); 1+2T last mlp_bwd; 2+2T+t dh[t+1] final; 2+3T+t skip_bwd(t) done; 2+4T+t conv_fwd(t) done; 2+5T readouts done;
+  // 1+t mlp_fwd(t); 1+T+t conv_bwd(t); 1+2T last mlp_bwd; 2+2T+t dh[t+1] final;
+  // 2+3T+t skip_bwd(t) done; 2+4T+t conv_fwd(t) done; 2+5T readouts done;
   // 3+5T first MLP part done; 4+5T first conv_bwd part done
   cudaEvent_t* ev = c->fork_ev;
   const int T = d.num_layers;
