@@ -88,11 +88,9 @@ class MACEMLXCalculator(Calculator):
         super().__init__(**kwargs)
         self._device = _resolve_device(device)
         model_dir = self._resolve_model(str(model_path))
-        self.model = MACEModel(model_dir, device=self._device)
-        self._head = head
-        heads = self.model.config.get("heads")
-        if head is not None and heads and head not in heads:
-            raise ValueError(f"Head '{head}' not found in model heads: {heads}")
+        # multi-head models: the named head, else the first (an unknown name raises ValueError)
+        self.model = MACEModel(model_dir, device=self._device, head=head)
+        self._head = self.model.head if len(self.model.heads) > 1 else head
         self.r_max = float(self.model.r_max)
         self.z_table = self.model.z_table
         self._skin = float(skin)

@@ -157,10 +157,11 @@ __device__ __forceinline__ void mma_k64_ta(uint32_t tmem_d, uint32_t a_hi, uint3
 
 // One CTA per 128-edge tile, 8 epilogue warps + 1 control warp, two CTAs per SM.
 // The activation operand A lives in TMEM (written with tcgen05.st), so shared
-// memory only holds the weight images (four chunk stages, refilled three
-// chunks ahead) and one 4 KB output staging slice per epilogue warp, whose
-// bulk store drains while the warp's group waits for its next chunk.  The
-// epilogue warp groups take alternate chunks.
+// memory only holds the weight images (two 64-column chunk stages, each
+// refilled as soon as the MMA that read it completes) and one 4 KB output
+// staging slice per epilogue warp, whose bulk store drains while the warp's
+// group waits for its next chunk.  Each 64-column chunk accumulates into one
+// of two TMEM buffers; epilogue group g drains its 32-column half 2c + g.
 template <int NB>
 __global__ void __maxnreg__(96) k_mlp_fwd_tc(MlpParams p) {
   extern __shared__ __align__(1024) unsigned char sm[];

@@ -79,13 +79,17 @@ def _ptr(t: torch.Tensor | None) -> int | None:
 
 class MACEModel:
     def __init__(self, model_dir: str | os.PathLike | None = None, *, config: dict | None = None,
-                 weights: dict | None = None, device: int | str | torch.device = 0):
+                 weights: dict | None = None, device: int | str | torch.device = 0, head: str | None = None):
+        """``head``: the head of a multi-head model whose energies are computed
+        (default: the first); an unknown name raises ``ValueError``."""
         if model_dir is not None:
             config, weights = load_model_dir(model_dir)
         if config is None or weights is None:
             raise ValueError("give a model directory or (config, weights)")
         self.config = config
-        self.spec = ModelSpec.from_config(config)
+        self.spec = ModelSpec.from_config(config, head=head)
+        self.heads = self.spec.heads
+        self.head = self.spec.heads[self.spec.head_idx]
         check_weights(self.spec, weights)
         dev = torch.device(device) if not isinstance(device, int) else torch.device("cuda", device)
         if dev.type != "cuda":

@@ -352,20 +352,27 @@ def _layer(spec: ModelSpec, lay: LayerSpec, w: dict, tb: _Tables) -> nv.LayerDes
         W = w[f"products.{t}.linear.weights.{q}"].astype(np.float64) * ins.path_weight
         d.f_prod[q] = tb.addf(W)
         d.f_prod_t[q] = tb.addf(W.T)
-    # readout
+    # readout: the selected head's column.  A multi-head non-linear readout masks
+    # its 16 H hidden scalars to the head's block of 16 before linear_2
+    # (blocks.py:602-609), so it equals a 16-wide readout on that block's
+    # linear_1 columns and linear_2 rows, keeping linear_2's 1/sqrt(16 H) path weight.
+    h = spec.head_idx
     if lay.readout_linear is not None:
         (ins,) = lay.readout_linear.instrs
         if ins.i_in != 0:
             raise UnsupportedModel("linear readout must read the scalar slot")
         d.readout_nonlinear = 0
-        d.f_ro1 = tb.addf(w[f"readouts.{t}.linear.weights.0"][:, 0].astype(np.float64) * ins.path_weight)
+        d.f_ro1 = tb.addf(w[f"readouts.{t}.linear.weights.0"][:, h].astype(np.float64) * ins.path_weight)
     else:
         (i1,) = lay.readout_1.instrs
         (i2,) = lay.readout_2.instrs
+        fph = i1.mul_out // spec.num_heads
+        rows = slice(h * fph, (h + 1) * fph)
         d.readout_nonlinear = 1
-        d.readout_hidden = i1.mul_out
-        d.f_ro1 = tb.addf(w[f"readouts.{t}.linear_1.weights.0"].astype(np.float64) * i1.path_weight)
-        d.f_ro2 = tb.addf(w[f"readouts.{t}.linear_2.weights.0"][:, 0].astype(np.float64) * i2.path_weight)
+        d.readout_hidden = fph
+        w1 = w[f"readouts.{t}.linear_1.weights.0"][:, rows].astype(np.float64) * i1.path_weight
+        d.f_ro1 = tb.addf(np.ascontiguousarray(w1))
+        d.f_ro2 = tb.addf(w[f"readouts.{t}.linear_2.weights.0"][rows, h].astype(np.float64) * i2.path_weight)
     # density normalisation: density_fn = bias-free Linear(num_bessel -> 1), weight (1, num_bessel)
     d.density = int(lay.density)
     d.f_density = tb.addf(w[f"interactions.{t}.density_fn.weight"].reshape(-1)) if lay.density else -1
@@ -394,8 +401,8 @@ class PackedModel:
         d.inv_avg_num_neighbors = 1.0 / spec.avg_num_neighbors
         d.scale = spec.scale
         d.shift = spec.shift
-        ae = np.asarray(weights.get("atomic_energies_fn.atomic_energies", spec.atomic_energies), dtype=np.float64)
-        d.f_e0 = tb.addf(ae.reshape(-1)[-spec.num_elements:])
+        ae = weights.get("atomic_energies_fn.atomic_energies", spec.atomic_energies)
+        d.f_e0 = tb.addf(spec.head_atomic_energies(ae))
         d.f_emb = tb.addf(weights["node_embedding.linear.weights.0"].astype(np.float64) / math.sqrt(spec.num_elements))
         d.f_bessel = tb.addf(weights["radial_embedding.bessel_fn.bessel_weights"])
         d.f_sh = tb.addf(np.concatenate([sh_coupling(2).ravel(), sh_coupling(3).ravel()]))

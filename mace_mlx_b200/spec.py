@@ -17,6 +17,10 @@ reference's module tree so that a ``weights.npz`` written for the reference
 * density-normalised blocks (``use_density_normalization``): ``blocks.py:282-490``
   (``density_fn`` = bias-free Linear(num_bessel -> 1) per layer)
 * Agnesi distance transform (``distance_transform``): ``radial.py:202-262``
+* multi-head models (``heads``): readouts of ``H x 0e`` and a ``16 H x 0e``
+  non-linear readout MLP (``model.py:89-93, 135-138``, ``blocks.py:553-609``),
+  per-head atomic energies and scale/shift (``model.py:302-326, 518-548``),
+  head chosen by name (``calculators.py:128-137``)
 * ZBL pair repulsion (``pair_repulsion``): ``radial.py:127-199``, wired in
   ``model.py:154-173, 213-231``
 """
@@ -244,6 +248,26 @@ class LayerSpec:
     readout_2: LinearSpec | None = None
 
 
+def resolve_head(heads: list[str], head: str | None) -> int:
+    """Index of the selected head: the first by default; a name that is not one
+    of a multi-head model's heads raises ``ValueError`` (``calculators.py:128-137``;
+    a single-head model ignores the name, as there)."""
+    if len(heads) == 1 or head is None:
+        return 0
+    if head not in heads:
+        raise ValueError(f"Head '{head}' not found in model heads: {heads}")
+    return heads.index(head)
+
+
+def _per_head(v, head_idx: int) -> float:
+    """A scale or shift entry: a scalar, or one value per head where a head past
+    the list's end takes the first (``model.py:527-548``)."""
+    if isinstance(v, (list, tuple)):
+        vals = [float(x) for x in v]
+        return vals[head_idx] if head_idx < len(vals) else vals[0]
+    return float(v)
+
+
 @dataclass
 class ModelSpec:
     config: dict
@@ -261,13 +285,30 @@ class ModelSpec:
     scale: float
     shift: float
     z_table: list[int] | None
-    atomic_energies: np.ndarray
+    atomic_energies: np.ndarray  # (num_elements,), or (num_heads, num_elements)
     irreps_sh: Irreps
     interaction_irreps: Irreps
     layers: list[LayerSpec] = field(default_factory=list)
     density: bool = False
     agnesi: dict | None = None  # {"q", "p", "a", "covalent_radii" (indexed by Z)}
     zbl: dict | None = None  # {"p", "a_exp", "a_prefactor", "covalent_radii" (indexed by Z)}
+    heads: list[str] = field(default_factory=lambda: ["Default"])
+    head_idx: int = 0  # the selected head; scale / shift above are already that head's
+
+    @property
+    def num_heads(self) -> int:
+        return len(self.heads)
+
+    def head_atomic_energies(self, ae) -> np.ndarray:
+        """The selected head's per-element energies from a 1-D or (heads, elements)
+        table: column ``head`` of ``onehot @ ae.T`` (``blocks.py:53-65``,
+        ``model.py:315-326``)."""
+        a = np.atleast_2d(np.asarray(ae, dtype=np.float64))
+        if self.num_heads == 1:
+            return a.reshape(-1)[-self.num_elements:]
+        if a.shape != (self.num_heads, self.num_elements):
+            raise UnsupportedModel(f"atomic energies of shape {a.shape} for {self.num_heads} heads")
+        return a[self.head_idx]
 
     def species_numbers(self) -> list[int]:
         """Atomic number of every model element index (z_table)."""
@@ -277,7 +318,8 @@ class ModelSpec:
 
     # ------------------------------------------------------------------
     @staticmethod
-    def from_config(config: dict) -> "ModelSpec":
+    def from_config(config: dict, head: str | None = None) -> "ModelSpec":
+        """``head``: the head name of a multi-head model (default: its first head)."""
         cfg = dict(config)
         model_type = cfg.get("model_type", "ScaleShiftMACE")
         density = bool(cfg.get("use_density_normalization", False))
@@ -298,9 +340,8 @@ class ModelSpec:
             raise UnsupportedModel("agnostic product blocks are not supported yet")
         if cfg.get("apply_cutoff", True) is False:
             raise UnsupportedModel("apply_cutoff=False models are not supported yet")
-        heads = cfg.get("heads")
-        if heads and len(heads) > 1:
-            raise UnsupportedModel("multi-head models are not supported yet")
+        heads = [str(h) for h in (cfg.get("heads") or ["Default"])]
+        head_idx = resolve_head(heads, head)
         inter_cls = cfg.get("interaction_cls", "RealAgnosticResidualInteractionBlock")
         if inter_cls not in SUPPORTED_INTERACTIONS:
             raise UnsupportedModel(f"interaction block {inter_cls} is not supported yet")
@@ -322,10 +363,10 @@ class ModelSpec:
         first_nonres = bool(cfg.get("first_interaction_nonresidual", False))
         ae = cfg.get("atomic_energies")
         ae = np.zeros(num_elements) if ae is None else np.asarray(ae, dtype=np.float64)
-        if ae.ndim == 2:
-            if ae.shape[0] != 1:
-                raise UnsupportedModel("multi-head atomic energies are not supported yet")
+        if ae.ndim == 2 and ae.shape[0] == 1 and len(heads) == 1:
             ae = ae[0]
+        if len(heads) > 1 and (ae.ndim != 2 or ae.shape[0] != len(heads)):
+            raise UnsupportedModel(f"a {len(heads)}-head model needs one row of atomic energies per head")
 
         sh = Irreps.spherical_harmonics(max_ell)
         C = hidden[0].mul
@@ -338,16 +379,15 @@ class ModelSpec:
             config=config, r_max=r_max, num_bessel=num_bessel, poly_p=poly_p,
             max_ell=max_ell, num_interactions=T, num_elements=num_elements,
             hidden=hidden, C=C, avg_num_neighbors=avg, radial_MLP=radial_MLP,
-            model_type=model_type, scale=float(cfg.get("scale", 1.0)),
-            shift=float(cfg.get("shift", 0.0)), z_table=cfg.get("z_table"),
+            model_type=model_type, scale=_per_head(cfg.get("scale", 1.0), head_idx),
+            shift=_per_head(cfg.get("shift", 0.0), head_idx), z_table=cfg.get("z_table"),
             atomic_energies=ae, irreps_sh=sh, interaction_irreps=inter_irreps,
-            density=density, agnesi=agnesi, zbl=zbl,
+            density=density, agnesi=agnesi, zbl=zbl, heads=heads, head_idx=head_idx,
         )
         if (agnesi or zbl) and spec.z_table is None:
             raise UnsupportedModel("the distance transform / pair repulsion need the config's z_table")
-        if isinstance(spec.scale, list) or isinstance(spec.shift, list):
-            raise UnsupportedModel("per-head scale/shift is not supported yet")
 
+        H = len(heads)
         layer_in = hidden_scalar
         for t in range(T):
             layer_hidden = hidden if t < T - 1 else hidden_scalar
@@ -373,10 +413,11 @@ class ModelSpec:
                 density=density,
             )
             if t < T - 1:
-                lay.readout_linear = LinearSpec.build(layer_hidden, Irreps("1x0e"))
+                lay.readout_linear = LinearSpec.build(layer_hidden, Irreps(f"{H}x0e"))
             else:
-                lay.readout_1 = LinearSpec.build(layer_hidden, Irreps("16x0e"))
-                lay.readout_2 = LinearSpec.build(Irreps("16x0e"), Irreps("1x0e"))
+                # 16 hidden scalars per head (model.py:135-138)
+                lay.readout_1 = LinearSpec.build(layer_hidden, Irreps(f"{16 * H}x0e"))
+                lay.readout_2 = LinearSpec.build(Irreps(f"{16 * H}x0e"), Irreps(f"{H}x0e"))
             spec.layers.append(lay)
             layer_in = layer_hidden
         return spec
@@ -385,7 +426,8 @@ class ModelSpec:
     def weight_shapes(self) -> dict[str, tuple[int, ...]]:
         """Every array of the converted ``weights.npz`` with its shape."""
         s: dict[str, tuple[int, ...]] = {
-            "atomic_energies_fn.atomic_energies": (self.num_elements,),
+            "atomic_energies_fn.atomic_energies": (self.num_elements,) if self.num_heads == 1
+            else (self.num_heads, self.num_elements),
             "node_embedding.linear.weights.0": (self.num_elements, self.C),
             "radial_embedding.bessel_fn.bessel_weights": (self.num_bessel,),
         }

@@ -54,7 +54,7 @@ def check_weights(spec: ModelSpec, weights: dict[str, np.ndarray]) -> None:
         if k not in weights:
             errs.append(f"missing {k}")
         elif tuple(weights[k].shape) != tuple(sh):
-            if k == "atomic_energies_fn.atomic_energies" and weights[k].size == sh[0]:
+            if k == "atomic_energies_fn.atomic_energies" and weights[k].size == int(np.prod(sh)):
                 continue
             errs.append(f"{k}: shape {tuple(weights[k].shape)} != expected {tuple(sh)}")
     if errs:
@@ -81,11 +81,14 @@ def random_config(
     use_density_normalization: bool = False,
     distance_transform: dict | None = None,
     pair_repulsion: dict | None = None,
+    heads: list[str] | None = None,
 ) -> dict:
     """A converted-model config.  ``use_density_normalization``,
     ``distance_transform`` (Agnesi; ``{}`` for the defaults) and
     ``pair_repulsion`` (ZBL; ``{}`` for the defaults) give the mpa-0 family's
-    blocks; the converter's key layout is kept (``converter.py:167-300``)."""
+    blocks; ``heads`` (two or more names) a multi-head model, whose
+    ``atomic_energies`` are then one row per head.  The converter's key
+    layout is kept (``converter.py:167-300``)."""
     hidden = hidden_irreps or ARCHS[arch]
     if z_table is None:
         z_table = list(range(1, num_elements + 1))
@@ -112,6 +115,10 @@ def random_config(
         pr = dict(ZBL_DEFAULTS)
         pr.update(pair_repulsion)
         extra["pair_repulsion"] = pr
+    if heads is not None and len(heads) > 1:
+        extra["heads"] = [str(h) for h in heads]
+        if atomic_energies is None:
+            atomic_energies = [[0.0] * num_elements for _ in heads]
     return extra | {
         "r_max": float(r_max),
         "num_bessel": int(num_bessel),

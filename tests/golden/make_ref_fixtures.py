@@ -58,13 +58,15 @@ def _run_case(name: str, ref_root: str) -> dict:
     """One case in the current process (float mode fixed by REFSHIM_FLOAT)."""
     rmodel, rcalc, mx = _import_reference(ref_root)
     from oracle.nl import neighbour_list
-    from ref_cases import CASES, reference_inputs
+    from ref_cases import CASE_HEADS, CASES, reference_inputs
     from mace_mlx_b200.weights import write_model_dir
 
     config, weights, st, stress = CASES[name]()
     with tempfile.TemporaryDirectory() as d:
         write_model_dir(d, config, weights)
         model = rmodel.load_model(d)
+    if name in CASE_HEADS:  # as the calculator selects a head (calculators.py:128-137)
+        model._head_idx = model.heads.index(CASE_HEADS[name])
 
     n = len(st)
     periodic = bool(np.any(st.pbc))

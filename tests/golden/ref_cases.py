@@ -35,6 +35,10 @@ def _scale_shift(cfg):
     cfg["scale"], cfg["shift"] = 1.3, -0.2
 
 
+def _scale_shift_per_head(cfg):
+    cfg["scale"], cfg["shift"] = [0.8, 1.3], [0.3, -0.2]
+
+
 def _mixed_si(seed, sigma=0.05):
     st = diamond_si(2, sigma, seed)
     st.numbers[::3] = 6
@@ -73,9 +77,19 @@ CASES = {
     "mpa_si64_mixed": lambda: _case("medium", _mixed_si(21, 0.15), 7, True, z_table=[6, 14], **MPA),
     "mpa_mol8": lambda: _case("medium", molecule_batch(8, 3), 8, False, z_table=[1, 6, 7, 8], avg=12.0, r_max=5.0,
                               first_interaction_nonresidual=True, **MPA),
+    # a two-head model (multi-head fine-tuning layout): per-head E0, scale and shift, the
+    # second head selected (CASE_HEADS), two species, with stress
+    "mh2_medium_si64mixed": lambda: _case("medium", _mixed_si(9), 9, True, z_table=[14, 6], avg=30.0,
+                                          heads=["pt_head", "Default"],
+                                          atomic_energies=[[-5.1, -7.9], [-5.4, -8.1]],
+                                          model_type="ScaleShiftMACE", edit=_scale_shift_per_head),
     # BASELINE config 1 (the headline) at its full size: medium Si1000, energy + forces
     "c1_medium_si1000": lambda: _case("medium", diamond_si(5, 0.05, 1), 1, False, avg=44.0),
 }
+
+
+# the head each multi-head case selects (the reference calculator's ``head`` argument)
+CASE_HEADS = {"mh2_medium_si64mixed": "Default"}
 
 
 def digest_config(config: dict) -> str:

@@ -143,3 +143,34 @@ def test_calculate_batch_matches_one_structure_at_a_time(model_dir):
             assert_parity(mine, want, len(atoms))
     with pytest.raises(NotImplementedError):
         calc.calculate_batch(periodic, ["energy", "stress"])
+
+
+def test_multi_head_calculator_selects_the_named_head(tmp_path):
+    """``head=`` picks the head (calculators.py:128-137): the default is the first
+    head; each head's energy, forces and stress match the oracle's masked
+    multi-head readout for that head."""
+    from mace_mlx_b200.spec import ModelSpec
+    from mace_mlx_b200.weights import random_config, random_weights, write_model_dir
+
+    cfg = random_config("medium", z_table=[14, 6], avg_num_neighbors=30.0, heads=["pt_head", "Default"],
+                        atomic_energies=[[-5.1, -7.9], [-5.4, -8.1]], model_type="ScaleShiftMACE")
+    cfg["scale"], cfg["shift"] = [0.8, 1.3], [0.3, -0.2]
+    weights = random_weights(ModelSpec.from_config(cfg), 5)
+    d = str(write_model_dir(tmp_path / "mh", cfg, weights))
+    st = diamond_si(2, 0.05, 31)
+    st.numbers[::4] = 6
+    i, j, S = neighbour_list(st.positions, st.cell, st.pbc, cfg["r_max"])
+    species = np.where(st.numbers == 14, 0, 1)
+    energies = {}
+    for head in (None, "pt_head", "Default"):
+        calc = MACECalculator(model_path=d, device="cuda", head=head, skin=0.0)
+        assert calc.model.head == (head or "pt_head")
+        atoms = Atoms(st.numbers, st.positions, st.cell, True)
+        atoms.calc = calc
+        gpu = {"energy": np.array([atoms.get_potential_energy()]), "forces": atoms.get_forces().astype(np.float64),
+               "stress": atoms.get_stress(), "node_energy": calc.results["node_energy"]}
+        ref = OracleMACE(cfg, weights, head=head).compute(st.positions, species, i, j, S, st.cell, stress=True)
+        assert_parity(gpu, ref, len(st), stress=True)
+        energies[head] = float(gpu["energy"][0])
+    assert energies[None] == energies["pt_head"]
+    assert abs(energies["pt_head"] - energies["Default"]) > 1.0

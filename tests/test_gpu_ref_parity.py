@@ -7,13 +7,14 @@ must match both within the BASELINE tolerances: energy 1e-5 eV/atom, forces
 1e-4 eV/A max-abs, stress 1e-6 eV/A^3, plus the relative bounds of
 ``helpers.assert_parity``; and its neighbour list must have exactly the
 reference run's edge count.  The cases include BASELINE configs 0 and 1 at
-their full sizes and three models of the mpa-0 family."""
+their full sizes, three models of the mpa-0 family and a two-head model with
+its second head selected."""
 
 import numpy as np
 import pytest
 import torch
 
-from golden.ref_cases import CASES, digest_weights
+from golden.ref_cases import CASE_HEADS, CASES, digest_weights
 from helpers import assert_parity, run_gpu
 from mace_mlx_b200.model import MACEModel
 
@@ -27,7 +28,7 @@ def test_cuda_step_matches_reference_execution(golden_dir, name):
     config, weights, st, _ = CASES[name]()
     assert str(fx["weights_digest"]) == digest_weights(weights)
     stress = bool(fx["stress_computed"])
-    m = MACEModel(config=config, weights=weights, device=0)
+    m = MACEModel(config=config, weights=weights, device=0, head=CASE_HEADS.get(name))
     gpu, edges, _ = run_gpu(m, st, virial=stress)
     assert edges.n_edges == int(fx["n_edges"])
     for suffix in ("", "_f32"):

@@ -14,7 +14,7 @@ import numpy as np
 import pytest
 import torch
 
-from golden.ref_cases import CASES, digest_config, digest_weights
+from golden.ref_cases import CASE_HEADS, CASES, digest_config, digest_weights
 from oracle.model import OracleMACE
 from oracle.nl import neighbour_list
 
@@ -53,7 +53,7 @@ def test_oracle_equals_the_reference_execution(golden_dir, name):
     species = np.array([lut[int(z)] for z in st.numbers])
     periodic = bool(np.any(st.pbc))
     cell = fx["cell"].astype(np.float32).astype(np.float64) if periodic else None
-    res = OracleMACE(config, weights).compute(fx["positions_f32"], species, i, j, S, cell,
+    res = OracleMACE(config, weights, head=CASE_HEADS.get(name)).compute(fx["positions_f32"], species, i, j, S, cell,
                                               stress=bool(fx["stress_computed"]), batch=st.batch,
                                               num_graphs=st.num_graphs)
 

@@ -76,11 +76,103 @@ def test_check_weights_reports_mismatch():
 
 def test_unsupported_features_raise():
     cfg = random_config("small")
-    for key, val in [("heads", ["a", "b"]), ("use_agnostic_product", True), ("apply_cutoff", False),
+    for key, val in [("use_agnostic_product", True), ("apply_cutoff", False),
                      ("interaction_cls", "RealAgnosticResidualNonLinearInteractionBlock")]:
         c = dict(cfg, **{key: val})
         with pytest.raises(UnsupportedModel):
             ModelSpec.from_config(c)
+
+
+def test_multi_head_spec_shapes_and_head_selection():
+    """Multi-head layout (model.py:89-93, 135-138, converter.py:176-200): readouts of
+    H x 0e, a 16 H-wide non-linear readout, (H, elements) atomic energies; per-head
+    scale/shift (model.py:527-548); head by name (calculators.py:128-137)."""
+    cfg = random_config("medium", z_table=[14, 6], heads=["pt_head", "r2scan", "Default"],
+                        atomic_energies=[[-1.0, -2.0], [-3.0, -4.0], [-5.0, -6.0]], model_type="ScaleShiftMACE")
+    cfg["scale"], cfg["shift"] = [1.5, 2.5], [0.1, 0.2]
+    sp = ModelSpec.from_config(cfg)
+    assert sp.num_heads == 3 and sp.head_idx == 0
+    shapes = sp.weight_shapes()
+    assert shapes["atomic_energies_fn.atomic_energies"] == (3, 2)
+    assert shapes["readouts.0.linear.weights.0"] == (sp.C, 3)
+    assert shapes["readouts.1.linear_1.weights.0"] == (sp.C, 48)
+    assert shapes["readouts.1.linear_2.weights.0"] == (48, 3)
+    # linear_2's path weight keeps the full 16 H fan-in
+    assert sp.layers[1].readout_2.instrs[0].path_weight == pytest.approx(1 / np.sqrt(48))
+    check_weights(sp, random_weights(sp, 0))
+    s1 = ModelSpec.from_config(cfg, head="r2scan")
+    assert s1.head_idx == 1 and (s1.scale, s1.shift) == (2.5, 0.2)
+    np.testing.assert_array_equal(s1.head_atomic_energies(cfg["atomic_energies"]), [-3.0, -4.0])
+    s2 = ModelSpec.from_config(cfg, head="Default")  # past the scale list's end: its first entry
+    assert s2.head_idx == 2 and (s2.scale, s2.shift) == (1.5, 0.1)
+    with pytest.raises(ValueError, match="not found"):
+        ModelSpec.from_config(cfg, head="nope")
+    # a single-head model ignores the head name, as the reference's calculator does
+    assert ModelSpec.from_config(random_config("small"), head="nope").head_idx == 0
+    bad = dict(cfg, atomic_energies=[0.0, 0.0])
+    with pytest.raises(UnsupportedModel):
+        ModelSpec.from_config(bad)
+
+
+def test_multi_head_pack_slices_the_head():
+    """The packed readout of head h is linear_1's columns and linear_2's rows of
+    the head's 16-scalar block, column h, with the path weights of the full layer."""
+    from mace_mlx_b200.pack import PackedModel
+
+    cfg = random_config("medium", z_table=[14], heads=["a", "b"], atomic_energies=[[-1.0], [-2.0]])
+    sp = ModelSpec.from_config(cfg, head="b")
+    w = random_weights(sp, 2)
+    pm = PackedModel(sp, w)
+    f = pm.floats
+    d0, d1 = pm.desc.layers[0], pm.desc.layers[1]
+    C = sp.C
+    np.testing.assert_allclose(f[d0.f_ro1:d0.f_ro1 + C], w["readouts.0.linear.weights.0"][:, 1] / np.sqrt(C),
+                               rtol=1e-6)
+    assert d1.readout_hidden == 16
+    w1 = w["readouts.1.linear_1.weights.0"][:, 16:32] / np.sqrt(C)
+    np.testing.assert_allclose(f[d1.f_ro1:d1.f_ro1 + C * 16].reshape(C, 16), w1, rtol=1e-6)
+    np.testing.assert_allclose(f[d1.f_ro2:d1.f_ro2 + 16], w["readouts.1.linear_2.weights.0"][16:32, 1] / np.sqrt(32),
+                               rtol=1e-6)
+    assert f[pm.desc.f_e0] == np.float32(-2.0)
+
+
+def test_masked_multi_head_readout_equals_the_sliced_single_head_model():
+    """The identity the packed readout relies on, in the float64 oracle: head h of
+    a two-head model (masked 32-scalar readout, blocks.py:602-609) equals a
+    single-head model holding the head's weight slices, linear_2 rescaled from the
+    1/sqrt(32) path weight to the single-head 1/sqrt(16)."""
+    from mace_mlx_b200.structures import diamond_si
+    from oracle.model import OracleMACE
+    from oracle.nl import neighbour_list
+
+    cfg = random_config("small", z_table=[14], heads=["a", "b"], atomic_energies=[[-1.0], [-2.0]],
+                        model_type="ScaleShiftMACE", avg_num_neighbors=20.0)
+    cfg["scale"], cfg["shift"] = [0.7, 1.2], [0.1, -0.3]
+    w = random_weights(ModelSpec.from_config(cfg), 4)
+    st = diamond_si(1, 0.05, 3)
+    i, j, S = neighbour_list(st.positions, st.cell, st.pbc, cfg["r_max"])
+    sp = np.zeros(len(st), int)
+    h = 1
+    one = {k: v for k, v in cfg.items() if k != "heads"}
+    one["atomic_energies"], one["scale"], one["shift"] = cfg["atomic_energies"][h], cfg["scale"][h], cfg["shift"][h]
+    w1 = dict(w)
+    w1["atomic_energies_fn.atomic_energies"] = w["atomic_energies_fn.atomic_energies"][h]
+    w1["readouts.0.linear.weights.0"] = w["readouts.0.linear.weights.0"][:, h:h + 1]
+    w1["readouts.1.linear_1.weights.0"] = w["readouts.1.linear_1.weights.0"][:, 16 * h:16 * h + 16]
+    w1["readouts.1.linear_2.weights.0"] = w["readouts.1.linear_2.weights.0"][16 * h:16 * h + 16, h:h + 1] * np.sqrt(0.5)
+    multi = OracleMACE(cfg, w, head="b").compute(st.positions, sp, i, j, S, st.cell, stress=True)
+    single = OracleMACE(one, w1).compute(st.positions, sp, i, j, S, st.cell, stress=True)
+    for k in ("energy", "node_energy", "forces", "stress"):
+        np.testing.assert_allclose(multi[k], single[k], rtol=1e-10, atol=1e-12)
+
+
+def test_unknown_head_raises_before_any_device_work():
+    from mace_mlx_b200.model import MACEModel
+
+    cfg = random_config("small", z_table=[14], heads=["a", "b"], atomic_energies=[[-1.0], [-2.0]])
+    w = random_weights(ModelSpec.from_config(cfg), 0)
+    with pytest.raises(ValueError, match="not found in model heads"):
+        MACEModel(config=cfg, weights=w, device=0, head="c")
 
 
 def test_mpa_family_config_and_weight_layout():
