@@ -575,8 +575,11 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
   const bool fork = !recompute && EA > 0 && !sys->halo && c->dw_layer[0] != nullptr && !c->single_stream;
   if (fork) {
     if (!c->aux) {
-      // lowest priority: when both streams have CTAs waiting, the node/conv
-      // chain (the step's critical path) is scheduled first
+      // lowest priority: in eager launches, when both streams have CTAs
+      // waiting, the node/conv chain (the step's critical path) is scheduled
+      // first.  A replayed graph runs every node at the priority of the
+      // stream it is launched into (instantiated without the per-node
+      // priority flag, which measured 3 % slower on Si1000).
       int least = 0, greatest = 0;
       MACE_CUDA_TRY(cudaDeviceGetStreamPriorityRange(&least, &greatest));
       MACE_CUDA_TRY(cudaStreamCreateWithPriority(&c->aux, cudaStreamNonBlocking, least));
@@ -1355,7 +1358,8 @@ int mace_forward_backward(mace_ctx* c, const mace_system* sys, const mace_output
   if (!same) {
     drop_graph(c);
     if (!c->cap_stream) {
-      // highest priority, which the captured kernel nodes keep in the graph
+      // highest priority; the captured nodes record it, but the graph is
+      // instantiated without per-node priorities (see the second stream above)
       int least = 0, greatest = 0;
       MACE_CUDA_TRY(cudaDeviceGetStreamPriorityRange(&least, &greatest));
       MACE_CUDA_TRY(cudaStreamCreateWithPriority(&c->cap_stream, cudaStreamNonBlocking, greatest));
