@@ -335,6 +335,10 @@ def _layer(spec: ModelSpec, lay: LayerSpec, w: dict, tb: _Tables) -> nv.LayerDes
                 Ws.append(w[f"{pre}.weights_max"])
             else:
                 Ws.append(w[f"{pre}.weights.{out.correlation - 1 - nu}"])
+        if lay.sc.num_elements == 1 and spec.num_elements > 1:
+            # species-agnostic product (one weight set, blocks.py:527-531): every
+            # element's row holds it, so the species-indexed kernels apply it to all nodes
+            Ws = [np.repeat(np.asarray(W), spec.num_elements, axis=0) for W in Ws]
         so.i_ent, so.f_G, so.n_ent = _sc_tables(out.U, Ws, so.L, tb)
         ent, G = sc_polynomial(out.U, Ws, so.L)
         sc_outs.append((ent, G, d.hid.off[o] // C))

@@ -12,7 +12,9 @@ reference's module tree so that a ``weights.npz`` written for the reference
 * o3.Linear instructions: ``linear.py:41-77`` (outer loop over input slots,
   inner over output slots, path weight ``1/sqrt(sum mul_in)`` per output)
 * skip_tp (FullyConnectedTensorProduct, uvw): ``tensor_product.py:1046-1110``
-* symmetric contraction weights: ``symmetric_contraction.py:159-261``
+* symmetric contraction weights: ``symmetric_contraction.py:159-261``; one
+  weight set for every element under ``use_agnostic_product`` (``model.py:250-258``,
+  ``blocks.py:510, 527-531``)
 * readouts: ``blocks.py:540-608``
 * density-normalised blocks (``use_density_normalization``): ``blocks.py:282-490``
   (``density_fn`` = bias-free Linear(num_bessel -> 1) per layer)
@@ -336,8 +338,8 @@ class ModelSpec:
                    "a_prefactor": float(pr.get("a_prefactor", ZBL_DEFAULTS["a_prefactor"]))}
             # the reference reads ase.data.covalent_radii at run time (radial.py:150-152)
             zbl["covalent_radii"] = list(COVALENT_RADII)
-        if cfg.get("use_agnostic_product"):
-            raise UnsupportedModel("agnostic product blocks are not supported yet")
+        # species-agnostic product: one symmetric-contraction weight set (model.py:250-258)
+        agnostic = bool(cfg.get("use_agnostic_product", False))
         if cfg.get("apply_cutoff", True) is False:
             raise UnsupportedModel("apply_cutoff=False models are not supported yet")
         heads = [str(h) for h in (cfg.get("heads") or ["Default"])]
@@ -407,7 +409,7 @@ class ModelSpec:
                 conv=conv,
                 mlp_widths=[num_bessel, *radial_MLP, conv.weight_numel],
                 linear=LinearSpec.build(conv.irreps_mid, inter_irreps),
-                sc=SCSpec.build(inter_irreps, layer_hidden, corr[t], num_elements),
+                sc=SCSpec.build(inter_irreps, layer_hidden, corr[t], 1 if agnostic else num_elements),
                 prod_linear=LinearSpec.build(layer_hidden, layer_hidden),
                 readout_nonlinear=(t == T - 1),
                 density=density,
@@ -447,9 +449,9 @@ class ModelSpec:
             q = f"products.{lay.index}"
             for c, out in enumerate(lay.sc.outputs):
                 cp = f"{q}.symmetric_contractions.contractions.{c}"
-                s[f"{cp}.weights_max"] = (self.num_elements, out.num_params[-1], lay.sc.C)
+                s[f"{cp}.weights_max"] = (lay.sc.num_elements, out.num_params[-1], lay.sc.C)
                 for j, nu in enumerate(range(out.correlation - 1, 0, -1)):
-                    s[f"{cp}.weights.{j}"] = (self.num_elements, out.num_params[nu - 1], lay.sc.C)
+                    s[f"{cp}.weights.{j}"] = (lay.sc.num_elements, out.num_params[nu - 1], lay.sc.C)
             for k, sh in enumerate(lay.prod_linear.weight_shapes()):
                 s[f"{q}.linear.weights.{k}"] = sh
             r = f"readouts.{lay.index}"

@@ -82,6 +82,7 @@ def random_config(
     distance_transform: dict | None = None,
     pair_repulsion: dict | None = None,
     heads: list[str] | None = None,
+    use_agnostic_product: bool = False,
 ) -> dict:
     """A converted-model config.  ``use_density_normalization``,
     ``distance_transform`` (Agnesi; ``{}`` for the defaults) and
@@ -115,6 +116,8 @@ def random_config(
         pr = dict(ZBL_DEFAULTS)
         pr.update(pair_repulsion)
         extra["pair_repulsion"] = pr
+    if use_agnostic_product:
+        extra["use_agnostic_product"] = True
     if heads is not None and len(heads) > 1:
         extra["heads"] = [str(h) for h in heads]
         if atomic_energies is None:

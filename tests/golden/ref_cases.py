@@ -83,6 +83,9 @@ CASES = {
                                           heads=["pt_head", "Default"],
                                           atomic_energies=[[-5.1, -7.9], [-5.4, -8.1]],
                                           model_type="ScaleShiftMACE", edit=_scale_shift_per_head),
+    # the species-agnostic product (one symmetric-contraction weight set), two species, with stress
+    "agnostic_medium_si64mixed": lambda: _case("medium", _mixed_si(12), 12, True, z_table=[14, 6], avg=30.0,
+                                               use_agnostic_product=True),
     # BASELINE config 1 (the headline) at its full size: medium Si1000, energy + forces
     "c1_medium_si1000": lambda: _case("medium", diamond_si(5, 0.05, 1), 1, False, avg=44.0),
 }

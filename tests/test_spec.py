@@ -76,7 +76,7 @@ def test_check_weights_reports_mismatch():
 
 def test_unsupported_features_raise():
     cfg = random_config("small")
-    for key, val in [("use_agnostic_product", True), ("apply_cutoff", False),
+    for key, val in [("apply_cutoff", False),
                      ("interaction_cls", "RealAgnosticResidualNonLinearInteractionBlock")]:
         c = dict(cfg, **{key: val})
         with pytest.raises(UnsupportedModel):
@@ -164,6 +164,46 @@ def test_masked_multi_head_readout_equals_the_sliced_single_head_model():
     single = OracleMACE(one, w1).compute(st.positions, sp, i, j, S, st.cell, stress=True)
     for k in ("energy", "node_energy", "forces", "stress"):
         np.testing.assert_allclose(multi[k], single[k], rtol=1e-10, atol=1e-12)
+
+
+def test_agnostic_product_layout_and_replicated_tables():
+    """use_agnostic_product: symmetric-contraction weights of one element
+    (model.py:250-258); the packed polynomial tables repeat them per element."""
+    from mace_mlx_b200.pack import PackedModel
+
+    cfg = random_config("medium", z_table=[14, 6, 8], use_agnostic_product=True)
+    sp = ModelSpec.from_config(cfg)
+    shapes = sp.weight_shapes()
+    assert shapes["products.0.symmetric_contractions.contractions.0.weights_max"][0] == 1
+    assert shapes["products.1.symmetric_contractions.contractions.0.weights.0"][0] == 1
+    assert shapes["interactions.0.skip_tp.tp.weights.0"][1] == 3  # the skip stays species-indexed
+    pm = PackedModel(sp, random_weights(sp, 1))
+    so = pm.desc.layers[0].sc[0]
+    G = pm.floats[so.f_G:so.f_G + 3 * so.n_ent * sp.C].reshape(3, so.n_ent, sp.C)
+    np.testing.assert_array_equal(G[0], G[1])
+    np.testing.assert_array_equal(G[0], G[2])
+
+
+def test_agnostic_product_equals_replicated_species_weights():
+    """In the float64 oracle, the agnostic product (all-ones node attributes,
+    blocks.py:527-531) equals the element-indexed product whose weights repeat
+    the single set for every element."""
+    from mace_mlx_b200.structures import diamond_si
+    from oracle.model import OracleMACE
+    from oracle.nl import neighbour_list
+
+    cfg = random_config("small", z_table=[14, 6], use_agnostic_product=True, avg_num_neighbors=20.0)
+    w = random_weights(ModelSpec.from_config(cfg), 6)
+    st = diamond_si(1, 0.05, 4)
+    st.numbers[::2] = 6
+    i, j, S = neighbour_list(st.positions, st.cell, st.pbc, cfg["r_max"])
+    sp = np.where(st.numbers == 14, 0, 1)
+    plain = {k: v for k, v in cfg.items() if k != "use_agnostic_product"}
+    w2 = {k: (np.repeat(v, 2, axis=0) if ".symmetric_contractions." in k else v) for k, v in w.items()}
+    a = OracleMACE(cfg, w).compute(st.positions, sp, i, j, S, st.cell, stress=True)
+    b = OracleMACE(plain, w2).compute(st.positions, sp, i, j, S, st.cell, stress=True)
+    for k in ("energy", "node_energy", "forces", "stress"):
+        np.testing.assert_allclose(a[k], b[k], rtol=1e-10, atol=1e-12)
 
 
 def test_unknown_head_raises_before_any_device_work():
