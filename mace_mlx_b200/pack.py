@@ -391,6 +391,10 @@ class PackedModel:
             raise UnsupportedModel("max_ell above 3 is not supported")
         if spec.num_interactions > nv.MAX_LAYERS:
             raise UnsupportedModel("too many interaction layers")
+        if any(lay.nonlinear is not None for lay in spec.layers):
+            raise UnsupportedModel("the mh-1 non-linear interaction block has no CUDA path")
+        if not spec.apply_cutoff:
+            raise UnsupportedModel("apply_cutoff=False models have no CUDA path")
         tb = _Tables()
         d = nv.ModelDesc()
         d.abi_version = nv.ABI_VERSION

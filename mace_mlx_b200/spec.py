@@ -38,7 +38,9 @@ from .cg import U_matrix_real, wigner_3j
 from .elements import AGNESI_DEFAULTS, COVALENT_RADII, ZBL_DEFAULTS
 from .irreps import Irrep, Irreps
 
+NONLINEAR_INTERACTION = "RealAgnosticResidualNonLinearInteractionBlock"
 SUPPORTED_INTERACTIONS = (
+    NONLINEAR_INTERACTION,
     "RealAgnosticResidualInteractionBlock",
     "RealAgnosticInteractionBlock",
     "RealAgnosticDensityInteractionBlock",
@@ -231,12 +233,34 @@ class SCSpec:
 
 
 @dataclass
+class NonLinearSpec:
+    """The mh-1 family's RealAgnosticResidualNonLinearInteractionBlock
+    (``blocks.py:611-807``): species embeddings concatenated to the radial
+    features, radial MLPs with biases and LayerNorm (``radial.py:344-357``), a
+    density MLP normalising the message by ``density * beta + alpha``, a
+    residual ``linear_res`` of ``linear_up``'s output, an equivariant gate
+    (``gate.py``) and ``linear_2``; ``skip_tp`` is a plain linear."""
+
+    edge_irreps: Irreps
+    C0: int  # scalar channels of the block's input (width of each species embedding)
+    aug_dim: int  # num_bessel + 2 C0: the radial MLPs' input
+    embed: LinearSpec  # one-hot (num_elements x 0e) -> C0 x 0e, source and target
+    skip_lin: LinearSpec  # irreps_in -> hidden
+    linear_res: LinearSpec  # edge_irreps -> gate input
+    linear_2: LinearSpec  # irreps_out -> irreps_out
+    gate_scalars: Irreps
+    gate_gates: Irreps
+    gate_gated: Irreps
+    density_widths: list[int]  # [aug_dim, 64, 1]
+
+
+@dataclass
 class LayerSpec:
     index: int
     irreps_in: Irreps
     hidden: Irreps  # product output irreps of this layer
     residual: bool
-    skip: SkipSpec
+    skip: SkipSpec | None  # None for the non-linear block (its skip is ``nonlinear.skip_lin``)
     linear_up: LinearSpec
     conv: ConvSpec
     mlp_widths: list[int]  # [num_bessel, *radial_MLP, weight_numel]
@@ -248,6 +272,78 @@ class LayerSpec:
     readout_linear: LinearSpec | None = None  # linear readout (not last)
     readout_1: LinearSpec | None = None  # nonlinear readout
     readout_2: LinearSpec | None = None
+    nonlinear: NonLinearSpec | None = None  # mh-1 non-linear interaction block
+
+
+def _add_readouts(lay: LayerSpec, t: int, T: int, layer_hidden: Irreps, H: int) -> None:
+    lay.readout_nonlinear = t == T - 1
+    if t < T - 1:
+        lay.readout_linear = LinearSpec.build(layer_hidden, Irreps(f"{H}x0e"))
+    else:
+        # 16 hidden scalars per head (model.py:135-138)
+        lay.readout_1 = LinearSpec.build(layer_hidden, Irreps(f"{16 * H}x0e"))
+        lay.readout_2 = LinearSpec.build(Irreps(f"{16 * H}x0e"), Irreps(f"{H}x0e"))
+
+
+def _nonlinear_layer(t: int, layer_in: Irreps, layer_hidden: Irreps, edge: Irreps, sh: Irreps,
+                     inter_irreps: Irreps, num_bessel: int, radial_MLP: list[int], num_elements: int,
+                     correlation: int, sc_elements: int) -> LayerSpec:
+    """One non-linear interaction block (blocks.py:628-743): gate irreps split
+    from irreps_out (scalars; one gate scalar block per non-scalar block; the
+    non-scalars), every linear of the block, the augmented radial-MLP input."""
+    C0 = layer_in.count("0e")
+    scal = Irreps([m for m in inter_irreps if m.ir.l == 0])
+    gated = Irreps([m for m in inter_irreps if m.ir.l > 0])
+    gates = Irreps([(m.mul, "0e") for m in gated])
+    nonlin = Irreps(list(scal) + list(gates) + list(gated))
+    conv = ConvSpec.build(edge, sh, inter_irreps)
+    aug = num_bessel + 2 * C0
+    nl = NonLinearSpec(
+        edge_irreps=edge, C0=C0, aug_dim=aug,
+        embed=LinearSpec.build(Irreps(f"{num_elements}x0e"), Irreps(f"{C0}x0e")),
+        skip_lin=LinearSpec.build(layer_in, layer_hidden),
+        linear_res=LinearSpec.build(edge, nonlin),
+        linear_2=LinearSpec.build(inter_irreps, inter_irreps),
+        gate_scalars=scal, gate_gates=gates, gate_gated=gated,
+        density_widths=[aug, 64, 1],
+    )
+    return LayerSpec(
+        index=t, irreps_in=layer_in, hidden=layer_hidden, residual=True, skip=None,
+        linear_up=LinearSpec.build(layer_in, edge), conv=conv,
+        mlp_widths=[aug, *radial_MLP, conv.weight_numel],
+        linear=LinearSpec.build(conv.irreps_mid, nonlin),  # linear_1
+        sc=SCSpec.build(inter_irreps, layer_hidden, correlation, sc_elements),
+        prod_linear=LinearSpec.build(layer_hidden, layer_hidden),
+        readout_nonlinear=False, nonlinear=nl,
+    )
+
+
+def _radial_mlp_ln_shapes(prefix: str, widths: list[int]) -> dict:
+    """Linear(bias) -> LayerNorm -> SiLU stacks (radial.py:344-357): module
+    index 3 j for the j-th Linear, 3 j + 1 for its LayerNorm."""
+    s = {}
+    for j in range(len(widths) - 1):
+        s[f"{prefix}.layers.{3 * j}.weight"] = (widths[j + 1], widths[j])
+        s[f"{prefix}.layers.{3 * j}.bias"] = (widths[j + 1],)
+        if j < len(widths) - 2:
+            s[f"{prefix}.layers.{3 * j + 1}.weight"] = (widths[j + 1],)
+            s[f"{prefix}.layers.{3 * j + 1}.bias"] = (widths[j + 1],)
+    return s
+
+
+def _nonlinear_weight_shapes(lay: LayerSpec, p: str) -> dict:
+    """The non-linear block's arrays besides linear_up (converter.py:677-780)."""
+    nl = lay.nonlinear
+    s: dict[str, tuple[int, ...]] = {}
+    for name, lin in (("source_embedding", nl.embed), ("target_embedding", nl.embed), ("skip_tp", nl.skip_lin),
+                      ("linear_res", nl.linear_res), ("linear_1", lay.linear), ("linear_2", nl.linear_2)):
+        for k, sh in enumerate(lin.weight_shapes()):
+            s[f"{p}.{name}.weights.{k}"] = sh
+    s.update(_radial_mlp_ln_shapes(f"{p}.conv_tp_weights", lay.mlp_widths))
+    s.update(_radial_mlp_ln_shapes(f"{p}.density_fn", nl.density_widths))
+    s[f"{p}.alpha"] = ()
+    s[f"{p}.beta"] = ()
+    return s
 
 
 def resolve_head(heads: list[str], head: str | None) -> int:
@@ -294,6 +390,7 @@ class ModelSpec:
     density: bool = False
     agnesi: dict | None = None  # {"q", "p", "a", "covalent_radii" (indexed by Z)}
     zbl: dict | None = None  # {"p", "a_exp", "a_prefactor", "covalent_radii" (indexed by Z)}
+    apply_cutoff: bool = True
     heads: list[str] = field(default_factory=lambda: ["Default"])
     head_idx: int = 0  # the selected head; scale / shift above are already that head's
 
@@ -340,8 +437,9 @@ class ModelSpec:
             zbl["covalent_radii"] = list(COVALENT_RADII)
         # species-agnostic product: one symmetric-contraction weight set (model.py:250-258)
         agnostic = bool(cfg.get("use_agnostic_product", False))
-        if cfg.get("apply_cutoff", True) is False:
-            raise UnsupportedModel("apply_cutoff=False models are not supported yet")
+        # apply_cutoff=False: the envelope multiplies the radial-MLP output and
+        # the edge densities instead of the Bessel features (radial.py:313-317)
+        apply_cutoff = bool(cfg.get("apply_cutoff", True))
         heads = [str(h) for h in (cfg.get("heads") or ["Default"])]
         head_idx = resolve_head(heads, head)
         inter_cls = cfg.get("interaction_cls", "RealAgnosticResidualInteractionBlock")
@@ -384,15 +482,26 @@ class ModelSpec:
             model_type=model_type, scale=_per_head(cfg.get("scale", 1.0), head_idx),
             shift=_per_head(cfg.get("shift", 0.0), head_idx), z_table=cfg.get("z_table"),
             atomic_energies=ae, irreps_sh=sh, interaction_irreps=inter_irreps,
-            density=density, agnesi=agnesi, zbl=zbl, heads=heads, head_idx=head_idx,
+            density=density, agnesi=agnesi, zbl=zbl, heads=heads, head_idx=head_idx, apply_cutoff=apply_cutoff,
         )
         if (agnesi or zbl) and spec.z_table is None:
             raise UnsupportedModel("the distance transform / pair repulsion need the config's z_table")
 
         H = len(heads)
         layer_in = hidden_scalar
+        nonlinear = inter_cls == NONLINEAR_INTERACTION
+        edge_cfg = Irreps(cfg["edge_irreps"]) if cfg.get("edge_irreps") else None
         for t in range(T):
             layer_hidden = hidden if t < T - 1 else hidden_scalar
+            if nonlinear:
+                # the first layer keeps the scalar part of edge_irreps (model.py:192-211)
+                edge = (edge_cfg.scalars() if t == 0 else edge_cfg) if edge_cfg is not None else layer_in
+                spec.layers.append(_nonlinear_layer(t, layer_in, layer_hidden, edge, sh, inter_irreps, num_bessel,
+                                                    radial_MLP, num_elements, corr[t],
+                                                    1 if agnostic else num_elements))
+                _add_readouts(spec.layers[-1], t, T, layer_hidden, H)
+                layer_in = layer_hidden
+                continue
             residual = not (t == 0 and first_nonres)
             if residual:
                 skip = SkipSpec.build(layer_in, num_elements, layer_hidden)
@@ -414,12 +523,7 @@ class ModelSpec:
                 readout_nonlinear=(t == T - 1),
                 density=density,
             )
-            if t < T - 1:
-                lay.readout_linear = LinearSpec.build(layer_hidden, Irreps(f"{H}x0e"))
-            else:
-                # 16 hidden scalars per head (model.py:135-138)
-                lay.readout_1 = LinearSpec.build(layer_hidden, Irreps(f"{16 * H}x0e"))
-                lay.readout_2 = LinearSpec.build(Irreps(f"{16 * H}x0e"), Irreps(f"{H}x0e"))
+            _add_readouts(lay, t, T, layer_hidden, H)
             spec.layers.append(lay)
             layer_in = layer_hidden
         return spec
@@ -437,6 +541,10 @@ class ModelSpec:
             p = f"interactions.{lay.index}"
             for k, sh in enumerate(lay.linear_up.weight_shapes()):
                 s[f"{p}.linear_up.weights.{k}"] = sh
+            if lay.nonlinear is not None:
+                s.update(_nonlinear_weight_shapes(lay, p))
+                self._product_readout_shapes(lay, s)
+                continue
             w = lay.mlp_widths
             for j in range(len(w) - 1):
                 s[f"{p}.conv_tp_weights.layers.{2 * j}.weight"] = (w[j + 1], w[j])
@@ -446,21 +554,25 @@ class ModelSpec:
                 s[f"{p}.linear.weights.{k}"] = sh
             for k, sh in enumerate(lay.skip.weight_shapes()):
                 s[f"{p}.skip_tp.tp.weights.{k}"] = sh
-            q = f"products.{lay.index}"
-            for c, out in enumerate(lay.sc.outputs):
-                cp = f"{q}.symmetric_contractions.contractions.{c}"
-                s[f"{cp}.weights_max"] = (lay.sc.num_elements, out.num_params[-1], lay.sc.C)
-                for j, nu in enumerate(range(out.correlation - 1, 0, -1)):
-                    s[f"{cp}.weights.{j}"] = (lay.sc.num_elements, out.num_params[nu - 1], lay.sc.C)
-            for k, sh in enumerate(lay.prod_linear.weight_shapes()):
-                s[f"{q}.linear.weights.{k}"] = sh
-            r = f"readouts.{lay.index}"
-            if lay.readout_linear is not None:
-                for k, sh in enumerate(lay.readout_linear.weight_shapes()):
-                    s[f"{r}.linear.weights.{k}"] = sh
-            else:
-                for k, sh in enumerate(lay.readout_1.weight_shapes()):
-                    s[f"{r}.linear_1.weights.{k}"] = sh
-                for k, sh in enumerate(lay.readout_2.weight_shapes()):
-                    s[f"{r}.linear_2.weights.{k}"] = sh
+            self._product_readout_shapes(lay, s)
         return s
+
+    @staticmethod
+    def _product_readout_shapes(lay: LayerSpec, s: dict) -> None:
+        q = f"products.{lay.index}"
+        for c, out in enumerate(lay.sc.outputs):
+            cp = f"{q}.symmetric_contractions.contractions.{c}"
+            s[f"{cp}.weights_max"] = (lay.sc.num_elements, out.num_params[-1], lay.sc.C)
+            for j, nu in enumerate(range(out.correlation - 1, 0, -1)):
+                s[f"{cp}.weights.{j}"] = (lay.sc.num_elements, out.num_params[nu - 1], lay.sc.C)
+        for k, sh in enumerate(lay.prod_linear.weight_shapes()):
+            s[f"{q}.linear.weights.{k}"] = sh
+        r = f"readouts.{lay.index}"
+        if lay.readout_linear is not None:
+            for k, sh in enumerate(lay.readout_linear.weight_shapes()):
+                s[f"{r}.linear.weights.{k}"] = sh
+        else:
+            for k, sh in enumerate(lay.readout_1.weight_shapes()):
+                s[f"{r}.linear_1.weights.{k}"] = sh
+            for k, sh in enumerate(lay.readout_2.weight_shapes()):
+                s[f"{r}.linear_2.weights.{k}"] = sh

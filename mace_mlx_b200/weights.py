@@ -83,13 +83,19 @@ def random_config(
     pair_repulsion: dict | None = None,
     heads: list[str] | None = None,
     use_agnostic_product: bool = False,
+    nonlinear_interaction: bool = False,
+    edge_irreps: str | None = None,
+    apply_cutoff: bool = True,
 ) -> dict:
     """A converted-model config.  ``use_density_normalization``,
     ``distance_transform`` (Agnesi; ``{}`` for the defaults) and
     ``pair_repulsion`` (ZBL; ``{}`` for the defaults) give the mpa-0 family's
     blocks; ``heads`` (two or more names) a multi-head model, whose
     ``atomic_energies`` are then one row per head.  The converter's key
-    layout is kept (``converter.py:167-300``)."""
+    layout is kept (``converter.py:167-300``).  ``nonlinear_interaction``
+    selects the mh-1 family's non-linear interaction block (with
+    ``edge_irreps``); ``apply_cutoff=False`` moves the envelope from the radial
+    features to the radial-MLP output and the edge densities."""
     hidden = hidden_irreps or ARCHS[arch]
     if z_table is None:
         z_table = list(range(1, num_elements + 1))
@@ -100,7 +106,13 @@ def random_config(
     else:
         inter_cls = "RealAgnosticInteractionBlock" if first_interaction_nonresidual else \
             "RealAgnosticResidualInteractionBlock"
+    if nonlinear_interaction:
+        inter_cls = "RealAgnosticResidualNonLinearInteractionBlock"
     extra = {}
+    if edge_irreps is not None:
+        extra["edge_irreps"] = str(edge_irreps)
+    if not apply_cutoff:
+        extra["apply_cutoff"] = False
     if use_density_normalization:
         extra["use_density_normalization"] = True
     if distance_transform is not None:
@@ -144,10 +156,37 @@ def random_config(
     }
 
 
+def _nonlinear_block_array(key: str, shape, rng) -> np.ndarray | None:
+    """Seeded values for the non-linear block's own arrays: torch's Linear
+    scale (fan-in) for the radial MLPs, LayerNorm gains near one, small biases,
+    and alpha / beta around the block's initial 20 / 0 with beta made non-zero
+    so that the density term is exercised."""
+    if key.endswith(".alpha"):
+        return np.asarray(rng.uniform(8.0, 20.0), dtype=np.float32)
+    if key.endswith(".beta"):
+        return np.asarray(rng.uniform(0.3, 1.0), dtype=np.float32)
+    if ".conv_tp_weights.layers." in key or ".density_fn.layers." in key:
+        idx = int(key.rsplit(".layers.", 1)[1].split(".")[0])
+        if idx % 3 == 0:  # Linear
+            if key.endswith(".weight"):
+                return (rng.standard_normal(shape) / np.sqrt(shape[1])).astype(np.float32)
+            return (0.1 * rng.standard_normal(shape)).astype(np.float32)
+        if key.endswith(".weight"):  # LayerNorm gain
+            return (1.0 + 0.1 * rng.standard_normal(shape)).astype(np.float32)
+        return (0.1 * rng.standard_normal(shape)).astype(np.float32)
+    return None
+
+
 def random_weights(spec: ModelSpec, seed: int) -> dict[str, np.ndarray]:
     rng = np.random.default_rng(seed)
     out: dict[str, np.ndarray] = {}
+    nonlinear = {lay.index for lay in spec.layers if lay.nonlinear is not None}
     for key, shape in spec.weight_shapes().items():
+        if key.startswith("interactions.") and int(key.split(".")[1]) in nonlinear:
+            v = _nonlinear_block_array(key, shape, rng)
+            if v is not None:
+                out[key] = v
+                continue
         if key == "atomic_energies_fn.atomic_energies":
             out[key] = np.asarray(spec.atomic_energies, dtype=np.float32)
         elif key.endswith("bessel_weights"):

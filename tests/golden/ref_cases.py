@@ -86,13 +86,29 @@ CASES = {
     # the species-agnostic product (one symmetric-contraction weight set), two species, with stress
     "agnostic_medium_si64mixed": lambda: _case("medium", _mixed_si(12), 12, True, z_table=[14, 6], avg=30.0,
                                                use_agnostic_product=True),
+    # the mh-1 family's shape: non-linear interaction blocks (edge irreps up to 2e), the
+    # agnostic product, the envelope on the radial-MLP output (apply_cutoff=False) and two
+    # heads with the second one selected; two species, with stress
+    "mh1_medium_si64mixed": lambda: _case("medium", _mixed_si(13), 13, True, z_table=[14, 6], avg=30.0,
+                                          nonlinear_interaction=True, edge_irreps="128x0e + 128x1o + 128x2e",
+                                          use_agnostic_product=True, apply_cutoff=False,
+                                          heads=["pt_head", "Default"],
+                                          atomic_energies=[[-5.1, -7.9], [-5.4, -8.1]],
+                                          model_type="ScaleShiftMACE", edit=_scale_shift_per_head),
+    # apply_cutoff=False with the standard residual blocks
+    "nocutoff_small_si64": lambda: _case("small", diamond_si(2, 0.05, 14), 14, True, z_table=[14],
+                                         apply_cutoff=False),
     # BASELINE config 1 (the headline) at its full size: medium Si1000, energy + forces
     "c1_medium_si1000": lambda: _case("medium", diamond_si(5, 0.05, 1), 1, False, avg=44.0),
 }
 
 
+# cases whose blocks the oracle restates but the CUDA path refuses (pack.py raises
+# UnsupportedModel): the mh-1 non-linear block and apply_cutoff=False
+NO_CUDA_PATH = ("mh1_medium_si64mixed", "nocutoff_small_si64")
+
 # the head each multi-head case selects (the reference calculator's ``head`` argument)
-CASE_HEADS = {"mh2_medium_si64mixed": "Default"}
+CASE_HEADS = {"mh2_medium_si64mixed": "Default", "mh1_medium_si64mixed": "Default"}
 
 
 def digest_config(config: dict) -> str:

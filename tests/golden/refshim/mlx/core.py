@@ -117,15 +117,20 @@ def _torch_dtype(d):
 # --------------------------------------------------------------------------
 # conversion helpers
 # --------------------------------------------------------------------------
+def _contig(a: np.ndarray) -> np.ndarray:
+    # a C-ordered copy that keeps 0-d arrays 0-d (np.ascontiguousarray makes them 1-d)
+    return a if a.flags.c_contiguous else a.copy(order="C")
+
+
 def _np_to_torch(a: np.ndarray) -> torch.Tensor:
     if a.dtype.kind == "f":
-        return torch.from_numpy(np.ascontiguousarray(a)).to(_F)
+        return torch.from_numpy(_contig(a)).to(_F)
     if a.dtype.kind == "b":
-        return torch.from_numpy(np.ascontiguousarray(a))
+        return torch.from_numpy(_contig(a))
     if a.dtype.kind in "iu":
         if a.dtype == np.uint32 or a.dtype == np.uint64:
             a = a.astype(np.int64)
-        return torch.from_numpy(np.ascontiguousarray(a))
+        return torch.from_numpy(_contig(a))
     raise TypeError(f"unsupported numpy dtype {a.dtype}")
 
 

@@ -14,7 +14,7 @@ import numpy as np
 import pytest
 import torch
 
-from golden.ref_cases import CASE_HEADS, CASES, digest_config, digest_weights
+from golden.ref_cases import CASE_HEADS, CASES, NO_CUDA_PATH, digest_config, digest_weights
 from oracle.model import OracleMACE
 from oracle.nl import neighbour_list
 
@@ -86,3 +86,13 @@ def test_reference_float32_run_is_within_tolerance_of_its_float64_run(golden_dir
     assert np.abs(fx["forces_f32"] - fx["forces"]).max() < 1e-4
     if bool(fx["stress_computed"]):
         assert np.abs(fx["stress_f32"] - fx["stress"]).max() < 1e-6
+
+
+@pytest.mark.parametrize("name", NO_CUDA_PATH)
+def test_cases_without_a_cuda_path_are_refused_when_packed(name):
+    from mace_mlx_b200.pack import PackedModel
+    from mace_mlx_b200.spec import ModelSpec, UnsupportedModel
+
+    config, weights, _, _ = CASES[name]()
+    with pytest.raises(UnsupportedModel, match="no CUDA path"):
+        PackedModel(ModelSpec.from_config(config, head=CASE_HEADS.get(name)), weights)

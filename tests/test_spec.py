@@ -75,12 +75,39 @@ def test_check_weights_reports_mismatch():
 
 
 def test_unsupported_features_raise():
-    cfg = random_config("small")
-    for key, val in [("apply_cutoff", False),
-                     ("interaction_cls", "RealAgnosticResidualNonLinearInteractionBlock")]:
-        c = dict(cfg, **{key: val})
+    """The spec (and so the oracle) reads the mh-1 block and apply_cutoff=False;
+    the CUDA path refuses both when the model is packed, and the spec refuses
+    an unknown interaction block and other gates."""
+    from mace_mlx_b200.pack import PackedModel
+
+    for kw in (dict(apply_cutoff=False), dict(nonlinear_interaction=True)):
+        cfg = random_config("small", z_table=[14], **kw)
+        sp = ModelSpec.from_config(cfg)
+        with pytest.raises(UnsupportedModel, match="no CUDA path"):
+            PackedModel(sp, random_weights(sp, 0))
+    for key, val in [("interaction_cls", "SomeOtherInteractionBlock"), ("gate", "tanh")]:
         with pytest.raises(UnsupportedModel):
-            ModelSpec.from_config(c)
+            ModelSpec.from_config(dict(random_config("small"), **{key: val}))
+
+
+def test_nonlinear_block_layout():
+    """mh-1 layout (blocks.py:628-743, model.py:192-211, converter.py:677-822):
+    scalar-only edge irreps in the first layer, gate input = scalars + one gate
+    block per non-scalar block + non-scalars, radial-MLP input num_bessel + 2 C,
+    LayerNorm MLP module indices 0/1/3/4/..., alpha and beta scalars."""
+    cfg = random_config("medium", z_table=[14, 6], nonlinear_interaction=True, edge_irreps="128x0e + 128x1o + 128x2e")
+    sp = ModelSpec.from_config(cfg)
+    l0, l1 = sp.layers
+    assert str(l0.nonlinear.edge_irreps) == "128x0e" and str(l1.nonlinear.edge_irreps) == "128x0e + 128x1o + 128x2e"
+    assert str(l1.linear.irreps_out) == "128x0e + 128x0e + 128x0e + 128x0e + 128x1o + 128x2e + 128x3o"
+    assert l0.mlp_widths[0] == sp.num_bessel + 2 * 128 and l0.nonlinear.density_widths == [l0.mlp_widths[0], 64, 1]
+    shapes = sp.weight_shapes()
+    assert shapes["interactions.0.conv_tp_weights.layers.9.weight"] == (l0.conv.weight_numel, 64)
+    assert shapes["interactions.0.conv_tp_weights.layers.7.bias"] == (64,)
+    assert shapes["interactions.1.density_fn.layers.3.weight"] == (1, 64)
+    assert shapes["interactions.1.source_embedding.weights.0"] == (2, 128)
+    assert shapes["interactions.1.alpha"] == () and "interactions.1.skip_tp.tp.weights.0" not in shapes
+    check_weights(sp, random_weights(sp, 0))
 
 
 def test_multi_head_spec_shapes_and_head_selection():
