@@ -95,6 +95,10 @@ CASES = {
                                           heads=["pt_head", "Default"],
                                           atomic_energies=[[-5.1, -7.9], [-5.4, -8.1]],
                                           model_type="ScaleShiftMACE", edit=_scale_shift_per_head),
+    # the non-linear block alone: large arch, edge irreps left to the block's input,
+    # species-indexed product, envelope on the radial features; four species, with stress
+    "nonlinear_large_lipso300": lambda: _case("large", lipso_box(300, 2), 15, True, z_table=[3, 8, 15, 16],
+                                              avg=50.0, nonlinear_interaction=True),
     # apply_cutoff=False with the standard residual blocks
     "nocutoff_small_si64": lambda: _case("small", diamond_si(2, 0.05, 14), 14, True, z_table=[14],
                                          apply_cutoff=False),
@@ -105,7 +109,7 @@ CASES = {
 
 # cases whose blocks the oracle restates but the CUDA path refuses (pack.py raises
 # UnsupportedModel): the mh-1 non-linear block and apply_cutoff=False
-NO_CUDA_PATH = ("mh1_medium_si64mixed", "nocutoff_small_si64")
+NO_CUDA_PATH = ("mh1_medium_si64mixed", "nonlinear_large_lipso300", "nocutoff_small_si64")
 
 # the head each multi-head case selects (the reference calculator's ``head`` argument)
 CASE_HEADS = {"mh2_medium_si64mixed": "Default", "mh1_medium_si64mixed": "Default"}

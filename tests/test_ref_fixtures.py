@@ -79,10 +79,14 @@ def test_oracle_equals_the_reference_execution(golden_dir, name):
 @pytest.mark.parametrize("name", list(CASES))
 def test_reference_float32_run_is_within_tolerance_of_its_float64_run(golden_dir, name):
     """The reference's own fp32 execution differs from its fp64 execution by
-    far less than the parity tolerances, so the fp64 fixtures are the pin."""
+    far less than the parity tolerances, so the fp64 fixtures are the pin.
+    The energy bound is 1e-6 eV/atom, or 1e-6 of the mean per-atom energy
+    where that is larger (fp32 rounding grows with the magnitude: the random
+    non-linear-block model on LiPSO-300 carries ~4 eV per atom)."""
     fx = load_fixture(golden_dir, name)
     n = len(fx["numbers"])
-    assert np.abs(fx["energy_f32"] - fx["energy"]).max() / n < 1e-6
+    e_scale = float(np.abs(fx["node_energy"]).mean())
+    assert np.abs(fx["energy_f32"] - fx["energy"]).max() / n < max(1e-6, 1e-6 * e_scale)
     assert np.abs(fx["forces_f32"] - fx["forces"]).max() < 1e-4
     if bool(fx["stress_computed"]):
         assert np.abs(fx["stress_f32"] - fx["stress"]).max() < 1e-6
