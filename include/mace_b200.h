@@ -51,7 +51,7 @@ extern "C" {
 #define MACE_ERR_UNSUPPORTED 6
 #define MACE_ERR_EDGES 7
 
-#define MACE_ABI_VERSION 7
+#define MACE_ABI_VERSION 8
 
 /* limits of the packed model description */
 #define MACE_MAX_LAYERS 4
@@ -200,6 +200,11 @@ typedef struct {
   float zbl_a_exp, zbl_a_prefactor;
   int64_t f_radius_zbl;           /* (num_elements) covalent radius per element index */
   int64_t f_znum;                 /* (num_elements) atomic number per element index (float) */
+  /* 1: apply_cutoff=False models (reference radial.py:294-321, blocks.py:163-164):
+   * the polynomial envelope multiplies each edge's radial-MLP output instead of
+   * its Bessel features; not combined with density-normalised layers */
+  int32_t envelope_on_weights;
+  int32_t reserved0;
   const float* floats; int64_t n_floats;    /* host pointers, copied at create */
   const int32_t* ints; int64_t n_ints;
 } mace_model_desc;

@@ -62,6 +62,10 @@ struct EdgeParams {
   float* v;               // (E,3)
   float* Y;               // (E,16)
   float* b;               // (E,nb)
+  // envelope_on_weights models: b holds the bare Bessel features, the envelope
+  // goes to cut (forward) and dcut is dE/d(envelope) (backward); else both null
+  float* cut;             // (E)
+  const float* dcut;      // (E)
   // backward
   const float* dY;  // (E,16)
   const float* db;  // (E,nb)
@@ -229,6 +233,11 @@ struct MlpParams {
   const float* tc_trunk;     // hidden 64 x 64 layers 1.., forward operands
   const float* tc_trunk_bwd; // the same, backward operands
   int* err_flag;             // set to 2 when a bounded wait gives up
+  // envelope_on_weights models (else null): the forward scales edge e's output
+  // row by cut[e]; the backward first adds dE/d(cut[e]) = (dout . out)[e] / cut[e]
+  // into dcut[e] and scales dout's row by cut[e] (both relative to this launch's edges)
+  const float* cut;
+  float* dcut;
 };
 int launch_mlp_fwd(const MlpParams& p, cudaStream_t s);
 int launch_mlp_bwd(const MlpParams& p, cudaStream_t s);

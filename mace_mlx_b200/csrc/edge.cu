@@ -142,10 +142,13 @@ __global__ void k_edge_fwd(EdgeParams p) {
   env = (x < 1.0f) ? env : 0.0f;
   float drt;
   const float rb = bessel_arg(p, e, g.r, &drt);
+  // envelope on the features, or (envelope_on_weights) kept for the radial-MLP output
+  const float bscale = p.cut ? 1.0f : env;
+  if (p.cut) p.cut[e] = env;
   for (int n = 0; n < p.nb; ++n) {
     float w = __ldg(p.bessel_w + n);
     float bes = pref * sinf(w * rb) / rb;
-    p.b[(int64_t)p.nb * e + n] = bes * env;
+    p.b[(int64_t)p.nb * e + n] = bes * bscale;
   }
 }
 
@@ -230,7 +233,12 @@ __global__ void k_edge_bwd(EdgeParams p) {
       for (int n = 0; n < p.nb; ++n) dbn[n] = fmaf(gx, __ldg(wd + n), dbn[n]);
     }
     float dr = 0.f;
-    for (int n = 0; n < p.nb; ++n) dr += dbn[n] * (dbes[n] * env + bes[n] * denv);
+    if (p.dcut) {  // b = bare Bessel features; the envelope scaled the radial-MLP output
+      for (int n = 0; n < p.nb; ++n) dr += dbn[n] * dbes[n];
+      dr = fmaf(p.dcut[e], denv, dr);
+    } else {
+      for (int n = 0; n < p.nb; ++n) dr += dbn[n] * (dbes[n] * env + bes[n] * denv);
+    }
     if (p.zbl) {
       const int s_n = p.snd[e], r_n = p.rcv[e];
       const int zs = p.species[s_n], zr = p.species[r_n];

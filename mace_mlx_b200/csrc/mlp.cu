@@ -213,10 +213,55 @@ int check_mlp(const MlpParams& p) {
   return MACE_OK;
 }
 
-}  // namespace
+// apply_cutoff=False models (reference blocks.py:163-164, radial.py:313-317):
+// the envelope multiplies the radial-MLP output, w_e = cut_e * MLP(b_e).  One
+// warp per edge walks the edge's row of the tiled output (lane j takes the
+// columns j, j + 32, ...; each 32-column step is one 128-byte line).
+__global__ void k_cut_scale(float* out, const float* cut, int64_t E, int W, int nch) {
+  const int64_t e = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (e >= E) return;
+  const float c = cut[e];
+  for (int k = lane; k < W; k += 32) out[wt_index(e, k, nch)] *= c;
+}
 
-int launch_mlp_fwd(const MlpParams& p, cudaStream_t s) {
-  if (p.E == 0) return MACE_OK;
+// Backward of the scaling: dE/dcut_e = sum_k dw[e][k] * w_raw[e][k] with
+// w_raw = w / cut_e (an edge whose envelope is 0 has dcut/dr = 0 as well, so
+// it adds nothing), accumulated over layers into dcut; then dw[e] *= cut_e,
+// the gradient the MLP backward takes.  Fixed shuffle tree: deterministic.
+__global__ void k_cut_bwd(float* dout, const float* out, const float* cut, float* dcut, int64_t E, int W, int nch) {
+  const int64_t e = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (e >= E) return;
+  const float c = cut[e];
+  float acc = 0.f;
+  for (int k = lane; k < W; k += 32) {
+    const int64_t i = wt_index(e, k, nch);
+    const float g = dout[i];
+    acc = fmaf(g, out[i], acc);
+    dout[i] = g * c;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (lane == 0 && c > 0.f) dcut[e] += acc / c;
+}
+
+int cut_scale(const MlpParams& p, cudaStream_t s) {
+  const int W = p.widths[p.n_layers];
+  k_cut_scale<<<(unsigned)((p.E * 32 + 255) / 256), 256, 0, s>>>(p.out, p.cut, p.E, W, wt_nchunk(W));
+  MACE_LAUNCH_CHECK("mlp_cut_scale");
+  return MACE_OK;
+}
+
+int cut_bwd(const MlpParams& p, cudaStream_t s) {
+  const int W = p.widths[p.n_layers];
+  k_cut_bwd<<<(unsigned)((p.E * 32 + 255) / 256), 256, 0, s>>>(const_cast<float*>(p.dout), p.out, p.cut, p.dcut,
+                                                               p.E, W, wt_nchunk(W));
+  MACE_LAUNCH_CHECK("mlp_cut_bwd");
+  return MACE_OK;
+}
+
+int mlp_fwd_any(const MlpParams& p, cudaStream_t s) {
   if (mlp_tc_supported(p)) return launch_mlp_fwd_tc(p, s);
   int rc = check_mlp(p);
   if (rc) return rc;
@@ -227,8 +272,21 @@ int launch_mlp_fwd(const MlpParams& p, cudaStream_t s) {
   }
 }
 
+}  // namespace
+
+int launch_mlp_fwd(const MlpParams& p, cudaStream_t s) {
+  if (p.E == 0) return MACE_OK;
+  int rc = mlp_fwd_any(p, s);
+  if (rc || !p.cut) return rc;
+  return cut_scale(p, s);
+}
+
 int launch_mlp_bwd(const MlpParams& p, cudaStream_t s) {
   if (p.E == 0) return MACE_OK;
+  if (p.cut) {
+    int rc = cut_bwd(p, s);
+    if (rc) return rc;
+  }
   if (mlp_tc_supported(p)) return launch_mlp_bwd_tc(p, s);
   int rc = check_mlp(p);
   if (rc) return rc;

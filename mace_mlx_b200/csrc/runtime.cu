@@ -76,6 +76,7 @@ struct mace_ctx {
   // edge buffers
   float *v = nullptr, *Y = nullptr, *b = nullptr, *dY = nullptr, *db = nullptr, *dv = nullptr,
         *dw = nullptr;
+  float *cut = nullptr, *dcut = nullptr;  // (E) envelope and its gradient (envelope_on_weights models)
   double* vir_part = nullptr;
   // node buffers
   std::vector<float*> h;   // h[t], t = 0..T   (N, row_t)
@@ -272,6 +273,11 @@ int reserve(mace_ctx* c, int64_t N, int64_t E, int64_t EC) {
   TRY(alloc(c, &c->dY, E * 16));
   TRY(alloc(c, &c->db, E * d.num_bessel));
   TRY(alloc(c, &c->dv, E * 3));
+  c->cut = c->dcut = nullptr;
+  if (d.envelope_on_weights) {
+    TRY(alloc(c, &c->cut, E));
+    TRY(alloc(c, &c->dcut, E));
+  }
   TRY(alloc(c, &c->dw, wt_floats(EC, wmax)));
   // padding rows of the last edge tile are read (never used) by the MLP backward
   if (cudaMemset(c->dw, 0, (size_t)wt_floats(EC, wmax) * sizeof(float)) != cudaSuccess ||
@@ -446,6 +452,10 @@ MlpParams mlp_params(mace_ctx* c, int t, int64_t e0, int64_t ne) {
   p.out = c->lb[t].w;
   p.dout = c->dw_layer[t] ? c->dw_layer[t] : c->dw;
   p.db = c->db + e0 * c->desc.num_bessel;
+  if (c->desc.envelope_on_weights) {
+    p.cut = c->cut + e0;
+    p.dcut = c->dcut + e0;
+  }
   const bool tc_ok = !c->mlp_cuda_cores && L.f_mlp_tc >= 0 && L.f_mlp_tc_bwd >= 0 && L.f_mlp_tc_trunk >= 0 &&
                      L.f_mlp_tc_trunk_bwd >= 0;
   p.tc_img = tc_ok ? F(c, L.f_mlp_tc) : nullptr;
@@ -634,6 +644,8 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
   ep.dY = c->dY;
   ep.db = c->db;
   ep.dv = c->dv;
+  ep.cut = d.envelope_on_weights ? c->cut : nullptr;
+  ep.dcut = d.envelope_on_weights ? c->dcut : nullptr;
   ep.virial_part = (flags & MACE_WANT_VIRIAL) ? c->vir_part : nullptr;
   ep.species = sys->species;
   ep.agnesi = d.agnesi;
@@ -862,6 +874,7 @@ int forward_backward(mace_ctx* c, const mace_system* sys, const mace_outputs* ou
   if (E > 0) {
     MACE_CUDA_TRY(cudaMemsetAsync(c->dY, 0, sizeof(float) * E * 16, s));
     MACE_CUDA_TRY(cudaMemsetAsync(c->db, 0, sizeof(float) * E * d.num_bessel, s));
+    if (d.envelope_on_weights) MACE_CUDA_TRY(cudaMemsetAsync(c->dcut, 0, sizeof(float) * E, s));
   }
   for (int t = T - 1; t >= 0; --t) {
     const mace_layer_desc& L = d.layers[t];
@@ -1231,6 +1244,11 @@ int mace_ctx_create(const mace_model_desc* desc, int device, mace_ctx** out) {
     return fail(MACE_ERR_UNSUPPORTED, "number of interaction layers out of range");
   if (desc->max_ell < 0 || desc->max_ell > 3) return fail(MACE_ERR_UNSUPPORTED, "max_ell must be <= 3");
   if (desc->C % 32 != 0 || desc->C > 128) return fail(MACE_ERR_UNSUPPORTED, "channels must be 32, 64, 96 or 128");
+  if (desc->envelope_on_weights) {
+    for (int t = 0; t < desc->num_layers; ++t)
+      if (desc->layers[t].density)
+        return fail(MACE_ERR_UNSUPPORTED, "envelope_on_weights with density-normalised layers is not supported");
+  }
   int ndev = 0;
   if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev)
     return fail(MACE_ERR_CUDA, "no such CUDA device");

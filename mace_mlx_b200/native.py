@@ -19,7 +19,7 @@ MACE_ERR_TIMEOUT = 4
 MACE_ERR_NCCL = 5
 MACE_ERR_UNSUPPORTED = 6
 MACE_ERR_EDGES = 7
-ABI_VERSION = 7
+ABI_VERSION = 8
 
 MAX_LAYERS = 4
 MAX_IN = 4
@@ -89,6 +89,7 @@ class ModelDesc(C.Structure):
         ("agnesi", i32), ("agnesi_q", f32), ("agnesi_p", f32), ("agnesi_a", f32), ("f_radius_agnesi", i64),
         ("zbl", i32), ("zbl_p", i32), ("zbl_a_exp", f32), ("zbl_a_prefactor", f32),
         ("f_radius_zbl", i64), ("f_znum", i64),
+        ("envelope_on_weights", i32), ("reserved0", i32),
         ("floats", C.POINTER(f32)), ("n_floats", i64),
         ("ints", C.POINTER(i32)), ("n_ints", i64),
     ]

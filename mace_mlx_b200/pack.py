@@ -393,8 +393,8 @@ class PackedModel:
             raise UnsupportedModel("too many interaction layers")
         if any(lay.nonlinear is not None for lay in spec.layers):
             raise UnsupportedModel("the mh-1 non-linear interaction block has no CUDA path")
-        if not spec.apply_cutoff:
-            raise UnsupportedModel("apply_cutoff=False models have no CUDA path")
+        if not spec.apply_cutoff and any(lay.density for lay in spec.layers):
+            raise UnsupportedModel("apply_cutoff=False with density-normalised blocks has no CUDA path")
         tb = _Tables()
         d = nv.ModelDesc()
         d.abi_version = nv.ABI_VERSION
@@ -404,6 +404,7 @@ class PackedModel:
         d.max_ell = spec.max_ell
         d.poly_p = spec.poly_p
         d.scale_shift = int(spec.model_type == "ScaleShiftMACE")
+        d.envelope_on_weights = int(not spec.apply_cutoff)
         d.C = spec.C
         d.r_max = spec.r_max
         d.inv_avg_num_neighbors = 1.0 / spec.avg_num_neighbors

@@ -108,8 +108,8 @@ CASES = {
 
 
 # cases whose blocks the oracle restates but the CUDA path refuses (pack.py raises
-# UnsupportedModel): the mh-1 non-linear block and apply_cutoff=False
-NO_CUDA_PATH = ("mh1_medium_si64mixed", "nonlinear_large_lipso300", "nocutoff_small_si64")
+# UnsupportedModel): the mh-1 non-linear block
+NO_CUDA_PATH = ("mh1_medium_si64mixed", "nonlinear_large_lipso300")
 
 # the head each multi-head case selects (the reference calculator's ``head`` argument)
 CASE_HEADS = {"mh2_medium_si64mixed": "Default", "mh1_medium_si64mixed": "Default"}

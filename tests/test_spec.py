@@ -75,16 +75,19 @@ def test_check_weights_reports_mismatch():
 
 
 def test_unsupported_features_raise():
-    """The spec (and so the oracle) reads the mh-1 block and apply_cutoff=False;
-    the CUDA path refuses both when the model is packed, and the spec refuses
-    an unknown interaction block and other gates."""
+    """The spec (and so the oracle) reads the mh-1 block and apply_cutoff=False
+    with density-normalised blocks; the CUDA path refuses both when the model
+    is packed (apply_cutoff=False alone packs, with the envelope flag set), and
+    the spec refuses an unknown interaction block and other gates."""
     from mace_mlx_b200.pack import PackedModel
 
-    for kw in (dict(apply_cutoff=False), dict(nonlinear_interaction=True)):
+    for kw in (dict(apply_cutoff=False, use_density_normalization=True), dict(nonlinear_interaction=True)):
         cfg = random_config("small", z_table=[14], **kw)
         sp = ModelSpec.from_config(cfg)
         with pytest.raises(UnsupportedModel, match="no CUDA path"):
             PackedModel(sp, random_weights(sp, 0))
+    sp = ModelSpec.from_config(random_config("small", z_table=[14], apply_cutoff=False))
+    assert PackedModel(sp, random_weights(sp, 0)).desc.envelope_on_weights == 1
     for key, val in [("interaction_cls", "SomeOtherInteractionBlock"), ("gate", "tanh")]:
         with pytest.raises(UnsupportedModel):
             ModelSpec.from_config(dict(random_config("small"), **{key: val}))
